@@ -1,0 +1,102 @@
+// Shared device helpers for the androidllm B200 kernels (sm_100a).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define ALM_DEV __device__ __forceinline__
+
+namespace alm {
+
+constexpr int kWarp = 32;
+#define kNegInf (-__int_as_float(0x7f800000))
+
+// ---------------------------------------------------------------------------
+// loads
+// ---------------------------------------------------------------------------
+// Weights are streamed once per forward: read-only path, no L1 allocation.
+ALM_DEV uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+ALM_DEV uint32_t ld_nc_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
+// Programmatic dependent launch: wait for the producer grid's results / let
+// the next grid in the stream start its prologue.  No-ops without PDL.
+ALM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ALM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---------------------------------------------------------------------------
+// bit tricks for int4/int8 -> fp16 (exact small integers)
+// ---------------------------------------------------------------------------
+// (a & b) | c in one LOP3.
+ALM_DEV uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+ALM_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+ALM_DEV uint32_t h2u(half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+ALM_DEV half2 u2h(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
+
+// ---------------------------------------------------------------------------
+// tensor core: D = A(16x16, row) * B(16x8, col) + D, fp16 in, fp32 accumulate
+// A regs: {a0a1: (g, 2t..2t+1)} {a2a3: (g+8, 2t..)} {a4a5: (g, 2t+8..)} {a6a7: (g+8, 2t+8..)}
+// B regs: {b0b1: (k=2t..2t+1, n=g)} {b2b3: (k=2t+8.., n=g)}
+// D: {d0,d1: (g, 2t..2t+1)} {d2,d3: (g+8, 2t..2t+1)}        g = lane/4, t = lane%4
+// ---------------------------------------------------------------------------
+ALM_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                      uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+ALM_DEV void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+ALM_DEV void ldmatrix_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1) : "r"(a));
+}
+ALM_DEV void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, const void* p) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1) : "r"(a));
+}
+
+// fp32 arithmetic with no contraction, so results match numpy's separately
+// rounded operations.
+ALM_DEV float fmul(float a, float b) { return __fmul_rn(a, b); }
+ALM_DEV float fadd(float a, float b) { return __fadd_rn(a, b); }
+ALM_DEV float fsub(float a, float b) { return __fsub_rn(a, b); }
+ALM_DEV float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+ALM_DEV float round_h(float a) { return __half2float(__float2half_rn(a)); }
+
+ALM_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+ALM_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace alm

@@ -1,0 +1,151 @@
+// Internal kernel interfaces shared by the .cu files of libandroidllm_b200.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace alm {
+
+// Largest number of activation rows (tokens) one forward processes.
+constexpr int kMaxRows = 16;
+// Attention position chunk and row group.
+constexpr int kAttnChunk = 64;
+constexpr int kAttnRows = 16;
+// Superchunk of positions the P.V kernel stages in shared memory at once.
+constexpr int kPvSpan = 1024;
+
+// ---------------------------------------------------------------------------
+// Tiled quantized weight ("qtile" layout).
+//
+// Rows are grouped in tiles of 16, columns in k-blocks of 64.  For each
+// (tile, kblock) the 32 lanes of a warp hold exactly the m16n8k16 A fragments
+// of four k16 steps, so one coalesced 512 B (int4) / 1 KB (int8) / 2 KB
+// (fp16) warp load feeds 4 tensor-core MMAs with no shuffles:
+//   int4: lane word s (s = k16 step) = nibbles
+//         [(g,c) (g+8,c) (g,c+8) (g+8,c+8) (g,c+1) (g+8,c+1) (g,c+9) (g+8,c+9)]
+//         with c = 16 s + 2 t, each stored offset-binary (q + 8);
+//   int8: lane words 2s, 2s+1 = bytes [(g,c) (g,c+1) (g,c+8) (g,c+9)] and the
+//         same for row g+8, offset-binary (q + 128); the two 16 B halves of a
+//         lane are stored 512 B apart so each is a coalesced warp load;
+//   fp16: lane uint4 s = the four A registers of step s.
+// Scales: per (tile, scale block) eight half2 {s(g), s(g+8)}, g = 0..7.
+// ---------------------------------------------------------------------------
+struct QTile {
+  const uint4* data = nullptr;
+  const half2* scales = nullptr;
+  int bits = 4;       // 4, 8 or 16 (fp16, no scales)
+  int block = 64;     // scale block along K (32 or a multiple of 64)
+  int n_rows = 0;     // logical output rows
+  int n_tiles = 0;    // ceil(n_rows / 16)
+  int k_blocks = 0;   // ceil(k_pad / 64)
+  int nsb = 0;        // scale blocks per tile row group
+  int k_real = 0;     // real input length (activation columns)
+  // split-K launch shape
+  int ksw = 1;        // warps splitting K inside a CTA (1, 2, 4, 8)
+  int ksg = 1;        // CTAs splitting K
+  int kps = 1;        // k-blocks per split
+  unsigned* counters = nullptr;  // one per CTA column, self-resetting
+};
+
+// An activation operand: either raw fp16 rows, or the un-normalised residual
+// sum of the previous layer with its RMSNorm still to apply:
+//   x = fp16((f32(v) / sqrt(sum(ss[m, :]) / H + eps)) * f32(w))
+// where ss holds per-16-row-tile partial sums of squares written by the
+// producing kernel (fixed order, so the result is independent of M).
+struct ActIn {
+  const half* x = nullptr;
+  int ld = 0;
+  const float* ss = nullptr;
+  int n_ss = 0;
+  const half* w = nullptr;
+  float eps = 0.f;
+  int H = 0;
+};
+
+enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+
+struct Epi {
+  half* out = nullptr;   // STORE / RESID / SWIGLU / LOGITS output rows
+  int ldo = 0;
+  int n_out = 0;         // valid output columns (rows of W, or I for SwiGLU)
+  // QKV: q (fp32) and the paged K/V cache of one layer
+  float* q = nullptr;
+  int ldq = 0;
+  half* kcache = nullptr;
+  half* vcache = nullptr;
+  const int* page_table = nullptr;
+  int page_size = 16;
+  int heads = 0, kv_heads = 0, head_dim = 0;
+  const half* rope = nullptr;   // (max_len, head_dim) fp16 [cos | sin]
+  // RESID
+  ActIn res;
+  float* ss_out = nullptr;      // (M, n_tiles) partial sums of squares
+  // LOGITS: per-CTA argmax partials (M, gridDim.x)
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+};
+
+struct StepIO {
+  const int* pos = nullptr;     // device: position of activation row 0
+};
+
+// Scratch for cross-CTA split-K partial sums.
+struct SplitScratch {
+  float* part = nullptr;
+  size_t part_floats = 0;
+};
+
+// Set per-kernel shared-memory limits on the current device (once per
+// device, before any launch or stream capture).
+cudaError_t gemv_init_attrs();
+cudaError_t attention_init_attrs();
+cudaError_t rows_init_attrs();
+
+// launchers (return cudaError_t of the launch)
+cudaError_t launch_repack(const void* const* src, const half* const* src_scales, int n_src,
+                          const int* dst_src_row, QTile& w, uint4* data, half2* scales,
+                          int k_pad, cudaStream_t st);
+cudaError_t launch_dequant(const QTile& w, half* out, cudaStream_t st);
+cudaError_t launch_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
+                        const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st);
+
+struct AttnArgs {
+  const float* q = nullptr;  int ldq = 0;
+  const half* kcache = nullptr;
+  const half* vcache = nullptr;
+  const int* page_table = nullptr;
+  int page_size = 16;
+  int heads = 0, kv_heads = 0, head_dim = 0;
+  int M = 1;
+  const int* pos = nullptr;
+  int max_ctx = 0;           // capacity: grid sized for this many positions
+  float* scores = nullptr;   // (kv_heads, n_rg, 16, score_ld)
+  int score_ld = 0;
+  float* stats = nullptr;    // (kv_heads, n_rg, n_chunks_max, 16, 2)
+  half* ctx = nullptr;       // (M, heads * head_dim)
+  int ldc = 0;
+};
+cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
+
+// embedding gather: x0[m] = dequant(embed[token_m])
+struct EmbedArgs {
+  const void* table = nullptr;   // int4 packed / int8 / fp16 rows
+  const half* scale = nullptr;   // (vocab, nsb) or null for fp16
+  int bits = 16, block = 0, nsb = 0, hidden = 0, row_bytes = 0, vocab = 0;
+  const int* tokens = nullptr;   // (M) device
+  half* out = nullptr;           // (M, hidden)
+  int M = 1;
+  int* err = nullptr;            // set to 1 on an out-of-range token
+};
+cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
+
+// out[m] = fp16(rmsnorm(x_m)) where x is an ActIn (possibly deferred-norm),
+// optionally followed by a second RMSNorm with weight w2 (the final norm).
+cudaError_t launch_rownorm(const ActIn& in, int M, const half* w2, float eps2, half* out,
+                           int ldo, bool pdl, cudaStream_t st);
+
+// argmax over CTA partials -> tokens (M)
+cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_part, int M,
+                                int* out, bool pdl, cudaStream_t st);
+
+}  // namespace alm

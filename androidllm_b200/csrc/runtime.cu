@@ -1,0 +1,1229 @@
+// C ABI of libandroidllm_b200: contexts, weights, models, paged KV cache,
+// forward passes and the graph-replayed speculative step.
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/androidllm_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace alm {
+cudaError_t launch_spec_prep_draft(const int* state, int* cand, const int* d_argmax, int i, int* tokens,
+                                   int* pos, cudaStream_t st);
+cudaError_t launch_spec_prep_verify(const int* state, int* cand, const int* d_argmax, int k, int* tokens,
+                                    int* pos, cudaStream_t st);
+cudaError_t launch_spec_accept_greedy(int* state, const int* cand, const int* t_argmax, int k, int* out_tokens,
+                                      int* out_accepted, int cap_tokens, int cap_steps, cudaStream_t st);
+}  // namespace alm
+
+using namespace alm;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define ALM_CUDA(expr)                                                                         \
+  do {                                                                                         \
+    cudaError_t e_ = (expr);                                                                   \
+    if (e_ != cudaSuccess) return fail(ALM_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+#define ALM_REQ(cond, msg)                    \
+  do {                                        \
+    if (!(cond)) return fail(ALM_ERR_ARG, msg); \
+  } while (0)
+#define ALM_TRY(expr)        \
+  do {                       \
+    int rc_ = (expr);        \
+    if (rc_ != ALM_OK) return rc_; \
+  } while (0)
+
+int n_sms_of(int device) {
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  return n;
+}
+
+int pow2_floor(int v) {
+  int p = 1;
+  while (p * 2 <= v) p *= 2;
+  return p;
+}
+int pow2_ceil(int v) {
+  int p = 1;
+  while (p < v) p *= 2;
+  return p;
+}
+
+// Split-K shape for a weight: enough warps to cover the SMs, at least a few
+// k-blocks per warp, power-of-two splits, x staging within shared memory.
+void choose_split(QTile& t, int n_sms) {
+  const int kps_min = t.bits == 4 ? 6 : t.bits == 8 ? 3 : 2;
+  const int want = n_sms * 16;
+  const int s_max = pow2_floor(std::max(1, t.k_blocks / kps_min));
+  int s = pow2_ceil(std::max(1, (want + t.n_tiles - 1) / t.n_tiles));
+  s = std::min(s, s_max);
+  t.ksw = std::min(s, 8);
+  t.ksg = s / t.ksw;
+  t.kps = (t.k_blocks + s - 1) / s;
+  while (t.ksw * t.kps > 80 && t.ksw > 1) {   // keep x staging <= 160 KB at M = 16
+    t.ksw /= 2;
+    t.ksg *= 2;
+  }
+  t.ksg = std::max(1, (((t.k_blocks + t.kps - 1) / t.kps) + t.ksw - 1) / t.ksw);
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------
+// objects
+// ----------------------------------------------------------------------------
+struct alm_ctx {
+  int device = 0;
+  int n_sms = 148;
+  cudaStream_t stream = nullptr;
+};
+
+struct alm_qweight {
+  alm_ctx* ctx = nullptr;
+  QTile t;
+  uint4* data = nullptr;
+  half2* scales = nullptr;
+  unsigned* counters = nullptr;
+  int out = 0, in = 0, in_real = 0;
+};
+
+namespace {
+
+struct Layer {
+  alm_qweight* qkv = nullptr;
+  alm_qweight* o = nullptr;
+  alm_qweight* gu = nullptr;
+  alm_qweight* down = nullptr;
+  half* n_in = nullptr;
+  half* n_post = nullptr;
+};
+
+struct Work {
+  int* tokens = nullptr;
+  int* pos = nullptr;
+  int* err = nullptr;
+  half* x0 = nullptr;
+  half* s1 = nullptr;
+  half* s2 = nullptr;
+  float* ss1 = nullptr;
+  float* ss2 = nullptr;
+  float* q = nullptr;
+  half* ctx = nullptr;
+  half* h = nullptr;
+  half* xn = nullptr;
+  half* xout = nullptr;
+  half* logits = nullptr;
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+  int n_am = 0;
+  int* argmax = nullptr;
+  float* part = nullptr;
+  size_t part_floats = 0;
+  float* scores = nullptr;
+  float* stats = nullptr;
+  int attn_ctx = 0;       // capacity of the attention scratch (positions)
+  int* pinned = nullptr;  // host staging for small copies
+};
+
+int dev_alloc(void** p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  ALM_CUDA(cudaMalloc(p, bytes));
+  return ALM_OK;
+}
+template <typename T>
+int dev_alloc_t(T** p, size_t count) {
+  return dev_alloc(reinterpret_cast<void**>(p), count * sizeof(T));
+}
+void dev_free(void* p) {
+  if (p) cudaFree(p);
+}
+
+}  // namespace
+
+struct alm_model {
+  alm_ctx* ctx = nullptr;
+  alm_model_config cfg{};
+  half* rope = nullptr;
+  std::vector<Layer> layers;
+  void* embed_table = nullptr;
+  half* embed_scale = nullptr;
+  int embed_bits = 0, embed_block = 0, embed_nsb = 0, embed_row_bytes = 0;
+  alm_qweight* head = nullptr;   // owned
+  half* final_norm = nullptr;
+  bool finalized = false;
+  Work ws;
+};
+
+struct alm_kv {
+  alm_ctx* ctx = nullptr;
+  int n_layers = 0, kv_heads = 0, head_dim = 0, page_size = 16, n_pages = 0, max_len = 0;
+  size_t layer_elems = 0;
+  half* k = nullptr;
+  half* v = nullptr;
+  int* page_table = nullptr;
+};
+
+struct alm_spec {
+  alm_model* target = nullptr;
+  alm_model* draft = nullptr;
+  alm_kv* tkv = nullptr;
+  alm_kv* dkv = nullptr;
+  int k = 0;
+  int* state = nullptr;      // device [4]
+  int* cand = nullptr;       // device [k]
+  int* out_tokens = nullptr; // device ring
+  int* out_acc = nullptr;
+  int cap_steps = 0, cap_tokens = 0;
+  cudaGraphExec_t graph = nullptr;
+  int* pinned = nullptr;     // host: 4 + cap_tokens + cap_steps
+};
+
+namespace {
+
+struct DeviceGuard {
+  explicit DeviceGuard(int d) { cudaSetDevice(d); }
+};
+
+// --------------------------------------------------------------------------
+// weight building
+// --------------------------------------------------------------------------
+size_t src_bytes(int bits, int rows, int k_pad) {
+  return bits == 4 ? static_cast<size_t>(rows) * k_pad / 2
+                   : bits == 8 ? static_cast<size_t>(rows) * k_pad : static_cast<size_t>(rows) * k_pad * 2;
+}
+
+int check_format(int bits, int block, int in, int in_real) {
+  ALM_REQ(bits == 4 || bits == 8 || bits == 16, "bits must be 4, 8 or 16");
+  ALM_REQ(in > 0 && in_real > 0 && in_real <= in, "invalid in / in_real");
+  if (bits != 16) {
+    ALM_REQ(block == 32 || (block > 0 && block % 64 == 0), "block must be 32 or a multiple of 64");
+    ALM_REQ(in % block == 0, "in must be a multiple of block");
+  }
+  if (bits == 4) ALM_REQ(in % 2 == 0, "int4 rows need an even length");
+  return ALM_OK;
+}
+
+// Build one qtile weight from up to 3 sources with a destination row map
+// (dst row -> (src << 24) | src row, or -1).
+int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::vector<int>& dst_map,
+                  int n_rows, alm_qweight** out) {
+  const int bits = srcs[0].bits, block = srcs[0].block, in = srcs[0].in, in_real = srcs[0].in_real;
+  for (int i = 0; i < n_src; ++i) {
+    ALM_TRY(check_format(srcs[i].bits, srcs[i].block, srcs[i].in, srcs[i].in_real));
+    ALM_REQ(srcs[i].bits == bits && srcs[i].in == in && srcs[i].in_real == in_real &&
+                (bits == 16 || srcs[i].block == block),
+            "fused projections must share bits, block and input size");
+    ALM_REQ(srcs[i].packed_host != nullptr && (bits == 16 || srcs[i].scale_host != nullptr),
+            "missing weight data");
+  }
+  auto* w = new alm_qweight();
+  w->ctx = ctx;
+  w->out = n_rows;
+  w->in = in;
+  w->in_real = in_real;
+  QTile& t = w->t;
+  t.bits = bits;
+  t.block = bits == 16 ? 64 : block;
+  t.n_rows = n_rows;
+  t.n_tiles = (n_rows + 15) / 16;
+  t.k_blocks = (in + 63) / 64;
+  t.nsb = bits == 16 ? 0 : (block == 32 ? 2 * t.k_blocks : in / block);
+  t.k_real = in_real;
+  choose_split(t, ctx->n_sms);
+
+  const int vec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
+  std::vector<void*> tmp;
+  auto cleanup = [&]() {
+    for (void* p : tmp) cudaFree(p);
+  };
+  int rc = ALM_OK;
+  const void* dsrc[3] = {nullptr, nullptr, nullptr};
+  const half* dscale[3] = {nullptr, nullptr, nullptr};
+  int* dmap = nullptr;
+  do {
+    if ((rc = dev_alloc_t(&w->data, static_cast<size_t>(t.n_tiles) * t.k_blocks * vec * kWarp)) != ALM_OK) break;
+    if (bits != 16 &&
+        (rc = dev_alloc_t(&w->scales, static_cast<size_t>(t.n_tiles) * t.nsb * 8)) != ALM_OK)
+      break;
+    for (int i = 0; i < n_src && rc == ALM_OK; ++i) {
+      void* p = nullptr;
+      const size_t nb = src_bytes(bits, srcs[i].out, in);
+      if ((rc = dev_alloc(&p, nb)) != ALM_OK) break;
+      tmp.push_back(p);
+      if (cudaMemcpy(p, srcs[i].packed_host, nb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        rc = fail(ALM_ERR_CUDA, "weight upload failed");
+        break;
+      }
+      dsrc[i] = p;
+      if (bits != 16) {
+        void* s = nullptr;
+        const size_t sb = static_cast<size_t>(srcs[i].out) * (in / block) * sizeof(half);
+        if ((rc = dev_alloc(&s, sb)) != ALM_OK) break;
+        tmp.push_back(s);
+        if (cudaMemcpy(s, srcs[i].scale_host, sb, cudaMemcpyHostToDevice) != cudaSuccess) {
+          rc = fail(ALM_ERR_CUDA, "scale upload failed");
+          break;
+        }
+        dscale[i] = static_cast<const half*>(s);
+      }
+    }
+    if (rc != ALM_OK) break;
+    if ((rc = dev_alloc_t(&dmap, dst_map.size())) != ALM_OK) break;
+    tmp.push_back(dmap);
+    if (cudaMemcpy(dmap, dst_map.data(), dst_map.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, "row map upload failed");
+      break;
+    }
+    cudaError_t e = launch_repack(dsrc, dscale, n_src, dmap, t, w->data, w->scales, in, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, std::string("repack: ") + cudaGetErrorString(e));
+      break;
+    }
+    const int grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+    if ((rc = dev_alloc_t(&w->counters, grid_x)) != ALM_OK) break;
+    if (cudaMemset(w->counters, 0, grid_x * sizeof(unsigned)) != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, "counter init failed");
+      break;
+    }
+  } while (false);
+  cleanup();
+  if (rc != ALM_OK) {
+    alm_qweight_free(w);
+    return rc;
+  }
+  t.data = w->data;
+  t.scales = w->scales;
+  t.counters = w->counters;
+  *out = w;
+  return ALM_OK;
+}
+
+std::vector<int> identity_map(int rows) {
+  std::vector<int> m((rows + 15) / 16 * 16, -1);
+  for (int r = 0; r < rows; ++r) m[r] = r;
+  return m;
+}
+
+// Split-K scratch large enough for weight w (floats).
+size_t split_need(const alm_qweight* w) {
+  if (!w || w->t.ksg <= 1) return 0;
+  return static_cast<size_t>(w->t.ksg) * (w->t.n_tiles + 8) * kWarp * 8;
+}
+
+int ensure_part(Work& ws, size_t need) {
+  if (need <= ws.part_floats) return ALM_OK;
+  dev_free(ws.part);
+  ws.part = nullptr;
+  ws.part_floats = 0;
+  ALM_TRY(dev_alloc_t(&ws.part, need));
+  ws.part_floats = need;
+  return ALM_OK;
+}
+
+int ensure_attn(alm_model* m, int max_ctx) {
+  Work& ws = m->ws;
+  if (max_ctx <= ws.attn_ctx) return ALM_OK;
+  const int gq = m->cfg.heads / m->cfg.kv_heads;
+  const int n_rg = (kMaxRows * gq + kAttnRows - 1) / kAttnRows;
+  const int cap = (max_ctx + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+  dev_free(ws.scores);
+  dev_free(ws.stats);
+  ws.scores = nullptr;
+  ws.stats = nullptr;
+  ws.attn_ctx = 0;
+  ALM_TRY(dev_alloc_t(&ws.scores, static_cast<size_t>(m->cfg.kv_heads) * n_rg * kAttnRows * cap));
+  ALM_TRY(dev_alloc_t(&ws.stats, static_cast<size_t>(m->cfg.kv_heads) * n_rg * (cap / kAttnChunk) * kAttnRows * 2));
+  ws.attn_ctx = cap;
+  return ALM_OK;
+}
+
+// --------------------------------------------------------------------------
+// forward enqueue (no host synchronisation)
+// --------------------------------------------------------------------------
+SplitScratch scratch_of(alm_model* m) { return SplitScratch{m->ws.part, m->ws.part_floats}; }
+
+int n_h_tiles(const alm_model* m) { return (m->cfg.hidden + 15) / 16; }
+
+ActIn raw_in(const half* x, int ld, int H) {
+  ActIn a;
+  a.x = x;
+  a.ld = ld;
+  a.H = H;
+  return a;
+}
+ActIn deferred_in(const alm_model* m, const half* s, const float* ss, const half* w) {
+  ActIn a;
+  a.x = s;
+  a.ld = m->cfg.hidden;
+  a.ss = ss;
+  a.n_ss = n_h_tiles(m);
+  a.w = w;
+  a.eps = m->cfg.rms_eps;
+  a.H = m->cfg.hidden;
+  return a;
+}
+
+#define ALM_LAUNCH(expr)                                                                             \
+  do {                                                                                               \
+    cudaError_t e_ = (expr);                                                                         \
+    if (e_ != cudaSuccess) return fail(ALM_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool pdl) {
+  const alm_model_config& c = m->cfg;
+  Layer& L = m->layers[li];
+  Work& ws = m->ws;
+  cudaStream_t st = m->ctx->stream;
+  StepIO io{ws.pos};
+  const SplitScratch scr = scratch_of(m);
+  const int qdim = c.heads * c.head_dim;
+
+  Epi e;
+  e.q = ws.q;
+  e.ldq = qdim;
+  e.kcache = kv->k + static_cast<size_t>(li) * kv->layer_elems;
+  e.vcache = kv->v + static_cast<size_t>(li) * kv->layer_elems;
+  e.page_table = kv->page_table;
+  e.page_size = kv->page_size;
+  e.heads = c.heads;
+  e.kv_heads = c.kv_heads;
+  e.head_dim = c.head_dim;
+  e.rope = m->rope;
+  ALM_LAUNCH(launch_gemv(L.qkv->t, in, M, EPI_QKV, e, io, scr, pdl, st));
+
+  AttnArgs a;
+  a.q = ws.q;
+  a.ldq = qdim;
+  a.kcache = e.kcache;
+  a.vcache = e.vcache;
+  a.page_table = kv->page_table;
+  a.page_size = kv->page_size;
+  a.heads = c.heads;
+  a.kv_heads = c.kv_heads;
+  a.head_dim = c.head_dim;
+  a.M = M;
+  a.pos = ws.pos;
+  a.max_ctx = kv->max_len;
+  a.scores = ws.scores;
+  a.score_ld = ws.attn_ctx;
+  a.stats = ws.stats;
+  a.ctx = ws.ctx;
+  a.ldc = qdim;
+  ALM_LAUNCH(launch_attention(a, pdl, st));
+
+  Epi eo;
+  eo.out = ws.s1;
+  eo.ldo = c.hidden;
+  eo.n_out = c.hidden;
+  eo.res = in;
+  eo.ss_out = ws.ss1;
+  ALM_LAUNCH(launch_gemv(L.o->t, raw_in(ws.ctx, qdim, qdim), M, EPI_RESID, eo, io, scr, pdl, st));
+
+  const ActIn n1 = deferred_in(m, ws.s1, ws.ss1, L.n_in);
+  Epi eg;
+  eg.out = ws.h;
+  eg.ldo = c.intermediate;
+  eg.n_out = c.intermediate;
+  ALM_LAUNCH(launch_gemv(L.gu->t, n1, M, EPI_SWIGLU, eg, io, scr, pdl, st));
+
+  Epi ed;
+  ed.out = ws.s2;
+  ed.ldo = c.hidden;
+  ed.n_out = c.hidden;
+  ed.res = n1;
+  ed.ss_out = ws.ss2;
+  ALM_LAUNCH(launch_gemv(L.down->t, raw_in(ws.h, c.intermediate, c.intermediate), M, EPI_RESID, ed, io, scr,
+                         pdl, st));
+  return ALM_OK;
+}
+
+// Head on normalised rows `x` (M, hidden) already in ws.xn.
+int enqueue_head(alm_model* m, int M, bool pdl) {
+  Work& ws = m->ws;
+  Epi e;
+  e.out = ws.logits;
+  e.ldo = m->cfg.vocab;
+  e.n_out = m->cfg.vocab;
+  e.am_val = ws.am_val;
+  e.am_idx = ws.am_idx;
+  const ActIn in = raw_in(ws.xn, m->cfg.hidden, m->cfg.hidden);
+  ALM_LAUNCH(launch_gemv(m->head->t, in, M, EPI_LOGITS, e, StepIO{ws.pos}, scratch_of(m), pdl, m->ctx->stream));
+  ALM_LAUNCH(launch_argmax_final(ws.am_val, ws.am_idx, ws.n_am, M, ws.argmax, pdl, m->ctx->stream));
+  return ALM_OK;
+}
+
+// Embedding (tokens already in ws.tokens, position in ws.pos) -> all layers ->
+// final norms -> head.
+int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
+  Work& ws = m->ws;
+  EmbedArgs ea;
+  ea.table = m->embed_table;
+  ea.scale = m->embed_scale;
+  ea.bits = m->embed_bits;
+  ea.block = m->embed_block;
+  ea.nsb = m->embed_nsb;
+  ea.hidden = m->cfg.hidden;
+  ea.row_bytes = m->embed_row_bytes;
+  ea.vocab = m->cfg.vocab;
+  ea.tokens = ws.tokens;
+  ea.out = ws.x0;
+  ea.M = M;
+  ea.err = ws.err;
+  ALM_LAUNCH(launch_embed(ea, pdl, m->ctx->stream));
+  ActIn in = raw_in(ws.x0, m->cfg.hidden, m->cfg.hidden);
+  for (int li = 0; li < m->cfg.layers; ++li) {
+    ALM_TRY(enqueue_layer(m, li, kv, M, in, pdl));
+    in = deferred_in(m, ws.s2, ws.ss2, m->layers[li].n_post);
+  }
+  if (!head) return ALM_OK;
+  ALM_LAUNCH(launch_rownorm(in, M, m->final_norm, m->cfg.rms_eps, ws.xn, m->cfg.hidden, pdl, m->ctx->stream));
+  return enqueue_head(m, M, pdl);
+}
+
+int check_ready(alm_model* m) {
+  ALM_REQ(m != nullptr, "null model");
+  if (!m->finalized) return fail(ALM_ERR_STATE, "model not finalized");
+  return ALM_OK;
+}
+
+int check_layers(alm_model* m) {
+  for (int i = 0; i < m->cfg.layers; ++i)
+    if (!m->layers[i].qkv) return fail(ALM_ERR_STATE, "layer " + std::to_string(i) + " not set");
+  return ALM_OK;
+}
+
+int check_kv(alm_model* m, alm_kv* kv, int rows, int pos0) {
+  ALM_REQ(kv != nullptr, "null kv");
+  ALM_REQ(kv->n_layers == m->cfg.layers && kv->kv_heads == m->cfg.kv_heads && kv->head_dim == m->cfg.head_dim,
+          "kv cache shape mismatch");
+  ALM_REQ(rows >= 1 && rows <= kMaxRows, "rows must be in 1..16");
+  ALM_REQ(pos0 >= 0 && pos0 + rows <= kv->max_len, "pos out of kv cache range");
+  ALM_REQ(pos0 + rows <= m->cfg.max_len, "pos out of rope table range");
+  return ensure_attn(m, kv->max_len);
+}
+
+int sync_and_check(alm_model* m) {
+  ALM_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  int err = 0;
+  ALM_CUDA(cudaMemcpy(&err, m->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) {
+    cudaMemset(m->ws.err, 0, sizeof(int));
+    return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
+  }
+  return ALM_OK;
+}
+
+int set_pos(alm_model* m, int pos0) {
+  m->ws.pinned[0] = pos0;
+  ALM_CUDA(cudaMemcpyAsync(m->ws.pos, m->ws.pinned, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  return ALM_OK;
+}
+
+int copy_logits_out(alm_model* m, int rows, float* logits_host, int32_t* argmax_host) {
+  cudaStream_t st = m->ctx->stream;
+  if (logits_host) {
+    std::vector<half> tmp(static_cast<size_t>(rows) * m->cfg.vocab);
+    ALM_CUDA(cudaMemcpyAsync(tmp.data(), m->ws.logits, tmp.size() * sizeof(half), cudaMemcpyDeviceToHost, st));
+    ALM_CUDA(cudaStreamSynchronize(st));
+    for (size_t i = 0; i < tmp.size(); ++i) logits_host[i] = __half2float(tmp[i]);
+  }
+  if (argmax_host) {
+    ALM_CUDA(cudaMemcpyAsync(argmax_host, m->ws.argmax, rows * sizeof(int), cudaMemcpyDeviceToHost, st));
+    ALM_CUDA(cudaStreamSynchronize(st));
+  }
+  return ALM_OK;
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+const char* alm_last_error(void) { return g_err.c_str(); }
+int alm_abi_version(void) { return 100; }
+
+int alm_ctx_create(int device, alm_ctx** out) {
+  ALM_REQ(out != nullptr, "null out");
+  int n = 0;
+  ALM_CUDA(cudaGetDeviceCount(&n));
+  ALM_REQ(device >= 0 && device < n, "no such CUDA device");
+  ALM_CUDA(cudaSetDevice(device));
+  {
+    cudaError_t e = gemv_init_attrs();
+    if (e == cudaSuccess) e = attention_init_attrs();
+    if (e == cudaSuccess) e = rows_init_attrs();
+    if (e != cudaSuccess) return fail(ALM_ERR_CUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
+  }
+  auto* c = new alm_ctx();
+  c->device = device;
+  c->n_sms = n_sms_of(device);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete c;
+    return fail(ALM_ERR_CUDA, "stream creation failed");
+  }
+  *out = c;
+  return ALM_OK;
+}
+
+int alm_ctx_destroy(alm_ctx* ctx) {
+  if (!ctx) return ALM_OK;
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return ALM_OK;
+}
+
+int alm_ctx_sync(alm_ctx* ctx) {
+  ALM_REQ(ctx, "null ctx");
+  DeviceGuard g(ctx->device);
+  ALM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return ALM_OK;
+}
+
+int alm_dev_alloc(alm_ctx* ctx, size_t bytes, void** out_dev) {
+  ALM_REQ(ctx && out_dev, "null argument");
+  DeviceGuard g(ctx->device);
+  return dev_alloc(out_dev, bytes);
+}
+int alm_dev_free(alm_ctx* ctx, void* dev) {
+  ALM_REQ(ctx, "null ctx");
+  DeviceGuard g(ctx->device);
+  ALM_CUDA(cudaFree(dev));
+  return ALM_OK;
+}
+int alm_copy_h2d(alm_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes) {
+  ALM_REQ(ctx && dst_dev && src_host, "null argument");
+  DeviceGuard g(ctx->device);
+  ALM_CUDA(cudaMemcpyAsync(dst_dev, src_host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return ALM_OK;
+}
+int alm_copy_d2h(alm_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes) {
+  ALM_REQ(ctx && dst_host && src_dev, "null argument");
+  DeviceGuard g(ctx->device);
+  ALM_CUDA(cudaMemcpyAsync(dst_host, src_dev, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return ALM_OK;
+}
+
+// ---- weights -----------------------------------------------------------------
+int alm_qweight_upload(alm_ctx* ctx, const void* packed_host, const void* scale_host, int bits, int block,
+                       int out, int in, int in_real, alm_qweight** w) {
+  ALM_REQ(ctx && w, "null argument");
+  ALM_REQ(out > 0, "out must be positive");
+  DeviceGuard g(ctx->device);
+  alm_proj_src s{packed_host, scale_host, bits, block, out, in, in_real};
+  return build_qweight(ctx, &s, 1, identity_map(out), out, w);
+}
+
+int alm_qweight_free(alm_qweight* w) {
+  if (!w) return ALM_OK;
+  DeviceGuard g(w->ctx->device);
+  dev_free(w->data);
+  dev_free(w->scales);
+  dev_free(w->counters);
+  delete w;
+  return ALM_OK;
+}
+
+int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host) {
+  ALM_REQ(ctx && w && out_host, "null argument");
+  DeviceGuard g(ctx->device);
+  half* d = nullptr;
+  const size_t n = static_cast<size_t>(w->out) * w->in_real;
+  ALM_TRY(dev_alloc_t(&d, n));
+  cudaError_t e = launch_dequant(w->t, d, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out_host, d, n * sizeof(half), cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(d);
+  if (e != cudaSuccess) return fail(ALM_ERR_CUDA, std::string("dequant: ") + cudaGetErrorString(e));
+  return ALM_OK;
+}
+
+int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m, uint16_t* y_dev,
+                int ldy) {
+  ALM_REQ(ctx && w && x_dev && y_dev, "null argument");
+  ALM_REQ(m >= 1 && m <= kMaxRows, "m must be in 1..16");
+  ALM_REQ(ldx >= w->in_real && ldy >= w->out, "leading dimension too small");
+  DeviceGuard g(ctx->device);
+  static thread_local std::vector<std::pair<alm_ctx*, std::pair<float*, size_t>>> scratch;
+  SplitScratch scr;
+  const size_t need = split_need(w);
+  if (need) {
+    std::pair<float*, size_t>* slot = nullptr;
+    for (auto& p : scratch)
+      if (p.first == ctx) slot = &p.second;
+    if (!slot) {
+      scratch.push_back({ctx, {nullptr, 0}});
+      slot = &scratch.back().second;
+    }
+    if (slot->second < need) {
+      dev_free(slot->first);
+      slot->first = nullptr;
+      slot->second = 0;
+      ALM_TRY(dev_alloc_t(&slot->first, need));
+      slot->second = need;
+    }
+    scr.part = slot->first;
+    scr.part_floats = slot->second;
+  }
+  Epi e;
+  e.out = reinterpret_cast<half*>(y_dev);
+  e.ldo = ldy;
+  e.n_out = w->out;
+  ActIn in = raw_in(reinterpret_cast<const half*>(x_dev), ldx, w->in_real);
+  ALM_CUDA(launch_gemv(w->t, in, m, EPI_STORE, e, StepIO{}, scr, false, ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return ALM_OK;
+}
+
+int alm_matmul_f16_f16(alm_ctx* ctx, const uint16_t* a_host, const uint16_t* b_host, uint16_t* out_host, int m,
+                       int k, int n) {
+  ALM_REQ(ctx && a_host && b_host && out_host, "null argument");
+  ALM_REQ(m >= 1 && m <= kMaxRows && k > 0 && n > 0, "shape out of range (m in 1..16)");
+  DeviceGuard g(ctx->device);
+  alm_qweight* w = nullptr;
+  ALM_TRY(alm_qweight_upload(ctx, b_host, nullptr, 16, 0, n, k, k, &w));
+  uint16_t *x = nullptr, *y = nullptr;
+  int rc = dev_alloc_t(&x, static_cast<size_t>(m) * k);
+  if (rc == ALM_OK) rc = dev_alloc_t(&y, static_cast<size_t>(m) * n);
+  if (rc == ALM_OK) rc = alm_copy_h2d(ctx, x, a_host, static_cast<size_t>(m) * k * 2);
+  if (rc == ALM_OK) rc = alm_qmatmul(ctx, w, x, k, m, y, n);
+  if (rc == ALM_OK) rc = alm_copy_d2h(ctx, out_host, y, static_cast<size_t>(m) * n * 2);
+  dev_free(x);
+  dev_free(y);
+  alm_qweight_free(w);
+  return rc;
+}
+
+// ---- model -------------------------------------------------------------------
+int alm_model_create(alm_ctx* ctx, const alm_model_config* cfg, const uint16_t* rope_host, alm_model** out) {
+  ALM_REQ(ctx && cfg && rope_host && out, "null argument");
+  const alm_model_config& c = *cfg;
+  ALM_REQ(c.hidden > 0 && c.layers > 0 && c.heads > 0 && c.kv_heads > 0 && c.vocab > 0 && c.intermediate > 0,
+          "invalid config");
+  ALM_REQ(c.heads % c.kv_heads == 0, "heads must be a multiple of kv_heads");
+  ALM_REQ(c.head_dim % 16 == 0 && c.head_dim <= 256, "head_dim must be a multiple of 16, <= 256");
+  ALM_REQ(c.intermediate % 8 == 0, "intermediate must be a multiple of 8");
+  ALM_REQ(c.max_len > 0, "invalid max_len");
+  DeviceGuard g(ctx->device);
+  auto* m = new alm_model();
+  m->ctx = ctx;
+  m->cfg = c;
+  m->layers.resize(c.layers);
+  const size_t n = static_cast<size_t>(c.max_len) * c.head_dim;
+  int rc = dev_alloc_t(&m->rope, n);
+  if (rc == ALM_OK && cudaMemcpy(m->rope, rope_host, n * sizeof(half), cudaMemcpyHostToDevice) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "rope upload failed");
+  if (rc != ALM_OK) {
+    alm_model_destroy(m);
+    return rc;
+  }
+  *out = m;
+  return ALM_OK;
+}
+
+int alm_model_destroy(alm_model* m) {
+  if (!m) return ALM_OK;
+  DeviceGuard g(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  for (Layer& L : m->layers) {
+    alm_qweight_free(L.qkv);
+    alm_qweight_free(L.o);
+    alm_qweight_free(L.gu);
+    alm_qweight_free(L.down);
+    dev_free(L.n_in);
+    dev_free(L.n_post);
+  }
+  alm_qweight_free(m->head);
+  dev_free(m->rope);
+  dev_free(m->embed_table);
+  dev_free(m->embed_scale);
+  dev_free(m->final_norm);
+  Work& w = m->ws;
+  for (void* p : {(void*)w.tokens, (void*)w.pos, (void*)w.err, (void*)w.x0, (void*)w.s1, (void*)w.s2,
+                  (void*)w.ss1, (void*)w.ss2, (void*)w.q, (void*)w.ctx, (void*)w.h, (void*)w.xn, (void*)w.xout,
+                  (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
+                  (void*)w.scores, (void*)w.stats})
+    dev_free(p);
+  if (w.pinned) cudaFreeHost(w.pinned);
+  delete m;
+  return ALM_OK;
+}
+
+int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint16_t* n_in_host,
+                        const uint16_t* n_post_host) {
+  ALM_REQ(m && p && n_in_host && n_post_host, "null argument");
+  ALM_REQ(li >= 0 && li < m->cfg.layers, "layer index out of range");
+  const alm_model_config& c = m->cfg;
+  const int hd = c.head_dim, half_d = hd / 2;
+  const int qd = c.heads * hd, kd = c.kv_heads * hd;
+  ALM_REQ(p[0].out == qd && p[1].out == kd && p[2].out == kd, "q/k/v output sizes do not match the config");
+  ALM_REQ(p[0].in_real == c.hidden && p[3].out == c.hidden && p[3].in_real == qd, "q/o sizes do not match");
+  ALM_REQ(p[4].out == c.intermediate && p[5].out == c.intermediate && p[6].out == c.hidden &&
+              p[6].in_real == c.intermediate && p[4].in_real == c.hidden,
+          "gate/up/down sizes do not match");
+  DeviceGuard g(m->ctx->device);
+  Layer& L = m->layers[li];
+  // fused QKV: q and k rows permuted so tile rows g / g+8 are RoPE pairs
+  // (d, d + head_dim/2) of one head; v rows in order.
+  std::vector<int> qkv_map(qd + 2 * kd, -1);
+  auto rope_rows = [&](int src, int n_heads, int dst0) {
+    for (int h = 0; h < n_heads; ++h)
+      for (int d = 0; d < hd; ++d) {
+        const int lo = d < half_d;
+        const int dd = lo ? d : d - half_d;
+        const int dst = dst0 + h * hd + (dd / 8) * 16 + (lo ? 0 : 8) + dd % 8;
+        qkv_map[dst] = (src << 24) | (h * hd + d);
+      }
+  };
+  rope_rows(0, c.heads, 0);
+  rope_rows(1, c.kv_heads, qd);
+  for (int r = 0; r < kd; ++r) qkv_map[qd + kd + r] = (2 << 24) | r;
+  // fused gate/up: tile rows g = gate j, g + 8 = up j (j = 8 * tile + g)
+  std::vector<int> gu_map((2 * c.intermediate + 15) / 16 * 16, -1);
+  for (int j = 0; j < c.intermediate; ++j) {
+    gu_map[(j / 8) * 16 + j % 8] = (0 << 24) | j;
+    gu_map[(j / 8) * 16 + 8 + j % 8] = (1 << 24) | j;
+  }
+  alm_qweight *qkv = nullptr, *o = nullptr, *gu = nullptr, *dn = nullptr;
+  int rc = build_qweight(m->ctx, &p[0], 3, qkv_map, qd + 2 * kd, &qkv);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, &o);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[4], 2, gu_map, 2 * c.intermediate, &gu);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, &dn);
+  half *nin = nullptr, *npost = nullptr;
+  if (rc == ALM_OK) rc = dev_alloc_t(&nin, c.hidden);
+  if (rc == ALM_OK) rc = dev_alloc_t(&npost, c.hidden);
+  if (rc == ALM_OK && (cudaMemcpy(nin, n_in_host, c.hidden * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+                       cudaMemcpy(npost, n_post_host, c.hidden * 2, cudaMemcpyHostToDevice) != cudaSuccess))
+    rc = fail(ALM_ERR_CUDA, "norm upload failed");
+  if (rc != ALM_OK) {
+    alm_qweight_free(qkv);
+    alm_qweight_free(o);
+    alm_qweight_free(gu);
+    alm_qweight_free(dn);
+    dev_free(nin);
+    dev_free(npost);
+    return rc;
+  }
+  alm_qweight_free(L.qkv);
+  alm_qweight_free(L.o);
+  alm_qweight_free(L.gu);
+  alm_qweight_free(L.down);
+  dev_free(L.n_in);
+  dev_free(L.n_post);
+  L = Layer{qkv, o, gu, dn, nin, npost};
+  m->finalized = false;
+  return ALM_OK;
+}
+
+int alm_model_set_embed(alm_model* m, const void* table_host, const void* scale_host, int bits, int block) {
+  ALM_REQ(m && table_host, "null argument");
+  const alm_model_config& c = m->cfg;
+  ALM_REQ(bits == 16 || ((bits == 4 || bits == 8) && scale_host && block > 0 && c.hidden % block == 0),
+          "embedding must be fp16 or int4/int8 with a block dividing hidden");
+  DeviceGuard g(m->ctx->device);
+  dev_free(m->embed_table);
+  dev_free(m->embed_scale);
+  m->embed_table = nullptr;
+  m->embed_scale = nullptr;
+  const int row_bytes = bits == 16 ? c.hidden * 2 : bits == 8 ? c.hidden : c.hidden / 2;
+  const size_t nb = static_cast<size_t>(c.vocab) * row_bytes;
+  ALM_TRY(dev_alloc(&m->embed_table, nb));
+  ALM_CUDA(cudaMemcpy(m->embed_table, table_host, nb, cudaMemcpyHostToDevice));
+  m->embed_bits = bits;
+  m->embed_block = bits == 16 ? c.hidden : block;
+  m->embed_nsb = bits == 16 ? 0 : c.hidden / block;
+  m->embed_row_bytes = row_bytes;
+  if (bits != 16) {
+    const size_t sb = static_cast<size_t>(c.vocab) * m->embed_nsb * sizeof(half);
+    ALM_TRY(dev_alloc(reinterpret_cast<void**>(&m->embed_scale), sb));
+    ALM_CUDA(cudaMemcpy(m->embed_scale, scale_host, sb, cudaMemcpyHostToDevice));
+  }
+  m->finalized = false;
+  return ALM_OK;
+}
+
+int alm_model_set_final_norm(alm_model* m, const uint16_t* w_host) {
+  ALM_REQ(m && w_host, "null argument");
+  DeviceGuard g(m->ctx->device);
+  dev_free(m->final_norm);
+  m->final_norm = nullptr;
+  ALM_TRY(dev_alloc_t(&m->final_norm, m->cfg.hidden));
+  ALM_CUDA(cudaMemcpy(m->final_norm, w_host, m->cfg.hidden * 2, cudaMemcpyHostToDevice));
+  return ALM_OK;
+}
+
+int alm_model_set_head(alm_model* m, const alm_proj_src* head) {
+  ALM_REQ(m && head, "null argument");
+  ALM_REQ(head->out == m->cfg.vocab && head->in_real == m->cfg.hidden, "head must be (vocab, hidden)");
+  DeviceGuard g(m->ctx->device);
+  alm_qweight* w = nullptr;
+  ALM_TRY(build_qweight(m->ctx, head, 1, identity_map(head->out), head->out, &w));
+  alm_qweight_free(m->head);
+  m->head = w;
+  m->finalized = false;
+  return ALM_OK;
+}
+
+int alm_model_finalize(alm_model* m) {
+  ALM_REQ(m, "null model");
+  DeviceGuard g(m->ctx->device);
+  const alm_model_config& c = m->cfg;
+  if (!m->embed_table) return fail(ALM_ERR_STATE, "embedding not set");
+  if (!m->final_norm) return fail(ALM_ERR_STATE, "final norm not set");
+  if (!m->head) {
+    // tied head: the embedding table in the tile layout
+    alm_proj_src s{m->embed_table, m->embed_scale, m->embed_bits, m->embed_block, c.vocab, c.hidden, c.hidden};
+    // the sources must be host memory: copy the device table back once
+    const size_t nb = static_cast<size_t>(c.vocab) * m->embed_row_bytes;
+    std::vector<uint8_t> host_tbl(nb);
+    ALM_CUDA(cudaMemcpy(host_tbl.data(), m->embed_table, nb, cudaMemcpyDeviceToHost));
+    std::vector<uint8_t> host_scl;
+    if (m->embed_bits != 16) {
+      host_scl.resize(static_cast<size_t>(c.vocab) * m->embed_nsb * sizeof(half));
+      ALM_CUDA(cudaMemcpy(host_scl.data(), m->embed_scale, host_scl.size(), cudaMemcpyDeviceToHost));
+    }
+    s.packed_host = host_tbl.data();
+    s.scale_host = m->embed_bits != 16 ? host_scl.data() : nullptr;
+    alm_qweight* w = nullptr;
+    ALM_TRY(build_qweight(m->ctx, &s, 1, identity_map(c.vocab), c.vocab, &w));
+    m->head = w;
+  }
+  Work& ws = m->ws;
+  if (!ws.x0) {
+    const int H = c.hidden, ht = n_h_tiles(m), qd = c.heads * c.head_dim;
+    ALM_TRY(dev_alloc_t(&ws.tokens, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.pos, 1));
+    ALM_TRY(dev_alloc_t(&ws.err, 1));
+    ALM_CUDA(cudaMemset(ws.err, 0, sizeof(int)));
+    ALM_TRY(dev_alloc_t(&ws.x0, static_cast<size_t>(kMaxRows) * H));
+    ALM_TRY(dev_alloc_t(&ws.s1, static_cast<size_t>(kMaxRows) * H));
+    ALM_TRY(dev_alloc_t(&ws.s2, static_cast<size_t>(kMaxRows) * H));
+    ALM_TRY(dev_alloc_t(&ws.ss1, static_cast<size_t>(kMaxRows) * ht));
+    ALM_TRY(dev_alloc_t(&ws.ss2, static_cast<size_t>(kMaxRows) * ht));
+    ALM_TRY(dev_alloc_t(&ws.q, static_cast<size_t>(kMaxRows) * qd));
+    ALM_TRY(dev_alloc_t(&ws.ctx, static_cast<size_t>(kMaxRows) * qd));
+    ALM_TRY(dev_alloc_t(&ws.h, static_cast<size_t>(kMaxRows) * c.intermediate));
+    ALM_TRY(dev_alloc_t(&ws.xn, static_cast<size_t>(kMaxRows) * H));
+    ALM_TRY(dev_alloc_t(&ws.xout, static_cast<size_t>(kMaxRows) * H));
+    ALM_TRY(dev_alloc_t(&ws.logits, static_cast<size_t>(kMaxRows) * c.vocab));
+    ALM_TRY(dev_alloc_t(&ws.argmax, kMaxRows));
+    ALM_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ws.pinned), 64 * sizeof(int)));
+  }
+  // per-CTA argmax partials of the head
+  const int ntc = 8 / m->head->t.ksw;
+  const int n_am = (m->head->t.n_tiles + ntc - 1) / ntc;
+  if (n_am > ws.n_am) {
+    dev_free(ws.am_val);
+    dev_free(ws.am_idx);
+    ws.am_val = nullptr;
+    ws.am_idx = nullptr;
+    ALM_TRY(dev_alloc_t(&ws.am_val, static_cast<size_t>(kMaxRows) * n_am));
+    ALM_TRY(dev_alloc_t(&ws.am_idx, static_cast<size_t>(kMaxRows) * n_am));
+  }
+  ws.n_am = n_am;
+  size_t need = split_need(m->head);
+  for (const Layer& L : m->layers)
+    need = std::max({need, split_need(L.qkv), split_need(L.o), split_need(L.gu), split_need(L.down)});
+  ALM_TRY(ensure_part(ws, need));
+  m->finalized = true;
+  return ALM_OK;
+}
+
+// ---- KV ------------------------------------------------------------------------
+int alm_kv_create(alm_ctx* ctx, const alm_model* m, int max_len, int page_size, alm_kv** out) {
+  ALM_REQ(ctx && m && out, "null argument");
+  ALM_REQ(max_len > 0 && page_size > 0 && page_size <= 256, "invalid kv geometry");
+  DeviceGuard g(ctx->device);
+  auto* kv = new alm_kv();
+  kv->ctx = ctx;
+  kv->n_layers = m->cfg.layers;
+  kv->kv_heads = m->cfg.kv_heads;
+  kv->head_dim = m->cfg.head_dim;
+  kv->page_size = page_size;
+  kv->n_pages = (max_len + page_size - 1) / page_size;
+  kv->max_len = max_len;
+  kv->layer_elems = static_cast<size_t>(kv->n_pages) * page_size * kv->kv_heads * kv->head_dim;
+  int rc = dev_alloc_t(&kv->k, kv->layer_elems * kv->n_layers);
+  if (rc == ALM_OK) rc = dev_alloc_t(&kv->v, kv->layer_elems * kv->n_layers);
+  if (rc == ALM_OK) rc = dev_alloc_t(&kv->page_table, kv->n_pages);
+  if (rc == ALM_OK) {
+    std::vector<int> pt(kv->n_pages);
+    for (int i = 0; i < kv->n_pages; ++i) pt[i] = i;
+    if (cudaMemcpy(kv->page_table, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "page table upload failed");
+  }
+  if (rc == ALM_OK) rc = alm_kv_zero(kv);
+  if (rc != ALM_OK) {
+    alm_kv_destroy(kv);
+    return rc;
+  }
+  *out = kv;
+  return ALM_OK;
+}
+
+int alm_kv_destroy(alm_kv* kv) {
+  if (!kv) return ALM_OK;
+  DeviceGuard g(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  dev_free(kv->k);
+  dev_free(kv->v);
+  dev_free(kv->page_table);
+  delete kv;
+  return ALM_OK;
+}
+
+int alm_kv_zero(alm_kv* kv) {
+  ALM_REQ(kv, "null kv");
+  DeviceGuard g(kv->ctx->device);
+  ALM_CUDA(cudaMemsetAsync(kv->k, 0, kv->layer_elems * kv->n_layers * sizeof(half), kv->ctx->stream));
+  ALM_CUDA(cudaMemsetAsync(kv->v, 0, kv->layer_elems * kv->n_layers * sizeof(half), kv->ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(kv->ctx->stream));
+  return ALM_OK;
+}
+
+static int kv_copy(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host,
+                   const uint16_t* k_in, const uint16_t* v_in) {
+  ALM_REQ(kv, "null kv");
+  ALM_REQ(layer >= 0 && layer < kv->n_layers && pos0 >= 0 && n >= 0 && pos0 + n <= kv->max_len,
+          "kv range out of bounds");
+  DeviceGuard g(kv->ctx->device);
+  const size_t row = static_cast<size_t>(kv->head_dim) * sizeof(half);
+  std::vector<int> pt(kv->n_pages);
+  ALM_CUDA(cudaMemcpy(pt.data(), kv->page_table, pt.size() * sizeof(int), cudaMemcpyDeviceToHost));
+  for (int which = 0; which < 2; ++which) {
+    half* base = (which == 0 ? kv->k : kv->v) + static_cast<size_t>(layer) * kv->layer_elems;
+    uint16_t* out = which == 0 ? k_host : v_host;
+    const uint16_t* in = which == 0 ? k_in : v_in;
+    if (!out && !in) continue;
+    for (int i = 0; i < n; ++i) {
+      const int p = pos0 + i;
+      for (int h = 0; h < kv->kv_heads; ++h) {
+        half* src = base + ((static_cast<size_t>(pt[p / kv->page_size]) * kv->kv_heads + h) * kv->page_size +
+                            p % kv->page_size) * kv->head_dim;
+        const size_t off = (static_cast<size_t>(i) * kv->kv_heads + h) * kv->head_dim;
+        if (out) ALM_CUDA(cudaMemcpy(out + off, src, row, cudaMemcpyDeviceToHost));
+        else ALM_CUDA(cudaMemcpy(src, in + off, row, cudaMemcpyHostToDevice));
+      }
+    }
+  }
+  return ALM_OK;
+}
+
+int alm_kv_read(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host) {
+  return kv_copy(kv, layer, pos0, n, k_host, v_host, nullptr, nullptr);
+}
+int alm_kv_write(alm_kv* kv, int layer, int pos0, int n, const uint16_t* k_host, const uint16_t* v_host) {
+  return kv_copy(kv, layer, pos0, n, nullptr, nullptr, k_host, v_host);
+}
+
+// ---- forward --------------------------------------------------------------------
+int alm_layer_forward(alm_model* m, int layer, alm_kv* kv, const uint16_t* x_host, int rows, int pos0,
+                      uint16_t* out_host) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(x_host && out_host, "null argument");
+  ALM_REQ(layer >= 0 && layer < m->cfg.layers, "layer index out of range");
+  if (!m->layers[layer].qkv) return fail(ALM_ERR_STATE, "layer " + std::to_string(layer) + " not set");
+  DeviceGuard g(m->ctx->device);
+  ALM_TRY(check_kv(m, kv, rows, pos0));
+  cudaStream_t st = m->ctx->stream;
+  const size_t nb = static_cast<size_t>(rows) * m->cfg.hidden * sizeof(half);
+  ALM_TRY(set_pos(m, pos0));
+  ALM_CUDA(cudaMemcpyAsync(m->ws.x0, x_host, nb, cudaMemcpyHostToDevice, st));
+  ALM_TRY(enqueue_layer(m, layer, kv, rows, raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), false));
+  const ActIn o = deferred_in(m, m->ws.s2, m->ws.ss2, m->layers[layer].n_post);
+  ALM_CUDA(launch_rownorm(o, rows, nullptr, 0.f, m->ws.xout, m->cfg.hidden, false, st));
+  ALM_CUDA(cudaMemcpyAsync(out_host, m->ws.xout, nb, cudaMemcpyDeviceToHost, st));
+  return sync_and_check(m);
+}
+
+int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logits_host, int32_t* argmax_host) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(x_host, "null argument");
+  ALM_REQ(rows >= 1 && rows <= kMaxRows, "rows must be in 1..16");
+  DeviceGuard g(m->ctx->device);
+  cudaStream_t st = m->ctx->stream;
+  ALM_CUDA(cudaMemcpyAsync(m->ws.x0, x_host, static_cast<size_t>(rows) * m->cfg.hidden * 2,
+                           cudaMemcpyHostToDevice, st));
+  ALM_CUDA(launch_rownorm(raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), rows, m->final_norm, m->cfg.rms_eps,
+                          m->ws.xn, m->cfg.hidden, false, st));
+  ALM_TRY(enqueue_head(m, rows, false));
+  ALM_TRY(sync_and_check(m));
+  return copy_logits_out(m, rows, logits_host, argmax_host);
+}
+
+int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0, float* logits_host,
+                int32_t* argmax_host) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(tokens_host, "null argument");
+  ALM_TRY(check_layers(m));
+  DeviceGuard g(m->ctx->device);
+  ALM_TRY(check_kv(m, kv, rows, pos0));
+  cudaStream_t st = m->ctx->stream;
+  ALM_TRY(set_pos(m, pos0));
+  ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host, rows * sizeof(int), cudaMemcpyHostToDevice, st));
+  const bool head = logits_host != nullptr || argmax_host != nullptr;
+  ALM_TRY(enqueue_forward(m, kv, rows, head, false));
+  ALM_TRY(sync_and_check(m));
+  return copy_logits_out(m, rows, logits_host, argmax_host);
+}
+
+// ---- speculative decoding -----------------------------------------------------------
+static int enqueue_spec_step(alm_spec* s) {
+  alm_model* d = s->draft;
+  alm_model* t = s->target;
+  cudaStream_t st = t->ctx->stream;
+  for (int i = 0; i < s->k; ++i) {
+    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
+    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, false));
+  }
+  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
+  ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, false));
+  ALM_CUDA(launch_spec_accept_greedy(s->state, s->cand, t->ws.argmax, s->k, s->out_tokens, s->out_acc,
+                                     s->cap_tokens, s->cap_steps, st));
+  return ALM_OK;
+}
+
+int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_kv* draft_kv, int k,
+                    alm_spec** out) {
+  ALM_TRY(check_ready(target));
+  ALM_TRY(check_ready(draft));
+  ALM_TRY(check_layers(target));
+  ALM_TRY(check_layers(draft));
+  ALM_REQ(out, "null argument");
+  ALM_REQ(target->ctx == draft->ctx, "target and draft must share a context");
+  ALM_REQ(k >= 1 && k + 1 <= kMaxRows, "k must be in 1..15");
+  ALM_REQ(target->cfg.vocab == draft->cfg.vocab, "target and draft vocabularies differ");
+  DeviceGuard g(target->ctx->device);
+  ALM_TRY(check_kv(target, target_kv, k + 1, 0));
+  ALM_TRY(check_kv(draft, draft_kv, 1, 0));
+  auto* s = new alm_spec();
+  s->target = target;
+  s->draft = draft;
+  s->tkv = target_kv;
+  s->dkv = draft_kv;
+  s->k = k;
+  s->cap_steps = 1024;
+  s->cap_tokens = s->cap_steps * (k + 1);
+  int rc = dev_alloc_t(&s->state, 4);
+  if (rc == ALM_OK) rc = dev_alloc_t(&s->cand, k);
+  if (rc == ALM_OK) rc = dev_alloc_t(&s->out_tokens, s->cap_tokens);
+  if (rc == ALM_OK) rc = dev_alloc_t(&s->out_acc, s->cap_steps);
+  if (rc == ALM_OK && cudaMallocHost(reinterpret_cast<void**>(&s->pinned),
+                                     (4 + s->cap_tokens + s->cap_steps) * sizeof(int)) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "pinned allocation failed");
+  if (rc == ALM_OK && cudaMemset(s->state, 0, 4 * sizeof(int)) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "state init failed");
+  if (rc == ALM_OK) {
+    cudaStream_t st = target->ctx->stream;
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, "graph capture failed to start");
+    } else {
+      rc = enqueue_spec_step(s);
+      cudaError_t e = cudaStreamEndCapture(st, &graph);
+      if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+      if (rc == ALM_OK) {
+        e = cudaGraphInstantiate(&s->graph, graph, 0);
+        if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
+      }
+      if (graph) cudaGraphDestroy(graph);
+    }
+  }
+  if (rc != ALM_OK) {
+    alm_spec_destroy(s);
+    return rc;
+  }
+  *out = s;
+  return ALM_OK;
+}
+
+int alm_spec_destroy(alm_spec* s) {
+  if (!s) return ALM_OK;
+  DeviceGuard g(s->target->ctx->device);
+  cudaStreamSynchronize(s->target->ctx->stream);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  dev_free(s->state);
+  dev_free(s->cand);
+  dev_free(s->out_tokens);
+  dev_free(s->out_acc);
+  if (s->pinned) cudaFreeHost(s->pinned);
+  delete s;
+  return ALM_OK;
+}
+
+int alm_spec_begin(alm_spec* s, int32_t token, int pos) {
+  ALM_REQ(s, "null spec");
+  ALM_REQ(token >= 0 && token < s->target->cfg.vocab, "token out of range");
+  ALM_REQ(pos >= 0, "negative position");
+  DeviceGuard g(s->target->ctx->device);
+  s->pinned[0] = token;
+  s->pinned[1] = pos;
+  s->pinned[2] = 0;
+  s->pinned[3] = 0;
+  cudaStream_t st = s->target->ctx->stream;
+  ALM_CUDA(cudaMemcpyAsync(s->state, s->pinned, 4 * sizeof(int), cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaStreamSynchronize(st));
+  return ALM_OK;
+}
+
+int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos) {
+  ALM_REQ(s && token && pos, "null argument");
+  DeviceGuard g(s->target->ctx->device);
+  int st4[4];
+  ALM_CUDA(cudaMemcpy(st4, s->state, sizeof(st4), cudaMemcpyDeviceToHost));
+  *token = st4[0];
+  *pos = st4[1];
+  return ALM_OK;
+}
+
+int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emitted_host,
+                 int32_t* accepted_host) {
+  ALM_REQ(s && emitted_host && n_emitted_host, "null argument");
+  ALM_REQ(n_steps >= 1 && n_steps <= s->cap_steps, "n_steps out of range (1..1024)");
+  DeviceGuard g(s->target->ctx->device);
+  cudaStream_t st = s->target->ctx->stream;
+  int cur[4];
+  ALM_CUDA(cudaMemcpy(cur, s->state, sizeof(cur), cudaMemcpyDeviceToHost));
+  const int last_pos = cur[1] + n_steps * (s->k + 1) + s->k;
+  ALM_REQ(last_pos < s->tkv->max_len && last_pos < s->dkv->max_len, "speculative steps would overflow the kv cache");
+  ALM_REQ(last_pos < s->target->cfg.max_len && last_pos < s->draft->cfg.max_len, "position beyond the rope table");
+  ALM_CUDA(cudaMemsetAsync(s->state + 2, 0, 2 * sizeof(int), st));
+  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(s->graph, st));
+  int* h = s->pinned;
+  ALM_CUDA(cudaMemcpyAsync(h, s->state, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+  ALM_CUDA(cudaStreamSynchronize(st));
+  const int n_emit = h[2];
+  ALM_CUDA(cudaMemcpyAsync(h + 4, s->out_tokens, n_emit * sizeof(int), cudaMemcpyDeviceToHost, st));
+  ALM_CUDA(cudaMemcpyAsync(h + 4 + s->cap_tokens, s->out_acc, n_steps * sizeof(int), cudaMemcpyDeviceToHost, st));
+  ALM_CUDA(cudaStreamSynchronize(st));
+  std::memcpy(emitted_host, h + 4, n_emit * sizeof(int));
+  *n_emitted_host = n_emit;
+  if (accepted_host) std::memcpy(accepted_host, h + 4 + s->cap_tokens, n_steps * sizeof(int));
+  int err = 0;
+  ALM_CUDA(cudaMemcpy(&err, s->target->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+  int err2 = 0;
+  ALM_CUDA(cudaMemcpy(&err2, s->draft->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err || err2) return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
+  return ALM_OK;
+}
+
+}  // extern "C"

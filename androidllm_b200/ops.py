@@ -1,0 +1,386 @@
+"""Python objects over the C ABI: context, quantized weights, device models,
+paged KV caches and the speculative decoder.  numpy in, numpy out; device
+memory is owned by the library."""
+import atexit
+import ctypes
+import json
+import os
+
+import numpy as np
+
+from . import safetensors
+from ._lib import ModelConfig, ProjSrc, check, lib, ptr
+
+PROJ_BASES = ("q", "k", "v", "o", "gate", "up", "down")   # androidllm/shard.py:111
+
+# At interpreter exit the order of finalizers is arbitrary (a context could go
+# before the models on it); the process teardown frees device memory anyway.
+_EXITING = []
+atexit.register(lambda: _EXITING.append(True))
+
+
+def _f16(a):
+    return np.ascontiguousarray(np.asarray(a), dtype=np.float16)
+
+
+class Context:
+    """One device + one stream."""
+
+    def __init__(self, device=0):
+        h = ctypes.c_void_p()
+        check(lib.alm_ctx_create(int(device), ctypes.byref(h)))
+        self.h = h
+        self.device = device
+
+    def sync(self):
+        check(lib.alm_ctx_sync(self.h))
+
+    def close(self):
+        if self.h:
+            lib.alm_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_DEFAULT = {}
+
+
+def default_context(device=0):
+    ctx = _DEFAULT.get(device)
+    if ctx is None or ctx.h is None:
+        ctx = _DEFAULT[device] = Context(device)
+    return ctx
+
+
+class DeviceBuffer:
+    def __init__(self, ctx, nbytes):
+        h = ctypes.c_void_p()
+        check(lib.alm_dev_alloc(ctx.h, int(nbytes), ctypes.byref(h)))
+        self.ctx, self.h, self.nbytes = ctx, h, int(nbytes)
+
+    def upload(self, a):
+        a = np.ascontiguousarray(a)
+        check(lib.alm_copy_h2d(self.ctx.h, self.h, ptr(a), a.nbytes))
+
+    def download(self, out):
+        check(lib.alm_copy_d2h(self.ctx.h, ptr(out), self.h, out.nbytes))
+        return out
+
+    def free(self):
+        if self.h:
+            lib.alm_dev_free(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class QuantProj:
+    """One projection in the shard format: codes, scales and manifest meta."""
+
+    def __init__(self, packed, scale, bits, block, out, in_, in_real=None):
+        self.bits = int(bits)
+        if self.bits == 16:
+            self.packed = _f16(packed)
+            self.scale = None
+        else:
+            dt = np.uint8 if self.bits == 4 else np.int8
+            self.packed = np.ascontiguousarray(packed, dtype=dt)
+            self.scale = _f16(scale)
+        self.block = int(block)
+        self.out = int(out)
+        self.in_ = int(in_)
+        self.in_real = int(in_real if in_real is not None else in_)
+
+    @classmethod
+    def from_fp16(cls, w):
+        w = _f16(w)
+        return cls(w, None, 16, 0, w.shape[0], w.shape[1])
+
+    def src(self):
+        return ProjSrc(ptr(self.packed), ptr(self.scale), self.bits, self.block, self.out, self.in_,
+                       self.in_real)
+
+
+class QWeight:
+    """A weight uploaded and repacked into the tensor-core tile layout."""
+
+    def __init__(self, ctx, proj):
+        h = ctypes.c_void_p()
+        check(lib.alm_qweight_upload(ctx.h, ptr(proj.packed), ptr(proj.scale), proj.bits, proj.block,
+                                     proj.out, proj.in_, proj.in_real, ctypes.byref(h)))
+        self.ctx, self.h, self.proj = ctx, h, proj
+
+    def dequant(self):
+        """fp16 (out, in_real): bit-exact androidllm dequantize_packed (sliced)."""
+        out = np.empty((self.proj.out, self.proj.in_real), np.float16)
+        check(lib.alm_qweight_dequant(self.ctx.h, self.h, ptr(out)))
+        return out
+
+    def matmul(self, x):
+        """fp16(x (m, in_real) . W^T), m <= 16, fp32 accumulation."""
+        x = _f16(x)
+        m = x.shape[0]
+        xb = DeviceBuffer(self.ctx, x.nbytes)
+        yb = DeviceBuffer(self.ctx, m * self.proj.out * 2)
+        xb.upload(x)
+        check(lib.alm_qmatmul(self.ctx.h, self.h, xb.h, x.shape[1], m, yb.h, self.proj.out))
+        return yb.download(np.empty((m, self.proj.out), np.float16))
+
+    def free(self):
+        if self.h:
+            lib.alm_qweight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def matmul_f16(a, b, ctx=None):
+    """``a @ b.T`` for fp16 a (m, k) and b (n, k) on the GPU (androidllm/neon.py:39-51)."""
+    a, b = _f16(a), _f16(b)
+    ctx = ctx or default_context()
+    out = np.empty((a.shape[0], b.shape[0]), np.float16)
+    check(lib.alm_matmul_f16_f16(ctx.h, ptr(a), ptr(b), ptr(out), a.shape[0], a.shape[1], b.shape[0]))
+    return out
+
+
+def precompute_rope(head_dim, max_len, theta=10000.0):
+    """[cos | sin] table, float64 angles stored fp16 (androidllm/models/llama.py:27-31)."""
+    inv = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim))
+    ang = np.outer(np.arange(max_len, dtype=np.float64), inv)
+    return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float16)
+
+
+def config_of(canon):
+    return ModelConfig(canon["hidden"], canon["layers"], canon["heads"], canon["kv_heads"],
+                       canon["head_dim"], canon["intermediate"], canon["vocab"],
+                       int(canon["max_len"]), float(canon["rms_eps"]))
+
+
+def _as_proj(w):
+    return w if isinstance(w, QuantProj) else QuantProj.from_fp16(w)
+
+
+class DeviceModel:
+    """A target or draft model resident in HBM (alm_model)."""
+
+    def __init__(self, ctx, canon):
+        self.ctx = ctx
+        self.canon = dict(canon)
+        self.rope = precompute_rope(canon["head_dim"], int(canon["max_len"]), float(canon["rope_theta"]))
+        h = ctypes.c_void_p()
+        cfg = config_of(canon)
+        check(lib.alm_model_create(ctx.h, ctypes.byref(cfg), ptr(self.rope), ctypes.byref(h)))
+        self.h = h
+        self._layer_src = [None] * canon["layers"]
+
+    # -- assembly ---------------------------------------------------------------
+    def set_layer(self, li, layer):
+        """``layer``: {q,k,v,o,gate,up,down: QuantProj or fp16 (out, in) array,
+        n_in, n_post: fp16 (hidden,)}."""
+        projs = [_as_proj(layer[b]) for b in PROJ_BASES]
+        arr = (ProjSrc * 7)(*[p.src() for p in projs])
+        n_in, n_post = _f16(layer["n_in"]).reshape(-1), _f16(layer["n_post"]).reshape(-1)
+        check(lib.alm_model_set_layer(self.h, int(li), arr, ptr(n_in), ptr(n_post)))
+        self._layer_src[li] = layer
+
+    def set_embed(self, table, scale=None, bits=16, block=0):
+        table = _f16(table) if bits == 16 else np.ascontiguousarray(table)
+        scale = None if scale is None else _f16(scale)
+        check(lib.alm_model_set_embed(self.h, ptr(table), ptr(scale), int(bits), int(block)))
+
+    def set_final_norm(self, w):
+        w = _f16(w).reshape(-1)
+        check(lib.alm_model_set_final_norm(self.h, ptr(w)))
+
+    def set_head(self, proj):
+        proj = _as_proj(proj)
+        src = proj.src()
+        check(lib.alm_model_set_head(self.h, ctypes.byref(src)))
+
+    def finalize(self):
+        check(lib.alm_model_finalize(self.h))
+
+    @classmethod
+    def from_dir(cls, ctx, model_dir, layers=None):
+        """Load an androidllm shard directory straight to the device (no host
+        dequantization, androidllm/engine.py:90-116,160-174)."""
+        man = load_manifest(model_dir)
+        canon = man["config"]
+        m = cls(ctx, canon)
+        m.manifest = man
+        n = canon["layers"] if layers is None else layers
+        for i in range(n):
+            m.set_layer(i, read_layer(model_dir, man, i))
+        emb = os.path.join(model_dir, "embeddings.safetensors")
+        eq = man.get("embed_quant") or {}
+        if eq:
+            m.set_embed(safetensors.read_tensor(emb, "embed.q"), safetensors.read_tensor(emb, "embed.scale"),
+                        eq["bits"], eq["block"])
+        else:
+            m.set_embed(safetensors.read_tensor(emb, "embed"))
+        m.set_final_norm(safetensors.read_tensor(os.path.join(model_dir, "norms.safetensors"), "final_norm"))
+        if man.get("has_lm_head"):
+            path = os.path.join(model_dir, "lm_head.safetensors")
+            lq = man.get("lm_head_quant") or {}
+            if lq:
+                m.set_head(QuantProj(safetensors.read_tensor(path, "lm_head.q"),
+                                     safetensors.read_tensor(path, "lm_head.scale"), lq["bits"], lq["block"],
+                                     lq["out"], lq["in"]))
+            else:
+                m.set_head(safetensors.read_tensor(path, "lm_head"))
+        m.finalize()
+        return m
+
+    # -- compute ------------------------------------------------------------------
+    def layer_forward(self, li, kv, x, pos0):
+        x = _f16(x)
+        x = x.reshape(-1, self.canon["hidden"])
+        out = np.empty_like(x)
+        check(lib.alm_layer_forward(self.h, int(li), kv.h, ptr(x), x.shape[0], int(pos0), ptr(out)))
+        return out
+
+    def head_logits(self, x, want_logits=True):
+        x = _f16(x).reshape(-1, self.canon["hidden"])
+        rows = x.shape[0]
+        lg = np.empty((rows, self.canon["vocab"]), np.float32) if want_logits else None
+        am = np.empty(rows, np.int32)
+        check(lib.alm_head_logits(self.h, ptr(x), rows, ptr(lg), ptr(am)))
+        return lg, am
+
+    def forward(self, kv, tokens, pos0, logits=False, argmax=True):
+        tok = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        rows = tok.size
+        lg = np.empty((rows, self.canon["vocab"]), np.float32) if logits else None
+        am = np.empty(rows, np.int32) if argmax else None
+        check(lib.alm_forward(self.h, kv.h, ptr(tok), rows, int(pos0), ptr(lg), ptr(am)))
+        return lg, am
+
+    def close(self):
+        if self.h:
+            lib.alm_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def load_manifest(model_dir):
+    with open(os.path.join(model_dir, "manifest.json"), encoding="utf-8") as f:
+        return json.load(f)
+
+
+def read_layer(model_dir, man, i):
+    """Layer i as QuantProj entries + norms (androidllm/engine.py:160-174 without dequant)."""
+    path = os.path.join(model_dir, f"layer_{i}.safetensors")
+    header, _ = safetensors.read_header(path)
+    layer = {}
+    for base, qm in man["quant"]["layers"][str(i)].items():
+        layer[base] = QuantProj(safetensors.read_tensor(path, base + ".q", header),
+                                safetensors.read_tensor(path, base + ".scale", header),
+                                qm["bits"], qm["block"], qm["out"], qm["in"], qm.get("in_real", qm["in"]))
+    layer["n_in"] = safetensors.read_tensor(path, "input_layernorm.weight", header)
+    layer["n_post"] = safetensors.read_tensor(path, "post_attention_layernorm.weight", header)
+    return layer
+
+
+class DeviceKV:
+    """Paged fp16 KV cache of every layer of one model (alm_kv)."""
+
+    def __init__(self, model, max_len, page_size=16):
+        h = ctypes.c_void_p()
+        check(lib.alm_kv_create(model.ctx.h, model.h, int(max_len), int(page_size), ctypes.byref(h)))
+        self.h = h
+        self.model = model
+        self.max_len = int(max_len)
+        self.page_size = int(page_size)
+
+    def zero(self):
+        check(lib.alm_kv_zero(self.h))
+
+    def read(self, layer, pos0, n):
+        c = self.model.canon
+        shape = (n, c["kv_heads"], c["head_dim"])
+        k, v = np.empty(shape, np.float16), np.empty(shape, np.float16)
+        check(lib.alm_kv_read(self.h, int(layer), int(pos0), int(n), ptr(k), ptr(v)))
+        return k, v
+
+    def write(self, layer, pos0, k, v):
+        k, v = _f16(k), _f16(v)
+        check(lib.alm_kv_write(self.h, int(layer), int(pos0), k.shape[0], ptr(k), ptr(v)))
+
+    def close(self):
+        if self.h:
+            lib.alm_kv_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SpecDecoder:
+    """Greedy speculative decoding on the device (alm_spec)."""
+
+    def __init__(self, target, draft, target_kv, draft_kv, k):
+        h = ctypes.c_void_p()
+        check(lib.alm_spec_create(target.h, draft.h, target_kv.h, draft_kv.h, int(k), ctypes.byref(h)))
+        self.h = h
+        self.k = int(k)
+        self._keep = (target, draft, target_kv, draft_kv)
+
+    def begin(self, token, pos):
+        check(lib.alm_spec_begin(self.h, int(token), int(pos)))
+
+    def run(self, n_steps=1):
+        """Run n_steps steps; returns (emitted tokens, accepted count per step)."""
+        emitted = np.empty(n_steps * (self.k + 1), np.int32)
+        n = np.zeros(1, np.int32)
+        acc = np.empty(n_steps, np.int32)
+        check(lib.alm_spec_run(self.h, int(n_steps), ptr(emitted), ptr(n), ptr(acc)))
+        return emitted[: int(n[0])].tolist(), acc.tolist()
+
+    def state(self):
+        t, p = ctypes.c_int32(), ctypes.c_int32()
+        check(lib.alm_spec_state(self.h, ctypes.byref(t), ctypes.byref(p)))
+        return t.value, p.value
+
+    def close(self):
+        if self.h:
+            lib.alm_spec_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        if _EXITING:
+            return
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,178 @@
+/*
+ * libandroidllm_b200 — C ABI of the B200 speculative-decode verify path.
+ *
+ * The entry points replace androidllm's native kernels and the numpy work of
+ * its hot path (paths relative to the androidllm project root):
+ *   - src/androidllm_neon.c:71      matmul_f16_f16 (ctypes, androidllm/neon.py:18-51)
+ *   - androidllm_rs/src/lib.rs:226  layer_forward  (PyO3, androidllm/models/llama.py:71-94)
+ *   - androidllm_rs/src/lib.rs:300  head_logits    (PyO3, androidllm/models/llama.py:130-142)
+ *   - androidllm_rs/src/lib.rs:339  sample / androidllm/engine.py:26-61 (greedy pick)
+ *   - androidllm/quant.py:58-65     dequantize_packed (per layer per token in engine.py:160-174)
+ *   - androidllm/models/llama.py:148-164  prepare_kv
+ *   - androidllm/engine.py:288-320  _spec_step (draft K, verify, accept)
+ *
+ * Conventions: every function returns 0 on success and a nonzero status on
+ * error; alm_last_error() then describes the failure (thread-local).  Plain
+ * pointers and sizes only.  "_host" arguments are host memory borrowed for the
+ * duration of the call; "_dev" arguments are device memory of the context's
+ * device.  fp16 data is passed as raw IEEE binary16 (uint16_t).  Each context
+ * owns one CUDA stream; calls on one context must not overlap in time.
+ */
+#ifndef ANDROIDLLM_B200_H
+#define ANDROIDLLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ALM_API __attribute__((visibility("default")))
+#else
+#define ALM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct alm_ctx alm_ctx;
+typedef struct alm_qweight alm_qweight;
+typedef struct alm_model alm_model;
+typedef struct alm_kv alm_kv;
+typedef struct alm_spec alm_spec;
+
+/* ---- status ---------------------------------------------------------------- */
+enum {
+  ALM_OK = 0,
+  ALM_ERR_ARG = 1,    /* invalid argument (shape, range, null pointer) */
+  ALM_ERR_CUDA = 2,   /* CUDA runtime error */
+  ALM_ERR_STATE = 3,  /* object not ready (e.g. model layer missing) */
+  ALM_ERR_TOKEN = 4   /* a token id outside the vocabulary reached the device */
+};
+
+/* Human-readable description of the last error on this thread. */
+ALM_API const char* alm_last_error(void);
+/* ABI version (major * 100 + minor). */
+ALM_API int alm_abi_version(void);
+
+/* ---- context ---------------------------------------------------------------- */
+/* Create a context (device + stream). */
+ALM_API int alm_ctx_create(int device, alm_ctx** out);
+ALM_API int alm_ctx_destroy(alm_ctx* ctx);
+ALM_API int alm_ctx_sync(alm_ctx* ctx);
+/* Device memory helpers for hosts without their own device-memory library. */
+ALM_API int alm_dev_alloc(alm_ctx* ctx, size_t bytes, void** out_dev);
+ALM_API int alm_dev_free(alm_ctx* ctx, void* dev);
+ALM_API int alm_copy_h2d(alm_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+ALM_API int alm_copy_d2h(alm_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
+
+/* ---- quantized weights (androidllm/quant.py format) --------------------------- */
+/* Upload one projection in the shard format (androidllm/shard.py:109-120):
+ *   bits 4: packed (out, in/2) uint8, even column in the low nibble;
+ *   bits 8: (out, in) int8;   bits 16: (out, in) fp16, scale_host NULL.
+ *   scale_host: (out, in/block) fp16.  `in` is the stored (padded) input dim,
+ *   `in_real` the real one (manifest "in_real").  The weight is repacked on
+ *   the device into the tensor-core tile layout.                              */
+ALM_API int alm_qweight_upload(alm_ctx* ctx, const void* packed_host, const void* scale_host, int bits,
+                       int block, int out, int in, int in_real, alm_qweight** w);
+ALM_API int alm_qweight_free(alm_qweight* w);
+/* Replaces androidllm/quant.py:58-65 dequantize_packed (sliced to in_real):
+ * writes fp16 (out, in_real) to out_host; bit-exact. */
+ALM_API int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host);
+/* y(m, out) = fp16(x(m, in_real) . W^T), fp32 accumulation, 1 <= m <= 16.
+ * Device buffers; row strides in elements. */
+ALM_API int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m,
+                uint16_t* y_dev, int ldy);
+/* Replaces src/androidllm_neon.c:71 matmul_f16_f16 (out = a . b^T, raw fp16,
+ * host buffers, m <= 16): the weight b is uploaded per call. */
+ALM_API int alm_matmul_f16_f16(alm_ctx* ctx, const uint16_t* a_host, const uint16_t* b_host,
+                       uint16_t* out_host, int m, int k, int n);
+
+/* ---- model ------------------------------------------------------------------- */
+/* androidllm canon config (androidllm/config.py:34-48). */
+typedef struct alm_model_config {
+  int hidden, layers, heads, kv_heads, head_dim, intermediate, vocab;
+  int max_len;          /* rows of the RoPE table */
+  float rms_eps;
+} alm_model_config;
+
+/* One projection in shard format (see alm_qweight_upload). */
+typedef struct alm_proj_src {
+  const void* packed_host;
+  const void* scale_host;
+  int bits, block, out, in, in_real;
+} alm_proj_src;
+
+/* rope_host: (max_len, head_dim) fp16 [cos | sin] table, androidllm/models/llama.py:27-31. */
+ALM_API int alm_model_create(alm_ctx* ctx, const alm_model_config* cfg, const uint16_t* rope_host,
+                     alm_model** out);
+ALM_API int alm_model_destroy(alm_model* m);
+/* proj: 7 entries in the order q, k, v, o, gate, up, down (shard.py:111 bases);
+ * n_in / n_post: (hidden) fp16 input_layernorm / post_attention_layernorm. */
+ALM_API int alm_model_set_layer(alm_model* m, int layer, const alm_proj_src* proj, const uint16_t* n_in_host,
+                        const uint16_t* n_post_host);
+/* Embedding rows (vocab, hidden): bits 16 = fp16 table (scale NULL), or the
+ * shard's quantized embedding (embed.q / embed.scale with its block). */
+ALM_API int alm_model_set_embed(alm_model* m, const void* table_host, const void* scale_host, int bits, int block);
+/* Final norm (hidden) fp16. */
+ALM_API int alm_model_set_final_norm(alm_model* m, const uint16_t* w_host);
+/* Untied LM head (vocab, hidden) in shard format; without it the head is the
+ * embedding table (tied, androidllm/models/llama.py:145). */
+ALM_API int alm_model_set_head(alm_model* m, const alm_proj_src* head);
+/* Validate and allocate work buffers; required before any forward. */
+ALM_API int alm_model_finalize(alm_model* m);
+
+/* ---- paged KV cache (replaces androidllm/models/llama.py:148-164 prepare_kv) -- */
+/* fp16 K and V for every layer, `max_len` positions in pages of page_size
+ * positions (identity page table, zero-initialised). */
+ALM_API int alm_kv_create(alm_ctx* ctx, const alm_model* m, int max_len, int page_size, alm_kv** out);
+ALM_API int alm_kv_destroy(alm_kv* kv);
+ALM_API int alm_kv_zero(alm_kv* kv);
+/* Copy positions [pos0, pos0+n) of one layer out as (n, kv_heads, head_dim)
+ * fp16 K and V (the reference cache layout); either pointer may be NULL. */
+ALM_API int alm_kv_read(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host);
+/* Copy (n, kv_heads, head_dim) fp16 rows into the cache at [pos0, pos0+n). */
+ALM_API int alm_kv_write(alm_kv* kv, int layer, int pos0, int n, const uint16_t* k_host, const uint16_t* v_host);
+
+/* ---- forward ------------------------------------------------------------------ */
+/* Replaces androidllm_rs/src/lib.rs:226 layer_forward (and llama.py:96-128):
+ * one post-norm decoder layer over m consecutive positions pos0..pos0+m-1
+ * (m = 1 for a decode step, m = k+1 for a verify pass); writes K/V at those
+ * positions; x_host, out_host: (m, hidden) fp16. */
+ALM_API int alm_layer_forward(alm_model* m, int layer, alm_kv* kv, const uint16_t* x_host, int rows, int pos0,
+                      uint16_t* out_host);
+/* Replaces androidllm_rs/src/lib.rs:300 head_logits (llama.py:130-146):
+ * logits of hidden states x (rows, hidden): fp16-rounded values as fp32
+ * (rows, vocab); argmax_host (rows) gets the first maximal index.  Either
+ * output may be NULL. */
+ALM_API int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logits_host,
+                    int32_t* argmax_host);
+/* Embedding + every layer + final norm + head for tokens at positions
+ * pos0..pos0+rows-1 (androidllm/engine.py:255-286 without sampling). */
+ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
+                float* logits_host, int32_t* argmax_host);
+
+/* ---- speculative decoding (androidllm/engine.py:288-320) ----------------------- */
+/* A greedy speculative decoder: K draft steps (M = 1 forwards of `draft`)
+ * then one (K+1)-row verify forward of `target` and the acceptance, all on
+ * the device and replayed as one CUDA graph per step.  Greedy rule of
+ * engine.py:306-320: accept while the target's pick equals the candidate,
+ * then emit the target's correction (or the bonus token after K accepts). */
+ALM_API int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_kv* draft_kv, int k,
+                    alm_spec** out);
+ALM_API int alm_spec_destroy(alm_spec* s);
+/* Set the step state: `token` is the id at position `pos` (the prompt's last
+ * token after prefill, engine.py:353-354). */
+ALM_API int alm_spec_begin(alm_spec* s, int32_t token, int pos);
+/* Run n_steps speculative steps back to back on the device.  emitted_host
+ * receives the emitted tokens in order (capacity n_steps * (k+1)),
+ * n_emitted_host their count, accepted_host (optional, n_steps) the number
+ * of accepted draft tokens of each step.  The state advances. */
+ALM_API int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emitted_host,
+                 int32_t* accepted_host);
+/* Current (token, pos) state. */
+ALM_API int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ANDROIDLLM_B200_H */
