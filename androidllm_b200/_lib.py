@@ -74,6 +74,9 @@ SIGNATURES = {
     "alm_spec_begin": [_P, ctypes.c_int32, _I],
     "alm_spec_run": [_P, _I, _P, _P, _P],
     "alm_spec_state": [_P, _PI32, _PI32],
+    "alm_spec_kernel_count": [_P, _PI32],
+    "alm_spec_bench": [_P, _I, ctypes.POINTER(ctypes.c_float), _PI32],
+    "alm_bench_qmatmul": [_P, _PP, _I, _P, _I, _P, _I, ctypes.POINTER(ctypes.c_float)],
 }
 _RESTYPE = {"alm_last_error": ctypes.c_char_p}
 

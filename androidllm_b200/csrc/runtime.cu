@@ -188,6 +188,7 @@ struct alm_spec {
   int cap_steps = 0, cap_tokens = 0;
   cudaGraphExec_t graph = nullptr;
   int* pinned = nullptr;     // host: 4 + cap_tokens + cap_steps
+  int n_kernels = 0;         // kernel nodes in the step graph
 };
 
 namespace {
@@ -1142,6 +1143,14 @@ int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_
       cudaError_t e = cudaStreamEndCapture(st, &graph);
       if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
       if (rc == ALM_OK) {
+        size_t n_nodes = 0;
+        cudaGraphGetNodes(graph, nullptr, &n_nodes);
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        if (n_nodes) cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
+        for (cudaGraphNode_t nd : nodes) {
+          cudaGraphNodeType ty;
+          if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->n_kernels;
+        }
         e = cudaGraphInstantiate(&s->graph, graph, 0);
         if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
       }
@@ -1224,6 +1233,76 @@ int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emi
   ALM_CUDA(cudaMemcpy(&err2, s->draft->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
   if (err || err2) return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
   return ALM_OK;
+}
+
+int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels) {
+  ALM_REQ(s && n_kernels, "null argument");
+  *n_kernels = s->n_kernels;
+  return ALM_OK;
+}
+
+int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted) {
+  ALM_REQ(s && ms && n_emitted, "null argument");
+  ALM_REQ(n_steps >= 1 && n_steps <= s->cap_steps, "n_steps out of range (1..1024)");
+  DeviceGuard g(s->target->ctx->device);
+  cudaStream_t st = s->target->ctx->stream;
+  int cur[4];
+  ALM_CUDA(cudaMemcpy(cur, s->state, sizeof(cur), cudaMemcpyDeviceToHost));
+  const int last_pos = cur[1] + n_steps * (s->k + 1) + s->k;
+  ALM_REQ(last_pos < s->tkv->max_len && last_pos < s->dkv->max_len, "speculative steps would overflow the kv cache");
+  cudaEvent_t e0, e1;
+  ALM_CUDA(cudaEventCreate(&e0));
+  ALM_CUDA(cudaEventCreate(&e1));
+  ALM_CUDA(cudaMemsetAsync(s->state + 2, 0, 2 * sizeof(int), st));
+  ALM_CUDA(cudaEventRecord(e0, st));
+  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(s->graph, st));
+  ALM_CUDA(cudaEventRecord(e1, st));
+  ALM_CUDA(cudaEventSynchronize(e1));
+  ALM_CUDA(cudaEventElapsedTime(ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  int st4[4];
+  ALM_CUDA(cudaMemcpy(st4, s->state, sizeof(st4), cudaMemcpyDeviceToHost));
+  *n_emitted = st4[2];
+  return ALM_OK;
+}
+
+int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint16_t* x_dev, int m,
+                      uint16_t* y_dev, int iters, float* avg_us) {
+  ALM_REQ(ctx && ws && n_w > 0 && x_dev && y_dev && avg_us, "null argument");
+  ALM_REQ(m >= 1 && m <= kMaxRows && iters >= 1, "m must be in 1..16");
+  for (int i = 0; i < n_w; ++i)
+    ALM_REQ(ws[i] && ws[i]->out == ws[0]->out && ws[i]->in_real == ws[0]->in_real, "weights must share a shape");
+  DeviceGuard g(ctx->device);
+  size_t need = 0;
+  for (int i = 0; i < n_w; ++i) need = std::max(need, split_need(ws[i]));
+  float* part = nullptr;
+  if (need) ALM_TRY(dev_alloc_t(&part, need));
+  SplitScratch scr{part, need};
+  Epi e;
+  e.out = reinterpret_cast<half*>(y_dev);
+  e.ldo = ws[0]->out;
+  e.n_out = ws[0]->out;
+  const ActIn in = raw_in(reinterpret_cast<const half*>(x_dev), ws[0]->in_real, ws[0]->in_real);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int rc = ALM_OK;
+  cudaError_t err = cudaEventCreate(&e0);
+  if (err == cudaSuccess) err = cudaEventCreate(&e1);
+  for (int i = 0; err == cudaSuccess && i < n_w; ++i)   // warm-up
+    err = launch_gemv(ws[i]->t, in, m, EPI_STORE, e, StepIO{}, scr, false, ctx->stream);
+  if (err == cudaSuccess) err = cudaEventRecord(e0, ctx->stream);
+  for (int i = 0; err == cudaSuccess && i < iters; ++i)
+    err = launch_gemv(ws[i % n_w]->t, in, m, EPI_STORE, e, StepIO{}, scr, false, ctx->stream);
+  if (err == cudaSuccess) err = cudaEventRecord(e1, ctx->stream);
+  if (err == cudaSuccess) err = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
+  if (err != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("bench: ") + cudaGetErrorString(err));
+  else *avg_us = ms * 1000.f / iters;
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  dev_free(part);
+  return rc;
 }
 
 }  // extern "C"

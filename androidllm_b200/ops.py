@@ -153,6 +153,21 @@ class QWeight:
             pass
 
 
+def bench_qmatmul(ctx, weights, x, iters):
+    """Mean device time (us) of one dequant-GEMV launch, cycling through
+    ``weights`` (QWeight of one shape) so their total can exceed L2."""
+    x = _f16(x)
+    m = x.shape[0]
+    out = weights[0].proj.out
+    xb = DeviceBuffer(ctx, x.nbytes)
+    yb = DeviceBuffer(ctx, m * out * 2)
+    xb.upload(x)
+    arr = (ctypes.c_void_p * len(weights))(*[w.h.value for w in weights])
+    us = ctypes.c_float()
+    check(lib.alm_bench_qmatmul(ctx.h, arr, len(weights), xb.h, m, yb.h, int(iters), ctypes.byref(us)))
+    return us.value
+
+
 def matmul_f16(a, b, ctx=None):
     """``a @ b.T`` for fp16 a (m, k) and b (n, k) on the GPU (androidllm/neon.py:39-51)."""
     a, b = _f16(a), _f16(b)
@@ -366,6 +381,17 @@ class SpecDecoder:
         acc = np.empty(n_steps, np.int32)
         check(lib.alm_spec_run(self.h, int(n_steps), ptr(emitted), ptr(n), ptr(acc)))
         return emitted[: int(n[0])].tolist(), acc.tolist()
+
+    def bench(self, n_steps):
+        """Device-timed replay of n_steps steps: (ms, emitted tokens)."""
+        ms, n = ctypes.c_float(), ctypes.c_int32()
+        check(lib.alm_spec_bench(self.h, int(n_steps), ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
+    def kernel_count(self):
+        n = ctypes.c_int32()
+        check(lib.alm_spec_kernel_count(self.h, ctypes.byref(n)))
+        return n.value
 
     def state(self):
         t, p = ctypes.c_int32(), ctypes.c_int32()

@@ -105,6 +105,88 @@ def shard_from_tensors(source, canon, out, attn_bits=4, mlp_bits=8, block=64, em
     return manifest
 
 
+def _synth_layer_task(args):
+    """Quantize and write one layer of a seeded synthetic model (worker)."""
+    from . import synth
+    canon, seed, out, li, attn_bits, mlp_bits, block = args
+    specs = synth.tensor_specs(canon)
+    weights, norms, meta = {}, {}, {}
+    prefix = f"model.layers.{li}."
+    for idx, (name, shape, kind) in enumerate(specs):
+        if not name.startswith(prefix):
+            continue
+        w = synth.make_tensor(seed, idx, shape, kind)
+        k, key = classify(name)
+        if k == "norm":
+            norms[key[1]] = w.astype(np.float16)
+            continue
+        bits = attn_bits if k == "attn" else mlp_bits
+        q, sc = quantize_matrix(w, bits=bits, block=block)
+        base = key[1].split("_")[0]
+        weights[base + ".q"] = codes_for_storage(q, bits)
+        weights[base + ".scale"] = sc.astype(np.float16)
+        meta[base] = {"bits": bits, "block": block, "out": int(q.shape[0]), "in": int(q.shape[1]),
+                      "in_real": int(w.shape[1]), "packed": "U8" if bits == 4 else "I8"}
+    tensors = dict(weights)
+    tensors.update(norms)
+    safetensors.write(os.path.join(out, f"layer_{li}.safetensors"), tensors)
+    return li, meta
+
+
+def write_synthetic(canon, seed, out, attn_bits=4, mlp_bits=8, block=64, embed_bits=8, workers=8):
+    """Write the seeded synthetic model of ``synth.synth_tensors(canon, seed)``
+    as a shard directory, layers in parallel (spawned worker processes).
+    Produces the same files as :func:`shard_from_tensors` on those tensors."""
+    import multiprocessing as mp
+
+    from . import synth
+    os.makedirs(out, exist_ok=True)
+    tasks = [(canon, seed, out, li, attn_bits, mlp_bits, block) for li in range(canon["layers"])]
+    if workers > 1:
+        with mp.get_context("spawn").Pool(workers) as pool:
+            results = pool.map(_synth_layer_task, tasks)
+    else:
+        results = [_synth_layer_task(t) for t in tasks]
+    qmeta = {str(li): meta for li, meta in sorted(results)}
+    glob_src = {}
+    for idx, (name, shape, kind) in enumerate(synth.tensor_specs(canon)):
+        if classify(name)[0] == "global":
+            glob_src[name] = (idx, shape, kind)
+    glob, embed_quant, head_quant = {}, {}, {}
+    for name, (idx, shape, kind) in glob_src.items():
+        key = classify(name)[1]
+        w = synth.make_tensor(seed, idx, shape, kind)
+        if key in ("embed", "lm_head") and embed_bits:
+            q, sc, meta = _quant_global(w, embed_bits)
+            glob[key + ".q"], glob[key + ".scale"] = q, sc
+            if key == "embed":
+                embed_quant = meta
+            else:
+                head_quant = meta
+        else:
+            glob[key] = w.astype(np.float16)
+        del w
+    safetensors.write(os.path.join(out, "embeddings.safetensors"),
+                      {k: v for k, v in glob.items() if k.startswith("embed")})
+    safetensors.write(os.path.join(out, "norms.safetensors"), {"final_norm": glob["final_norm"]})
+    if "lm_head" in glob or head_quant:
+        safetensors.write(os.path.join(out, "lm_head.safetensors"),
+                          {k: v for k, v in glob.items() if k.startswith("lm_head")})
+    manifest = {
+        "format": "androidllm/v1",
+        "name": canon["name"],
+        "config": canon,
+        "quant": {"attn_bits": attn_bits, "mlp_bits": mlp_bits, "block": block, "layers": qmeta},
+        "embed_quant": embed_quant,
+        "lm_head_quant": head_quant,
+        "tied": canon["tied"],
+        "has_lm_head": bool(head_quant) or "lm_head" in glob,
+    }
+    with open(os.path.join(out, "manifest.json"), "w", encoding="utf-8") as f:
+        json.dump(manifest, f, indent=2)
+    return manifest
+
+
 def prefix_draft(target_dir, draft_dir, n_layers, name=None):
     """A draft made of the target's first ``n_layers`` layers.
 

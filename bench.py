@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Speculative-decode throughput of the androidllm verify path on B200.
+
+Workload (default): Qwen2.5-1.5B-shaped target (hidden 1536, 28 layers, 12/2
+heads, head_dim 128, FFN 8960, vocab 151936, tied int8 per-row embedding,
+int4 attention / int8 MLP, block-64 symmetric) with a Qwen2.5-0.5B-shaped int4
+draft, k = 4, greedy, batch 1, 512-token prompt and 256-token episodes.
+Weights are seeded random-init (N(0, 0.02)), written in androidllm's shard
+format and loaded through the public engine API.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one speculative step (k draft forwards, one (k+1)-row verify
+forward, acceptance).  ``value`` is whole-job tokens/s with every input
+resident in HBM (device-timed graph replays); ``e2e`` is the same metric
+through ``LayerStreamingEngine.generate`` with a host round trip per step.
+With N > 1 each rank runs an independent replica (no data-path collective).
+``--impl reference`` times the CPU restatement of the reference numpy path
+(the oracle port) on this host on a bounded sample.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "spec-decode tokens/sec (k=4) at Qwen2.5-1.5B int4"
+PROMPT_LEN = 512
+EPISODE_TOKENS = 256
+SPEC_K = 4
+CACHE = os.environ.get("ALM_BENCH_CACHE", "/tmp/androidllm_b200_bench")
+REF_MAX_SAMPLES = 96
+
+WORKLOADS = {
+    # name: (target canon, target bits, draft canon, draft bits)
+    "qwen2.5-1.5b": ("qwen2.5-1.5b", dict(attn_bits=4, mlp_bits=8, block=64, embed_bits=8),
+                     "qwen2.5-0.5b", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=8)),
+    "toy": ("toy", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=0), None, None),
+}
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# --------------------------------------------------------------------------
+# models
+# --------------------------------------------------------------------------
+def ensure_model(canon_name, kw, seed):
+    from androidllm_b200 import shard, synth
+    canon = dict(synth.CANONS[canon_name])
+    tag = f"{canon_name}-s{seed}-a{kw['attn_bits']}m{kw['mlp_bits']}e{kw['embed_bits']}"
+    out = os.path.join(CACHE, tag)
+    if not os.path.exists(os.path.join(out, ".complete")):
+        shard.write_synthetic(canon, seed, out, workers=min(16, os.cpu_count() or 4), **kw)
+        open(os.path.join(out, ".complete"), "w").close()
+    return out
+
+
+def prepare_models(workload):
+    tname, tkw, dname, dkw = WORKLOADS[workload]
+    tdir = ensure_model(tname, tkw, seed=1)
+    if dname is None:
+        from androidllm_b200 import shard
+        ddir = os.path.join(CACHE, f"{tname}-draft2")
+        if not os.path.exists(os.path.join(ddir, "manifest.json")):
+            shard.prefix_draft(tdir, ddir, 2)
+        return tdir, ddir
+    return tdir, ensure_model(dname, dkw, seed=2)
+
+
+# --------------------------------------------------------------------------
+# algorithmic bytes
+# --------------------------------------------------------------------------
+def gemv_bytes(n, k, m, bits, block=64):
+    w = n * k * bits // 8
+    s = 0 if bits == 16 else n * (k // block) * 2
+    return w + s + m * k * 2 + m * n * 2
+
+
+def forward_weight_bytes(man):
+    """Weight + scale bytes one forward streams (all layers + head)."""
+    total = 0
+    for li, projs in man["quant"]["layers"].items():
+        for base, q in projs.items():
+            total += q["out"] * q["in"] * q["bits"] // 8 + q["out"] * (q["in"] // q["block"]) * 2
+    c = man["config"]
+    hq = man.get("lm_head_quant") or man.get("embed_quant") or {}
+    if hq:
+        total += c["vocab"] * c["hidden"] * hq["bits"] // 8 + c["vocab"] * (c["hidden"] // hq["block"]) * 2
+    else:
+        total += c["vocab"] * c["hidden"] * 2
+    return total
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.device = vis.split(",")[device] if vis else device
+        self.proc = None
+        self.path = os.path.join(CACHE, f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        os.makedirs(CACHE, exist_ok=True)
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.device), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference numpy path (bounded sample)
+# --------------------------------------------------------------------------
+class CpuSample:
+    """Times the reference numpy computation (oracle restatement of
+    androidllm/models/llama.py) for the workload's shapes: one target layer,
+    one draft layer (each at position PROMPT_LEN) and a 1/layers slice of each
+    LM head per sample, then extrapolates the time of one speculative step."""
+
+    def __init__(self, workload):
+        from androidllm_b200 import synth
+        from oracle import llama
+        tname, _, dname, _ = WORKLOADS[workload]
+        self.llama = llama
+        self.tc = dict(synth.CANONS[tname])
+        self.dc = dict(synth.CANONS[dname or tname], layers=2 if dname is None else synth.CANONS[dname]["layers"])
+        rng = np.random.default_rng(0)
+        self.t = self._setup(self.tc, rng)
+        self.d = self._setup(self.dc, rng)
+
+    def _setup(self, c, rng):
+        h, hd, nh, nkv, i = c["hidden"], c["head_dim"], c["heads"], c["kv_heads"], c["intermediate"]
+        mk = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02).astype(np.float16)  # noqa: E731
+        layer = {"q": mk(nh * hd, h), "k": mk(nkv * hd, h), "v": mk(nkv * hd, h), "o": mk(h, nh * hd),
+                 "gate": mk(i, h), "up": mk(i, h), "down": mk(h, i),
+                 "n_in": np.ones(h, np.float16), "n_post": np.ones(h, np.float16)}
+        canon = dict(c, max_len=PROMPT_LEN + 8)
+        model = self.llama.OracleModel(canon, None, np.ones(h, np.float16), None)
+        kv = (mk(PROMPT_LEN + 8, nkv, hd) * 50, mk(PROMPT_LEN + 8, nkv, hd) * 50)
+        n_slice = -(-c["vocab"] // c["layers"])
+        head_slice = mk(n_slice, h)
+        x = (rng.standard_normal((1, h)).astype(np.float16))
+        return {"c": c, "layer": layer, "model": model, "kv": kv, "head": head_slice, "x": x}
+
+    def _one(self, s):
+        t0 = time.perf_counter()
+        s["model"].layer_forward(s["x"], s["layer"], s["kv"], PROMPT_LEN)
+        t1 = time.perf_counter()
+        h = self.llama.rms_norm(s["x"], s["model"].final_norm)
+        self.llama.matmul_f16(h.astype(np.float16), s["head"])
+        t2 = time.perf_counter()
+        # per full token: layers x layer time + layers x (1/layers of the head)
+        return s["c"]["layers"] * ((t1 - t0) + (t2 - t1))
+
+    def step(self, tokens_per_step, k=SPEC_K):
+        """Seconds of one reference speculative step (androidllm/engine.py:288-320):
+        k draft tokens, then one target token per emitted token."""
+        t_target = self._one(self.t)
+        t_draft = self._one(self.d)
+        return k * t_draft + tokens_per_step * t_target, t_target, t_draft
+
+
+def cpu_baseline(workload, tokens_per_step, samples):
+    s = CpuSample(workload)
+    s.step(tokens_per_step)       # warm-up
+    times = []
+    t0 = time.perf_counter()
+    tt = td = 0.0
+    for _ in range(samples):
+        st, a, b = s.step(tokens_per_step)
+        times.append(st)
+        tt += a
+        td += b
+    wall = time.perf_counter() - t0
+    step_s = statistics.mean(times)
+    return {
+        "value": tokens_per_step / step_s,
+        "unit": "tokens/s",
+        "cores": 1,
+        "kind": "port",
+        "sample": (f"{samples} samples of one target layer + one draft layer at position {PROMPT_LEN} "
+                   f"and a 1/layers slice of each fp16 LM head (numpy fp16 matmul, 1 thread), "
+                   f"extrapolated to a full step of {SPEC_K} draft tokens + {tokens_per_step:.2f} target "
+                   f"tokens with resident dequantized weights (the reference's default streaming engine "
+                   f"also dequantizes every layer per token); {wall:.1f}s of CPU work"),
+        "target_token_s": tt / samples,
+        "draft_token_s": td / samples,
+    }
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    tokens_per_step = 1.0
+    t0 = time.perf_counter()
+    # each sample is ~0.3 s of numpy work at the 1.5B shapes; cap the count so
+    # the arm ends within a few minutes whatever --steps is
+    cb = cpu_baseline(args.workload, tokens_per_step, min(REF_MAX_SAMPLES, max(1, args.steps)))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * tokens_per_step / cb["value"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(args, world),
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, world):
+    return {"workload": args.workload + " spec-decode (draft qwen2.5-0.5b shape, int4)"
+            if args.workload == "qwen2.5-1.5b" else args.workload,
+            "target": "qwen2.5-1.5b: int4 attention, int8 MLP, tied int8 per-row head, block 64",
+            "draft": "qwen2.5-0.5b: int4, tied int8 per-row head", "k": SPEC_K, "batch": 1,
+            "prompt_len": PROMPT_LEN, "episode_tokens": EPISODE_TOKENS, "temperature": 0,
+            "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "l2": "weights (2.8 GB streamed per step) exceed the 126 MB L2; no flush needed"}
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+def run_ours(args):
+    rank, world, local = dist_env()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if rank == 0:
+        tdir, ddir = prepare_models(args.workload)
+    if dist is not None:
+        dist.barrier()
+        tdir, ddir = prepare_models(args.workload)
+    os.environ.setdefault("ANDROIDLLM_MAX_CTX", "4096")
+
+    from androidllm_b200.engine import LayerStreamingEngine
+    from androidllm_b200.ops import QuantProj, QWeight, bench_qmatmul
+    eng = LayerStreamingEngine(tdir, draft_dir=ddir, spec_k=SPEC_K, device=local)
+    prompt = np.random.default_rng(123).integers(0, eng.canon["vocab"], PROMPT_LEN).tolist()
+
+    # e2e through the public API: generate() with a host round trip per step
+    eng.generate(prompt, max_new_tokens=16, temperature=0)          # warm-up (graph, caches)
+    out = eng.generate(prompt, max_new_tokens=EPISODE_TOKENS, temperature=0)
+    dec = eng.last_decode
+    e2e = {"value": len(out) / dec["seconds"], "unit": "tokens/s",
+           # per step: the (token, pos) state in (16 B), the state + emitted
+           # tokens + accepted count out
+           "h2d_bytes_per_step": 16,
+           "d2h_bytes_per_step": 16 + 4 * (len(out) / max(1, dec["steps"])) + 4,
+           "steps": dec["steps"], "tokens": len(out)}
+
+    # device-resident throughput: episodes of up to EPISODE_TOKENS steps from
+    # the post-prompt state, graph replays timed with CUDA events
+    spec = eng._spec_decoder()
+    state0 = (prompt[-1], PROMPT_LEN - 1)
+    eng._target_kv().cache.zero()
+    eng._prefill(eng._kv, prompt[:-1], 0)
+    eng._draft_kv().cache.zero()
+    eng.draft._prefill(eng.draft._kv, prompt, 0)
+
+    def episodes(n_steps):
+        ms_tot, tok_tot, left = 0.0, 0, n_steps
+        while left > 0:
+            n = min(left, EPISODE_TOKENS)
+            spec.begin(*state0)
+            ms, tok = spec.bench(n)
+            ms_tot += ms
+            tok_tot += tok
+            left -= n
+        return ms_tot, tok_tot
+
+    episodes(max(3, args.warmup))
+    if dist is not None:
+        import torch
+        dist.barrier()
+        torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_wall = time.perf_counter()
+        ms, tokens = episodes(args.steps)
+        t_wall = time.perf_counter() - t_wall
+    if dist is not None:
+        import torch
+        t = torch.tensor([ms, float(tokens)], dtype=torch.float64, device="cuda")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        torch.cuda.synchronize()
+        ms_max, tokens_all = float(mx[0]), int(sm[1])
+        dist.barrier()
+    else:
+        ms_max, tokens_all = ms, tokens
+    value = tokens_all / (ms_max / 1000.0)
+    ms_per_step = ms_max / args.steps
+
+    # roofline of the dominant kernel: the fused gate/up dequant-GEMV of the
+    # target verify pass (int8, N = 2 x 8960, K = 1536, M = k+1 = 5), timed in
+    # isolation over rotating weight copies larger than L2
+    c = eng.canon
+    n_gu, k_gu, m = 2 * c["intermediate"], c["hidden"], SPEC_K + 1
+    rng = np.random.default_rng(7)
+    copies = []
+    for i in range(6):
+        q = rng.integers(-127, 128, size=(n_gu, k_gu), dtype=np.int8)
+        s = (np.abs(rng.standard_normal((n_gu, k_gu // 64))) * 0.003 + 1e-4).astype(np.float16)
+        copies.append(QWeight(eng.ctx, QuantProj(q, s, 8, 64, n_gu, k_gu)))
+    x = rng.standard_normal((m, k_gu)).astype(np.float16)
+    us = bench_qmatmul(eng.ctx, copies, x, 600)
+    alg = gemv_bytes(n_gu, k_gu, m, 8)
+    peaks = load_peaks()
+    achieved = alg / (us * 1e-6) / 1e9
+    roofline = {"kernel": "gemv_kernel<8,1,*> fused gate/up, int8, N=17920 K=1536 M=5",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3),
+                "peak_source": peaks["source"], "algorithmic_bytes": alg, "avg_launch_us": round(us, 2),
+                "traffic": None}
+    step_bytes = SPEC_K * forward_weight_bytes(eng.draft.manifest) + forward_weight_bytes(eng.manifest)
+    step_roof = step_bytes / (ms_per_step * 1e-3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": workload_config(args, world),
+        "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "roofline": roofline,
+        "step_roofline": {"weight_bytes_per_step": step_bytes, "achieved_gbs": round(step_roof, 1),
+                          "frac": round(step_roof / peaks["hbm_gbs"], 3)},
+        "tokens_per_step": round(tokens_all / (args.steps * world), 3),
+        "gpu_launches": spec.kernel_count() * args.steps,
+        "clocks": clk.summary(),
+        "wall_s_timed": round(t_wall, 3),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.workload, tokens_per_step=line["tokens_per_step"], samples=args.cpu_samples)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    spec.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen2.5-1.5b")
+    ap.add_argument("--cpu-samples", type=int, default=6)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -171,6 +171,19 @@ ALM_API int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_
                  int32_t* accepted_host);
 /* Current (token, pos) state. */
 ALM_API int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos);
+/* Number of kernel nodes in one speculative step's CUDA graph. */
+ALM_API int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels);
+
+/* ---- measurement ---------------------------------------------------------------- */
+/* Replay n_steps speculative steps back to back and time them with CUDA
+ * events on the context's stream: *ms = device time, *n_emitted = tokens.
+ * The state advances as in alm_spec_run. */
+ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted);
+/* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
+ * n_w weights of one shape (so their total can exceed L2); *avg_us is the
+ * mean device time of one launch. */
+ALM_API int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint16_t* x_dev, int m,
+                              uint16_t* y_dev, int iters, float* avg_us);
 
 #ifdef __cplusplus
 }
