@@ -75,6 +75,7 @@ SIGNATURES = {
     "alm_spec_run": [_P, _I, _P, _P, _P],
     "alm_spec_state": [_P, _PI32, _PI32],
     "alm_spec_kernel_count": [_P, _PI32],
+    "alm_profiler_range": [_I],
     "alm_spec_bench": [_P, _I, ctypes.POINTER(ctypes.c_float), _PI32],
     "alm_bench_qmatmul": [_P, _PP, _I, _P, _I, _P, _I, ctypes.POINTER(ctypes.c_float)],
 }

@@ -27,6 +27,7 @@ namespace alm {
 namespace {
 
 constexpr int kAttnThreads = 128;
+constexpr int kPvThreads = 256;
 
 ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
   uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -60,28 +61,60 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
 
-  // Q rows -> fp16 hi/lo
-  for (int i = tid; i < kAttnRows * hd; i += kAttnThreads) {
-    const int rl = i / hd, d = i % hd;
-    const int r = rg * kAttnRows + rl;
-    float v = 0.f;
-    if (r < n_rows) {
-      const int m = r / gq, head = kvh * gq + r % gq;
-      v = a.q[static_cast<size_t>(m) * a.ldq + head * hd + d];
+  // Q rows -> fp16 hi/lo (float4 loads, all issued before use)
+  {
+    const int per_row = hd / 4;
+    const int n4 = kAttnRows * per_row;
+    for (int base = 0; base < n4; base += kAttnThreads * 4) {
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        const int rl = i / per_row, d4 = i % per_row;
+        const int r = rg * kAttnRows + rl;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4 && r < n_rows) {
+          const int m = r / gq, head = kvh * gq + r % gq;
+          v[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        if (i >= n4) break;
+        const int rl = i / per_row, d = (i % per_row) * 4;
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const half h = __float2half_rn(vv[e]);
+          qhi[rl * ld + d + e] = h;
+          qlo[rl * ld + d + e] = __float2half_rn(vv[e] - __half2float(h));
+        }
+      }
     }
-    const half h = __float2half_rn(v);
-    qhi[rl * ld + d] = h;
-    qlo[rl * ld + d] = __float2half_rn(v - __half2float(h));
   }
-  // K chunk (16-byte vectors)
-  const int vec_per_row = hd / 8;
-  for (int i = tid; i < kAttnChunk * vec_per_row; i += kAttnThreads) {
-    const int pl = i / vec_per_row, v8 = i % vec_per_row;
-    const int p = c0 + pl;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (p < n_ctx)
-      val = reinterpret_cast<const uint4*>(kv_row(a.kcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p))[v8];
-    *reinterpret_cast<uint4*>(ks + pl * ld + v8 * 8) = val;
+  // K chunk (16-byte vectors, all issued before use)
+  {
+    const int vec_per_row = hd / 8;
+    const int nv = kAttnChunk * vec_per_row;
+    for (int base = 0; base < nv; base += kAttnThreads * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        const int p = c0 + i / vec_per_row;
+        v[j] = make_uint4(0, 0, 0, 0);
+        if (i < nv && p < n_ctx)
+          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, a.page_table, a.page_size, a.kv_heads, kvh,
+                                                              hd, p)) + i % vec_per_row);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        if (i >= nv) break;
+        *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = v[j];
+      }
+    }
   }
   __syncthreads();
 
@@ -159,16 +192,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
     st[0] = s_max[tid];
     st[1] = l;
   }
+  grid_dep_launch();
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
+__global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int kVld = 24;                 // V slice row stride (halves): conflict-free
   constexpr int kPld = kPvSpan + 8;        // P row stride (halves)
+  constexpr int kWarpsPv = kPvThreads / kWarp;
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kVld]
   half* ps = vs + kPvSpan * kVld;                    // [16][kPld]
   __shared__ float s_m[kAttnRows], s_l[kAttnRows];
-  __shared__ float s_acc[4][kWarp][8];
+  __shared__ float s_acc[kWarpsPv][kWarp][8];
 
   grid_dep_wait();
   const int ds = blockIdx.x, kvh = blockIdx.y, rg = blockIdx.z;
@@ -182,17 +217,44 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
 
-  if (tid < kAttnRows) {
+  // row max / sum from the chunk statistics: one warp per row, lane l takes
+  // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
+  // a row's last position contribute exact zeros)
+  {
     const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
-    float mx = kNegInf;
-    for (int c = 0; c < n_chunks; ++c) mx = fmaxf(mx, st[(c * kAttnRows + tid) * 2]);
-    float l = 0.f;
-    for (int c = 0; c < n_chunks; ++c) {
-      const float mc = st[(c * kAttnRows + tid) * 2];
-      if (mc != kNegInf) l = fadd(l, fmul(st[(c * kAttnRows + tid) * 2 + 1], expf(mc - mx)));
+    for (int rl = warp; rl < kAttnRows; rl += kWarpsPv) {
+      float mc[4], lc[4];
+      float mx = kNegInf;
+      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = base + j * 32 + lane;
+          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc[j]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float l = 0.f;
+      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = base + j * 32 + lane;
+          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+          lc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2 + 1) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (mc[j] != kNegInf) l = fadd(l, fmul(lc[j], expf(mc[j] - mx)));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
+      if (lane == 0) {
+        s_m[rl] = mx;
+        s_l[rl] = l;
+      }
     }
-    s_m[tid] = mx;
-    s_l[tid] = l;
   }
   __syncthreads();
 
@@ -201,29 +263,57 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
     const int span = min(kPvSpan, n_ctx - base);
     const int span_pad = (span + 15) & ~15;
     // V slice: 16 dims (two 16 B vectors) per position
-    for (int i = tid; i < span_pad * 2; i += kAttnThreads) {
-      const int pl = i >> 1, hv = i & 1;
-      const int p = base + pl;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (p < n_ctx)
-        val = reinterpret_cast<const uint4*>(
-            kv_row(a.vcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16)[hv];
-      *reinterpret_cast<uint4*>(vs + pl * kVld + hv * 8) = val;
-    }
-    // P = fp16(exp(s - max) / sum)
-    for (int i = tid; i < kAttnRows * span_pad; i += kAttnThreads) {
-      const int rl = i / span_pad, pl = i % span_pad;
-      const int p = base + pl;
-      float pv = 0.f;
-      const int r = rg * kAttnRows + rl;
-      if (r < n_rows && p < n_ctx) {
-        const float s = a.scores[(srow0 + rl) * a.score_ld + p];
-        if (s != kNegInf) pv = fdiv(expf(s - s_m[rl]), s_l[rl]);
+    const int nv = span_pad * 2;
+    for (int b0 = 0; b0 < nv; b0 += kPvThreads * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kPvThreads + tid;
+        const int p = base + (i >> 1);
+        v[j] = make_uint4(0, 0, 0, 0);
+        if (i < nv && p < n_ctx)
+          v[j] = __ldcg(reinterpret_cast<const uint4*>(
+                            kv_row(a.vcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
+                        (i & 1));
       }
-      ps[rl * kPld + pl] = __float2half_rn(pv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kPvThreads + tid;
+        if (i >= nv) break;
+        *reinterpret_cast<uint4*>(vs + (i >> 1) * kVld + (i & 1) * 8) = v[j];
+      }
+    }
+    // P = fp16(exp(s - max) / sum), 4 scores per float4 load
+    const int per_row4 = span_pad / 4;
+    const int np = kAttnRows * per_row4;
+    for (int b0 = 0; b0 < np; b0 += kPvThreads * 8) {
+      float4 sv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kPvThreads + tid;
+        const int rl = i / per_row4, p = base + (i % per_row4) * 4;
+        const int r = rg * kAttnRows + rl;
+        sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+        if (i < np && r < n_rows)
+          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + rl) * a.score_ld + p));
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kPvThreads + tid;
+        if (i >= np) break;
+        const int rl = i / per_row4, pl = (i % per_row4) * 4;
+        const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int p = base + pl + e;
+          float pv = 0.f;
+          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - s_m[rl]), s_l[rl]);
+          ps[rl * kPld + pl + e] = __float2half_rn(pv);
+        }
+      }
     }
     __syncthreads();
-    for (int kk = warp; kk < span_pad / 16; kk += 4) {
+    for (int kk = warp; kk < span_pad / 16; kk += kWarpsPv) {
       uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
       ldmatrix_x4(a0, a1, a2, a3, ps + (lane % 16) * kPld + kk * 16 + (lane / 16) * 8);
       // matrices: (k0-7, n0-7) (k8-15, n0-7) (k0-7, n8-15) (k8-15, n8-15)
@@ -241,6 +331,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
 #pragma unroll
     for (int e = 0; e < 4; ++e) s_acc[warp][lane][nt * 4 + e] = acc[nt][e];
   __syncthreads();
+  grid_dep_launch();
   if (warp == 0) {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -248,7 +339,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float v = s_acc[0][lane][nt * 4 + e];
-        for (int w2 = 1; w2 < 4; ++w2) v = fadd(v, s_acc[w2][lane][nt * 4 + e]);
+        for (int w2 = 1; w2 < kWarpsPv; ++w2) v = fadd(v, s_acc[w2][lane][nt * 4 + e]);
         const int r = rg * kAttnRows + g + 8 * (e >> 1);
         if (r < n_rows) {
           const int m = r / gq, head = kvh * gq + r % gq;
@@ -294,6 +385,7 @@ cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
                        static_cast<size_t>(kAttnRows) * (kPvSpan + 8) * sizeof(half);
   cudaLaunchConfig_t c2 = c1;
   c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, n_rg);
+  c2.blockDim = dim3(kPvThreads);
   c2.dynamicSmemBytes = smem2;
   return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);
 }

@@ -21,6 +21,7 @@
 // androidllm/models/llama.py:96-146.
 #include <algorithm>
 
+#include "act.cuh"
 #include "kernels.cuh"
 #include "qtile.cuh"
 
@@ -34,28 +35,16 @@ constexpr size_t kGemvMaxSmem = 200 * 1024;   // x staging limit (dynamic shared
 template <int BITS>
 struct Pipe { static constexpr int U = BITS == 4 ? 8 : BITS == 8 ? 4 : 2; };
 
-// 1 / RMS denominator inputs: returns sqrt(mean + eps) for row m of an ActIn
-// with deferred norm.  Sequential sum over the per-tile partials.
-ALM_DEV float row_denominator(const ActIn& a, int m) {
-  const float* p = a.ss + static_cast<size_t>(m) * a.n_ss;
-  float s = 0.f;
-  for (int i = 0; i < a.n_ss; ++i) s = fadd(s, p[i]);
-  return sqrtf(fadd(fdiv(s, static_cast<float>(a.H)), a.eps));
-}
-
-// Activation element (m, k) as fp32 (an fp16 value).
-ALM_DEV float act_value(const ActIn& a, int m, int k, float denom) {
-  const float v = __half2float(a.x[static_cast<size_t>(m) * a.ld + k]);
-  if (a.ss == nullptr) return v;
-  return round_h(fmul(fdiv(v, denom), __half2float(a.w[k])));
-}
+// Chunks of 8 activation columns staged per thread per batch (all loads of a
+// batch are issued before any is used, so a batch costs one memory round trip).
+constexpr int kStageBatch = 4;
 
 ALM_DEV bool better(float v1, int i1, float v2, int i2) {
   return v1 > v2 || (v1 == v2 && i1 < i2);
 }
 
 template <int BITS, int NT8, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M, Epi epi, StepIO io,
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, int M, Epi epi, StepIO io,
                                                         float* __restrict__ part) {
   extern __shared__ uint4 xs[];  // [kb_local][NT8][2][32] uint4
   __shared__ float red[kWarps][kWarp][NT8 * 4];
@@ -100,40 +89,60 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M
 
   grid_dep_wait();
 
-  // ---- row denominators of deferred norms ---------------------------------
-  if (threadIdx.x < M) {
-    if (in.ss) s_den_in[threadIdx.x] = row_denominator(in, threadIdx.x);
-    if constexpr (EPI == EPI_RESID)
-      if (epi.res.ss) s_den_res[threadIdx.x] = row_denominator(epi.res, threadIdx.x);
+  // ---- row denominators of deferred norms (one warp per row) ------------------
+  for (int m = warp; m < M; m += kWarps) {
+    if (in.ss) {
+      const float d = row_denominator(in, m);
+      if (lane == 0) s_den_in[m] = d;
+    }
+    if constexpr (EPI == EPI_RESID) {
+      if (epi.res.ss) {
+        const float d = row_denominator(epi.res, m);
+        if (lane == 0) s_den_res[m] = d;
+      }
+    }
   }
   __syncthreads();
 
   // ---- stage activations as B fragments ------------------------------------
   {
     uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-    const int rows = NT8 * 8;
-    const int n_chunks = cta_nkb * 8 * rows;   // 8-column chunks
-    for (int c = threadIdx.x; c < n_chunks; c += kThreads) {
-      const int m = c / (cta_nkb * 8);
-      const int rem = c % (cta_nkb * 8);
-      const int kbl = rem / 8, c8 = rem % 8;
-      const int col0 = (cta_kb0 + kbl) * 64 + c8 * 8;
-      float v[8];
-      if (m < M) {
-        const float den = in.ss ? s_den_in[m] : 1.f;
+    const int per_row = cta_nkb * 8;           // 8-column chunks per row
+    const int n_chunks = per_row * NT8 * 8;
+    const bool deferred = in.ss != nullptr;
+    for (int base = 0; base < n_chunks; base += kThreads * kStageBatch) {
+      uint4 raw[kStageBatch], wv[kStageBatch];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (col0 + j < w.k_real) ? act_value(in, m, col0 + j, den) : 0.f;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int c = base + j * kThreads + threadIdx.x;
+        const int m = c / per_row;
+        const int col0 = cta_kb0 * 64 + (c % per_row) * 8;
+        const bool ok = c < n_chunks && m < M;
+        raw[j] = ok ? load_row8(in, m, col0, w.k_real) : make_uint4(0, 0, 0, 0);
+        wv[j] = (ok && deferred) ? load_w8(in.w, col0, w.k_real, in.vec) : make_uint4(0, 0, 0, 0);
       }
-      const int s = c8 >> 1, hi8 = c8 & 1;
-      const int nt = m >> 3, h = s >> 1, r = (s & 1) * 2 + hi8;
 #pragma unroll
-      for (int tt = 0; tt < 4; ++tt) {
-        const int ln = (m & 7) * 4 + tt;
-        const half2 hv = __floats2half2_rn(v[2 * tt], v[2 * tt + 1]);
-        xw[(((kbl * NT8 + nt) * 2 + h) * kWarp + ln) * 4 + r] = h2u(hv);
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int c = base + j * kThreads + threadIdx.x;
+        if (c >= n_chunks) break;
+        const int m = c / per_row;
+        const int rem = c % per_row;
+        const int kbl = rem / 8, c8 = rem % 8;
+        const int s = c8 >> 1, hi8 = c8 & 1;
+        const int nt = m >> 3, h = s >> 1, r = (s & 1) * 2 + hi8;
+        uint32_t words[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+        if (deferred && m < M) {
+          const float den = s_den_in[m];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a0 = norm_value(u4_half(raw[j], 2 * q), den, u4_half(wv[j], 2 * q));
+            const float a1 = norm_value(u4_half(raw[j], 2 * q + 1), den, u4_half(wv[j], 2 * q + 1));
+            words[q] = h2u(__floats2half2_rn(a0, a1));
+          }
+        }
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt)
+          xw[(((kbl * NT8 + nt) * 2 + h) * kWarp + (m & 7) * 4 + tt) * 4 + r] = words[tt];
       }
     }
   }
@@ -258,6 +267,16 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M
         const bool is_q = tile < tq;
         const int head = is_q ? tile / tph : (tile - tq) / tph;
         const int dlo = (tile % tph) * 8 + g, dhi = dlo + half_d;
+        float cs[NT8][2], sn[NT8][2];
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = nt * 8 + 2 * t + j;
+            const size_t rb = static_cast<size_t>(m < M ? pos0 + m : pos0) * hd;
+            cs[nt][j] = __half2float(__ldg(epi.rope + rb + dlo));
+            sn[nt][j] = __half2float(__ldg(epi.rope + rb + half_d + dlo));
+          }
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
@@ -266,10 +285,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M
             if (m >= M) continue;
             const int pos = pos0 + m;
             const float a = round_h(acc[nt][j]), b = round_h(acc[nt][2 + j]);
-            const float c = __half2float(epi.rope[static_cast<size_t>(pos) * hd + dlo]);
-            const float sn = __half2float(epi.rope[static_cast<size_t>(pos) * hd + half_d + dlo]);
-            const float rlo = fsub(fmul(a, c), fmul(b, sn));
-            const float rhi = fadd(fmul(a, sn), fmul(b, c));
+            const float c = cs[nt][j];
+            const float sv = sn[nt][j];
+            const float rlo = fsub(fmul(a, c), fmul(b, sv));
+            const float rhi = fadd(fmul(a, sv), fmul(b, c));
             if (is_q) {
               float* q = epi.q + static_cast<size_t>(m) * epi.ldq + head * hd;
               q[dlo] = rlo;
@@ -302,6 +321,23 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M
     }
   } else if constexpr (EPI == EPI_RESID) {
     if (owner) {
+      const ActIn& rs = epi.res;
+      float rv[NT8][2][2], rw[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = tile * 16 + g + 8 * r;
+        rw[r] = (rs.ss && row < epi.n_out) ? __half2float(__ldg(rs.w + row)) : 1.f;
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = nt * 8 + 2 * t + j, row = tile * 16 + g + 8 * r;
+            const bool ok = m < M && row < epi.n_out;
+            rv[nt][r][j] = ok ? __half2float(__ldcg(rs.x + static_cast<size_t>(m) * rs.ld + row)) : 0.f;
+          }
 #pragma unroll
       for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
@@ -313,8 +349,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(QTile w, ActIn in, int M
             const int row = tile * 16 + g + 8 * r;
             if (m < M && row < epi.n_out) {
               const float o = round_h(acc[nt][2 * r + j]);
-              const float rv = act_value(epi.res, m, row, epi.res.ss ? s_den_res[m] : 1.f);
-              const half s16 = __float2half_rn(fadd(rv, o));
+              const float res = rs.ss ? norm_value(rv[nt][r][j], s_den_res[m], rw[r]) : rv[nt][r][j];
+              const half s16 = __float2half_rn(fadd(res, o));
               epi.out[static_cast<size_t>(m) * epi.ldo + row] = s16;
               const float sf = __half2float(s16);
               sq = r == 0 ? fmul(sf, sf) : fadd(sq, fmul(sf, sf));
@@ -451,9 +487,13 @@ cudaError_t gemv_init_attrs() {
   return e;
 }
 
-cudaError_t launch_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
+cudaError_t launch_gemv(const QTile& w, const ActIn& in_, int M, EpiKind kind, const Epi& epi_,
                         const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st) {
   if (M < 1 || M > kMaxRows) return cudaErrorInvalidValue;
+  ActIn in = in_;
+  set_vec(in);
+  Epi epi = epi_;
+  if (epi.res.x) set_vec(epi.res);
   if (w.ksg > 1) {
     const size_t need = static_cast<size_t>(w.ksg) * (w.n_tiles + kWarps) * kWarp * 8;
     if (scr.part == nullptr || scr.part_floats < need || w.counters == nullptr) return cudaErrorInvalidValue;

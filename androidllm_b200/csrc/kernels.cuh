@@ -60,7 +60,16 @@ struct ActIn {
   const half* w = nullptr;
   float eps = 0.f;
   int H = 0;
+  int vec = 0;   // rows (and norm weights) allow 16-byte loads; set by the launchers
 };
+
+// 16-byte loads are allowed when the base is 16-byte aligned and the row
+// stride is a multiple of 8 halves.
+inline void set_vec(ActIn& a) {
+  const bool ok = (reinterpret_cast<uintptr_t>(a.x) % 16 == 0) && (a.ld % 8 == 0) &&
+                  (a.w == nullptr || reinterpret_cast<uintptr_t>(a.w) % 16 == 0);
+  a.vec = ok ? 1 : 0;
+}
 
 enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
 

@@ -1,5 +1,6 @@
 // Row kernels of the forward: embedding gather, materialised RMSNorm(s) and
 // the final argmax over per-CTA partials of the logits GEMV.
+#include "act.cuh"
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -55,23 +56,42 @@ ALM_DEV float block_sum(float v, float* red) {
 __global__ void rownorm_kernel(ActIn in, const half* w2, float eps2, half* out, int ldo) {
   extern __shared__ half xrow[];
   __shared__ float red[kRowThreads / kWarp];
+  __shared__ float s_den;
   grid_dep_wait();
   const int m = blockIdx.x;
   const int H = in.H;
-  float den = 1.f;
-  if (in.ss) {
-    const float* p = in.ss + static_cast<size_t>(m) * in.n_ss;
-    float s = 0.f;
-    for (int i = 0; i < in.n_ss; ++i) s = fadd(s, p[i]);
-    den = sqrtf(fadd(fdiv(s, static_cast<float>(H)), in.eps));
+  if (in.ss && threadIdx.x < kWarp) {
+    const float d = row_denominator(in, m);
+    if (threadIdx.x == 0) s_den = d;
   }
+  __syncthreads();
+  const float den = in.ss ? s_den : 1.f;
   float sq = 0.f;
-  for (int k = threadIdx.x; k < H; k += blockDim.x) {
-    float v = __half2float(in.x[static_cast<size_t>(m) * in.ld + k]);
-    if (in.ss) v = round_h(fmul(fdiv(v, den), __half2float(in.w[k])));
-    xrow[k] = __float2half_rn(v);
-    sq = fadd(sq, fmul(v, v));
+  const int n8 = (H + 7) / 8;
+  for (int base = 0; base < n8; base += kRowThreads * 4) {
+    uint4 raw[4], wv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = base + j * kRowThreads + threadIdx.x;
+      raw[j] = c < n8 ? load_row8(in, m, c * 8, H) : make_uint4(0, 0, 0, 0);
+      wv[j] = (c < n8 && in.ss) ? load_w8(in.w, c * 8, H, in.vec) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = base + j * kRowThreads + threadIdx.x;
+      if (c >= n8) break;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = c * 8 + e;
+        if (k >= H) break;
+        float v = u4_half(raw[j], e);
+        if (in.ss) v = norm_value(v, den, u4_half(wv[j], e));
+        xrow[k] = __float2half_rn(v);
+        sq = fadd(sq, fmul(v, v));
+      }
+    }
   }
+  __syncthreads();
   half* o = out + static_cast<size_t>(m) * ldo;
   if (w2 == nullptr) {
     for (int k = threadIdx.x; k < H; k += blockDim.x) o[k] = xrow[k];
@@ -80,7 +100,7 @@ __global__ void rownorm_kernel(ActIn in, const half* w2, float eps2, half* out, 
   const float tot = block_sum(sq, red);
   const float den2 = sqrtf(fadd(fdiv(tot, static_cast<float>(H)), eps2));
   for (int k = threadIdx.x; k < H; k += blockDim.x)
-    o[k] = __float2half_rn(fmul(fdiv(__half2float(xrow[k]), den2), __half2float(w2[k])));
+    o[k] = __float2half_rn(fmul(fdiv(__half2float(xrow[k]), den2), __half2float(__ldg(w2 + k))));
 }
 
 ALM_DEV bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
@@ -92,10 +112,18 @@ __global__ void argmax_final_kernel(const float* am_val, const int* am_idx, int 
   const int m = blockIdx.x;
   float bv = kNegInf;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n_part; i += blockDim.x) {
-    const float v = am_val[static_cast<size_t>(m) * n_part + i];
-    const int ix = am_idx[static_cast<size_t>(m) * n_part + i];
-    if (better(v, ix, bv, bi)) { bv = v; bi = ix; }
+  for (int base = 0; base < n_part; base += blockDim.x * 8) {
+    float v[8];
+    int ix[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = base + j * blockDim.x + threadIdx.x;
+      v[j] = i < n_part ? __ldcg(am_val + static_cast<size_t>(m) * n_part + i) : kNegInf;
+      ix[j] = i < n_part ? __ldcg(am_idx + static_cast<size_t>(m) * n_part + i) : 0x7fffffff;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (better(v[j], ix[j], bv, bi)) { bv = v[j]; bi = ix[j]; }
   }
   sv[threadIdx.x] = bv;
   si[threadIdx.x] = bi;
@@ -135,9 +163,11 @@ cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st) {
   return cudaLaunchKernelEx(&c, embed_kernel, a);
 }
 
-cudaError_t launch_rownorm(const ActIn& in, int M, const half* w2, float eps2, half* out, int ldo,
+cudaError_t launch_rownorm(const ActIn& in_, int M, const half* w2, float eps2, half* out, int ldo,
                            bool pdl, cudaStream_t st) {
-  if (in.H > 24576) return cudaErrorInvalidValue;
+  if (in_.H > 24576) return cudaErrorInvalidValue;
+  ActIn in = in_;
+  set_vec(in);
   cudaLaunchAttribute attr[1];
   const size_t smem = static_cast<size_t>(in.H) * sizeof(half);
   cudaLaunchConfig_t c = row_cfg(M, smem, pdl, st, attr);

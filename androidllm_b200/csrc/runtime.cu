@@ -1,5 +1,7 @@
 // C ABI of libandroidllm_b200: contexts, weights, models, paged KV cache,
 // forward passes and the graph-replayed speculative step.
+#include <cuda_profiler_api.h>
+
 #include <algorithm>
 #include <cstring>
 #include <string>
@@ -88,6 +90,7 @@ struct alm_ctx {
   int device = 0;
   int n_sms = 148;
   cudaStream_t stream = nullptr;
+  bool pdl = true;   // programmatic dependent launch between forward kernels
 };
 
 struct alm_qweight {
@@ -134,6 +137,7 @@ struct Work {
   float* scores = nullptr;
   float* stats = nullptr;
   int attn_ctx = 0;       // capacity of the attention scratch (positions)
+  int score_ld = 0;       // row stride of the score scratch
   int* pinned = nullptr;  // host staging for small copies
 };
 
@@ -345,9 +349,12 @@ int ensure_attn(alm_model* m, int max_ctx) {
   ws.scores = nullptr;
   ws.stats = nullptr;
   ws.attn_ctx = 0;
-  ALM_TRY(dev_alloc_t(&ws.scores, static_cast<size_t>(m->cfg.kv_heads) * n_rg * kAttnRows * cap));
+  // rows padded by one chunk: the P.V kernel reads whole 16-position groups
+  const int ld = cap + kAttnChunk;
+  ALM_TRY(dev_alloc_t(&ws.scores, static_cast<size_t>(m->cfg.kv_heads) * n_rg * kAttnRows * ld));
   ALM_TRY(dev_alloc_t(&ws.stats, static_cast<size_t>(m->cfg.kv_heads) * n_rg * (cap / kAttnChunk) * kAttnRows * 2));
   ws.attn_ctx = cap;
+  ws.score_ld = ld;
   return ALM_OK;
 }
 
@@ -419,7 +426,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.pos = ws.pos;
   a.max_ctx = kv->max_len;
   a.scores = ws.scores;
-  a.score_ld = ws.attn_ctx;
+  a.score_ld = ws.score_ld;
   a.stats = ws.stats;
   a.ctx = ws.ctx;
   a.ldc = qdim;
@@ -574,6 +581,10 @@ int alm_ctx_create(int device, alm_ctx** out) {
   auto* c = new alm_ctx();
   c->device = device;
   c->n_sms = n_sms_of(device);
+  {
+    const char* e = getenv("ALM_NO_PDL");
+    c->pdl = !(e && e[0] == '1');
+  }
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
     return fail(ALM_ERR_CUDA, "stream creation failed");
@@ -1049,9 +1060,10 @@ int alm_layer_forward(alm_model* m, int layer, alm_kv* kv, const uint16_t* x_hos
   const size_t nb = static_cast<size_t>(rows) * m->cfg.hidden * sizeof(half);
   ALM_TRY(set_pos(m, pos0));
   ALM_CUDA(cudaMemcpyAsync(m->ws.x0, x_host, nb, cudaMemcpyHostToDevice, st));
-  ALM_TRY(enqueue_layer(m, layer, kv, rows, raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), false));
+  const bool pdl = m->ctx->pdl;
+  ALM_TRY(enqueue_layer(m, layer, kv, rows, raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), pdl));
   const ActIn o = deferred_in(m, m->ws.s2, m->ws.ss2, m->layers[layer].n_post);
-  ALM_CUDA(launch_rownorm(o, rows, nullptr, 0.f, m->ws.xout, m->cfg.hidden, false, st));
+  ALM_CUDA(launch_rownorm(o, rows, nullptr, 0.f, m->ws.xout, m->cfg.hidden, pdl, st));
   ALM_CUDA(cudaMemcpyAsync(out_host, m->ws.xout, nb, cudaMemcpyDeviceToHost, st));
   return sync_and_check(m);
 }
@@ -1065,8 +1077,8 @@ int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logit
   ALM_CUDA(cudaMemcpyAsync(m->ws.x0, x_host, static_cast<size_t>(rows) * m->cfg.hidden * 2,
                            cudaMemcpyHostToDevice, st));
   ALM_CUDA(launch_rownorm(raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), rows, m->final_norm, m->cfg.rms_eps,
-                          m->ws.xn, m->cfg.hidden, false, st));
-  ALM_TRY(enqueue_head(m, rows, false));
+                          m->ws.xn, m->cfg.hidden, m->ctx->pdl, st));
+  ALM_TRY(enqueue_head(m, rows, m->ctx->pdl));
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
 }
@@ -1082,7 +1094,7 @@ int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, 
   ALM_TRY(set_pos(m, pos0));
   ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host, rows * sizeof(int), cudaMemcpyHostToDevice, st));
   const bool head = logits_host != nullptr || argmax_host != nullptr;
-  ALM_TRY(enqueue_forward(m, kv, rows, head, false));
+  ALM_TRY(enqueue_forward(m, kv, rows, head, m->ctx->pdl));
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
 }
@@ -1094,10 +1106,10 @@ static int enqueue_spec_step(alm_spec* s) {
   cudaStream_t st = t->ctx->stream;
   for (int i = 0; i < s->k; ++i) {
     ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
-    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, false));
+    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
   }
   ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
-  ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, false));
+  ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
   ALM_CUDA(launch_spec_accept_greedy(s->state, s->cand, t->ws.argmax, s->k, s->out_tokens, s->out_acc,
                                      s->cap_tokens, s->cap_steps, st));
   return ALM_OK;
@@ -1238,6 +1250,11 @@ int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emi
 int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels) {
   ALM_REQ(s && n_kernels, "null argument");
   *n_kernels = s->n_kernels;
+  return ALM_OK;
+}
+
+int alm_profiler_range(int start) {
+  ALM_CUDA(start ? cudaProfilerStart() : cudaProfilerStop());
   return ALM_OK;
 }
 

@@ -179,6 +179,9 @@ ALM_API int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels);
  * events on the context's stream: *ms = device time, *n_emitted = tokens.
  * The state advances as in alm_spec_run. */
 ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted);
+/* Start (1) or stop (0) the CUDA profiler's capture range, so a profiler
+ * started with capture disabled records only the work in between. */
+ALM_API int alm_profiler_range(int start);
 /* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
  * n_w weights of one shape (so their total can exceed L2); *avg_us is the
  * mean device time of one launch. */
