@@ -53,6 +53,7 @@ SIGNATURES = {
     "alm_qweight_free": [_P],
     "alm_qweight_dequant": [_P, _P, _P],
     "alm_qmatmul": [_P, _P, _P, _I, _I, _P, _I],
+    "alm_qmatmul_noalloc": [_P, _P, _P, _I, _I, _P, _I],
     "alm_matmul_f16_f16": [_P, _P, _P, _P, _I, _I, _I],
     "alm_model_create": [_P, ctypes.POINTER(ModelConfig), _P, _PP],
     "alm_model_destroy": [_P],

@@ -1323,3 +1323,21 @@ int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint1
 }
 
 }  // extern "C"
+
+// ---- internal accessors for entry points defined in other files ----------------
+int alm_internal_fail(int code, const char* msg) { return fail(code, msg); }
+
+int alm_internal_qweight_tile(const alm_qweight* w, QTile* t, int* out_rows, int* in_real) {
+  ALM_REQ(w && t && out_rows && in_real, "null argument");
+  *t = w->t;
+  *out_rows = w->out;
+  *in_real = w->in_real;
+  return ALM_OK;
+}
+
+int alm_internal_ctx(alm_ctx* ctx, int* device, cudaStream_t* stream) {
+  ALM_REQ(ctx && device && stream, "null argument");
+  *device = ctx->device;
+  *stream = ctx->stream;
+  return ALM_OK;
+}

@@ -82,6 +82,20 @@ ALM_API int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* ou
  * Device buffers; row strides in elements. */
 ALM_API int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m,
                 uint16_t* y_dev, int ldy);
+/* alm_qmatmul without any device allocation.  No counterpart in the
+ * reference (its CPU kernels never allocate device memory).  For callers that
+ * cannot call cudaMalloc once running: real-time loops that cannot take the
+ * implicit synchronisation of cudaMalloc/cudaFree, and hosts that reserve
+ * their device memory up front and forbid later driver allocations.  The
+ * split-K scratch is a fixed array inside the library (1 MiB of partial sums
+ * + 4096 counters, held by every GPU that loads the library until exit);
+ * weights whose split needs more are rejected with ALM_ERR_ARG.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress) and
+ * should come before any stream capture.  All calls on a device share the
+ * array, so calls that overlap on the GPU race; the counters are cleared at
+ * the start of each call. */
+ALM_API int alm_qmatmul_noalloc(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m,
+                                uint16_t* y_dev, int ldy);
 /* Replaces src/androidllm_neon.c:71 matmul_f16_f16 (out = a . b^T, raw fp16,
  * host buffers, m <= 16): the weight b is uploaded per call. */
 ALM_API int alm_matmul_f16_f16(alm_ctx* ctx, const uint16_t* a_host, const uint16_t* b_host,
