@@ -51,6 +51,8 @@ SIGNATURES = {
     "alm_copy_d2h": [_P, _P, _P, ctypes.c_size_t],
     "alm_qweight_upload": [_P, _P, _P, _I, _I, _I, _I, _I, _PP],
     "alm_qweight_free": [_P],
+    "alm_qweight_set_split": [_P, _I, _I],
+    "alm_qweight_get_split": [_P, _PI32, _PI32, _PI32],
     "alm_qweight_dequant": [_P, _P, _P],
     "alm_qmatmul": [_P, _P, _P, _I, _I, _P, _I],
     "alm_qmatmul_noalloc": [_P, _P, _P, _I, _I, _P, _I],

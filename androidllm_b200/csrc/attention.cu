@@ -28,6 +28,7 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kPvThreads = 256;
+constexpr int kPvRows = 4;   // query rows per P.V CTA
 
 ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
   uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -195,18 +196,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   grid_dep_launch();
 }
 
+// P.V for (16-dim slice, kv head, group of kPvRows query rows).  Few rows
+// per CTA keep the exp/divide work of forming P small; the rows ride in an
+// m16 tile (rows >= kPvRows are zero) so the product still runs on tensor
+// cores.
 __global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int kVld = 24;                 // V slice row stride (halves): conflict-free
   constexpr int kPld = kPvSpan + 8;        // P row stride (halves)
   constexpr int kWarpsPv = kPvThreads / kWarp;
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kVld]
-  half* ps = vs + kPvSpan * kVld;                    // [16][kPld]
-  __shared__ float s_m[kAttnRows], s_l[kAttnRows];
+  half* ps = vs + kPvSpan * kVld;                    // [kPvRows][kPld]
+  __shared__ float s_m[kPvRows], s_l[kPvRows];
   __shared__ float s_acc[kWarpsPv][kWarp][8];
 
   grid_dep_wait();
-  const int ds = blockIdx.x, kvh = blockIdx.y, rg = blockIdx.z;
+  const int ds = blockIdx.x, kvh = blockIdx.y, grp = blockIdx.z;
   const int hd = a.head_dim;
   const int pos0 = *a.pos;
   const int n_ctx = pos0 + a.M;
@@ -214,15 +219,19 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_c
   const int gq = a.heads / a.kv_heads;
   const int n_rows = a.M * gq;
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
+  const int r0 = grp * kPvRows;                      // first query row of this CTA
+  if (r0 >= n_rows) return;
+  const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
+  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
 
   // row max / sum from the chunk statistics: one warp per row, lane l takes
   // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
   // a row's last position contribute exact zeros)
   {
     const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
-    for (int rl = warp; rl < kAttnRows; rl += kWarpsPv) {
+    for (int i = warp; i < kPvRows; i += kWarpsPv) {
+      const int rl = rl0 + i;
       float mc[4], lc[4];
       float mx = kNegInf;
       for (int base = 0; base < n_chunks; base += 32 * 4) {
@@ -251,13 +260,14 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_c
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
       if (lane == 0) {
-        s_m[rl] = mx;
-        s_l[rl] = l;
+        s_m[i] = mx;
+        s_l[i] = l;
       }
     }
   }
   __syncthreads();
 
+  const int g = lane >> 2, t = lane & 3;
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   for (int base = 0; base < n_ctx; base += kPvSpan) {
     const int span = min(kPvSpan, n_ctx - base);
@@ -283,45 +293,49 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_c
         *reinterpret_cast<uint4*>(vs + (i >> 1) * kVld + (i & 1) * 8) = v[j];
       }
     }
-    // P = fp16(exp(s - max) / sum), 4 scores per float4 load
+    // P = fp16(exp(s - max) / sum) for this CTA's rows, 4 scores per load
     const int per_row4 = span_pad / 4;
-    const int np = kAttnRows * per_row4;
-    for (int b0 = 0; b0 < np; b0 += kPvThreads * 8) {
-      float4 sv[8];
+    const int np = kPvRows * per_row4;
+    for (int b0 = 0; b0 < np; b0 += kPvThreads * 4) {
+      float4 sv[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const int i = b0 + j * kPvThreads + tid;
-        const int rl = i / per_row4, p = base + (i % per_row4) * 4;
-        const int r = rg * kAttnRows + rl;
+        const int i_row = i / per_row4, p = base + (i % per_row4) * 4;
         sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
-        if (i < np && r < n_rows)
-          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + rl) * a.score_ld + p));
+        if (i < np && r0 + i_row < n_rows)
+          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const int i = b0 + j * kPvThreads + tid;
         if (i >= np) break;
-        const int rl = i / per_row4, pl = (i % per_row4) * 4;
+        const int i_row = i / per_row4, pl = (i % per_row4) * 4;
         const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = base + pl + e;
           float pv = 0.f;
-          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - s_m[rl]), s_l[rl]);
-          ps[rl * kPld + pl + e] = __float2half_rn(pv);
+          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - s_m[i_row]), s_l[i_row]);
+          ps[i_row * kPld + pl + e] = __float2half_rn(pv);
         }
       }
     }
     __syncthreads();
     for (int kk = warp; kk < span_pad / 16; kk += kWarpsPv) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldmatrix_x4(a0, a1, a2, a3, ps + (lane % 16) * kPld + kk * 16 + (lane / 16) * 8);
+      // A: rows g < kPvRows hold P, rows g+8 and g >= kPvRows are zero
+      uint32_t a0 = 0, a2 = 0;
+      if (g < kPvRows) {
+        a0 = *reinterpret_cast<const uint32_t*>(ps + g * kPld + kk * 16 + 2 * t);
+        a2 = *reinterpret_cast<const uint32_t*>(ps + g * kPld + kk * 16 + 8 + 2 * t);
+      }
+      uint32_t b0, b1, b2, b3;
       // matrices: (k0-7, n0-7) (k8-15, n0-7) (k0-7, n8-15) (k8-15, n8-15)
       const int vrow = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
       const int vcol = (lane / 16) * 8;
       ldmatrix_x4_trans(b0, b1, b2, b3, vs + vrow * kVld + vcol);
-      mma16816(acc[0], a0, a1, a2, a3, b0, b1);
-      mma16816(acc[1], a0, a1, a2, a3, b2, b3);
+      mma16816(acc[0], a0, 0u, a2, 0u, b0, b1);
+      mma16816(acc[1], a0, 0u, a2, 0u, b2, b3);
     }
     __syncthreads();
   }
@@ -332,18 +346,17 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_c
     for (int e = 0; e < 4; ++e) s_acc[warp][lane][nt * 4 + e] = acc[nt][e];
   __syncthreads();
   grid_dep_launch();
-  if (warp == 0) {
-    const int g = lane >> 2, t = lane & 3;
+  if (warp == 0 && g < kPvRows) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 2; ++e) {       // rows g only (d2, d3 belong to zero rows g+8)
         float v = s_acc[0][lane][nt * 4 + e];
         for (int w2 = 1; w2 < kWarpsPv; ++w2) v = fadd(v, s_acc[w2][lane][nt * 4 + e]);
-        const int r = rg * kAttnRows + g + 8 * (e >> 1);
+        const int r = r0 + g;
         if (r < n_rows) {
           const int m = r / gq, head = kvh * gq + r % gq;
-          const int d = ds * 16 + nt * 8 + 2 * t + (e & 1);
+          const int d = ds * 16 + nt * 8 + 2 * t + e;
           a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + d] = __float2half_rn(v);
         }
       }
@@ -357,7 +370,7 @@ cudaError_t attention_init_attrs() {
                                        static_cast<int>((2 * kAttnRows + kAttnChunk) * (256 + 8) * sizeof(half)));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(attn_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kPvSpan * 24 * sizeof(half) + kAttnRows * (kPvSpan + 8) * sizeof(half)));
+                              static_cast<int>(kPvSpan * 24 * sizeof(half) + kPvRows * (kPvSpan + 8) * sizeof(half)));
 }
 
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
@@ -382,9 +395,9 @@ cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
   if (e != cudaSuccess) return e;
 
   const size_t smem2 = static_cast<size_t>(kPvSpan) * 24 * sizeof(half) +
-                       static_cast<size_t>(kAttnRows) * (kPvSpan + 8) * sizeof(half);
+                       static_cast<size_t>(kPvRows) * (kPvSpan + 8) * sizeof(half);
   cudaLaunchConfig_t c2 = c1;
-  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, n_rg);
+  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, (a.M * gq + kPvRows - 1) / kPvRows);
   c2.blockDim = dim3(kPvThreads);
   c2.dynamicSmemBytes = smem2;
   return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);

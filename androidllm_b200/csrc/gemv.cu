@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
   {
     uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
     const int per_row = cta_nkb * 8;           // 8-column chunks per row
-    const int n_chunks = per_row * NT8 * 8;
+    const int n_chunks = per_row * M;          // rows >= M are zeroed in registers, not staged
     const bool deferred = in.ss != nullptr;
     for (int base = 0; base < n_chunks; base += kThreads * kStageBatch) {
       uint4 raw[kStageBatch], wv[kStageBatch];
@@ -169,8 +169,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
         uint4 xf[NT8][2];
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt) {
-          xf[nt][0] = xs[((kbl * NT8 + nt) * 2 + 0) * kWarp + lane];
-          xf[nt][1] = xs[((kbl * NT8 + nt) * 2 + 1) * kWarp + lane];
+          const bool live = nt * 8 + g < M;   // B column g of n8 tile nt is activation row nt*8+g
+          xf[nt][0] = live ? xs[((kbl * NT8 + nt) * 2 + 0) * kWarp + lane] : make_uint4(0, 0, 0, 0);
+          xf[nt][1] = live ? xs[((kbl * NT8 + nt) * 2 + 1) * kWarp + lane] : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {

@@ -2,17 +2,16 @@
 // fixed-size device array that lives in the library image, for callers that
 // must not allocate device memory once they are running.
 //
-// Who needs it: code that runs inside a CUDA stream capture (a cudaMalloc
-// there either breaks the capture or is not allowed by the capture mode),
-// real-time loops that cannot afford the implicit device synchronisation a
-// cudaMalloc/cudaFree may cause, and hosts that give the library a fixed
-// memory budget at start-up and forbid driver allocations afterwards.
+// Who needs it: real-time loops that cannot afford the implicit device
+// synchronisation a cudaMalloc/cudaFree may cause, and hosts that give the
+// library a fixed memory budget at start-up and forbid driver allocations
+// afterwards.
 // alm_qmatmul allocates its split-K partial-sum buffer lazily with
 // cudaMalloc; this entry point instead uses the array below, whose address is
 // resolved once per device.
 //
 // Limits and sharing:
-//   * the array holds kNoAllocPartFloats fp32 partial sums (1 MiB) and
+//   * the array holds kNoAllocPartFloats fp32 partial sums (2 MiB) and
 //     kNoAllocCounters column counters; weights whose split needs more are
 //     rejected with ALM_ERR_ARG;
 //   * every GPU that loads the library reserves this memory until exit;
@@ -32,7 +31,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocPartFloats = 256 * 1024;   // 1 MiB of fp32 partial sums
+constexpr size_t kNoAllocPartFloats = 512 * 1024;   // 2 MiB of fp32 partial sums
 constexpr size_t kNoAllocCounters = 4096;           // CTA-column counters
 constexpr size_t kNoAllocBytes = kNoAllocPartFloats * sizeof(float) + kNoAllocCounters * sizeof(unsigned);
 

@@ -63,22 +63,44 @@ int pow2_ceil(int v) {
   return p;
 }
 
-// Split-K shape for a weight: enough warps to cover the SMs, at least a few
-// k-blocks per warp, power-of-two splits, x staging within shared memory.
-void choose_split(QTile& t, int n_sms) {
-  const int kps_min = t.bits == 4 ? 6 : t.bits == 8 ? 3 : 2;
-  const int want = n_sms * 16;
-  const int s_max = pow2_floor(std::max(1, t.k_blocks / kps_min));
-  int s = pow2_ceil(std::max(1, (want + t.n_tiles - 1) / t.n_tiles));
-  s = std::min(s, s_max);
-  t.ksw = std::min(s, 8);
-  t.ksg = s / t.ksw;
+// Split-K launch shape of a weight.  Small matrices (a few hundred tiles or
+// fewer) are latency-bound: spread them so the grid holds about two CTAs per
+// SM, down to one k-block per warp, splitting K across CTAs when needed.
+// Large matrices stream enough bytes per warp as they are: split K only
+// inside the CTA and only as far as needed to reach two CTAs per SM.
+void set_split(QTile& t, int ksw, int ksg) {
+  t.ksw = ksw;
+  const int s = ksw * ksg;
   t.kps = (t.k_blocks + s - 1) / s;
-  while (t.ksw * t.kps > 80 && t.ksw > 1) {   // keep x staging <= 160 KB at M = 16
-    t.ksw /= 2;
-    t.ksg *= 2;
+  // drop CTA rows that would get no k-blocks
+  t.ksg = std::max(1, (((t.k_blocks + t.kps - 1) / t.kps) + ksw - 1) / ksw);
+}
+
+// Launch shapes measured best on B200 (graph-replayed, PDL) for the step's
+// shapes: narrow matrices let all 8 warps of a CTA split K and avoid cross-CTA
+// splits (their ticket + reduction costs more than it saves) unless K is
+// long; wide matrices give each warp whole tiles to stream.
+void choose_split(QTile& t, int n_sms) {
+  (void)n_sms;
+  const int kb = t.k_blocks;
+  int ksw, ksg;
+  if (t.n_tiles > 2048) {
+    ksw = 1;
+    ksg = 1;
+  } else if (t.n_tiles > 256) {
+    ksw = 2;
+    ksg = (kb + 23) / 24;
+  } else if (kb > 100) {
+    ksw = 2;
+    ksg = (kb + 11) / 12;
+  } else {
+    ksw = 8;
+    ksg = (kb + 23) / 24;
   }
-  t.ksg = std::max(1, (((t.k_blocks + t.kps - 1) / t.kps) + t.ksw - 1) / t.ksw);
+  ksw = std::min(ksw, std::max(1, pow2_floor(kb)));
+  ksg = std::max(1, std::min(ksg, kb / ksw));
+  set_split(t, ksw, ksg);
+  while (t.ksw * t.kps > 80 && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
 }
 
 }  // namespace
@@ -643,6 +665,33 @@ int alm_qweight_upload(alm_ctx* ctx, const void* packed_host, const void* scale_
   DeviceGuard g(ctx->device);
   alm_proj_src s{packed_host, scale_host, bits, block, out, in, in_real};
   return build_qweight(ctx, &s, 1, identity_map(out), out, w);
+}
+
+int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg) {
+  ALM_REQ(w, "null weight");
+  ALM_REQ((ksw == 1 || ksw == 2 || ksw == 4 || ksw == 8) && ksg >= 1 && ksw * ksg <= w->t.k_blocks,
+          "ksw must be 1, 2, 4 or 8 and ksw * ksg at most the number of 64-column blocks");
+  DeviceGuard g(w->ctx->device);
+  QTile t = w->t;
+  set_split(t, ksw, ksg);
+  ALM_REQ(t.ksw * t.kps <= 100, "per-CTA activation staging would exceed shared memory");
+  const int grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+  unsigned* counters = nullptr;
+  ALM_TRY(dev_alloc_t(&counters, grid_x));
+  ALM_CUDA(cudaMemset(counters, 0, grid_x * sizeof(unsigned)));
+  dev_free(w->counters);
+  w->counters = counters;
+  t.counters = counters;
+  w->t = t;
+  return ALM_OK;
+}
+
+int alm_qweight_get_split(const alm_qweight* w, int* ksw, int* ksg, int* kps) {
+  ALM_REQ(w && ksw && ksg && kps, "null argument");
+  *ksw = w->t.ksw;
+  *ksg = w->t.ksg;
+  *kps = w->t.kps;
+  return ALM_OK;
 }
 
 int alm_qweight_free(alm_qweight* w) {
@@ -1301,21 +1350,37 @@ int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint1
   e.ldo = ws[0]->out;
   e.n_out = ws[0]->out;
   const ActIn in = raw_in(reinterpret_cast<const half*>(x_dev), ws[0]->in_real, ws[0]->in_real);
+  // launches are replayed from a CUDA graph (with programmatic dependent
+  // launch, as inside a forward) so the host launch rate does not cap them
   cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
   int rc = ALM_OK;
   cudaError_t err = cudaEventCreate(&e0);
   if (err == cudaSuccess) err = cudaEventCreate(&e1);
   for (int i = 0; err == cudaSuccess && i < n_w; ++i)   // warm-up
     err = launch_gemv(ws[i]->t, in, m, EPI_STORE, e, StepIO{}, scr, false, ctx->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(ctx->stream);
+  if (err == cudaSuccess) err = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+  if (err == cudaSuccess) {
+    cudaError_t le = cudaSuccess;
+    for (int i = 0; le == cudaSuccess && i < iters; ++i)
+      le = launch_gemv(ws[i % n_w]->t, in, m, EPI_STORE, e, StepIO{}, scr, ctx->pdl, ctx->stream);
+    err = cudaStreamEndCapture(ctx->stream, &graph);
+    if (err == cudaSuccess) err = le;
+  }
+  if (err == cudaSuccess) err = cudaGraphInstantiate(&exec, graph, 0);
+  if (err == cudaSuccess) err = cudaGraphLaunch(exec, ctx->stream);   // warm replay
   if (err == cudaSuccess) err = cudaEventRecord(e0, ctx->stream);
-  for (int i = 0; err == cudaSuccess && i < iters; ++i)
-    err = launch_gemv(ws[i % n_w]->t, in, m, EPI_STORE, e, StepIO{}, scr, false, ctx->stream);
+  if (err == cudaSuccess) err = cudaGraphLaunch(exec, ctx->stream);
   if (err == cudaSuccess) err = cudaEventRecord(e1, ctx->stream);
   if (err == cudaSuccess) err = cudaEventSynchronize(e1);
   float ms = 0.f;
   if (err == cudaSuccess) err = cudaEventElapsedTime(&ms, e0, e1);
   if (err != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("bench: ") + cudaGetErrorString(err));
   else *avg_us = ms * 1000.f / iters;
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
   if (e0) cudaEventDestroy(e0);
   if (e1) cudaEventDestroy(e1);
   dev_free(part);

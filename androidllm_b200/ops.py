@@ -123,6 +123,14 @@ class QWeight:
                                      proj.out, proj.in_, proj.in_real, ctypes.byref(h)))
         self.ctx, self.h, self.proj = ctx, h, proj
 
+    def set_split(self, ksw, ksg):
+        check(lib.alm_qweight_set_split(self.h, int(ksw), int(ksg)))
+
+    def split(self):
+        a, b, c = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check(lib.alm_qweight_get_split(self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)))
+        return a.value, b.value, c.value
+
     def dequant(self):
         """fp16 (out, in_real): bit-exact androidllm dequantize_packed (sliced)."""
         out = np.empty((self.proj.out, self.proj.in_real), np.float16)

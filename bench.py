@@ -395,6 +395,68 @@ def run_ours(args):
     return 0
 
 
+# --------------------------------------------------------------------------
+# profiling helpers (used with Nsight Compute; see profiles/)
+# --------------------------------------------------------------------------
+def run_profile(args):
+    """Load the workload, then run --profile N speculative steps inside a CUDA
+    profiler capture range (start ncu with --profile-from-start off).  A short
+    prompt keeps the launches before the range few; the steps run at position
+    600, the middle of a 512-prompt / 256-token episode."""
+    from androidllm_b200._lib import lib
+    from androidllm_b200.ops import Context, DeviceKV, DeviceModel, SpecDecoder
+    tdir, ddir = prepare_models(args.workload)
+    ctx = Context(0)
+    t, d = DeviceModel.from_dir(ctx, tdir), DeviceModel.from_dir(ctx, ddir)
+    tkv, dkv = DeviceKV(t, 1024), DeviceKV(d, 1024)
+    prompt = np.random.default_rng(123).integers(0, t.canon["vocab"], 16).tolist()
+    t.forward(tkv, prompt[:15], 0, logits=False, argmax=False)
+    d.forward(dkv, prompt, 0, logits=False, argmax=False)
+    s = SpecDecoder(t, d, tkv, dkv, SPEC_K)
+    s.begin(prompt[-1], 600)
+    s.bench(2)
+    s.begin(prompt[-1], 600)
+    lib.alm_profiler_range(1)
+    ms, _ = s.bench(args.profile)
+    lib.alm_profiler_range(0)
+    print(json.dumps({"profile_steps": args.profile, "ms_per_step": ms / args.profile,
+                      "kernels_per_step": s.kernel_count()}))
+    return 0
+
+
+def summarize_ncu(path):
+    """Aggregate an ncu --csv launch list (gpu__time_duration.sum) by kernel."""
+    import collections
+    import csv
+    import re
+    with open(path) as f:
+        rows = list(csv.reader(f))
+    hdr = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    h = rows[hdr]
+    ki, mi, vi = h.index("Kernel Name"), h.index("Metric Name"), h.index("Metric Value")
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    epi = {"0": "store", "1": "qkv+rope", "2": "resid", "3": "swiglu", "4": "logits"}
+    for r in rows[hdr + 1:]:
+        if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
+            continue
+        name = r[ki]
+        m = re.search(r"gemv_kernel<\(int\)(\d+), \(int\)(\d+), \(int\)(\d+)>|gemv_kernel<(\d+), (\d+), (\d+)>", name)
+        if m:
+            g = [x for x in m.groups() if x is not None]
+            name = f"gemv_kernel<int{g[0]}, nt8={g[1]}, {epi.get(g[2], g[2])}>"
+        else:
+            name = re.sub(r"\(.*", "", name).split("::")[-1]
+        agg[name][0] += 1
+        agg[name][1] += float(r[vi].replace(",", ""))
+    tot = sum(v[1] for v in agg.values())
+    out = [f"{'kernel':48s} {'launches':>8s} {'total_us':>10s} {'share':>7s}"]
+    for k, (n, v) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        out.append(f"{k:48s} {n:8d} {v / 1000:10.1f} {100 * v / tot:6.1f}%")
+    out.append(f"{'total':48s} {sum(v[0] for v in agg.values()):8d} {tot / 1000:10.1f}")
+    print("\n".join(out))
+    return 0
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -414,7 +476,14 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen2.5-1.5b")
     ap.add_argument("--cpu-samples", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="run N steps inside a profiler capture range and exit")
+    ap.add_argument("--summarize-ncu", metavar="CSV", help="aggregate an ncu launch list and exit")
     args = ap.parse_args()
+    if args.summarize_ncu:
+        return summarize_ncu(args.summarize_ncu)
+    if args.profile:
+        return run_profile(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

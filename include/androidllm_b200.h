@@ -75,6 +75,11 @@ ALM_API int alm_copy_d2h(alm_ctx* ctx, void* dst_host, const void* src_dev, size
 ALM_API int alm_qweight_upload(alm_ctx* ctx, const void* packed_host, const void* scale_host, int bits,
                        int block, int out, int in, int in_real, alm_qweight** w);
 ALM_API int alm_qweight_free(alm_qweight* w);
+/* Launch shape of the weight's GEMV: ksw warps split K inside a CTA (1, 2, 4
+ * or 8), ksg CTAs split it further (tuning; the default is chosen at upload).
+ * A weight already inside a model must not be changed while a forward runs. */
+ALM_API int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg);
+ALM_API int alm_qweight_get_split(const alm_qweight* w, int* ksw, int* ksg, int* kps);
 /* Replaces androidllm/quant.py:58-65 dequantize_packed (sliced to in_real):
  * writes fp16 (out, in_real) to out_host; bit-exact. */
 ALM_API int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host);
@@ -87,7 +92,7 @@ ALM_API int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_de
  * cannot call cudaMalloc once running: real-time loops that cannot take the
  * implicit synchronisation of cudaMalloc/cudaFree, and hosts that reserve
  * their device memory up front and forbid later driver allocations.  The
- * split-K scratch is a fixed array inside the library (1 MiB of partial sums
+ * split-K scratch is a fixed array inside the library (2 MiB of partial sums
  * + 4096 counters, held by every GPU that loads the library until exit);
  * weights whose split needs more are rejected with ALM_ERR_ARG.  The first
  * call on a device resolves the array's address (cudaGetSymbolAddress) and
