@@ -27,6 +27,59 @@ ALM_DEV uint32_t ld_nc_u32(const void* p) {
   return r;
 }
 
+// ---------------------------------------------------------------------------
+// bulk copies (TMA engine, no multicast) into shared memory with mbarriers
+// ---------------------------------------------------------------------------
+// Spin limit of every mbarrier wait: after this many polls the waiter gives
+// up and reports an error instead of hanging (a copy of valid memory completes
+// in microseconds).
+constexpr unsigned kSpinLimit = 1u << 24;
+
+ALM_DEV uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+ALM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+ALM_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+ALM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+ALM_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16
+ALM_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+ALM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity`; false if the limit ran out.
+ALM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (unsigned i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+ALM_DEV uint4 lds128(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_addr(p)));
+  return r;
+}
+ALM_DEV uint32_t lds32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(smem_addr(p)));
+  return r;
+}
+
 // Programmatic dependent launch: wait for the producer grid's results / let
 // the next grid in the stream start its prologue.  No-ops without PDL.
 ALM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -30,10 +30,22 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / kWarp;
-constexpr size_t kGemvMaxSmem = 200 * 1024;   // x staging limit (dynamic shared memory)
+constexpr size_t kGemvMaxSmem = 200 * 1024;   // dynamic shared memory limit per CTA
 
+// Weight ring: each warp streams its contiguous run of records into
+// kSlots shared-memory slots of Pipe<BITS>::kItems records each, one bulk copy
+// (TMA engine) per slot, while it decodes the previous slots.
+constexpr int kSlots = 3;
 template <int BITS>
-struct Pipe { static constexpr int U = BITS == 4 ? 8 : BITS == 8 ? 4 : 2; };
+struct Pipe { static constexpr int kItems = BITS == 4 ? 4 : BITS == 8 ? 2 : 1; };
+
+// Dynamic shared memory of one CTA: activation fragments, weight rings, mbarriers.
+inline size_t gemv_smem_bytes(const QTile& w, int nt8, int items) {
+  const int cta_nkb = w.ksw * w.kps < w.k_blocks ? w.ksw * w.kps : w.k_blocks;
+  const size_t x = static_cast<size_t>(cta_nkb) * nt8 * 2 * kWarp * sizeof(uint4);
+  const size_t ring = static_cast<size_t>(kWarps) * kSlots * items * w.rec_u4 * sizeof(uint4);
+  return x + ring + kWarps * kSlots * sizeof(uint64_t);
+}
 
 // Chunks of 8 activation columns staged per thread per batch (all loads of a
 // batch are issued before any is used, so a batch costs one memory round trip).
@@ -46,7 +58,7 @@ ALM_DEV bool better(float v1, int i1, float v2, int i2) {
 template <int BITS, int NT8, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, int M, Epi epi, StepIO io,
                                                         float* __restrict__ part) {
-  extern __shared__ uint4 xs[];  // [kb_local][NT8][2][32] uint4
+  extern __shared__ uint4 xs[];  // [kb_local][NT8][2][32] uint4, then weight rings, then mbarriers
   __shared__ float red[kWarps][kWarp][NT8 * 4];
   __shared__ float s_den_in[kMaxRows];
   __shared__ float s_den_res[kMaxRows];
@@ -55,7 +67,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
   __shared__ int s_am_i[kWarps][NT8 * 8];
 
   constexpr int V = QTileTraits<BITS>::kVec;
-  constexpr int U = Pipe<BITS>::U;
+  constexpr int IPS = Pipe<BITS>::kItems;
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int g = lane >> 2, t = lane & 3;
   const int ksw = w.ksw, ntc = kWarps / ksw;
@@ -70,22 +82,29 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
   const int cta_kb1 = min(cta_kb0 + ksw * w.kps, w.k_blocks);
   const int cta_nkb = max(0, cta_kb1 - cta_kb0);
 
-  // ---- weight prefetch (does not depend on the previous kernel) ----------
-  uint4 buf[U][V];
-  uint32_t sbuf[U][2];
-  auto load_kb = [&](int u, int kb) {
-#pragma unroll
-    for (int v = 0; v < V; ++v) buf[u][v] = ld_stream(qtile_ptr<BITS>(w.data, w.k_blocks, tile, kb, v, lane));
-    if constexpr (BITS != 16) {
-      const size_t sbase = static_cast<size_t>(tile) * w.nsb;
-      sbuf[u][0] = ld_nc_u32(w.scales + (sbase + scale_block(w.block, kb, 0)) * 8 + g);
-      sbuf[u][1] = w.block == 32 ? ld_nc_u32(w.scales + (sbase + scale_block(w.block, kb, 2)) * 8 + g)
-                                 : sbuf[u][0];
-    }
+  // ---- weight stream (does not depend on the previous kernel) -------------
+  const int rec_bytes = w.rec_u4 * 16;
+  const int slot_bytes = IPS * rec_bytes;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(xs + static_cast<size_t>(cta_nkb) * NT8 * 2 * kWarp) +
+                        static_cast<size_t>(warp) * kSlots * slot_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(xs) +
+                                               static_cast<size_t>(cta_nkb) * NT8 * 2 * kWarp * 16 +
+                                               static_cast<size_t>(kWarps) * kSlots * slot_bytes) + warp * kSlots;
+  const unsigned char* gsrc = reinterpret_cast<const unsigned char*>(
+      w.data + (static_cast<size_t>(tile_ok ? tile : 0) * w.k_blocks + kb0) * w.rec_u4);
+  const int n_chunks = (n + IPS - 1) / IPS;
+  auto issue = [&](int c) {   // lane 0: bulk-copy chunk c into its slot
+    const int slot = c % kSlots;
+    const uint32_t bytes = static_cast<uint32_t>(min(IPS, n - c * IPS) * rec_bytes);
+    mbar_expect_tx(&bars[slot], bytes);
+    bulk_g2s(ring + slot * slot_bytes, gsrc + static_cast<size_t>(c) * slot_bytes, bytes, &bars[slot]);
   };
-#pragma unroll
-  for (int u = 0; u < U; ++u)
-    if (u < n) load_kb(u, kb0 + u);
+  if (lane == 0) {
+    for (int i = 0; i < kSlots; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    for (int c = 0; c < n_chunks && c < kSlots; ++c) issue(c);
+  }
+  __syncwarp();
 
   grid_dep_wait();
 
@@ -149,23 +168,42 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
   __syncthreads();
 
   // ---- main loop -------------------------------------------------------------
-  float acc[NT8][4];
+  // Two accumulator chains (even / odd k16 steps) so consecutive MMAs do not
+  // wait on each other; they are added in a fixed order at the end.
+  float acc[NT8][4], acc2[NT8][4];
 #pragma unroll
   for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[nt][j] = acc2[nt][j] = 0.f;
 
-  for (int base = 0; base < n; base += U) {
+  const bool two_sets = w.sb == 2;
+  int consumed = 0;
+  bool stream_ok = true;
+  for (int c = 0; c < n_chunks; ++c) {
+    const int slot = c % kSlots;
+    if (!mbar_wait(&bars[slot], static_cast<uint32_t>((c / kSlots) & 1))) {
+      stream_ok = false;
+      break;
+    }
+    const unsigned char* sp = ring + slot * slot_bytes;
+    const int cnt = min(IPS, n - c * IPS);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int i = base + u;
-      if (i < n) {
+    for (int j = 0; j < IPS; ++j) {
+      if (j < cnt) {
+        const unsigned char* rp = sp + j * rec_bytes;
         uint4 cur[V];
 #pragma unroll
-        for (int v = 0; v < V; ++v) cur[v] = buf[u][v];
-        const uint32_t sc0 = sbuf[u][0], sc1 = sbuf[u][1];
-        if (i + U < n) load_kb(u, kb0 + i + U);
-        const int kbl = kb0 + i - cta_kb0;
+        for (int v = 0; v < V; ++v) cur[v] = lds128(rp + v * 512 + lane * 16);
+        half2 sg_a = __float2half2_rn(1.f), sg8_a = sg_a, sg_b = sg_a, sg8_b = sg_a;
+        if constexpr (BITS != 16) {
+          const half2 sa = u2h(lds32(rp + V * 512 + g * 4));
+          const half2 sb2 = two_sets ? u2h(lds32(rp + V * 512 + 32 + g * 4)) : sa;
+          sg_a = __low2half2(sa);
+          sg8_a = __high2half2(sa);
+          sg_b = __low2half2(sb2);
+          sg8_b = __high2half2(sb2);
+        }
+        const int kbl = kb0 + c * IPS + j - cta_kb0;
         uint4 xf[NT8][2];
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt) {
@@ -175,20 +213,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(QTile w, ActIn in, in
         }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
-          const half2 sc = u2h(s >= 2 ? sc1 : sc0);
           uint32_t a0, a1, a2, a3;
-          decode_step<BITS>(cur, s, __low2half2(sc), __high2half2(sc), a0, a1, a2, a3);
+          decode_step<BITS>(cur, s, s >= 2 ? sg_b : sg_a, s >= 2 ? sg8_b : sg8_a, a0, a1, a2, a3);
 #pragma unroll
           for (int nt = 0; nt < NT8; ++nt) {
             const uint4& X = xf[nt][s >> 1];
             const uint32_t b0 = (s & 1) ? X.z : X.x;
             const uint32_t b1 = (s & 1) ? X.w : X.y;
-            mma16816(acc[nt], a0, a1, a2, a3, b0, b1);
+            mma16816((s & 1) ? acc2[nt] : acc[nt], a0, a1, a2, a3, b0, b1);
           }
         }
       }
     }
+    consumed = c + 1;
+    __syncwarp();
+    if (lane == 0 && c + kSlots < n_chunks) {
+      fence_proxy_async_smem();   // this slot's reads are done before the copy overwrites it
+      issue(c + kSlots);
+    }
   }
+  if (!stream_ok) {
+    // a copy never completed: report it and let every copy still in flight
+    // land before the CTA's shared memory is released
+    if (lane == 0 && io.err) atomicExch(io.err, 2);
+    const int issued = min(n_chunks, consumed + kSlots);
+    for (int c = consumed; c < issued; ++c) mbar_wait(&bars[c % kSlots], static_cast<uint32_t>((c / kSlots) & 1));
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[nt][j] = fadd(acc[nt][j], acc2[nt][j]);
 
   grid_dep_launch();
 
@@ -428,8 +482,7 @@ cudaError_t launch_t(const QTile& w, const ActIn& in, int M, const Epi& epi, con
                      const SplitScratch& scr, bool pdl, cudaStream_t st) {
   auto kern = gemv_kernel<BITS, NT8, EPI>;
   const int ntc = kWarps / w.ksw;
-  const int cta_nkb = std::min(w.ksw * w.kps, w.k_blocks);
-  const size_t smem = static_cast<size_t>(cta_nkb) * NT8 * 2 * kWarp * sizeof(uint4);
+  const size_t smem = gemv_smem_bytes(w, NT8, Pipe<BITS>::kItems);
   if (smem > kGemvMaxSmem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((w.n_tiles + ntc - 1) / ntc, w.ksg, 1);

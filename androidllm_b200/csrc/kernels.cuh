@@ -17,10 +17,12 @@ constexpr int kPvSpan = 1024;
 // ---------------------------------------------------------------------------
 // Tiled quantized weight ("qtile" layout).
 //
-// Rows are grouped in tiles of 16, columns in k-blocks of 64.  For each
-// (tile, kblock) the 32 lanes of a warp hold exactly the m16n8k16 A fragments
-// of four k16 steps, so one coalesced 512 B (int4) / 1 KB (int8) / 2 KB
-// (fp16) warp load feeds 4 tensor-core MMAs with no shuffles:
+// Rows are grouped in tiles of 16, columns in k-blocks of 64.  Each (tile,
+// k-block) is one record: the weight codes followed by their fp16 scales,
+// so a warp walks one contiguous stream of records with one pointer bump per
+// k-block.  In a record the 32 lanes of a warp hold exactly the m16n8k16 A
+// fragments of four k16 steps, so one coalesced 512 B (int4) / 1 KB (int8)
+// / 2 KB (fp16) warp load feeds 4 tensor-core MMAs with no shuffles:
 //   int4: lane word s (s = k16 step) = nibbles
 //         [(g,c) (g+8,c) (g,c+8) (g+8,c+8) (g,c+1) (g+8,c+1) (g,c+9) (g+8,c+9)]
 //         with c = 16 s + 2 t, each stored offset-binary (q + 8);
@@ -28,17 +30,19 @@ constexpr int kPvSpan = 1024;
 //         same for row g+8, offset-binary (q + 128); the two 16 B halves of a
 //         lane are stored 512 B apart so each is a coalesced warp load;
 //   fp16: lane uint4 s = the four A registers of step s.
-// Scales: per (tile, scale block) eight half2 {s(g), s(g+8)}, g = 0..7.
+// Scales (after the codes): eight half2 {s(g), s(g+8)}, g = 0..7, for the
+// record's 64 columns (two such sets for 32-column blocks: steps 0-1 and 2-3).
+// Blocks wider than 64 repeat their scale in every record.
 // ---------------------------------------------------------------------------
 struct QTile {
-  const uint4* data = nullptr;
-  const half2* scales = nullptr;
+  const uint4* data = nullptr;   // records, (tile, k-block) major
   int bits = 4;       // 4, 8 or 16 (fp16, no scales)
   int block = 64;     // scale block along K (32 or a multiple of 64)
   int n_rows = 0;     // logical output rows
   int n_tiles = 0;    // ceil(n_rows / 16)
   int k_blocks = 0;   // ceil(k_pad / 64)
-  int nsb = 0;        // scale blocks per tile row group
+  int rec_u4 = 0;     // record size in 16-byte units
+  int sb = 0;         // scale sets per record (0 for fp16, 1, or 2 for 32-column blocks)
   int k_real = 0;     // real input length (activation columns)
   // split-K launch shape
   int ksw = 1;        // warps splitting K inside a CTA (1, 2, 4, 8)
@@ -96,6 +100,7 @@ struct Epi {
 
 struct StepIO {
   const int* pos = nullptr;     // device: position of activation row 0
+  int* err = nullptr;           // device: set to 2 if a bounded wait gave up
 };
 
 // Scratch for cross-CTA split-K partial sums.
@@ -112,8 +117,7 @@ cudaError_t rows_init_attrs();
 
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_repack(const void* const* src, const half* const* src_scales, int n_src,
-                          const int* dst_src_row, QTile& w, uint4* data, half2* scales,
-                          int k_pad, cudaStream_t st);
+                          const int* dst_src_row, QTile& w, uint4* data, int k_pad, cudaStream_t st);
 cudaError_t launch_dequant(const QTile& w, half* out, cudaStream_t st);
 cudaError_t launch_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
                         const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st);

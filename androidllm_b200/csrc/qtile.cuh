@@ -8,6 +8,7 @@
 // fp16(f32(q) * f32(scale)) (androidllm/quant.py:58-65).
 #pragma once
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace alm {
 
@@ -20,11 +21,10 @@ struct QTileTraits<8> { static constexpr int kVec = 2; };
 template <>
 struct QTileTraits<16> { static constexpr int kVec = 4; };
 
-// Address of vector v (0..kVec-1) of lane `lane` for (tile, kb).
-template <int BITS>
-ALM_DEV const uint4* qtile_ptr(const uint4* base, int k_blocks, int tile, int kb, int v, int lane) {
-  constexpr int V = QTileTraits<BITS>::kVec;
-  return base + ((static_cast<size_t>(tile) * k_blocks + kb) * V + v) * kWarp + lane;
+// Record of (tile, kb); codes of vector v of `lane` at rec + v * 32 + lane,
+// scale words at reinterpret_cast<const uint32_t*>(rec + kVec * 32) + set * 8 + g.
+ALM_DEV const uint4* qtile_record(const QTile& w, int tile, int kb) {
+  return w.data + (static_cast<size_t>(tile) * w.k_blocks + kb) * w.rec_u4;
 }
 
 // Decode k16 step s of a lane's k64 data into A registers (row g: a0, a2;
@@ -62,11 +62,6 @@ ALM_DEV void decode_step(const uint4 (&wd)[QTileTraits<BITS>::kVec], int s, half
     a2 = v.z;
     a3 = v.w;
   }
-}
-
-// Scale block index of k16 step s of k-block kb.
-ALM_DEV int scale_block(int block, int kb, int s) {
-  return block == 32 ? 2 * kb + (s >> 1) : (kb * 64) / block;
 }
 
 }  // namespace alm

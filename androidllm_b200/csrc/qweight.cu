@@ -31,7 +31,7 @@ __device__ int fetch_code(const SrcSet& s, int desc, int col, int bits, int k_pa
 
 // One thread per (tile, kb, lane): assemble that lane's fragment data.
 __global__ void repack_kernel(SrcSet s, const int* __restrict__ dst_src_row, int bits, int n_tiles,
-                              int k_blocks, int k_pad, uint4* __restrict__ out) {
+                              int k_blocks, int k_pad, int rec_u4, uint4* __restrict__ out) {
   const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const long long total = static_cast<long long>(n_tiles) * k_blocks * kWarp;
   if (gid >= total) return;
@@ -77,30 +77,34 @@ __global__ void repack_kernel(SrcSet s, const int* __restrict__ dst_src_row, int
   }
   const int nvec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
   for (int v = 0; v < nvec; ++v) {
-    const size_t idx = ((static_cast<size_t>(tile) * k_blocks + kb) * nvec + v) * kWarp + lane;
+    const size_t idx = (static_cast<size_t>(tile) * k_blocks + kb) * rec_u4 + v * kWarp + lane;
     out[idx] = make_uint4(words[4 * v], words[4 * v + 1], words[4 * v + 2], words[4 * v + 3]);
   }
 }
 
-// One thread per (tile, scale block, g): half2 {scale(row g), scale(row g+8)}.
-__global__ void repack_scales_kernel(SrcSet s, const int* __restrict__ dst_src_row, int n_tiles,
-                                     int nsb, int src_nsb, half2* __restrict__ out) {
-  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= n_tiles * nsb * 8) return;
-  const int g = gid & 7;
-  const int sb = (gid >> 3) % nsb;
-  const int tile = (gid >> 3) / nsb;
+// One thread per (tile, kb, scale set, g): half2 {scale(row g), scale(row g+8)}
+// written after the codes of record (tile, kb).
+__global__ void repack_scales_kernel(SrcSet s, const int* __restrict__ dst_src_row, int n_tiles, int k_blocks,
+                                     int block, int sets, int src_nsb, int vec, int rec_u4, uint4* __restrict__ out) {
+  const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (gid >= static_cast<long long>(n_tiles) * k_blocks * sets * 8) return;
+  const int g = static_cast<int>(gid & 7);
+  const int set = static_cast<int>((gid >> 3) % sets);
+  const int kb = static_cast<int>((gid >> 3) / sets % k_blocks);
+  const int tile = static_cast<int>((gid >> 3) / sets / k_blocks);
+  const int sbk = block == 32 ? 2 * kb + set : (kb * 64) / block;   // source scale block
   half v[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int desc = dst_src_row[tile * 16 + g + 8 * h];
-    if (desc < 0 || sb >= src_nsb) {
+    if (desc < 0 || sbk >= src_nsb) {
       v[h] = __ushort_as_half(0);
     } else {
-      v[h] = s.scale[desc >> 24][static_cast<size_t>(desc & 0xffffff) * src_nsb + sb];
+      v[h] = s.scale[desc >> 24][static_cast<size_t>(desc & 0xffffff) * src_nsb + sbk];
     }
   }
-  out[gid] = __halves2half2(v[0], v[1]);
+  half2* sc = reinterpret_cast<half2*>(out + (static_cast<size_t>(tile) * k_blocks + kb) * rec_u4 + vec * kWarp);
+  sc[set * 8 + g] = __halves2half2(v[0], v[1]);
 }
 
 // Decode the qtile layout back to fp16 rows (out: n_rows x k_real).
@@ -114,14 +118,16 @@ __global__ void dequant_kernel(QTile w, half* __restrict__ out) {
   const int tile = static_cast<int>(gid / (static_cast<long long>(kWarp) * w.k_blocks));
   const int g = lane >> 2, t = lane & 3;
   constexpr int V = QTileTraits<BITS>::kVec;
+  const uint4* rec = qtile_record(w, tile, kb);
   uint4 wd[V];
 #pragma unroll
-  for (int v = 0; v < V; ++v) wd[v] = *qtile_ptr<BITS>(w.data, w.k_blocks, tile, kb, v, lane);
+  for (int v = 0; v < V; ++v) wd[v] = rec[v * kWarp + lane];
 #pragma unroll
   for (int st = 0; st < 4; ++st) {
     half2 sg = __float2half2_rn(1.f), sg8 = sg;
     if (BITS != 16) {
-      const half2 sc = w.scales[(static_cast<size_t>(tile) * w.nsb + scale_block(w.block, kb, st)) * 8 + g];
+      const int set = (w.sb == 2 && st >= 2) ? 1 : 0;
+      const half2 sc = reinterpret_cast<const half2*>(rec + V * kWarp)[set * 8 + g];
       sg = __low2half2(sc);
       sg8 = __high2half2(sc);
     }
@@ -147,8 +153,7 @@ __global__ void dequant_kernel(QTile w, half* __restrict__ out) {
 }  // namespace
 
 cudaError_t launch_repack(const void* const* src, const half* const* src_scales, int n_src,
-                          const int* dst_src_row, QTile& w, uint4* data, half2* scales,
-                          int k_pad, cudaStream_t st) {
+                          const int* dst_src_row, QTile& w, uint4* data, int k_pad, cudaStream_t st) {
   if (n_src < 1 || n_src > 3) return cudaErrorInvalidValue;
   SrcSet s{};
   for (int i = 0; i < n_src; ++i) {
@@ -158,13 +163,13 @@ cudaError_t launch_repack(const void* const* src, const half* const* src_scales,
   const long long total = static_cast<long long>(w.n_tiles) * w.k_blocks * kWarp;
   const int threads = 256;
   repack_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, st>>>(
-      s, dst_src_row, w.bits, w.n_tiles, w.k_blocks, k_pad, data);
+      s, dst_src_row, w.bits, w.n_tiles, w.k_blocks, k_pad, w.rec_u4, data);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || w.bits == 16) return e;
-  const int src_nsb = k_pad / w.block;
-  const int n = w.n_tiles * w.nsb * 8;
-  repack_scales_kernel<<<(n + threads - 1) / threads, threads, 0, st>>>(s, dst_src_row, w.n_tiles,
-                                                                         w.nsb, src_nsb, scales);
+  const int vec = w.bits == 4 ? 1 : 2;
+  const long long n = static_cast<long long>(w.n_tiles) * w.k_blocks * w.sb * 8;
+  repack_scales_kernel<<<static_cast<unsigned>((n + threads - 1) / threads), threads, 0, st>>>(
+      s, dst_src_row, w.n_tiles, w.k_blocks, w.block, w.sb, k_pad / w.block, vec, w.rec_u4, data);
   return cudaGetLastError();
 }
 

@@ -100,7 +100,7 @@ void choose_split(QTile& t, int n_sms) {
   ksw = std::min(ksw, std::max(1, pow2_floor(kb)));
   ksg = std::max(1, std::min(ksg, kb / ksw));
   set_split(t, ksw, ksg);
-  while (t.ksw * t.kps > 80 && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
+  while (t.ksw * t.kps > 64 && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
 }
 
 }  // namespace
@@ -119,7 +119,6 @@ struct alm_qweight {
   alm_ctx* ctx = nullptr;
   QTile t;
   uint4* data = nullptr;
-  half2* scales = nullptr;
   unsigned* counters = nullptr;
   int out = 0, in = 0, in_real = 0;
 };
@@ -266,11 +265,12 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
   t.n_rows = n_rows;
   t.n_tiles = (n_rows + 15) / 16;
   t.k_blocks = (in + 63) / 64;
-  t.nsb = bits == 16 ? 0 : (block == 32 ? 2 * t.k_blocks : in / block);
+  t.sb = bits == 16 ? 0 : (block == 32 ? 2 : 1);
   t.k_real = in_real;
   choose_split(t, ctx->n_sms);
 
   const int vec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
+  t.rec_u4 = vec * kWarp + t.sb * 2;   // codes + 8 half2 scales (32 B) per set
   std::vector<void*> tmp;
   auto cleanup = [&]() {
     for (void* p : tmp) cudaFree(p);
@@ -280,10 +280,7 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
   const half* dscale[3] = {nullptr, nullptr, nullptr};
   int* dmap = nullptr;
   do {
-    if ((rc = dev_alloc_t(&w->data, static_cast<size_t>(t.n_tiles) * t.k_blocks * vec * kWarp)) != ALM_OK) break;
-    if (bits != 16 &&
-        (rc = dev_alloc_t(&w->scales, static_cast<size_t>(t.n_tiles) * t.nsb * 8)) != ALM_OK)
-      break;
+    if ((rc = dev_alloc_t(&w->data, static_cast<size_t>(t.n_tiles) * t.k_blocks * t.rec_u4)) != ALM_OK) break;
     for (int i = 0; i < n_src && rc == ALM_OK; ++i) {
       void* p = nullptr;
       const size_t nb = src_bytes(bits, srcs[i].out, in);
@@ -313,7 +310,7 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
       rc = fail(ALM_ERR_CUDA, "row map upload failed");
       break;
     }
-    cudaError_t e = launch_repack(dsrc, dscale, n_src, dmap, t, w->data, w->scales, in, ctx->stream);
+    cudaError_t e = launch_repack(dsrc, dscale, n_src, dmap, t, w->data, in, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) {
       rc = fail(ALM_ERR_CUDA, std::string("repack: ") + cudaGetErrorString(e));
@@ -332,7 +329,6 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
     return rc;
   }
   t.data = w->data;
-  t.scales = w->scales;
   t.counters = w->counters;
   *out = w;
   return ALM_OK;
@@ -417,7 +413,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   Layer& L = m->layers[li];
   Work& ws = m->ws;
   cudaStream_t st = m->ctx->stream;
-  StepIO io{ws.pos};
+  StepIO io{ws.pos, ws.err};
   const SplitScratch scr = scratch_of(m);
   const int qdim = c.heads * c.head_dim;
 
@@ -490,7 +486,7 @@ int enqueue_head(alm_model* m, int M, bool pdl) {
   e.am_val = ws.am_val;
   e.am_idx = ws.am_idx;
   const ActIn in = raw_in(ws.xn, m->cfg.hidden, m->cfg.hidden);
-  ALM_LAUNCH(launch_gemv(m->head->t, in, M, EPI_LOGITS, e, StepIO{ws.pos}, scratch_of(m), pdl, m->ctx->stream));
+  ALM_LAUNCH(launch_gemv(m->head->t, in, M, EPI_LOGITS, e, StepIO{ws.pos, ws.err}, scratch_of(m), pdl, m->ctx->stream));
   ALM_LAUNCH(launch_argmax_final(ws.am_val, ws.am_idx, ws.n_am, M, ws.argmax, pdl, m->ctx->stream));
   return ALM_OK;
 }
@@ -551,6 +547,7 @@ int sync_and_check(alm_model* m) {
   ALM_CUDA(cudaMemcpy(&err, m->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
   if (err) {
     cudaMemset(m->ws.err, 0, sizeof(int));
+    if (err == 2) return fail(ALM_ERR_CUDA, "a device-side wait gave up (weight stream did not arrive)");
     return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
   }
   return ALM_OK;
@@ -674,7 +671,7 @@ int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg) {
   DeviceGuard g(w->ctx->device);
   QTile t = w->t;
   set_split(t, ksw, ksg);
-  ALM_REQ(t.ksw * t.kps <= 100, "per-CTA activation staging would exceed shared memory");
+  ALM_REQ(t.ksw * t.kps <= 64, "per-CTA activation staging would exceed shared memory");
   const int grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
   unsigned* counters = nullptr;
   ALM_TRY(dev_alloc_t(&counters, grid_x));
@@ -698,7 +695,6 @@ int alm_qweight_free(alm_qweight* w) {
   if (!w) return ALM_OK;
   DeviceGuard g(w->ctx->device);
   dev_free(w->data);
-  dev_free(w->scales);
   dev_free(w->counters);
   delete w;
   return ALM_OK;
@@ -1292,6 +1288,7 @@ int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emi
   ALM_CUDA(cudaMemcpy(&err, s->target->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
   int err2 = 0;
   ALM_CUDA(cudaMemcpy(&err2, s->draft->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err == 2 || err2 == 2) return fail(ALM_ERR_CUDA, "a device-side wait gave up (weight stream did not arrive)");
   if (err || err2) return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
   return ALM_OK;
 }

@@ -396,6 +396,69 @@ def run_ours(args):
 
 
 # --------------------------------------------------------------------------
+# isolated quantized-matmul sweep (block-64 int4 / int8, N(0, 0.02) weights)
+# --------------------------------------------------------------------------
+SWEEP_SHAPES = [(1536, 1536), (8960, 1536), (1536, 8960), (18944, 3584), (3584, 18944), (151936, 1536)]
+SWEEP_M = (1, 5, 8, 16, 40, 128)
+
+
+def run_sweep(args):
+    """GB/s of the dequant-GEMV per (N, K, bits, M), graph-replayed launches
+    cycling over weight copies larger than L2; one JSON line per case."""
+    from androidllm_b200.ops import Context, QuantProj, QWeight, bench_qmatmul
+    from androidllm_b200.quant import codes_for_storage, quantize_matrix
+    ctx = Context(0)
+    peaks = load_peaks()
+    rng = np.random.default_rng(3)
+    ms = [int(x) for x in args.sweep_m.split(",")]
+    for n, k in SWEEP_SHAPES:
+        for bits in (4, 8):
+            # quantize one N(0, 0.02) matrix with the format's own quantizer,
+            # then copy it so the rotation exceeds the 126 MB L2
+            w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+            q, sc = quantize_matrix(w, bits=bits, block=64)
+            proj = QuantProj(codes_for_storage(q, bits), sc, bits, 64, n, k)
+            del w, q
+            per = n * k * bits // 8
+            copies = max(2, min(12, int(400e6 // per) + 1))
+            ws = [QWeight(ctx, proj) for _ in range(copies)]
+            for m in ms:
+                rec = {"n": n, "k": k, "bits": bits, "m": m}
+                if m > 16:
+                    rec["note"] = "M > 16 needs the dense tcgen05 path (not built)"
+                    print(json.dumps(rec), flush=True)
+                    continue
+                x = rng.standard_normal((m, k)).astype(np.float16)
+                us = bench_qmatmul(ctx, ws, x, 200)
+                alg = gemv_bytes(n, k, m, bits)
+                gbs = alg / us / 1e3
+                rec.update({"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
+                            "tflops": round(2 * m * n * k / us / 1e6, 2), "split": list(ws[0].split())})
+                print(json.dumps(rec), flush=True)
+            del ws
+    return 0
+
+
+def run_gemv(args):
+    """One GEMV shape launched back to back (a small, bounded ncu target)."""
+    from androidllm_b200.ops import Context, QuantProj, QWeight, bench_qmatmul
+    n, k, bits, m = (int(v) for v in args.gemv.split(","))
+    ctx = Context(0)
+    rng = np.random.default_rng(0)
+    q = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8) if bits == 4 else \
+        rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    s = (np.abs(rng.standard_normal((n, k // 64))) * 0.003 + 1e-4).astype(np.float16)
+    copies = max(2, min(8, int(300e6 // (n * k * bits // 8)) + 1))
+    ws = [QWeight(ctx, QuantProj(q, s, bits, 64, n, k)) for _ in range(copies)]
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    us = bench_qmatmul(ctx, ws, x, 4 * copies)
+    alg = gemv_bytes(n, k, m, bits)
+    print(json.dumps({"n": n, "k": k, "bits": bits, "m": m, "us": us, "gbs": alg / us / 1e3,
+                      "split": list(ws[0].split())}))
+    return 0
+
+
+# --------------------------------------------------------------------------
 # profiling helpers (used with Nsight Compute; see profiles/)
 # --------------------------------------------------------------------------
 def run_profile(args):
@@ -479,7 +542,14 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="run N steps inside a profiler capture range and exit")
     ap.add_argument("--summarize-ncu", metavar="CSV", help="aggregate an ncu launch list and exit")
+    ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
+    ap.add_argument("--sweep-m", default=",".join(str(m) for m in SWEEP_M))
+    ap.add_argument("--gemv", metavar="N,K,BITS,M", help="time one GEMV shape repeatedly (profiling target)")
     args = ap.parse_args()
+    if args.sweep:
+        return run_sweep(args)
+    if args.gemv:
+        return run_gemv(args)
     if args.summarize_ncu:
         return summarize_ncu(args.summarize_ncu)
     if args.profile:
