@@ -45,6 +45,7 @@ SIGNATURES = {
     "alm_ctx_create": [_I, _PP],
     "alm_ctx_destroy": [_P],
     "alm_ctx_sync": [_P],
+    "alm_ctx_set_persistent": [_P, _I],
     "alm_dev_alloc": [_P, ctypes.c_size_t, _PP],
     "alm_dev_free": [_P, _P],
     "alm_copy_h2d": [_P, _P, _P, ctypes.c_size_t],
@@ -72,6 +73,7 @@ SIGNATURES = {
     "alm_layer_forward": [_P, _I, _P, _P, _I, _I, _P],
     "alm_head_logits": [_P, _P, _I, _P, _P],
     "alm_forward": [_P, _P, _P, _I, _I, _P, _P],
+    "alm_forward_trace": [_P, _P, _P, _I, _I, _P, _I, _P, _P],
     "alm_spec_create": [_P, _P, _P, _P, _I, _PP],
     "alm_spec_destroy": [_P],
     "alm_spec_begin": [_P, ctypes.c_int32, _I],

@@ -1,405 +1,55 @@
-// GQA decode / verify attention over the paged fp16 KV cache.
-//
-// Follows androidllm/models/llama.py:109-118 with its rounding points:
-// scores = (q_fp32 . k_fp16) / sqrt(head_dim) in fp32, softmax in fp32, the
-// normalised probabilities cast to fp16, then fp16(P) . fp16(V) accumulated
-// in fp32 and rounded to fp16.  Because P is rounded after normalisation, the
-// softmax needs the row max and sum before any P.V work, so the work is two
-// kernels:
-//
-//   scores: grid (chunk of 64 positions, kv head, group of 16 query rows).
-//           q is split into fp16 hi + lo parts so two tensor-core MMAs give
-//           the fp32 dot product to ~22 bits; writes masked scores and the
-//           chunk's (max, sum of exp) per row.
-//   pv:     grid (16-dim slice of head_dim, kv head, row group).  Combines the
-//           chunk statistics into the row max / sum, forms fp16 P while
-//           staging it in shared memory, and runs P.V on tensor cores over
-//           all positions (1024 at a time).
-//
-// Query rows of one kv head are (token m, q head within the group) pairs; row
-// (m, h) attends to positions 0 .. pos0 + m (causal over the verify rows).
-// Every per-row reduction has a fixed order that does not depend on how many
-// rows the pass carries.
-#include "common.cuh"
-#include "kernels.cuh"
+// Standalone launches of the two attention passes (bodies in attn_body.cuh).
+#include "attn_body.cuh"
 
 namespace alm {
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kPvThreads = 256;
-constexpr int kPvRows = 4;   // query rows per P.V CTA
-
-ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
-  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
-}
-
-ALM_DEV const half* kv_row(const half* cache, const int* pt, int page_size, int kv_heads, int kvh,
-                           int hd, int pos) {
-  const int page = pt[pos / page_size];
-  return cache + ((static_cast<size_t>(page) * kv_heads + kvh) * page_size + pos % page_size) * hd;
-}
-
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, float inv_sqrt_den) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int hd = a.head_dim, ld = hd + 8;
-  half* qhi = reinterpret_cast<half*>(smem_raw);
-  half* qlo = qhi + kAttnRows * ld;
-  half* ks = qlo + kAttnRows * ld;   // [64][ld]
-  __shared__ float s_red[4][kAttnRows];
-  __shared__ float s_max[kAttnRows];
-
+  __shared__ AttnShared sh;
   grid_dep_wait();
-  const int chunk = blockIdx.x, kvh = blockIdx.y, rg = blockIdx.z;
-  const int pos0 = *a.pos;
-  const int n_ctx = pos0 + a.M;
-  const int c0 = chunk * kAttnChunk;
-  if (c0 >= n_ctx) return;
-  const int gq = a.heads / a.kv_heads;
-  const int n_rows = a.M * gq;
-  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-
-  // Q rows -> fp16 hi/lo (float4 loads, all issued before use)
-  {
-    const int per_row = hd / 4;
-    const int n4 = kAttnRows * per_row;
-    for (int base = 0; base < n4; base += kAttnThreads * 4) {
-      float4 v[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        const int rl = i / per_row, d4 = i % per_row;
-        const int r = rg * kAttnRows + rl;
-        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n4 && r < n_rows) {
-          const int m = r / gq, head = kvh * gq + r % gq;
-          v[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        if (i >= n4) break;
-        const int rl = i / per_row, d = (i % per_row) * 4;
-        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const half h = __float2half_rn(vv[e]);
-          qhi[rl * ld + d + e] = h;
-          qlo[rl * ld + d + e] = __float2half_rn(vv[e] - __half2float(h));
-        }
-      }
-    }
-  }
-  // K chunk (16-byte vectors, all issued before use)
-  {
-    const int vec_per_row = hd / 8;
-    const int nv = kAttnChunk * vec_per_row;
-    for (int base = 0; base < nv; base += kAttnThreads * 8) {
-      uint4 v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        const int p = c0 + i / vec_per_row;
-        v[j] = make_uint4(0, 0, 0, 0);
-        if (i < nv && p < n_ctx)
-          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, a.page_table, a.page_size, a.kv_heads, kvh,
-                                                              hd, p)) + i % vec_per_row);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        if (i >= nv) break;
-        *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = v[j];
-      }
-    }
-  }
-  __syncthreads();
-
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for (int kk = 0; kk < hd / 16; ++kk) {
-    uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
-    const int arow = lane % 16, acol = kk * 16 + (lane / 16) * 8;
-    ldmatrix_x4(h0, h1, h2, h3, qhi + arow * ld + acol);
-    ldmatrix_x4(l0, l1, l2, l3, qlo + arow * ld + acol);
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      uint32_t b0, b1;
-      const int brow = warp * 16 + nt * 8 + (lane % 8);
-      const int bcol = kk * 16 + ((lane / 8) % 2) * 8;
-      ldmatrix_x2(b0, b1, ks + brow * ld + bcol);
-      mma16816(acc[nt], h0, h1, h2, h3, b0, b1);
-      mma16816(acc[nt], l0, l1, l2, l3, b0, b1);
-    }
-  }
-
-  // masked scores
-  const int g = lane >> 2, t = lane & 3;
-  float sc[2][4];
-  float rmax[2] = {kNegInf, kNegInf};
-  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int rl = g + 8 * (e >> 1);
-      const int r = rg * kAttnRows + rl;
-      const int p = c0 + warp * 16 + nt * 8 + 2 * t + (e & 1);
-      float s = kNegInf;
-      if (r < n_rows && p < n_ctx && p <= pos0 + r / gq) s = fdiv(acc[nt][e], inv_sqrt_den);
-      sc[nt][e] = s;
-      if (p < n_ctx) a.scores[(srow0 + rl) * a.score_ld + p] = s;
-      rmax[e >> 1] = fmaxf(rmax[e >> 1], s);
-    }
-  // row max over the chunk
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    rmax[h] = fmaxf(rmax[h], __shfl_xor_sync(0xffffffffu, rmax[h], 1));
-    rmax[h] = fmaxf(rmax[h], __shfl_xor_sync(0xffffffffu, rmax[h], 2));
-    if (t == 0) s_red[warp][g + 8 * h] = rmax[h];
-  }
-  __syncthreads();
-  if (tid < kAttnRows) {
-    float mx = kNegInf;
-    for (int w2 = 0; w2 < 4; ++w2) mx = fmaxf(mx, s_red[w2][tid]);
-    s_max[tid] = mx;
-  }
-  __syncthreads();
-  float rsum[2] = {0.f, 0.f};
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float mx = s_max[g + 8 * (e >> 1)];
-      const float ex = (sc[nt][e] == kNegInf) ? 0.f : expf(sc[nt][e] - mx);
-      rsum[e >> 1] = fadd(rsum[e >> 1], ex);
-    }
-  __syncthreads();
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    rsum[h] = fadd(rsum[h], __shfl_xor_sync(0xffffffffu, rsum[h], 1));
-    rsum[h] = fadd(rsum[h], __shfl_xor_sync(0xffffffffu, rsum[h], 2));
-    if (t == 0) s_red[warp][g + 8 * h] = rsum[h];
-  }
-  __syncthreads();
-  if (tid < kAttnRows) {
-    float l = 0.f;
-    for (int w2 = 0; w2 < 4; ++w2) l = fadd(l, s_red[w2][tid]);
-    const int n_chunks_max = gridDim.x;
-    float* st = a.stats + (((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max + chunk) * kAttnRows + tid) * 2;
-    st[0] = s_max[tid];
-    st[1] = l;
-  }
+  attn_scores_body(a, inv_sqrt_den, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.x, smem_raw, sh);
   grid_dep_launch();
 }
 
-// P.V for (16-dim slice, kv head, group of kPvRows query rows).  Few rows
-// per CTA keep the exp/divide work of forming P small; the rows ride in an
-// m16 tile (rows >= kPvRows are zero) so the product still runs on tensor
-// cores.
-__global__ void __launch_bounds__(kPvThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
+__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  constexpr int kVld = 24;                 // V slice row stride (halves): conflict-free
-  constexpr int kPld = kPvSpan + 8;        // P row stride (halves)
-  constexpr int kWarpsPv = kPvThreads / kWarp;
-  half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kVld]
-  half* ps = vs + kPvSpan * kVld;                    // [kPvRows][kPld]
-  __shared__ float s_m[kPvRows], s_l[kPvRows];
-  __shared__ float s_acc[kWarpsPv][kWarp][8];
-
+  __shared__ AttnShared sh;
   grid_dep_wait();
-  const int ds = blockIdx.x, kvh = blockIdx.y, grp = blockIdx.z;
-  const int hd = a.head_dim;
-  const int pos0 = *a.pos;
-  const int n_ctx = pos0 + a.M;
-  const int n_chunks = (n_ctx + kAttnChunk - 1) / kAttnChunk;
-  const int gq = a.heads / a.kv_heads;
-  const int n_rows = a.M * gq;
-  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
-  const int r0 = grp * kPvRows;                      // first query row of this CTA
-  if (r0 >= n_rows) return;
-  const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
-
-  // row max / sum from the chunk statistics: one warp per row, lane l takes
-  // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
-  // a row's last position contribute exact zeros)
-  {
-    const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
-    for (int i = warp; i < kPvRows; i += kWarpsPv) {
-      const int rl = rl0 + i;
-      float mc[4], lc[4];
-      float mx = kNegInf;
-      for (int base = 0; base < n_chunks; base += 32 * 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = base + j * 32 + lane;
-          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc[j]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float l = 0.f;
-      for (int base = 0; base < n_chunks; base += 32 * 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = base + j * 32 + lane;
-          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
-          lc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2 + 1) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (mc[j] != kNegInf) l = fadd(l, fmul(lc[j], expf(mc[j] - mx)));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
-      if (lane == 0) {
-        s_m[i] = mx;
-        s_l[i] = l;
-      }
-    }
-  }
-  __syncthreads();
-
-  const int g = lane >> 2, t = lane & 3;
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for (int base = 0; base < n_ctx; base += kPvSpan) {
-    const int span = min(kPvSpan, n_ctx - base);
-    const int span_pad = (span + 15) & ~15;
-    // V slice: 16 dims (two 16 B vectors) per position
-    const int nv = span_pad * 2;
-    for (int b0 = 0; b0 < nv; b0 += kPvThreads * 8) {
-      uint4 v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = b0 + j * kPvThreads + tid;
-        const int p = base + (i >> 1);
-        v[j] = make_uint4(0, 0, 0, 0);
-        if (i < nv && p < n_ctx)
-          v[j] = __ldcg(reinterpret_cast<const uint4*>(
-                            kv_row(a.vcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
-                        (i & 1));
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = b0 + j * kPvThreads + tid;
-        if (i >= nv) break;
-        *reinterpret_cast<uint4*>(vs + (i >> 1) * kVld + (i & 1) * 8) = v[j];
-      }
-    }
-    // P = fp16(exp(s - max) / sum) for this CTA's rows, 4 scores per load
-    const int per_row4 = span_pad / 4;
-    const int np = kPvRows * per_row4;
-    for (int b0 = 0; b0 < np; b0 += kPvThreads * 4) {
-      float4 sv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = b0 + j * kPvThreads + tid;
-        const int i_row = i / per_row4, p = base + (i % per_row4) * 4;
-        sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
-        if (i < np && r0 + i_row < n_rows)
-          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = b0 + j * kPvThreads + tid;
-        if (i >= np) break;
-        const int i_row = i / per_row4, pl = (i % per_row4) * 4;
-        const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int p = base + pl + e;
-          float pv = 0.f;
-          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - s_m[i_row]), s_l[i_row]);
-          ps[i_row * kPld + pl + e] = __float2half_rn(pv);
-        }
-      }
-    }
-    __syncthreads();
-    for (int kk = warp; kk < span_pad / 16; kk += kWarpsPv) {
-      // A: rows g < kPvRows hold P, rows g+8 and g >= kPvRows are zero
-      uint32_t a0 = 0, a2 = 0;
-      if (g < kPvRows) {
-        a0 = *reinterpret_cast<const uint32_t*>(ps + g * kPld + kk * 16 + 2 * t);
-        a2 = *reinterpret_cast<const uint32_t*>(ps + g * kPld + kk * 16 + 8 + 2 * t);
-      }
-      uint32_t b0, b1, b2, b3;
-      // matrices: (k0-7, n0-7) (k8-15, n0-7) (k0-7, n8-15) (k8-15, n8-15)
-      const int vrow = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
-      const int vcol = (lane / 16) * 8;
-      ldmatrix_x4_trans(b0, b1, b2, b3, vs + vrow * kVld + vcol);
-      mma16816(acc[0], a0, 0u, a2, 0u, b0, b1);
-      mma16816(acc[1], a0, 0u, a2, 0u, b2, b3);
-    }
-    __syncthreads();
-  }
-
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) s_acc[warp][lane][nt * 4 + e] = acc[nt][e];
-  __syncthreads();
-  grid_dep_launch();
-  if (warp == 0 && g < kPvRows) {
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {       // rows g only (d2, d3 belong to zero rows g+8)
-        float v = s_acc[0][lane][nt * 4 + e];
-        for (int w2 = 1; w2 < kWarpsPv; ++w2) v = fadd(v, s_acc[w2][lane][nt * 4 + e]);
-        const int r = r0 + g;
-        if (r < n_rows) {
-          const int m = r / gq, head = kvh * gq + r % gq;
-          const int d = ds * 16 + nt * 8 + 2 * t + e;
-          a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + d] = __float2half_rn(v);
-        }
-      }
-  }
+  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh);
 }
 
 }  // namespace
 
 cudaError_t attention_init_attrs() {
   cudaError_t e = cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>((2 * kAttnRows + kAttnChunk) * (256 + 8) * sizeof(half)));
+                                       static_cast<int>(attn_scores_smem(256)));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(attn_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kPvSpan * 24 * sizeof(half) + kPvRows * (kPvSpan + 8) * sizeof(half)));
+                              static_cast<int>(attn_pv_smem()));
 }
 
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
   if (a.head_dim % 16 || a.head_dim > 256 || a.heads % a.kv_heads) return cudaErrorInvalidValue;
-  const int gq = a.heads / a.kv_heads;
-  const int n_rg = (a.M * gq + kAttnRows - 1) / kAttnRows;
-  const int n_chunks_max = (a.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  const int n_chunks_max = attn_chunks_max(a);
   const float den = static_cast<float>(sqrt(static_cast<double>(a.head_dim)));
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
 
-  const size_t smem1 = static_cast<size_t>(2 * kAttnRows + kAttnChunk) * (a.head_dim + 8) * sizeof(half);
   cudaLaunchConfig_t c1 = {};
-  c1.gridDim = dim3(n_chunks_max, a.kv_heads, n_rg);
+  c1.gridDim = dim3(n_chunks_max, a.kv_heads, attn_row_groups(a));
   c1.blockDim = dim3(kAttnThreads);
-  c1.dynamicSmemBytes = smem1;
+  c1.dynamicSmemBytes = attn_scores_smem(a.head_dim);
   c1.stream = st;
   c1.attrs = attr;
   c1.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&c1, attn_scores_kernel, a, den);
   if (e != cudaSuccess) return e;
 
-  const size_t smem2 = static_cast<size_t>(kPvSpan) * 24 * sizeof(half) +
-                       static_cast<size_t>(kPvRows) * (kPvSpan + 8) * sizeof(half);
   cudaLaunchConfig_t c2 = c1;
-  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, (a.M * gq + kPvRows - 1) / kPvRows);
-  c2.blockDim = dim3(kPvThreads);
-  c2.dynamicSmemBytes = smem2;
+  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a));
+  c2.dynamicSmemBytes = attn_pv_smem();
   return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);
 }
 

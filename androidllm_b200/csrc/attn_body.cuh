@@ -1,0 +1,392 @@
+// Device bodies of GQA decode / verify attention over the paged fp16 KV cache,
+// shared by the standalone kernels (attention.cu) and the persistent forward
+// kernel (one virtual block per call).
+//
+// Follows androidllm/models/llama.py:109-118 with its rounding points:
+// scores = (q_fp32 . k_fp16) / sqrt(head_dim) in fp32, softmax in fp32, the
+// normalised probabilities cast to fp16, then fp16(P) . fp16(V) accumulated
+// in fp32 and rounded to fp16.  Because P is rounded after normalisation, the
+// softmax needs the row max and sum before any P.V work, so the work is two
+// passes:
+//
+//   scores: grid (chunk of 64 positions, kv head, group of 16 query rows).
+//           q is split into fp16 hi + lo parts so two tensor-core MMAs give
+//           the fp32 dot product to ~22 bits; writes masked scores and the
+//           chunk's (max, sum of exp) per row.  Warps 0-3 take 16 positions
+//           of the chunk each.
+//   pv:     grid (16-dim slice of head_dim, kv head, group of kPvRows rows).
+//           Combines the chunk statistics into the row max / sum, forms fp16
+//           P while staging it in shared memory, and runs P.V on tensor cores
+//           over all positions (kPvSpan at a time).
+//
+// Query rows of one kv head are (token m, q head within the group) pairs; row
+// (m, h) attends to positions 0 .. pos0 + m (causal over the verify rows).
+// Every per-row reduction has a fixed order that does not depend on how many
+// rows the pass carries.
+#pragma once
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace alm {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / kWarp;
+constexpr int kPvRows = 4;   // query rows per P.V block
+constexpr int kPvVld = 24;   // V slice row stride (halves): conflict-free
+constexpr int kPvPld = kPvSpan + 8;   // P row stride (halves)
+
+__host__ __device__ inline size_t attn_scores_smem(int hd) {
+  return static_cast<size_t>(2 * kAttnRows + kAttnChunk) * (hd + 8) * sizeof(half);
+}
+__host__ __device__ inline size_t attn_pv_smem() {
+  return static_cast<size_t>(kPvSpan) * kPvVld * sizeof(half) + static_cast<size_t>(kPvRows) * kPvPld * sizeof(half) +
+         static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float);
+}
+__host__ __device__ inline int attn_row_groups(const AttnArgs& a) {
+  return (a.M * (a.heads / a.kv_heads) + kAttnRows - 1) / kAttnRows;
+}
+__host__ __device__ inline int attn_pv_groups(const AttnArgs& a) {
+  return (a.M * (a.heads / a.kv_heads) + kPvRows - 1) / kPvRows;
+}
+__host__ __device__ inline int attn_chunks_max(const AttnArgs& a) { return (a.max_ctx + kAttnChunk - 1) / kAttnChunk; }
+
+struct AttnShared {
+  float red[kAttnWarps][kAttnRows];
+  float mx[kAttnRows];
+  float pm[kPvRows], pl[kPvRows];
+};
+
+ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+
+ALM_DEV const half* kv_row(const half* cache, const int* pt, int page_size, int kv_heads, int kvh,
+                           int hd, int pos) {
+  const int page = pt[pos / page_size];
+  return cache + ((static_cast<size_t>(page) * kv_heads + kvh) * page_size + pos % page_size) * hd;
+}
+
+// Scores of (chunk, kv head, row group); n_chunks_max = the grid's chunk count.
+ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, int kvh, int rg, int n_chunks_max,
+                              unsigned char* smem_raw, AttnShared& sh) {
+  const int hd = a.head_dim, ld = hd + 8;
+  half* qhi = reinterpret_cast<half*>(smem_raw);
+  half* qlo = qhi + kAttnRows * ld;
+  half* ks = qlo + kAttnRows * ld;   // [64][ld]
+
+  const int pos0 = *a.pos;
+  const int n_ctx = pos0 + a.M;
+  const int c0 = chunk * kAttnChunk;
+  if (c0 >= n_ctx) return;
+  const int gq = a.heads / a.kv_heads;
+  const int n_rows = a.M * gq;
+  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+
+  // Q rows -> fp16 hi/lo (float4 loads, all issued before use)
+  {
+    const int per_row = hd / 4;
+    const int n4 = kAttnRows * per_row;
+    for (int base = 0; base < n4; base += kAttnThreads * 4) {
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        const int rl = i / per_row, d4 = i % per_row;
+        const int r = rg * kAttnRows + rl;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4 && r < n_rows) {
+          const int m = r / gq, head = kvh * gq + r % gq;
+          v[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        if (i >= n4) break;
+        const int rl = i / per_row, d = (i % per_row) * 4;
+        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const half h = __float2half_rn(vv[e]);
+          qhi[rl * ld + d + e] = h;
+          qlo[rl * ld + d + e] = __float2half_rn(vv[e] - __half2float(h));
+        }
+      }
+    }
+  }
+  // K chunk (16-byte vectors, all issued before use)
+  {
+    const int vec_per_row = hd / 8;
+    const int nv = kAttnChunk * vec_per_row;
+    for (int base = 0; base < nv; base += kAttnThreads * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        const int p = c0 + i / vec_per_row;
+        v[j] = make_uint4(0, 0, 0, 0);
+        if (i < nv && p < n_ctx)
+          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, a.page_table, a.page_size, a.kv_heads, kvh,
+                                                              hd, p)) + i % vec_per_row);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * kAttnThreads + tid;
+        if (i >= nv) break;
+        *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = v[j];
+      }
+    }
+  }
+  __syncthreads();
+
+  // warps 0-3: positions c0 + 16 w .. c0 + 16 w + 15 (two n8 tiles); all
+  // warps take part in the staging above and in the block barriers below
+  constexpr int kScoreWarps = kAttnChunk / 16;
+  const bool mw = warp < kScoreWarps;
+  const int g = lane >> 2, t = lane & 3;
+  float sc[2][4];
+  float rmax[2] = {kNegInf, kNegInf};
+  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
+  if (mw) {
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int kk = 0; kk < hd / 16; ++kk) {
+      uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+      const int arow = lane % 16, acol = kk * 16 + (lane / 16) * 8;
+      ldmatrix_x4(h0, h1, h2, h3, qhi + arow * ld + acol);
+      ldmatrix_x4(l0, l1, l2, l3, qlo + arow * ld + acol);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        uint32_t b0, b1;
+        const int brow = warp * 16 + nt * 8 + (lane % 8);
+        const int bcol = kk * 16 + ((lane / 8) % 2) * 8;
+        ldmatrix_x2(b0, b1, ks + brow * ld + bcol);
+        mma16816(acc[nt], h0, h1, h2, h3, b0, b1);
+        mma16816(acc[nt], l0, l1, l2, l3, b0, b1);
+      }
+    }
+    // masked scores
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rl = g + 8 * (e >> 1);
+        const int r = rg * kAttnRows + rl;
+        const int p = c0 + warp * 16 + nt * 8 + 2 * t + (e & 1);
+        float s = kNegInf;
+        if (r < n_rows && p < n_ctx && p <= pos0 + r / gq) s = fdiv(acc[nt][e], inv_sqrt_den);
+        sc[nt][e] = s;
+        if (p < n_ctx) a.scores[(srow0 + rl) * a.score_ld + p] = s;
+        rmax[e >> 1] = fmaxf(rmax[e >> 1], s);
+      }
+    // row max over the chunk
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rmax[h] = fmaxf(rmax[h], __shfl_xor_sync(0xffffffffu, rmax[h], 1));
+      rmax[h] = fmaxf(rmax[h], __shfl_xor_sync(0xffffffffu, rmax[h], 2));
+      if (t == 0) sh.red[warp][g + 8 * h] = rmax[h];
+    }
+  }
+  __syncthreads();
+  if (tid < kAttnRows) {
+    float mx = kNegInf;
+    for (int w2 = 0; w2 < kScoreWarps; ++w2) mx = fmaxf(mx, sh.red[w2][tid]);
+    sh.mx[tid] = mx;
+  }
+  __syncthreads();
+  float rsum[2] = {0.f, 0.f};
+  if (mw) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mx = sh.mx[g + 8 * (e >> 1)];
+        const float ex = (sc[nt][e] == kNegInf) ? 0.f : expf(sc[nt][e] - mx);
+        rsum[e >> 1] = fadd(rsum[e >> 1], ex);
+      }
+  }
+  __syncthreads();
+  if (mw) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rsum[h] = fadd(rsum[h], __shfl_xor_sync(0xffffffffu, rsum[h], 1));
+      rsum[h] = fadd(rsum[h], __shfl_xor_sync(0xffffffffu, rsum[h], 2));
+      if (t == 0) sh.red[warp][g + 8 * h] = rsum[h];
+    }
+  }
+  __syncthreads();
+  if (tid < kAttnRows) {
+    float l = 0.f;
+    for (int w2 = 0; w2 < kScoreWarps; ++w2) l = fadd(l, sh.red[w2][tid]);
+    float* st = a.stats + (((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max + chunk) * kAttnRows + tid) * 2;
+    st[0] = sh.mx[tid];
+    st[1] = l;
+  }
+  __syncthreads();   // shared memory is reused by the caller's next block
+}
+
+// P.V for (16-dim slice, kv head, group of kPvRows query rows).  Few rows
+// per block keep the exp/divide work of forming P small; the rows ride in an
+// m16 tile (rows >= kPvRows are zero) so the product still runs on tensor
+// cores.
+ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, int grp, unsigned char* smem_raw,
+                          AttnShared& sh) {
+  half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
+  half* ps = vs + kPvSpan * kPvVld;                  // [kPvRows][kPvPld]
+  float* s_acc = reinterpret_cast<float*>(ps + kPvRows * kPvPld);   // [kAttnWarps][kWarp][8]
+
+  const int hd = a.head_dim;
+  const int pos0 = *a.pos;
+  const int n_ctx = pos0 + a.M;
+  const int n_chunks = (n_ctx + kAttnChunk - 1) / kAttnChunk;
+  const int gq = a.heads / a.kv_heads;
+  const int n_rows = a.M * gq;
+  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
+  const int r0 = grp * kPvRows;                      // first query row of this block
+  if (r0 >= n_rows) return;
+  const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
+
+  // row max / sum from the chunk statistics: one warp per row, lane l takes
+  // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
+  // a row's last position contribute exact zeros)
+  {
+    const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
+    for (int i = warp; i < kPvRows; i += kAttnWarps) {
+      const int rl = rl0 + i;
+      float mc[4], lc[4];
+      float mx = kNegInf;
+      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = base + j * 32 + lane;
+          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc[j]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float l = 0.f;
+      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = base + j * 32 + lane;
+          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+          lc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2 + 1) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (mc[j] != kNegInf) l = fadd(l, fmul(lc[j], expf(mc[j] - mx)));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
+      if (lane == 0) {
+        sh.pm[i] = mx;
+        sh.pl[i] = l;
+      }
+    }
+  }
+  __syncthreads();
+
+  const int g = lane >> 2, t = lane & 3;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int base = 0; base < n_ctx; base += kPvSpan) {
+    const int span = min(kPvSpan, n_ctx - base);
+    const int span_pad = (span + 15) & ~15;
+    // V slice: 16 dims (two 16 B vectors) per position
+    const int nv = span_pad * 2;
+    for (int b0 = 0; b0 < nv; b0 += kAttnThreads * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kAttnThreads + tid;
+        const int p = base + (i >> 1);
+        v[j] = make_uint4(0, 0, 0, 0);
+        if (i < nv && p < n_ctx)
+          v[j] = __ldcg(reinterpret_cast<const uint4*>(
+                            kv_row(a.vcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
+                        (i & 1));
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = b0 + j * kAttnThreads + tid;
+        if (i >= nv) break;
+        *reinterpret_cast<uint4*>(vs + (i >> 1) * kPvVld + (i & 1) * 8) = v[j];
+      }
+    }
+    // P = fp16(exp(s - max) / sum) for this block's rows, 4 scores per load
+    const int per_row4 = span_pad / 4;
+    const int np = kPvRows * per_row4;
+    for (int b0 = 0; b0 < np; b0 += kAttnThreads * 4) {
+      float4 sv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = b0 + j * kAttnThreads + tid;
+        const int i_row = i / per_row4, p = base + (i % per_row4) * 4;
+        sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+        if (i < np && r0 + i_row < n_rows)
+          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = b0 + j * kAttnThreads + tid;
+        if (i >= np) break;
+        const int i_row = i / per_row4, pl = (i % per_row4) * 4;
+        const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int p = base + pl + e;
+          float pv = 0.f;
+          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - sh.pm[i_row]), sh.pl[i_row]);
+          ps[i_row * kPvPld + pl + e] = __float2half_rn(pv);
+        }
+      }
+    }
+    __syncthreads();
+    for (int kk = warp; kk < span_pad / 16; kk += kAttnWarps) {
+      // A: rows g < kPvRows hold P, rows g+8 and g >= kPvRows are zero
+      uint32_t a0 = 0, a2 = 0;
+      if (g < kPvRows) {
+        a0 = *reinterpret_cast<const uint32_t*>(ps + g * kPvPld + kk * 16 + 2 * t);
+        a2 = *reinterpret_cast<const uint32_t*>(ps + g * kPvPld + kk * 16 + 8 + 2 * t);
+      }
+      uint32_t b0, b1, b2, b3;
+      // matrices: (k0-7, n0-7) (k8-15, n0-7) (k0-7, n8-15) (k8-15, n8-15)
+      const int vrow = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+      const int vcol = (lane / 16) * 8;
+      ldmatrix_x4_trans(b0, b1, b2, b3, vs + vrow * kPvVld + vcol);
+      mma16816(acc[0], a0, 0u, a2, 0u, b0, b1);
+      mma16816(acc[1], a0, 0u, a2, 0u, b2, b3);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s_acc[(warp * kWarp + lane) * 8 + nt * 4 + e] = acc[nt][e];
+  __syncthreads();
+  grid_dep_launch();
+  if (warp == 0 && g < kPvRows) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {       // rows g only (d2, d3 belong to zero rows g+8)
+        float v = s_acc[lane * 8 + nt * 4 + e];
+        for (int w2 = 1; w2 < kAttnWarps; ++w2) v = fadd(v, s_acc[(w2 * kWarp + lane) * 8 + nt * 4 + e]);
+        const int r = r0 + g;
+        if (r < n_rows) {
+          const int m = r / gq, head = kvh * gq + r % gq;
+          const int d = ds * 16 + nt * 8 + 2 * t + e;
+          a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + d] = __float2half_rn(v);
+        }
+      }
+  }
+  __syncthreads();   // shared memory is reused by the caller's next block
+}
+
+}  // namespace alm

@@ -30,10 +30,17 @@ ALM_DEV uint32_t ld_nc_u32(const void* p) {
 // ---------------------------------------------------------------------------
 // bulk copies (TMA engine, no multicast) into shared memory with mbarriers
 // ---------------------------------------------------------------------------
-// Spin limit of every mbarrier wait: after this many polls the waiter gives
-// up and reports an error instead of hanging (a copy of valid memory completes
-// in microseconds).
+// Limits of every mbarrier wait: after this many polls, or this much time on
+// the global timer, the waiter gives up and reports an error instead of
+// hanging (a copy of valid memory completes in microseconds).
 constexpr unsigned kSpinLimit = 1u << 24;
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;
+
+ALM_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 ALM_DEV uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 ALM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
@@ -64,21 +71,21 @@ ALM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase of `parity`; false if the limit ran out.
 ALM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (unsigned i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned i = 1; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+  }
   return false;
 }
-ALM_DEV uint4 lds128(const void* p) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_addr(p)));
-  return r;
-}
-ALM_DEV uint32_t lds32(const void* p) {
-  uint32_t r;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(smem_addr(p)));
-  return r;
-}
+// Plain loads: the compiler orders them after a preceding mbarrier wait (its
+// asm has a memory clobber) and may schedule them freely otherwise.
+ALM_DEV uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+ALM_DEV uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Argmax order: larger value first, then the smaller index.
+ALM_DEV bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
 
 // Programmatic dependent launch: wait for the producer grid's results / let
 // the next grid in the stream start its prologue.  No-ops without PDL.
@@ -110,7 +117,8 @@ ALM_DEV half2 u2h(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
 // ---------------------------------------------------------------------------
 ALM_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                       uint32_t b0, uint32_t b1) {
-  asm volatile(
+  // no side effects: not volatile, so independent MMAs can be interleaved
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

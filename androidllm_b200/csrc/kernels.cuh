@@ -69,7 +69,7 @@ struct ActIn {
 
 // 16-byte loads are allowed when the base is 16-byte aligned and the row
 // stride is a multiple of 8 halves.
-inline void set_vec(ActIn& a) {
+__host__ __device__ inline void set_vec(ActIn& a) {
   const bool ok = (reinterpret_cast<uintptr_t>(a.x) % 16 == 0) && (a.ld % 8 == 0) &&
                   (a.w == nullptr || reinterpret_cast<uintptr_t>(a.w) % 16 == 0);
   a.vec = ok ? 1 : 0;

@@ -9,6 +9,8 @@
 
 #include "../../include/androidllm_b200.h"
 #include "common.cuh"
+#include "forward.cuh"
+#include "gemv_body.cuh"
 #include "kernels.cuh"
 
 namespace alm {
@@ -57,11 +59,6 @@ int pow2_floor(int v) {
   while (p * 2 <= v) p *= 2;
   return p;
 }
-int pow2_ceil(int v) {
-  int p = 1;
-  while (p < v) p *= 2;
-  return p;
-}
 
 // Split-K launch shape of a weight.  Small matrices (a few hundred tiles or
 // fewer) are latency-bound: spread them so the grid holds about two CTAs per
@@ -75,6 +72,10 @@ void set_split(QTile& t, int ksw, int ksg) {
   // drop CTA rows that would get no k-blocks
   t.ksg = std::max(1, (((t.k_blocks + t.kps - 1) / t.kps) + ksw - 1) / ksw);
 }
+
+// Activation k-blocks one GEMV block may stage: bounds its shared memory so
+// the persistent forward kernel keeps two CTAs per SM.
+constexpr int kMaxStageKb = 48;
 
 // Launch shapes measured best on B200 (graph-replayed, PDL) for the step's
 // shapes: narrow matrices let all 8 warps of a CTA split K and avoid cross-CTA
@@ -100,7 +101,7 @@ void choose_split(QTile& t, int n_sms) {
   ksw = std::min(ksw, std::max(1, pow2_floor(kb)));
   ksg = std::max(1, std::min(ksg, kb / ksw));
   set_split(t, ksw, ksg);
-  while (t.ksw * t.kps > 64 && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
+  while (t.ksw * t.kps > kMaxStageKb && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
 }
 
 }  // namespace
@@ -112,7 +113,8 @@ struct alm_ctx {
   int device = 0;
   int n_sms = 148;
   cudaStream_t stream = nullptr;
-  bool pdl = true;   // programmatic dependent launch between forward kernels
+  bool pdl = true;       // programmatic dependent launch between forward kernels
+  bool persist = false;  // forwards of <= 8 rows as one persistent kernel
 };
 
 struct alm_qweight {
@@ -189,6 +191,11 @@ struct alm_model {
   half* final_norm = nullptr;
   bool finalized = false;
   Work ws;
+  // persistent forward kernel
+  FwdLayer* fwd_layers = nullptr;           // device, one per layer
+  unsigned long long* fwd_bar = nullptr;    // device grid-barrier counter
+  size_t fwd_smem = 0;
+  int fwd_grid = 0;                         // 0: not available for this model
 };
 
 struct alm_kv {
@@ -491,9 +498,113 @@ int enqueue_head(alm_model* m, int M, bool pdl) {
   return ALM_OK;
 }
 
+EmbedArgs embed_args(alm_model* m, int M) {
+  Work& ws = m->ws;
+  EmbedArgs ea;
+  ea.table = m->embed_table;
+  ea.scale = m->embed_scale;
+  ea.bits = m->embed_bits;
+  ea.block = m->embed_block;
+  ea.nsb = m->embed_nsb;
+  ea.hidden = m->cfg.hidden;
+  ea.row_bytes = m->embed_row_bytes;
+  ea.vocab = m->cfg.vocab;
+  ea.tokens = ws.tokens;
+  ea.out = ws.x0;
+  ea.M = M;
+  ea.err = ws.err;
+  return ea;
+}
+
+// Device layer table, barrier counter and launch shape of the persistent
+// forward kernel (fwd_grid stays 0 when the kernel cannot keep all its CTAs
+// resident, and forwards then use the standalone kernels).
+int build_forward(alm_model* m) {
+  const alm_model_config& c = m->cfg;
+  std::vector<FwdLayer> host(c.layers);
+  size_t stage = gemv_stage_bytes(m->head->t, 1);
+  for (int li = 0; li < c.layers; ++li) {
+    const Layer& L = m->layers[li];
+    host[li].qkv = L.qkv->t;
+    host[li].o = L.o->t;
+    host[li].gu = L.gu->t;
+    host[li].down = L.down->t;
+    host[li].n_in = L.n_in;
+    host[li].n_post = L.n_post;
+    for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down}) stage = std::max(stage, gemv_stage_bytes(w->t, 1));
+  }
+  if (!m->fwd_layers) ALM_TRY(dev_alloc_t(&m->fwd_layers, static_cast<size_t>(c.layers)));
+  ALM_CUDA(cudaMemcpy(m->fwd_layers, host.data(), host.size() * sizeof(FwdLayer), cudaMemcpyHostToDevice));
+  if (!m->fwd_bar) {
+    ALM_TRY(dev_alloc_t(&m->fwd_bar, 1));
+    ALM_CUDA(cudaMemset(m->fwd_bar, 0, sizeof(unsigned long long)));
+  }
+  m->fwd_grid = 0;
+  m->fwd_smem = forward_smem_bytes(stage, c.head_dim, c.hidden);
+  if (forward_barriers(c.layers, true) > kBarRound || c.head_dim % 16 || c.head_dim > 256) return ALM_OK;
+  int per_sm = 0;
+  if (forward_init_attrs(m->fwd_smem, &per_sm) != cudaSuccess) {
+    cudaGetLastError();
+    return ALM_OK;
+  }
+  if (per_sm >= 1) m->fwd_grid = m->ctx->n_sms * std::min(per_sm, 2);
+  return ALM_OK;
+}
+
+int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
+                               unsigned long long* trace = nullptr) {
+  const alm_model_config& c = m->cfg;
+  Work& ws = m->ws;
+  FwdParams p;
+  p.layers = m->fwd_layers;
+  p.n_layers = c.layers;
+  p.M = M;
+  p.hidden = c.hidden;
+  p.inter = c.intermediate;
+  p.heads = c.heads;
+  p.kv_heads = c.kv_heads;
+  p.head_dim = c.head_dim;
+  p.vocab = c.vocab;
+  p.eps = c.rms_eps;
+  p.sqrt_hd = static_cast<float>(sqrt(static_cast<double>(c.head_dim)));
+  p.embed = embed_args(m, M);
+  p.s1 = ws.s1;
+  p.s2 = ws.s2;
+  p.ss1 = ws.ss1;
+  p.ss2 = ws.ss2;
+  p.q = ws.q;
+  p.ctx = ws.ctx;
+  p.h = ws.h;
+  p.xn = ws.xn;
+  p.logits = ws.logits;
+  p.part = ws.part;
+  p.kcache = kv->k;
+  p.vcache = kv->v;
+  p.kv_layer_elems = kv->layer_elems;
+  p.page_table = kv->page_table;
+  p.page_size = kv->page_size;
+  p.max_ctx = kv->max_len;
+  p.scores = ws.scores;
+  p.score_ld = ws.score_ld;
+  p.stats = ws.stats;
+  p.rope = m->rope;
+  p.do_head = head ? 1 : 0;
+  p.head = m->head->t;
+  p.final_norm = m->final_norm;
+  p.am_val = ws.am_val;
+  p.am_idx = ws.am_idx;
+  p.argmax = ws.argmax;
+  p.io = StepIO{ws.pos, ws.err};
+  p.bar = m->fwd_bar;
+  p.trace = trace;
+  ALM_LAUNCH(launch_forward(p, m->fwd_grid, m->fwd_smem, m->ctx->stream));
+  return ALM_OK;
+}
+
 // Embedding (tokens already in ws.tokens, position in ws.pos) -> all layers ->
 // final norms -> head.
 int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
+  if (m->ctx->persist && m->fwd_grid > 0 && M <= 8) return enqueue_forward_persistent(m, kv, M, head);
   Work& ws = m->ws;
   EmbedArgs ea;
   ea.table = m->embed_table;
@@ -548,6 +659,7 @@ int sync_and_check(alm_model* m) {
   if (err) {
     cudaMemset(m->ws.err, 0, sizeof(int));
     if (err == 2) return fail(ALM_ERR_CUDA, "a device-side wait gave up (weight stream did not arrive)");
+    if (err == 3) return fail(ALM_ERR_CUDA, "a device-side wait gave up (grid barrier of the persistent forward)");
     return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
   }
   return ALM_OK;
@@ -603,6 +715,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
   {
     const char* e = getenv("ALM_NO_PDL");
     c->pdl = !(e && e[0] == '1');
+    const char* e2 = getenv("ALM_PERSIST");
+    c->persist = e2 && e2[0] == '1';
   }
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
@@ -618,6 +732,12 @@ int alm_ctx_destroy(alm_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
+  return ALM_OK;
+}
+
+int alm_ctx_set_persistent(alm_ctx* ctx, int enable) {
+  ALM_REQ(ctx, "null context");
+  ctx->persist = enable != 0;
   return ALM_OK;
 }
 
@@ -821,6 +941,8 @@ int alm_model_destroy(alm_model* m) {
                   (void*)w.scores, (void*)w.stats})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
+  dev_free(m->fwd_layers);
+  dev_free(m->fwd_bar);
   delete m;
   return ALM_OK;
 }
@@ -1001,6 +1123,7 @@ int alm_model_finalize(alm_model* m) {
   for (const Layer& L : m->layers)
     need = std::max({need, split_need(L.qkv), split_need(L.o), split_need(L.gu), split_need(L.down)});
   ALM_TRY(ensure_part(ws, need));
+  ALM_TRY(build_forward(m));
   m->finalized = true;
   return ALM_OK;
 }
@@ -1126,6 +1249,37 @@ int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logit
   ALM_TRY(enqueue_head(m, rows, m->ctx->pdl));
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
+}
+
+int alm_forward_trace(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
+                      uint64_t* trace_host, int cap, int* n_barriers, int* n_ctas) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(tokens_host && trace_host && n_barriers && n_ctas, "null argument");
+  ALM_TRY(check_layers(m));
+  ALM_REQ(rows >= 1 && rows <= 8, "rows must be in 1..8");
+  if (m->fwd_grid <= 0) return fail(ALM_ERR_STATE, "persistent forward kernel unavailable for this model");
+  DeviceGuard g(m->ctx->device);
+  ALM_TRY(check_kv(m, kv, rows, pos0));
+  const int nb = forward_barriers(m->cfg.layers, true);
+  const size_t n = static_cast<size_t>(nb) * (m->fwd_grid + 1);
+  ALM_REQ(cap >= 0 && static_cast<size_t>(cap) >= n, "trace buffer too small");
+  unsigned long long* dtrace = nullptr;
+  ALM_TRY(dev_alloc_t(&dtrace, n));
+  cudaStream_t st = m->ctx->stream;
+  int rc = set_pos(m, pos0);
+  if (rc == ALM_OK && cudaMemcpyAsync(m->ws.tokens, tokens_host, rows * sizeof(int), cudaMemcpyHostToDevice, st) !=
+                          cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "token upload failed");
+  if (rc == ALM_OK) rc = enqueue_forward_persistent(m, kv, rows, true, dtrace);
+  if (rc == ALM_OK) rc = sync_and_check(m);
+  if (rc == ALM_OK && cudaMemcpy(trace_host, dtrace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost) !=
+                          cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "trace download failed");
+  dev_free(dtrace);
+  if (rc != ALM_OK) return rc;
+  *n_barriers = nb;
+  *n_ctas = m->fwd_grid;
+  return ALM_OK;
 }
 
 int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0, float* logits_host,

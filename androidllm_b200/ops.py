@@ -35,6 +35,11 @@ class Context:
     def sync(self):
         check(lib.alm_ctx_sync(self.h))
 
+    def set_persistent(self, enable):
+        """Run forwards of <= 8 rows as one persistent kernel or as one launch
+        per layer operation (the default); both give bit-identical results."""
+        check(lib.alm_ctx_set_persistent(self.h, 1 if enable else 0))
+
     def close(self):
         if self.h:
             lib.alm_ctx_destroy(self.h)
@@ -296,6 +301,20 @@ class DeviceModel:
         am = np.empty(rows, np.int32) if argmax else None
         check(lib.alm_forward(self.h, kv.h, ptr(tok), rows, int(pos0), ptr(lg), ptr(am)))
         return lg, am
+
+    def forward_trace(self, kv, tokens, pos0):
+        """One persistent forward (with head) recording when every CTA
+        finished every phase.  Returns (arrive[n_barriers, n_ctas],
+        passed[n_barriers]) in global-timer nanoseconds."""
+        tok = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        n_bar = 1 + 6 * self.canon["layers"] + 2
+        cap = n_bar * (2 * 148 * 4 + 1)
+        buf = np.zeros(cap, np.uint64)
+        nb, nc = ctypes.c_int(), ctypes.c_int()
+        check(lib.alm_forward_trace(self.h, kv.h, ptr(tok), tok.size, int(pos0), ptr(buf), cap,
+                                    ctypes.byref(nb), ctypes.byref(nc)))
+        nb, nc = nb.value, nc.value
+        return buf[: nb * nc].reshape(nb, nc), buf[nb * nc: nb * nc + nb]
 
     def close(self):
         if self.h:

@@ -59,6 +59,11 @@ ALM_API int alm_abi_version(void);
 ALM_API int alm_ctx_create(int device, alm_ctx** out);
 ALM_API int alm_ctx_destroy(alm_ctx* ctx);
 ALM_API int alm_ctx_sync(alm_ctx* ctx);
+/* Forwards of up to 8 rows as one persistent kernel (enable = 1) or as one
+   launch per layer operation (enable = 0, the default; the environment
+   variable ALM_PERSIST=1 turns the persistent kernel on at context creation).
+   The results are bit-identical.  Graphs captured earlier keep their kernels. */
+ALM_API int alm_ctx_set_persistent(alm_ctx* ctx, int enable);
 /* Device memory helpers for hosts without their own device-memory library. */
 ALM_API int alm_dev_alloc(alm_ctx* ctx, size_t bytes, void** out_dev);
 ALM_API int alm_dev_free(alm_ctx* ctx, void* dev);
@@ -169,6 +174,14 @@ ALM_API int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, floa
  * pos0..pos0+rows-1 (androidllm/engine.py:255-286 without sampling). */
 ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
                 float* logits_host, int32_t* argmax_host);
+/* Profiling (no counterpart in the reference): alm_forward with the head,
+ * run as the persistent forward kernel (rows <= 8), recording global-timer
+ * nanoseconds.  trace_host receives n_barriers * n_ctas arrival times
+ * (barrier-major: when each CTA finished a phase) followed by n_barriers
+ * times at which CTA 0 passed each barrier; cap is its length in entries.
+ * Fails with ALM_ERR_STATE when the persistent kernel is unavailable. */
+ALM_API int alm_forward_trace(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
+                      uint64_t* trace_host, int cap, int* n_barriers, int* n_ctas);
 
 /* ---- speculative decoding (androidllm/engine.py:288-320) ----------------------- */
 /* A greedy speculative decoder: K draft steps (M = 1 forwards of `draft`)
