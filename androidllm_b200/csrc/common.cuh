@@ -52,12 +52,19 @@ ALM_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
+// L2 policy for data read once per forward (weights): evicted first, so the
+// stream does not push activations, the KV cache or kernel code out of L2.
+ALM_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 // global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16
-ALM_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+ALM_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
 ALM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

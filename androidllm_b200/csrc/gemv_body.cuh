@@ -146,7 +146,7 @@ ALM_DEV void ring_issue(const Ring& r, const GemvPlan& p, int rec_bytes, int ite
   unsigned char* dst = r.base + static_cast<size_t>(warp * kSlots + slot) * r.slot_bytes;
   const uint32_t bytes = static_cast<uint32_t>(min(items, p.n - c * items) * rec_bytes);
   mbar_expect_tx(bar, bytes);
-  bulk_g2s(dst, p.gsrc + static_cast<size_t>(c) * items * rec_bytes, bytes, bar);
+  bulk_g2s(dst, p.gsrc + static_cast<size_t>(c) * items * rec_bytes, bytes, bar, l2_evict_first());
 }
 
 // Issue the plan's first kSlots chunks (the ring must be drained and every
