@@ -80,6 +80,11 @@ SIGNATURES = {
     "alm_spec_run": [_P, _I, _P, _P, _P],
     "alm_spec_state": [_P, _PI32, _PI32],
     "alm_spec_kernel_count": [_P, _PI32],
+    "alm_spec_set_sampling": [_P, ctypes.c_float, ctypes.c_float, ctypes.c_float],
+    "alm_spec_set_uniforms": [_P, _P, _I],
+    "alm_spec_uniforms_used": [_P, _PI32],
+    "alm_sample": [_P, _P, _I, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],
+    "alm_model_sample": [_P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],
     "alm_profiler_range": [_I],
     "alm_spec_bench": [_P, _I, ctypes.POINTER(ctypes.c_float), _PI32],
     "alm_bench_qmatmul": [_P, _PP, _I, _P, _I, _P, _I, ctypes.POINTER(ctypes.c_float)],

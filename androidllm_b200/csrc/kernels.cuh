@@ -157,6 +157,25 @@ cudaError_t launch_embed(const EmbedArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_rownorm(const ActIn& in, int M, const half* w2, float eps2, half* out,
                            int ldo, bool pdl, cudaStream_t st);
 
+// Sampling of rows of fp16 logits (engine.py:26-45 semantics, fixed
+// arithmetic; see sample.cu).  Row r draws uniforms[*u_cursor + u_offset + r]
+// (u_cursor may be null: 0).  temperature <= 0 gives the argmax.
+struct SampleArgs {
+  const half* logits = nullptr;
+  int ld = 0;
+  int vocab = 0;
+  float temperature = 0.f;      // max(T, 1e-9) as fp32, or <= 0 for argmax
+  float top_p = 1.f;
+  float min_p = 0.f;
+  const double* uniforms = nullptr;
+  const int* u_cursor = nullptr;
+  int u_offset = 0;
+  float* scratch = nullptr;     // rows * vocab fp32
+  int* out = nullptr;           // rows
+};
+cudaError_t sample_init_attrs();
+cudaError_t launch_sample(const SampleArgs& a, int rows, bool pdl, cudaStream_t st);
+
 // argmax over CTA partials -> tokens (M)
 cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_part, int M,
                                 int* out, bool pdl, cudaStream_t st);

@@ -19,7 +19,7 @@ cudaError_t launch_spec_prep_draft(const int* state, int* cand, const int* d_arg
 cudaError_t launch_spec_prep_verify(const int* state, int* cand, const int* d_argmax, int k, int* tokens,
                                     int* pos, cudaStream_t st);
 cudaError_t launch_spec_accept_greedy(int* state, const int* cand, const int* t_argmax, int k, int* out_tokens,
-                                      int* out_accepted, int cap_tokens, int cap_steps, cudaStream_t st);
+                                      int* out_accepted, int cap_tokens, int cap_steps, int sampled, cudaStream_t st);
 }  // namespace alm
 
 using namespace alm;
@@ -157,6 +157,7 @@ struct Work {
   int* argmax = nullptr;
   float* part = nullptr;
   size_t part_floats = 0;
+  float* sample_scratch = nullptr;   // kMaxRows * vocab fp32 for the sampler
   float* scores = nullptr;
   float* stats = nullptr;
   int attn_ctx = 0;       // capacity of the attention scratch (positions)
@@ -221,6 +222,11 @@ struct alm_spec {
   cudaGraphExec_t graph = nullptr;
   int* pinned = nullptr;     // host: 4 + cap_tokens + cap_steps
   int n_kernels = 0;         // kernel nodes in the step graph
+  // sampling at temperature > 0 (engine.py:26-45 per draft and target row)
+  float temperature = 0.f;   // <= 0: greedy
+  float top_p = 1.f, min_p = 0.f;
+  double* uniforms = nullptr;  // device stream of uniform draws; state[4] = next unused
+  int n_uniforms = 0, cap_uniforms = 0;
 };
 
 namespace {
@@ -630,6 +636,31 @@ int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
   return enqueue_head(m, M, pdl);
 }
 
+// Sampler arguments for rows of a model's last logits, writing the picks
+// into its argmax buffer.
+SampleArgs sample_args(alm_model* m, float temperature, float top_p, float min_p, const double* uniforms,
+                       const int* cursor, int offset) {
+  SampleArgs a;
+  a.logits = m->ws.logits;
+  a.ld = m->cfg.vocab;
+  a.vocab = m->cfg.vocab;
+  a.temperature = temperature;
+  a.top_p = top_p;
+  a.min_p = min_p;
+  a.uniforms = uniforms;
+  a.u_cursor = cursor;
+  a.u_offset = offset;
+  a.scratch = m->ws.sample_scratch;
+  a.out = m->ws.argmax;
+  return a;
+}
+
+int ensure_sample_scratch(alm_model* m) {
+  if (!m->ws.sample_scratch)
+    ALM_TRY(dev_alloc_t(&m->ws.sample_scratch, static_cast<size_t>(kMaxRows) * m->cfg.vocab));
+  return ALM_OK;
+}
+
 int check_ready(alm_model* m) {
   ALM_REQ(m != nullptr, "null model");
   if (!m->finalized) return fail(ALM_ERR_STATE, "model not finalized");
@@ -707,6 +738,7 @@ int alm_ctx_create(int device, alm_ctx** out) {
     cudaError_t e = gemv_init_attrs();
     if (e == cudaSuccess) e = attention_init_attrs();
     if (e == cudaSuccess) e = rows_init_attrs();
+    if (e == cudaSuccess) e = sample_init_attrs();
     if (e != cudaSuccess) return fail(ALM_ERR_CUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
   }
   auto* c = new alm_ctx();
@@ -938,7 +970,7 @@ int alm_model_destroy(alm_model* m) {
   for (void* p : {(void*)w.tokens, (void*)w.pos, (void*)w.err, (void*)w.x0, (void*)w.s1, (void*)w.s2,
                   (void*)w.ss1, (void*)w.ss2, (void*)w.q, (void*)w.ctx, (void*)w.h, (void*)w.xn, (void*)w.xout,
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
-                  (void*)w.scores, (void*)w.stats})
+                  (void*)w.scores, (void*)w.stats, (void*)w.sample_scratch})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
   dev_free(m->fwd_layers);
@@ -1282,6 +1314,80 @@ int alm_forward_trace(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int 
   return ALM_OK;
 }
 
+int alm_sample(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature, float top_p,
+               float min_p, const double* uniforms_host, int32_t* out_host) {
+  ALM_REQ(ctx && logits_host && out_host && (uniforms_host || !(temperature > 0.f)), "null argument");
+  ALM_REQ(rows >= 1 && vocab >= 1, "empty logits");
+  ALM_REQ(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
+  ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const size_t n = static_cast<size_t>(rows) * vocab;
+  half* dl = nullptr;
+  float* scr = nullptr;
+  double* du = nullptr;
+  int* dout = nullptr;
+  int rc = dev_alloc_t(&dl, n);
+  if (rc == ALM_OK) rc = dev_alloc_t(&scr, n);
+  if (rc == ALM_OK) rc = dev_alloc_t(&du, static_cast<size_t>(rows));
+  if (rc == ALM_OK) rc = dev_alloc_t(&dout, static_cast<size_t>(rows));
+  if (rc == ALM_OK && (cudaMemcpyAsync(dl, logits_host, n * sizeof(half), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                       (uniforms_host && cudaMemcpyAsync(du, uniforms_host, rows * sizeof(double),
+                                                         cudaMemcpyHostToDevice, st) != cudaSuccess)))
+    rc = fail(ALM_ERR_CUDA, "upload failed");
+  if (rc == ALM_OK) {
+    SampleArgs a;
+    a.logits = dl;
+    a.ld = vocab;
+    a.vocab = vocab;
+    a.temperature = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
+    a.top_p = top_p;
+    a.min_p = min_p;
+    a.uniforms = du;
+    a.scratch = scr;
+    a.out = dout;
+    const cudaError_t e = launch_sample(a, rows, false, st);
+    if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("sample: ") + cudaGetErrorString(e));
+  }
+  if (rc == ALM_OK && (cudaMemcpyAsync(out_host, dout, rows * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                       cudaStreamSynchronize(st) != cudaSuccess))
+    rc = fail(ALM_ERR_CUDA, "sample failed");
+  dev_free(dl);
+  dev_free(scr);
+  dev_free(du);
+  dev_free(dout);
+  return rc;
+}
+
+int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
+                     const double* uniforms_host, int32_t* out_host) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(out_host && (uniforms_host || !(temperature > 0.f)), "null argument");
+  ALM_REQ(rows >= 1 && rows <= kMaxRows, "rows must be in 1..16");
+  ALM_REQ(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
+  ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
+  DeviceGuard g(m->ctx->device);
+  ALM_TRY(ensure_sample_scratch(m));
+  cudaStream_t st = m->ctx->stream;
+  double* du = nullptr;
+  ALM_TRY(dev_alloc_t(&du, static_cast<size_t>(rows)));
+  int rc = ALM_OK;
+  if (uniforms_host &&
+      cudaMemcpyAsync(du, uniforms_host, rows * sizeof(double), cudaMemcpyHostToDevice, st) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "upload failed");
+  if (rc == ALM_OK) {
+    const float t = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
+    const cudaError_t e = launch_sample(sample_args(m, t, top_p, min_p, du, nullptr, 0), rows, false, st);
+    if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("sample: ") + cudaGetErrorString(e));
+  }
+  if (rc == ALM_OK && (cudaMemcpyAsync(out_host, m->ws.argmax, rows * sizeof(int), cudaMemcpyDeviceToHost, st) !=
+                           cudaSuccess ||
+                       cudaStreamSynchronize(st) != cudaSuccess))
+    rc = fail(ALM_ERR_CUDA, "sample failed");
+  dev_free(du);
+  return rc;
+}
+
 int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0, float* logits_host,
                 int32_t* argmax_host) {
   ALM_TRY(check_ready(m));
@@ -1303,15 +1409,58 @@ static int enqueue_spec_step(alm_spec* s) {
   alm_model* d = s->draft;
   alm_model* t = s->target;
   cudaStream_t st = t->ctx->stream;
+  const bool sampled = s->temperature > 0.f;
   for (int i = 0; i < s->k; ++i) {
     ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
     ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
+    // draft candidate i: the draft's sample, draw k-step offset i
+    if (sampled)
+      ALM_CUDA(launch_sample(sample_args(d, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, i), 1,
+                             false, st));
   }
   ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
   ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
+  // target row j: the target's sample with draw k + j
+  if (sampled)
+    ALM_CUDA(launch_sample(sample_args(t, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, s->k),
+                           s->k + 1, false, st));
   ALM_CUDA(launch_spec_accept_greedy(s->state, s->cand, t->ws.argmax, s->k, s->out_tokens, s->out_acc,
-                                     s->cap_tokens, s->cap_steps, st));
+                                     s->cap_tokens, s->cap_steps, sampled ? 1 : 0, st));
   return ALM_OK;
+}
+
+// (Re)capture the step graph for the decoder's current sampling settings.
+static int capture_spec_graph(alm_spec* s) {
+  if (s->temperature > 0.f) {
+    ALM_TRY(ensure_sample_scratch(s->target));
+    ALM_TRY(ensure_sample_scratch(s->draft));
+  }
+  if (s->graph) {
+    cudaGraphExecDestroy(s->graph);
+    s->graph = nullptr;
+  }
+  s->n_kernels = 0;
+  cudaStream_t st = s->target->ctx->stream;
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return fail(ALM_ERR_CUDA, "graph capture failed to start");
+  int rc = enqueue_spec_step(s);
+  cudaError_t e = cudaStreamEndCapture(st, &graph);
+  if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+  if (rc == ALM_OK) {
+    size_t n_nodes = 0;
+    cudaGraphGetNodes(graph, nullptr, &n_nodes);
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (n_nodes) cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
+    for (cudaGraphNode_t nd : nodes) {
+      cudaGraphNodeType ty;
+      if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->n_kernels;
+    }
+    e = cudaGraphInstantiate(&s->graph, graph, 0);
+    if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
+  }
+  if (graph) cudaGraphDestroy(graph);
+  return rc;
 }
 
 int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_kv* draft_kv, int k,
@@ -1335,39 +1484,16 @@ int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_
   s->k = k;
   s->cap_steps = 1024;
   s->cap_tokens = s->cap_steps * (k + 1);
-  int rc = dev_alloc_t(&s->state, 4);
+  int rc = dev_alloc_t(&s->state, 8);
   if (rc == ALM_OK) rc = dev_alloc_t(&s->cand, k);
   if (rc == ALM_OK) rc = dev_alloc_t(&s->out_tokens, s->cap_tokens);
   if (rc == ALM_OK) rc = dev_alloc_t(&s->out_acc, s->cap_steps);
   if (rc == ALM_OK && cudaMallocHost(reinterpret_cast<void**>(&s->pinned),
                                      (4 + s->cap_tokens + s->cap_steps) * sizeof(int)) != cudaSuccess)
     rc = fail(ALM_ERR_CUDA, "pinned allocation failed");
-  if (rc == ALM_OK && cudaMemset(s->state, 0, 4 * sizeof(int)) != cudaSuccess)
+  if (rc == ALM_OK && cudaMemset(s->state, 0, 8 * sizeof(int)) != cudaSuccess)
     rc = fail(ALM_ERR_CUDA, "state init failed");
-  if (rc == ALM_OK) {
-    cudaStream_t st = target->ctx->stream;
-    cudaGraph_t graph = nullptr;
-    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-      rc = fail(ALM_ERR_CUDA, "graph capture failed to start");
-    } else {
-      rc = enqueue_spec_step(s);
-      cudaError_t e = cudaStreamEndCapture(st, &graph);
-      if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
-      if (rc == ALM_OK) {
-        size_t n_nodes = 0;
-        cudaGraphGetNodes(graph, nullptr, &n_nodes);
-        std::vector<cudaGraphNode_t> nodes(n_nodes);
-        if (n_nodes) cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
-        for (cudaGraphNode_t nd : nodes) {
-          cudaGraphNodeType ty;
-          if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->n_kernels;
-        }
-        e = cudaGraphInstantiate(&s->graph, graph, 0);
-        if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
-      }
-      if (graph) cudaGraphDestroy(graph);
-    }
-  }
+  if (rc == ALM_OK) rc = capture_spec_graph(s);
   if (rc != ALM_OK) {
     alm_spec_destroy(s);
     return rc;
@@ -1385,6 +1511,7 @@ int alm_spec_destroy(alm_spec* s) {
   dev_free(s->cand);
   dev_free(s->out_tokens);
   dev_free(s->out_acc);
+  dev_free(s->uniforms);
   if (s->pinned) cudaFreeHost(s->pinned);
   delete s;
   return ALM_OK;
@@ -1415,6 +1542,58 @@ int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos) {
   return ALM_OK;
 }
 
+// Sampling steps read up to 2k + 1 draws each beyond the cursor.
+static int check_uniforms(alm_spec* s, int n_steps) {
+  if (!(s->temperature > 0.f)) return ALM_OK;
+  int cursor = 0;
+  ALM_CUDA(cudaMemcpy(&cursor, s->state + 4, sizeof(int), cudaMemcpyDeviceToHost));
+  const long long need = static_cast<long long>(cursor) + static_cast<long long>(n_steps) * (2 * s->k + 1);
+  if (need > s->n_uniforms) return fail(ALM_ERR_ARG, "not enough uniform draws loaded (alm_spec_set_uniforms)");
+  return ALM_OK;
+}
+
+int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min_p) {
+  ALM_REQ(s, "null spec");
+  ALM_REQ(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
+  ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
+  DeviceGuard g(s->target->ctx->device);
+  ALM_CUDA(cudaStreamSynchronize(s->target->ctx->stream));
+  s->temperature = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
+  s->top_p = top_p;
+  s->min_p = min_p;
+  return capture_spec_graph(s);
+}
+
+int alm_spec_set_uniforms(alm_spec* s, const double* uniforms_host, int n) {
+  ALM_REQ(s && (uniforms_host || n == 0), "null argument");
+  ALM_REQ(n >= 0, "negative count");
+  DeviceGuard g(s->target->ctx->device);
+  cudaStream_t st = s->target->ctx->stream;
+  ALM_CUDA(cudaStreamSynchronize(st));
+  if (n > s->cap_uniforms) {
+    dev_free(s->uniforms);
+    s->uniforms = nullptr;
+    s->cap_uniforms = 0;
+    ALM_TRY(dev_alloc_t(&s->uniforms, static_cast<size_t>(n)));
+    s->cap_uniforms = n;
+    // the captured graph holds the buffer's address
+    if (s->temperature > 0.f) ALM_TRY(capture_spec_graph(s));
+  }
+  if (n) ALM_CUDA(cudaMemcpy(s->uniforms, uniforms_host, static_cast<size_t>(n) * sizeof(double),
+                             cudaMemcpyHostToDevice));
+  s->n_uniforms = n;
+  ALM_CUDA(cudaMemset(s->state + 4, 0, sizeof(int)));
+  return ALM_OK;
+}
+
+int alm_spec_uniforms_used(alm_spec* s, int32_t* used) {
+  ALM_REQ(s && used, "null argument");
+  DeviceGuard g(s->target->ctx->device);
+  ALM_CUDA(cudaStreamSynchronize(s->target->ctx->stream));
+  ALM_CUDA(cudaMemcpy(used, s->state + 4, sizeof(int), cudaMemcpyDeviceToHost));
+  return ALM_OK;
+}
+
 int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emitted_host,
                  int32_t* accepted_host) {
   ALM_REQ(s && emitted_host && n_emitted_host, "null argument");
@@ -1426,6 +1605,7 @@ int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emi
   const int last_pos = cur[1] + n_steps * (s->k + 1) + s->k;
   ALM_REQ(last_pos < s->tkv->max_len && last_pos < s->dkv->max_len, "speculative steps would overflow the kv cache");
   ALM_REQ(last_pos < s->target->cfg.max_len && last_pos < s->draft->cfg.max_len, "position beyond the rope table");
+  ALM_TRY(check_uniforms(s, n_steps));
   ALM_CUDA(cudaMemsetAsync(s->state + 2, 0, 2 * sizeof(int), st));
   for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(s->graph, st));
   int* h = s->pinned;
@@ -1467,6 +1647,7 @@ int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted) {
   ALM_CUDA(cudaMemcpy(cur, s->state, sizeof(cur), cudaMemcpyDeviceToHost));
   const int last_pos = cur[1] + n_steps * (s->k + 1) + s->k;
   ALM_REQ(last_pos < s->tkv->max_len && last_pos < s->dkv->max_len, "speculative steps would overflow the kv cache");
+  ALM_TRY(check_uniforms(s, n_steps));
   cudaEvent_t e0, e1;
   ALM_CUDA(cudaEventCreate(&e0));
   ALM_CUDA(cudaEventCreate(&e1));

@@ -3,7 +3,8 @@
 // (K+1)-row verify forward and the acceptance — runs without the host.
 //
 // state[0] = token at the current position, state[1] = that position,
-// state[2] = tokens emitted in this run, state[3] = steps in this run.
+// state[2] = tokens emitted in this run, state[3] = steps in this run,
+// state[4] = next unused uniform draw (sampling at temperature > 0).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -34,12 +35,17 @@ __global__ void spec_prep_verify_kernel(const int* state, int* cand, const int* 
 // engine.py:306-320: accept while target pick == candidate; emit the
 // accepted candidates and then the target's pick at the first mismatch (or
 // the bonus pick after K accepts).
+// With sampling, t_argmax holds the target's sampled tokens and the
+// candidates are the draft's samples (engine.py:296-320 at T > 0): the step
+// consumed k draft draws and n + 1 target draws, so the cursor advances by
+// k + n + 1 (the later rows' draws were not used).
 __global__ void spec_accept_greedy_kernel(int* state, const int* cand, const int* t_argmax, int k,
                                           int* out_tokens, int* out_accepted, int cap_tokens,
-                                          int cap_steps) {
+                                          int cap_steps, int sampled) {
   if (threadIdx.x != 0) return;
   int n = 0;
   while (n < k && t_argmax[n] == cand[n]) ++n;
+  if (sampled) state[4] += k + n + 1;
   const int base = state[2];
   for (int j = 0; j < n; ++j)
     if (base + j < cap_tokens) out_tokens[base + j] = cand[j];
@@ -64,9 +70,9 @@ cudaError_t launch_spec_prep_verify(const int* state, int* cand, const int* d_ar
   return cudaGetLastError();
 }
 cudaError_t launch_spec_accept_greedy(int* state, const int* cand, const int* t_argmax, int k, int* out_tokens,
-                                      int* out_accepted, int cap_tokens, int cap_steps, cudaStream_t st) {
+                                      int* out_accepted, int cap_tokens, int cap_steps, int sampled, cudaStream_t st) {
   spec_accept_greedy_kernel<<<1, 32, 0, st>>>(state, cand, t_argmax, k, out_tokens, out_accepted, cap_tokens,
-                                              cap_steps);
+                                              cap_steps, sampled);
   return cudaGetLastError();
 }
 

@@ -10,13 +10,18 @@ streaming was a phone's RAM; a B200 holds the model many times over):
   head, argmax) and a speculative step — K draft forwards, one (K+1)-row
   verify forward of the target and the acceptance — is one CUDA-graph replay
   with no host round trip inside it;
-* greedy acceptance follows ``engine.py:306-320``: accept while the target's
-  pick equals the draft's candidate, then emit the target's correction, or a
-  bonus token after K accepts.
+* acceptance follows ``engine.py:306-320``: accept while the target's pick
+  equals the draft's candidate, then emit the target's correction, or a
+  bonus token after K accepts.  At temperature > 0 both picks are samples
+  (``engine.py:26-45`` on the device, ``alm_sample``'s fixed arithmetic)
+  driven by one stream of uniform draws consumed in the reference's order:
+  the K draft samples, then one per verified target row up to the first
+  rejection; a plain step takes one draw.
 
-Out of the path and not carried over: prompt-prefix KV reuse, layer skipping,
-throttling, grammar masking (grammar disables speculation in the reference
-too) and the tokenizer.  Sampling at temperature > 0 is not available yet.
+``seed`` (not in the reference, whose generator is unseeded) makes the
+stream reproducible.  Out of the path and not carried over: prompt-prefix KV
+reuse, layer skipping, throttling, grammar masking (grammar disables
+speculation in the reference too) and the tokenizer.
 """
 import os
 import time
@@ -32,7 +37,7 @@ PREFILL_ROWS = 16
 
 
 class LayerStreamingEngine:
-    def __init__(self, model_dir, keep_layers=0, draft_dir=None, spec_k=0, device=0, _ctx=None):
+    def __init__(self, model_dir, keep_layers=0, draft_dir=None, spec_k=0, device=0, seed=None, _ctx=None):
         self.model_dir = model_dir
         self.manifest = load_manifest(model_dir)
         canon = self.manifest["config"]
@@ -46,7 +51,10 @@ class LayerStreamingEngine:
         self.model = LlamaModel.from_device(self.dm, embed=_EmbedRows(model_dir, self.manifest))
         self.ctx_len = min(int(canon["max_len"]), int(os.environ.get("ANDROIDLLM_MAX_CTX", "4096")))
         self._keep = self.n_layers
-        self._rng = np.random.default_rng()
+        self._rng = np.random.default_rng(seed)
+        self._u = np.empty(0, np.float64)   # drawn uniforms; self._u[self._u_used:] not consumed yet
+        self._u_used = 0
+        self._u_host_moved = False          # the host consumed draws after the last upload
         self.stats = {"cache_hits": 0, "cache_misses": self.n_layers, "load_ms": load_ms,
                       "load_calls": self.n_layers, "compute_ms": 0.0, "compute_tokens": 0,
                       "tokens_served": 0, "prefix_calls": 0, "prefix_tokens": 0,
@@ -111,24 +119,54 @@ class LayerStreamingEngine:
             self.dm.forward(kv.cache, chunk, pos0 + i, logits=False, argmax=False)
         self._account(t0, len(ids))
 
+    # -- uniform draws (one stream, consumed in the reference's order) ---------------
+    def _draws(self, n):
+        """Make at least n unconsumed draws available in self._u."""
+        if self._u.size - self._u_used < n:
+            self._u = np.concatenate([self._u[self._u_used:], self._rng.random(max(4096, n))])
+            self._u_used = 0
+
+    def _next_draw(self):
+        self._draws(1)
+        u = float(self._u[self._u_used])
+        self._u_used += 1
+        self._u_host_moved = True
+        return u
+
+    def _feed_spec(self, dec, temperature, top_p, min_p):
+        """Sampling settings and enough draws for one speculative step."""
+        dec.set_sampling(temperature, top_p, min_p)
+        if temperature > 0:
+            need = 2 * self.spec_k + 1
+            if dec._uniforms is not self._u or self._u_host_moved or self._u.size - self._u_used < need:
+                self._draws(need)
+                dec.set_uniforms(self._u[self._u_used:])
+                self._u = dec._uniforms
+                self._u_used = 0
+                self._u_host_moved = False
+
     def _step(self, kv, pos, token, temperature, top_p, min_p, grammar=None, buf_parts=None):
         """engine.py:278-286: embed, full forward at pos, pick the next token."""
-        _check_greedy(temperature, grammar)
+        _check_grammar(grammar)
         t0 = time.time()
         _, am = self.dm.forward(kv.cache, [token], pos)
         self._account(t0, 1)
+        if temperature > 0:
+            return int(self.dm.sample(1, temperature, top_p, min_p, [self._next_draw()])[0])
         return int(am[0])
 
     def _spec_step(self, kv, dkv, pos, token, temperature, top_p, min_p):
         """engine.py:288-320 on the device: returns (emitted, next_token,
         next_pos, n_draft_accepted)."""
-        _check_greedy(temperature, None)
         s = self._spec_decoder()
         if kv is not self._kv or dkv is not self.draft._kv:
             raise ValueError("speculative steps run on the engine's own KV caches")
+        self._feed_spec(s, temperature, top_p, min_p)
         s.begin(token, pos)
         t0 = time.time()
         emitted, acc = s.run(1)
+        if temperature > 0:
+            self._u_used = s.uniforms_used()
         self._account(t0, self.spec_k + 1)
         self.draft._account(t0, self.spec_k)
         self.stats["draft_tokens"] = self.stats.get("draft_tokens", 0) + self.spec_k
@@ -137,7 +175,7 @@ class LayerStreamingEngine:
     # -- generate ---------------------------------------------------------------------
     def generate(self, prompt_ids, max_new_tokens=64, temperature=0.8, top_p=0.9, min_p=0.0,
                  stop_ids=(), callback=None, grammar=None):
-        _check_greedy(temperature, grammar)
+        _check_grammar(grammar)
         prompt_ids = [int(t) for t in list(prompt_ids)[: self.ctx_len]]
         if not prompt_ids:
             raise ValueError("empty prompt")
@@ -167,8 +205,11 @@ class LayerStreamingEngine:
                 # one speculative step: the step's input state goes to the
                 # device, its emitted tokens come back (engine.py:369-387)
                 t0 = time.time()
+                self._feed_spec(dec, temperature, top_p, min_p)
                 dec.begin(token, pos)
                 emitted, accepted = dec.run(1)
+                if temperature > 0:
+                    self._u_used = dec.uniforms_used()
                 self._account(t0, self.spec_k + 1)
                 self.draft._account(t0, self.spec_k)
                 n_draft = accepted[0]
@@ -255,11 +296,9 @@ class LayerStreamingEngine:
         return snap
 
 
-def _check_greedy(temperature, grammar):
+def _check_grammar(grammar):
     if grammar is not None:
         raise NotImplementedError("grammar-constrained decoding is outside this engine")
-    if temperature > 0:
-        raise NotImplementedError("sampling at temperature > 0 is not available on the device yet")
 
 
 class _EmbedRows:

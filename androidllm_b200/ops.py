@@ -166,6 +166,20 @@ class QWeight:
             pass
 
 
+def sample(ctx, logits, temperature, top_p=1.0, min_p=0.0, uniforms=None):
+    """alm_sample: engine.py:26-45 on rows of fp16 logits (rows, vocab) with
+    the caller's uniform draws (one per row); temperature <= 0 is argmax."""
+    lg = _f16(np.atleast_2d(logits))
+    rows, vocab = lg.shape
+    u = np.ascontiguousarray(np.zeros(rows) if uniforms is None else uniforms, dtype=np.float64).reshape(-1)
+    if u.size != rows:
+        raise ValueError("one uniform draw per row")
+    out = np.empty(rows, np.int32)
+    check(lib.alm_sample(ctx.h, ptr(lg), rows, vocab, float(temperature), float(top_p), float(min_p), ptr(u),
+                         ptr(out)))
+    return out
+
+
 def bench_qmatmul(ctx, weights, x, iters):
     """Mean device time (us) of one dequant-GEMV launch, cycling through
     ``weights`` (QWeight of one shape) so their total can exceed L2."""
@@ -302,6 +316,14 @@ class DeviceModel:
         check(lib.alm_forward(self.h, kv.h, ptr(tok), rows, int(pos0), ptr(lg), ptr(am)))
         return lg, am
 
+    def sample(self, rows, temperature, top_p=1.0, min_p=0.0, uniforms=None):
+        """alm_model_sample: sample the first rows of the last forward's logits."""
+        u = np.ascontiguousarray(np.zeros(rows) if uniforms is None else uniforms, dtype=np.float64).reshape(-1)
+        out = np.empty(rows, np.int32)
+        check(lib.alm_model_sample(self.h, int(rows), float(temperature), float(top_p), float(min_p), ptr(u),
+                                   ptr(out)))
+        return out
+
     def forward_trace(self, kv, tokens, pos0):
         """One persistent forward (with head) recording when every CTA
         finished every phase.  Returns (arrive[n_barriers, n_ctas],
@@ -397,6 +419,8 @@ class SpecDecoder:
         self.h = h
         self.k = int(k)
         self._keep = (target, draft, target_kv, draft_kv)
+        self._sampling = (0.0, 1.0, 0.0)
+        self._uniforms = None
 
     def begin(self, token, pos):
         check(lib.alm_spec_begin(self.h, int(token), int(pos)))
@@ -408,6 +432,25 @@ class SpecDecoder:
         acc = np.empty(n_steps, np.int32)
         check(lib.alm_spec_run(self.h, int(n_steps), ptr(emitted), ptr(n), ptr(acc)))
         return emitted[: int(n[0])].tolist(), acc.tolist()
+
+    def set_sampling(self, temperature, top_p=1.0, min_p=0.0):
+        """Sampling steps at temperature > 0 (greedy at <= 0); re-captures the
+        step graph only when the settings change."""
+        key = (float(temperature) if temperature > 0 else 0.0, float(top_p), float(min_p))
+        if key != self._sampling:
+            check(lib.alm_spec_set_sampling(self.h, key[0], key[1], key[2]))
+            self._sampling = key
+
+    def set_uniforms(self, uniforms):
+        """Load the uniform draws the sampling steps consume (cursor reset)."""
+        u = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(-1)
+        check(lib.alm_spec_set_uniforms(self.h, ptr(u), u.size))
+        self._uniforms = u
+
+    def uniforms_used(self):
+        n = ctypes.c_int32()
+        check(lib.alm_spec_uniforms_used(self.h, ctypes.byref(n)))
+        return n.value
 
     def bench(self, n_steps):
         """Device-timed replay of n_steps steps: (ms, emitted tokens)."""

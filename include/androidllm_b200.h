@@ -170,6 +170,21 @@ ALM_API int alm_layer_forward(alm_model* m, int layer, alm_kv* kv, const uint16_
  * output may be NULL. */
 ALM_API int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logits_host,
                     int32_t* argmax_host);
+/* Replaces androidllm_rs/src/lib.rs:339 sample and androidllm/engine.py:26-45
+ * _sample for `rows` rows of fp16 logits (rows, vocab): temperature <= 0 gives
+ * the argmax (first index); otherwise softmax(l / T), the min-p filter when
+ * 0 < min_p < 1, the top-p nucleus when top_p < 1, then the inverse CDF at
+ * the caller's uniform draw uniforms_host[r] in [0, 1) (the draw numpy's
+ * Generator.choice takes; the Rust sampler's seed has no counterpart).  The
+ * arithmetic is fixed (reproducible exp, fixed-order sums, exact integer
+ * cumulative masses, ties in the nucleus by ascending index), so results
+ * are deterministic. */
+ALM_API int alm_sample(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature,
+                 float top_p, float min_p, const double* uniforms_host, int32_t* out_host);
+/* alm_sample on the first `rows` rows of the model's last computed logits
+ * (alm_forward with a head) without copying them to the host. */
+ALM_API int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
+                       const double* uniforms_host, int32_t* out_host);
 /* Embedding + every layer + final norm + head for tokens at positions
  * pos0..pos0+rows-1 (androidllm/engine.py:255-286 without sampling). */
 ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
@@ -205,6 +220,18 @@ ALM_API int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_
 ALM_API int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos);
 /* Number of kernel nodes in one speculative step's CUDA graph. */
 ALM_API int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels);
+/* Sampling steps (engine.py:296-320 at temperature > 0): every draft
+ * candidate is the draft's sample and every verify row the target's sample
+ * (alm_sample's rule), accepted while they agree.  temperature <= 0 restores
+ * the greedy step.  Re-captures the step graph. */
+ALM_API int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min_p);
+/* Load the stream of uniform draws in [0, 1) the sampling steps consume in
+ * the reference's order (the k draft samples, then one per target row up to
+ * the first rejection); resets the cursor to the stream's start.  A run of n
+ * steps needs cursor + n * (2k + 1) draws loaded. */
+ALM_API int alm_spec_set_uniforms(alm_spec* s, const double* uniforms_host, int n);
+/* Draws of the loaded stream consumed so far. */
+ALM_API int alm_spec_uniforms_used(alm_spec* s, int32_t* used);
 
 /* ---- measurement ---------------------------------------------------------------- */
 /* Replay n_steps speculative steps back to back and time them with CUDA

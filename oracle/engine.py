@@ -6,6 +6,9 @@ streaming, LRU, layer skipping, throttling, grammar masking and prefix reuse
 are not on the speculative-decode path and are left out.  Sampling draws from
 a numpy Generator exactly like ``engine.py:278-286`` (``_sample``, since the
 Rust sampler is not importable) so a seeded run reproduces the reference.
+With ``sampler="fixed"`` every sample is ``sampling.sample_fixed`` on the
+generator's next uniform draw instead (the device sampler's arithmetic; the
+same draws in the same order as ``rng.choice``).
 """
 import numpy as np
 
@@ -13,7 +16,7 @@ from . import io, llama, sampling
 
 
 class OracleEngine:
-    def __init__(self, model_dir, draft_dir=None, spec_k=0, seed=None):
+    def __init__(self, model_dir, draft_dir=None, spec_k=0, seed=None, sampler="reference"):
         canon, embed, fnorm, head, layers = io.load_model(model_dir)
         self.canon = canon
         self.model = llama.OracleModel(canon, embed, fnorm, head)
@@ -21,11 +24,19 @@ class OracleEngine:
         self.n_layers = canon["layers"]
         self.ctx_len = min(int(canon["max_len"]), 4096)          # engine.py:119-120
         self.rng = np.random.default_rng(seed)
+        self.sampler = sampler
         self.spec_k = max(0, int(spec_k))
         self.draft = OracleEngine(draft_dir) if draft_dir else None
         self.stats = {"tokens_served": 0, "draft_tokens": 0, "spec_accepted": 0,
                       "spec_bonus": 0, "spec_steps": 0}
         self.trace = []   # (kind, logits) of every sampled position, for margins
+
+    def _sample(self, lg, temperature, top_p, min_p):
+        if self.sampler == "fixed":
+            if temperature <= 0:
+                return int(np.argmax(np.asarray(lg, dtype=np.float32).reshape(-1)))
+            return sampling.sample_fixed(lg, temperature, top_p, min_p, self.rng.random())
+        return sampling.sample_reference(lg, temperature, top_p, min_p, self.rng)
 
     # engine.py:255-264
     def _forward(self, x, kv, pos):
@@ -42,7 +53,7 @@ class OracleEngine:
         lg = self._score(x)
         if record is not None:
             record.append(lg)
-        return sampling.sample_reference(lg, temperature, top_p, min_p, self.rng)
+        return self._sample(lg, temperature, top_p, min_p)
 
     # engine.py:288-320
     def _spec_step(self, kv, dkv, pos, token, temperature, top_p, min_p):
@@ -51,8 +62,7 @@ class OracleEngine:
         dtok, dpos = token, pos
         for _ in range(self.spec_k):
             dx = d._forward(d.model.embed[dtok].reshape(1, d.model.hidden), dkv, dpos)
-            cands.append(sampling.sample_reference(d._score(dx), temperature, top_p, min_p,
-                                                   self.rng))
+            cands.append(self._sample(d._score(dx), temperature, top_p, min_p))
             dtok = cands[-1]
             dpos += 1
         self.stats["draft_tokens"] += self.spec_k

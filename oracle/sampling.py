@@ -207,3 +207,81 @@ def accept_rejection(p_target, q_draft, draft_tokens, u_accept, u_resample):
         return emitted, i
     emitted.append(sample_probs(p_target[len(draft_tokens)], u_resample))
     return emitted, len(draft_tokens)
+
+
+# --------------------------------------------------------------------------
+# the device sampler's arithmetic (engine.py:26-45 semantics, fixed order)
+# --------------------------------------------------------------------------
+# The GPU sampler follows engine.py:26-45 step for step (softmax of l / T,
+# min-p keep and renormalise, top-p nucleus in descending-probability order,
+# inverse CDF on one uniform draw) with this fixed arithmetic, restated here
+# so tests can demand identical tokens:
+#   * exp is ``rexp``;
+#   * a block sum is the kernel's: thread t (of SAMPLE_THREADS) adds elements
+#     t, t + SAMPLE_THREADS, ... in order; the 32 lanes of a warp are then
+#     added in lane order and the warp totals in warp order;
+#   * probability masses are fixed point, floor(p * 2^52) as uint64, so the
+#     nucleus and the CDF walk are exact integer arithmetic;
+#   * the nucleus order is descending probability, ties by ascending index
+#     (the reference's argsort leaves tie order to its sort implementation);
+#   * temperature, top_p and min_p act as fp32 values, as numpy 2 applies a
+#     Python float to fp32 arrays; the uniform draw is fp64.
+# It differs from the reference only by fp32 rounding (its exp and pairwise
+# sums), i.e. when a draw lands within rounding of a CDF or nucleus boundary.
+
+SAMPLE_THREADS = 1024
+MASS_SCALE = float(2 ** 52)
+
+
+def block_total(v):
+    """The sampler's fixed-order fp32 block sum (see above)."""
+    v = np.asarray(v, dtype=np.float32).reshape(-1)
+    pad = (-v.size) % SAMPLE_THREADS
+    w = np.concatenate([v, np.zeros(pad, np.float32)]).reshape(-1, SAMPLE_THREADS)
+    per_thread = np.cumsum(w, axis=0, dtype=np.float32)[-1]
+    per_warp = np.cumsum(per_thread.reshape(-1, 32), axis=1, dtype=np.float32)[:, -1]
+    return np.cumsum(per_warp, dtype=np.float32)[-1]
+
+
+def fixed_probs(logits, temperature, min_p=0.0):
+    """engine.py:29-36 with the sampler's arithmetic: fp32 probabilities."""
+    lg = np.asarray(logits, dtype=np.float32).reshape(-1)
+    t = np.float32(max(float(temperature), 1e-9))
+    z = ((lg - np.max(lg)) / t).astype(np.float32)
+    e = rexp(z)
+    p = (e / block_total(e)).astype(np.float32)
+    if min_p and 0 < min_p < 1.0:
+        # numpy 2 (NEP 50): a Python float meeting fp32 data computes in fp32
+        keep = p >= np.float32(min_p) * np.max(p)
+        p2 = np.where(keep, p, np.float32(0.0)).astype(np.float32)
+        p = (p2 / block_total(p2)).astype(np.float32)
+    return p
+
+
+def fixed_masses(p):
+    return (np.asarray(p, dtype=np.float32).astype(np.float64) * MASS_SCALE).astype(np.uint64)
+
+
+def sample_fixed(logits, temperature, top_p, min_p, u):
+    """The device sampler: engine.py:26-45 given the uniform draw ``u``."""
+    lg = np.asarray(logits, dtype=np.float32).reshape(-1)
+    if temperature <= 0:
+        return int(np.argmax(lg))
+    p = fixed_probs(lg, temperature, min_p)
+    m = fixed_masses(p)
+    if top_p < 1.0:
+        keys = p.view(np.uint32)
+        order = np.lexsort((np.arange(p.size), ~keys))     # descending, ties by index
+        cum = np.cumsum(m[order], dtype=np.uint64)
+        budget = np.uint64(float(np.float32(top_p)) * MASS_SCALE)   # top_p meets fp32 cumsums
+        n_keep = int(np.searchsorted(cum, budget, side="right"))   # cum <= budget
+        n_keep = max(n_keep, 1)
+        kept = order[:n_keep]
+        total = int(cum[n_keep - 1])
+        target = np.uint64(min(int(np.uint64(float(u) * float(total))), total - 1))
+        j = int(np.searchsorted(cum[:n_keep], target, side="right"))   # first cum > target
+        return int(kept[j])
+    cum = np.cumsum(m, dtype=np.uint64)
+    total = int(cum[-1])
+    target = np.uint64(min(int(np.uint64(float(u) * float(total))), total - 1))
+    return int(np.searchsorted(cum, target, side="right"))
