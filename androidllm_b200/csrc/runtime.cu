@@ -90,7 +90,7 @@ void choose_split(QTile& t, int n_sms) {
     ksg = 1;
   } else if (t.n_tiles > 256) {
     ksw = 2;
-    ksg = (kb + 23) / 24;
+    ksg = 1;
   } else if (kb > 100) {
     ksw = 2;
     ksg = (kb + 11) / 12;
