@@ -73,9 +73,8 @@ void set_split(QTile& t, int ksw, int ksg) {
   t.ksg = std::max(1, (((t.k_blocks + t.kps - 1) / t.kps) + ksw - 1) / ksw);
 }
 
-// Activation k-blocks one GEMV block may stage: bounds its shared memory so
-// the persistent forward kernel keeps two CTAs per SM.
-constexpr int kMaxStageKb = 48;
+// Activation k-blocks one GEMV block may stage (64 KB of fragments at M <= 8).
+constexpr int kMaxStageKb = 64;
 
 // Launch shapes measured best on B200 (graph-replayed, PDL) for the step's
 // shapes: narrow matrices let all 8 warps of a CTA split K and avoid cross-CTA
@@ -91,6 +90,9 @@ void choose_split(QTile& t, int n_sms) {
   } else if (t.n_tiles > 256) {
     ksw = 2;
     ksg = 1;
+  } else if (kb > 100 && t.n_tiles >= 128) {
+    ksw = 1;   // long K, enough tiles: one warp per tile, ~37 k-blocks per CTA
+    ksg = (kb + 36) / 37;
   } else if (kb > 100) {
     ksw = 2;
     ksg = (kb + 11) / 12;

@@ -487,6 +487,44 @@ def run_profile(args):
     return 0
 
 
+_PHASES = ("qkv", "scores", "pv", "o", "gu", "down")
+
+
+def run_trace_forward(args):
+    """Per-phase timeline of the persistent forward kernel (global timer of
+    CTA 0: its own work in each phase, then its wait at the grid barrier) for
+    the draft (1 row) and the target (5 rows) at position 600."""
+    from androidllm_b200.ops import Context, DeviceKV, DeviceModel
+    tdir, ddir = prepare_models(args.workload)
+    ctx = Context(0)
+    for tag, d, rows in (("draft", ddir, 1), ("target", tdir, 5)):
+        m = DeviceModel.from_dir(ctx, d)
+        kv = DeviceKV(m, 1024)
+        toks = np.random.default_rng(5).integers(0, m.canon["vocab"], 608).tolist()
+        for i in range(0, 592, 16):
+            m.forward(kv, toks[i:i + 16], i, logits=False, argmax=False)
+        for _ in range(args.trace_forward):
+            arrive, passed = m.forward_trace(kv, toks[600:600 + rows], 600)
+        arrive, passed = arrive.astype(np.int64), passed.astype(np.int64)
+        names = ["embed"] + list(_PHASES) * m.canon["layers"] + ["rownorm", "head"]
+        work, wait = {}, {}
+        prev = int(arrive[0, 0])
+        for b in range(arrive.shape[0]):
+            if b > 0:
+                work.setdefault(names[b], []).append(int(arrive[b, 0]) - prev)
+            wait.setdefault(names[b], []).append(int(passed[b]) - int(arrive[b, 0]))
+            prev = int(passed[b])
+        out = {"model": tag, "rows": rows, "ctas": int(arrive.shape[1]),
+               "total_us": round((int(passed[-1]) - int(arrive[0, 0])) / 1e3, 1), "phases": {}}
+        for n in dict.fromkeys(names[1:]):
+            out["phases"][n] = {"work_us": round(float(np.median(work[n])) / 1e3, 2),
+                                "barrier_wait_us": round(float(np.median(wait[n])) / 1e3, 2)}
+        print(json.dumps(out), flush=True)
+        kv.close()
+        m.close()
+    return 0
+
+
 def summarize_ncu(path):
     """Aggregate an ncu --csv launch list (gpu__time_duration.sum) by kernel."""
     import collections
@@ -542,6 +580,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="run N steps inside a profiler capture range and exit")
     ap.add_argument("--summarize-ncu", metavar="CSV", help="aggregate an ncu launch list and exit")
+    ap.add_argument("--trace-forward", type=int, default=0, metavar="N",
+                    help="run N traced persistent forwards per model and print the phase timeline")
     ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
     ap.add_argument("--sweep-m", default=",".join(str(m) for m in SWEEP_M))
     ap.add_argument("--gemv", metavar="N,K,BITS,M", help="time one GEMV shape repeatedly (profiling target)")
@@ -554,6 +594,8 @@ def main():
         return summarize_ncu(args.summarize_ncu)
     if args.profile:
         return run_profile(args)
+    if args.trace_forward:
+        return run_trace_forward(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
