@@ -269,6 +269,17 @@ def workload_config(args, world):
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
+def _profiled_traffic(name):
+    """DRAM bytes per launch of the roofline kernel from its committed ncu
+    summary (profiles/), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(path) as f:
+            return json.load(f)["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     dist = None
@@ -366,7 +377,7 @@ def run_ours(args):
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3),
                 "peak_source": peaks["source"], "algorithmic_bytes": alg, "avg_launch_us": round(us, 2),
-                "traffic": None}
+                "traffic": _profiled_traffic("gemv_int8_17920x1536_m5_dram.json")}
     step_bytes = SPEC_K * forward_weight_bytes(eng.draft.manifest) + forward_weight_bytes(eng.manifest)
     step_roof = step_bytes / (ms_per_step * 1e-3) / 1e9
 
@@ -476,6 +487,9 @@ def run_profile(args):
     t.forward(tkv, prompt[:15], 0, logits=False, argmax=False)
     d.forward(dkv, prompt, 0, logits=False, argmax=False)
     s = SpecDecoder(t, d, tkv, dkv, SPEC_K)
+    if args.temperature > 0:
+        s.set_sampling(args.temperature, args.top_p, 0.0)
+        s.set_uniforms(np.random.default_rng(7).random(64 * (2 * SPEC_K + 1)))
     s.begin(prompt[-1], 600)
     s.bench(2)
     s.begin(prompt[-1], 600)
@@ -580,6 +594,9 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="run N steps inside a profiler capture range and exit")
     ap.add_argument("--summarize-ncu", metavar="CSV", help="aggregate an ncu launch list and exit")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="--profile: sampling steps at this temperature (0: greedy)")
+    ap.add_argument("--top-p", type=float, default=0.9, help="--profile: nucleus of the sampling steps")
     ap.add_argument("--trace-forward", type=int, default=0, metavar="N",
                     help="run N traced persistent forwards per model and print the phase timeline")
     ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
