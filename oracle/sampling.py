@@ -217,9 +217,12 @@ def accept_rejection(p_target, q_draft, draft_tokens, u_accept, u_resample):
 # inverse CDF on one uniform draw) with this fixed arithmetic, restated here
 # so tests can demand identical tokens:
 #   * exp is ``rexp``;
-#   * a block sum is the kernel's: thread t (of SAMPLE_THREADS) adds elements
-#     t, t + SAMPLE_THREADS, ... in order; the 32 lanes of a warp are then
-#     added in lane order and the warp totals in warp order;
+#   * a row is split into SAMPLE_CTAS contiguous slices of ceil(V / SAMPLE_CTAS)
+#     elements (one CTA of a thread-block cluster each); a sum is the
+#     kernel's: in each slice thread t (of SAMPLE_THREADS) adds the slice's
+#     elements t, t + SAMPLE_THREADS, ... in order, the 32 lanes of a warp are
+#     added in lane order, the warp totals in warp order, and the slice
+#     totals in slice order;
 #   * probability masses are fixed point, floor(p * 2^52) as uint64, so the
 #     nucleus and the CDF walk are exact integer arithmetic;
 #   * the nucleus order is descending probability, ties by ascending index
@@ -230,17 +233,28 @@ def accept_rejection(p_target, q_draft, draft_tokens, u_accept, u_resample):
 # sums), i.e. when a draw lands within rounding of a CDF or nucleus boundary.
 
 SAMPLE_THREADS = 1024
+SAMPLE_CTAS = 8
 MASS_SCALE = float(2 ** 52)
 
 
-def block_total(v):
-    """The sampler's fixed-order fp32 block sum (see above)."""
-    v = np.asarray(v, dtype=np.float32).reshape(-1)
+def _slice_total(v):
     pad = (-v.size) % SAMPLE_THREADS
     w = np.concatenate([v, np.zeros(pad, np.float32)]).reshape(-1, SAMPLE_THREADS)
     per_thread = np.cumsum(w, axis=0, dtype=np.float32)[-1]
     per_warp = np.cumsum(per_thread.reshape(-1, 32), axis=1, dtype=np.float32)[:, -1]
     return np.cumsum(per_warp, dtype=np.float32)[-1]
+
+
+def block_total(v):
+    """The sampler's fixed-order fp32 sum of a row (see above)."""
+    v = np.asarray(v, dtype=np.float32).reshape(-1)
+    per = -(-v.size // SAMPLE_CTAS)
+    acc = np.float32(0.0)
+    for c in range(SAMPLE_CTAS):
+        part = v[c * per:(c + 1) * per]
+        if part.size:
+            acc = np.float32(acc + _slice_total(part))
+    return acc
 
 
 def fixed_probs(logits, temperature, min_p=0.0):
