@@ -280,6 +280,17 @@ def _profiled_traffic(name):
         return None
 
 
+def combine_ranks(dist, ms, tokens, device):
+    """Replicas: the slowest rank's device time and every rank's tokens."""
+    import torch
+    t = torch.tensor([ms, float(tokens)], dtype=torch.float64, device=device)
+    mx = t.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    sm = t.clone()
+    dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    return float(mx[0]), int(sm[1])
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     dist = None
@@ -344,13 +355,8 @@ def run_ours(args):
         t_wall = time.perf_counter() - t_wall
     if dist is not None:
         import torch
-        t = torch.tensor([ms, float(tokens)], dtype=torch.float64, device="cuda")
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = t.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         torch.cuda.synchronize()
-        ms_max, tokens_all = float(mx[0]), int(sm[1])
+        ms_max, tokens_all = combine_ranks(dist, ms, tokens, "cuda")
         dist.barrier()
     else:
         ms_max, tokens_all = ms, tokens
