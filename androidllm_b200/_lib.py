@@ -46,6 +46,7 @@ SIGNATURES = {
     "alm_ctx_destroy": [_P],
     "alm_ctx_sync": [_P],
     "alm_ctx_set_persistent": [_P, _I],
+    "alm_ctx_set_gemv_layout": [_P, _I],
     "alm_dev_alloc": [_P, ctypes.c_size_t, _PP],
     "alm_dev_free": [_P, _P],
     "alm_copy_h2d": [_P, _P, _P, ctypes.c_size_t],

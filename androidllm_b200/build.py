@@ -41,19 +41,35 @@ def up_to_date():
     return all(os.path.getmtime(f) <= t for f in sources() + headers() + [__file__])
 
 
-def build(force=False, verbose=False, ptxas_info=False):
-    if not force and up_to_date():
-        return LIB
-    cmd = [NVCC, *FLAGS, "-shared", "-o", LIB + ".tmp", *sources(), "-lcudart"]
-    if ptxas_info:
-        cmd.insert(1, "-Xptxas=-v")
+def _run(cmd, verbose):
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    return subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+
+
+def _finish(proc):
+    out, err = proc.communicate()
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{out}\n{err}")
+    return err
+
+
+def build(force=False, verbose=False, ptxas_info=False):
+    """Compile every translation unit in parallel, then link the library."""
+    if not force and up_to_date():
+        return LIB
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    extra = ["-Xptxas=-v"] if ptxas_info else []
+    jobs, objs = [], []
+    for src in sources():
+        obj = os.path.join(objdir, os.path.basename(src) + ".o")
+        objs.append(obj)
+        jobs.append(_run([NVCC, *extra, *FLAGS, "-c", src, "-o", obj], verbose))
+    errs = [_finish(p) for p in jobs]
     if ptxas_info or verbose:
-        print(res.stderr, file=sys.stderr)
+        print("".join(errs), file=sys.stderr)
+    _finish(_run([NVCC, *FLAGS, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart"], verbose))
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

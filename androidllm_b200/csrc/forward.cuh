@@ -7,6 +7,8 @@ namespace alm {
 // Barrier arrivals reserved per launch (per CTA); a forward needs
 // forward_barriers() of them.
 constexpr int kBarRound = 4096;
+// Rows (verify tokens) a persistent forward takes: one n8 MMA tile.
+constexpr int kPersistRows = 8;
 
 // Device copy of one layer's weights and norms.
 struct FwdLayer {

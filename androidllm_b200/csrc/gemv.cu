@@ -1,24 +1,3 @@
-// Fused dequant-GEMV for the verify path: y(M, N) = x(M, K) . W(N, K)^T with
-// W in the qtile layout (int4 / int8 block-quant, or fp16), M <= 16 rows.
-//
-// Work split: a CTA of 8 warps covers (8 / ksw) row tiles of 16; the ksw warps
-// of a tile split its K range, and `ksg` CTAs split K further.  Each warp
-// streams its contiguous run of k64 blocks straight from HBM into registers
-// (a rolling prefetch of U blocks), decodes them to exact fp16 weights and
-// feeds mma.sync m16n8k16 with fp32 accumulation.  The activation rows are
-// staged once per CTA in shared memory, already laid out as B fragments
-// (deferred RMSNorm of the previous layer is applied while staging).
-//
-// Partial sums are combined in a fixed order (warp order inside a CTA, then
-// split order across CTAs by the last CTA to finish a column), so every
-// output element is summed in the same order for any M: a verify pass of k+1
-// rows produces exactly the values of k+1 single-row passes.
-//
-// Epilogues (fused): STORE fp16; QKV = fp16 round, RoPE in fp32, K/V written
-// to the paged cache; RESID = fp16 residual add plus per-tile sums of
-// squares for the next RMSNorm; SWIGLU on interleaved gate/up rows; LOGITS =
-// fp16 logits plus per-CTA argmax partials.  The rounding points follow
-// androidllm/models/llama.py:96-146.
 // Standalone launches of the fused dequant-GEMV (one CTA per virtual block of
 // the body in gemv_body.cuh) for forwards the persistent forward kernel does
 // not run, alm_qmatmul and the shape benchmarks.
@@ -33,8 +12,8 @@ constexpr size_t kGemvMaxSmem = 200 * 1024;   // dynamic shared memory limit per
 
 // Dynamic shared memory of one CTA: weight rings with their mbarriers, then
 // the activation fragments.
-inline size_t gemv_smem_bytes(const QTile& w, int nt8) {
-  return ring_bytes(gemv_slot_bytes(w)) + gemv_stage_bytes(w, nt8);
+inline size_t gemv_smem_bytes(const QTile& w, int rows) {
+  return ring_bytes(gemv_slot_bytes(w)) + gemv_stage_bytes(w, rows);
 }
 
 template <int BITS, int NT8, int EPI>
@@ -56,7 +35,7 @@ template <int BITS, int NT8, int EPI>
 cudaError_t launch_t(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                      const SplitScratch& scr, bool pdl, cudaStream_t st) {
   auto kern = gemv_kernel<BITS, NT8, EPI>;
-  const size_t smem = gemv_smem_bytes(w, NT8);
+  const size_t smem = gemv_smem_bytes(w, M);
   if (smem > kGemvMaxSmem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemv_grid_x(w), w.ksg, 1);
@@ -106,7 +85,8 @@ cudaError_t set_attrs_nt() {
 }  // namespace
 
 cudaError_t gemv_init_attrs() {
-  cudaError_t e = set_attrs_nt<4, 1>();
+  cudaError_t e = tc_gemv_init_attrs();
+  if (e == cudaSuccess) e = set_attrs_nt<4, 1>();
   if (e == cudaSuccess) e = set_attrs_nt<4, 2>();
   if (e == cudaSuccess) e = set_attrs_nt<8, 1>();
   if (e == cudaSuccess) e = set_attrs_nt<8, 2>();
@@ -114,6 +94,14 @@ cudaError_t gemv_init_attrs() {
   if (e == cudaSuccess) e = set_attrs_nt<16, 2>();
   return e;
 }
+
+size_t gemv_part_floats(const QTile& w) {
+  if (w.ksg <= 1) return 0;
+  if (w.layout == kLayoutRow) return static_cast<size_t>(w.ksg) * kMaxRows * w.n_rb * kRowBlock;
+  return static_cast<size_t>(w.ksg) * (w.n_tiles + kGemvWarps) * kWarp * 8;
+}
+
+int gemv_out_blocks(const QTile& w) { return w.layout == kLayoutRow ? w.n_rb : gemv_grid_x(w); }
 
 cudaError_t launch_gemv(const QTile& w, const ActIn& in_, int M, EpiKind kind, const Epi& epi_,
                         const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st) {
@@ -123,9 +111,10 @@ cudaError_t launch_gemv(const QTile& w, const ActIn& in_, int M, EpiKind kind, c
   Epi epi = epi_;
   if (epi.res.x) set_vec(epi.res);
   if (w.ksg > 1) {
-    const size_t need = static_cast<size_t>(w.ksg) * (w.n_tiles + kGemvWarps) * kWarp * 8;
-    if (scr.part == nullptr || scr.part_floats < need || w.counters == nullptr) return cudaErrorInvalidValue;
+    if (scr.part == nullptr || scr.part_floats < gemv_part_floats(w) || w.counters == nullptr)
+      return cudaErrorInvalidValue;
   }
+  if (w.layout == kLayoutRow) return launch_tc_gemv(w, in, M, kind, epi, io, scr, pdl, st);
   switch (w.bits) {
     case 4: return dispatch_nt<4>(kind, w, in, M, epi, io, scr, pdl, st);
     case 8: return dispatch_nt<8>(kind, w, in, M, epi, io, scr, pdl, st);

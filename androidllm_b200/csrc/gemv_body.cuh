@@ -13,7 +13,10 @@
 // completion), decodes them to exact fp16 weights and feeds mma.sync
 // m16n8k16 with fp32 accumulation.  The activation rows are staged once per
 // block in shared memory, already laid out as B fragments (deferred RMSNorm
-// of the previous layer is applied while staging).
+// of the previous layer is applied while staging).  Only the M real rows are
+// staged; lanes whose B column is a padding row read row M-1 instead, which
+// changes only output columns that are never stored (an MMA column depends
+// on its own B column alone).
 //
 // The ring and its mbarriers persist for the CTA's lifetime: each warp counts
 // the chunks that went through its ring (`seq`), which gives every chunk its
@@ -58,8 +61,11 @@ constexpr int kStageBatch = 4;
 __host__ __device__ inline int gemv_cta_nkb(const QTile& w) {
   return w.ksw * w.kps < w.k_blocks ? w.ksw * w.kps : w.k_blocks;
 }
-__host__ __device__ inline size_t gemv_stage_bytes(const QTile& w, int nt8) {
-  return static_cast<size_t>(gemv_cta_nkb(w)) * nt8 * 2 * kWarp * 16;
+// Activation staging: per k-block, two halves (k16 steps 0-1 and 2-3), per
+// row, per t = lane % 4 one uint4 {b0, b1 of the even step, b0, b1 of the odd
+// step}: 128 bytes per row and k-block.
+__host__ __device__ inline size_t gemv_stage_bytes(const QTile& w, int rows) {
+  return static_cast<size_t>(gemv_cta_nkb(w)) * rows * 128;
 }
 __host__ __device__ inline int gemv_grid_x(const QTile& w) {
   const int ntc = kGemvWarps / w.ksw;
@@ -138,15 +144,18 @@ ALM_DEV GemvPlan gemv_plan(const QTile& w, int items, int vx, int vy, int gx) {
   return p;
 }
 
-// Lane 0: bulk-copy chunk c of the plan into the ring position seq + c.
-ALM_DEV void ring_issue(const Ring& r, const GemvPlan& p, int rec_bytes, int items, uint32_t seq, int c) {
+// Lane 0: bulk-copy chunk c of the plan into ring slot `slot`.
+ALM_DEV void ring_issue_slot(const Ring& r, const GemvPlan& p, int rec_bytes, int items, int slot, int c) {
   const int warp = threadIdx.x / kWarp;
-  const int slot = static_cast<int>((seq + static_cast<uint32_t>(c)) % kSlots);
   uint64_t* bar = &r.bars[warp * kSlots + slot];
   unsigned char* dst = r.base + static_cast<size_t>(warp * kSlots + slot) * r.slot_bytes;
   const uint32_t bytes = static_cast<uint32_t>(min(items, p.n - c * items) * rec_bytes);
   mbar_expect_tx(bar, bytes);
   bulk_g2s(dst, p.gsrc + static_cast<size_t>(c) * items * rec_bytes, bytes, bar, l2_evict_first());
+}
+// Lane 0: bulk-copy chunk c of the plan into the ring position seq + c.
+ALM_DEV void ring_issue(const Ring& r, const GemvPlan& p, int rec_bytes, int items, uint32_t seq, int c) {
+  ring_issue_slot(r, p, rec_bytes, items, static_cast<int>((seq + static_cast<uint32_t>(c)) % kSlots), c);
 }
 
 // Issue the plan's first kSlots chunks (the ring must be drained and every
@@ -203,7 +212,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
   {
     uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
     const int per_row = cta_nkb * 8;           // 8-column chunks per row
-    const int n_stage = per_row * M;           // rows >= M are zeroed in registers, not staged
+    const int n_stage = per_row * M;
     const bool deferred = in.ss != nullptr;
     for (int base = 0; base < n_stage; base += kGemvThreads * kStageBatch) {
       uint4 raw[kStageBatch], wv[kStageBatch];
@@ -212,7 +221,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         const int c = base + j * kGemvThreads + threadIdx.x;
         const int m = c / per_row;
         const int col0 = cta_kb0 * 64 + (c % per_row) * 8;
-        const bool ok = c < n_stage && m < M;
+        const bool ok = c < n_stage;
         raw[j] = ok ? load_row8(in, m, col0, w.k_real) : make_uint4(0, 0, 0, 0);
         wv[j] = (ok && deferred) ? load_w8(in.w, col0, w.k_real, in.vec) : make_uint4(0, 0, 0, 0);
       }
@@ -224,9 +233,9 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         const int rem = c % per_row;
         const int kbl = rem / 8, c8 = rem % 8;
         const int s = c8 >> 1, hi8 = c8 & 1;
-        const int nt = m >> 3, h = s >> 1, r = (s & 1) * 2 + hi8;
+        const int h = s >> 1, r = (s & 1) * 2 + hi8;
         uint32_t words[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
-        if (deferred && m < M) {
+        if (deferred) {
           const float den = sh.den_in[m];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -237,7 +246,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         }
 #pragma unroll
         for (int tt = 0; tt < 4; ++tt)
-          xw[(((kbl * NT8 + nt) * 2 + h) * kWarp + (m & 7) * 4 + tt) * 4 + r] = words[tt];
+          xw[((((kbl * 2 + h) * M + m) * 4 + tt) * 4) + r] = words[tt];
       }
     }
   }
@@ -252,13 +261,19 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[nt][j] = acc2[nt][j] = 0.f;
 
+  // B fragments of this lane: row nt * 8 + g (padding columns read row M-1),
+  // 4 * M uint4 per half k-block
+  const uint4* xrow[NT8];
+#pragma unroll
+  for (int nt = 0; nt < NT8; ++nt) xrow[nt] = xs + min(nt * 8 + g, M - 1) * 4 + t;
+  const int xhalf = 4 * M;
   const bool two_sets = w.sb == 2;
   int consumed = 0;
   bool stream_ok = true;
+  int slot = static_cast<int>(seq % kSlots);
+  uint32_t phase = (seq / kSlots) & 1u;
   for (int c = 0; c < n_chunks; ++c) {
-    const uint32_t s_pos = seq + static_cast<uint32_t>(c);
-    const int slot = static_cast<int>(s_pos % kSlots);
-    if (!mbar_wait(&bars[slot], (s_pos / kSlots) & 1u)) {
+    if (!mbar_wait(&bars[slot], phase)) {
       stream_ok = false;
       break;
     }
@@ -284,9 +299,8 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         uint4 xf[NT8][2];
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt) {
-          const bool live = nt * 8 + g < M;   // B column g of n8 tile nt is activation row nt*8+g
-          xf[nt][0] = live ? xs[((kbl * NT8 + nt) * 2 + 0) * kWarp + lane] : make_uint4(0, 0, 0, 0);
-          xf[nt][1] = live ? xs[((kbl * NT8 + nt) * 2 + 1) * kWarp + lane] : make_uint4(0, 0, 0, 0);
+          xf[nt][0] = xrow[nt][(2 * kbl) * xhalf];
+          xf[nt][1] = xrow[nt][(2 * kbl + 1) * xhalf];
         }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
@@ -306,7 +320,11 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
     __syncwarp();
     if (lane == 0 && c + kSlots < n_chunks) {
       fence_proxy_async_smem();   // this slot's reads are done before the copy overwrites it
-      ring_issue(ring, p, rec_bytes, IPS, seq, c + kSlots);
+      ring_issue_slot(ring, p, rec_bytes, IPS, slot, c + kSlots);
+    }
+    if (++slot == kSlots) {
+      slot = 0;
+      phase ^= 1u;
     }
   }
   int issued = n_chunks;

@@ -49,7 +49,33 @@ struct QTile {
   int ksg = 1;        // CTAs splitting K
   int kps = 1;        // k-blocks per split
   unsigned* counters = nullptr;  // one per CTA column, self-resetting
+  // record layout: kLayoutTile (above) or kLayoutRow (below)
+  int layout = 0;
+  int n_rb = 0;       // row layout: 128-row blocks
+  int wg = 1;         // row layout: decoding warpgroups per CTA (1, 2, 4)
 };
+
+// ---------------------------------------------------------------------------
+// Row-record layout ("qrow"), streamed by the tcgen05 GEMV (tc_gemv.cu).
+//
+// Rows are grouped in blocks of 128 (one tcgen05 MMA tile) and, inside a
+// block, in four groups of 32 (one warp, one tensor-memory lane quarter).
+// Each (group, k-block of 64) is one record, contiguous along k for a group:
+// record index ((rb * 4 + group) * k_blocks + kb).  A record holds, for row t
+// of the group, 16-byte parts at p * 512 + t * 16 (so every warp load is
+// 512 contiguous bytes), then 32 fp16 scales (row t at 2 t):
+//   int4 (2 parts): part p word j = nibbles of k = 32 p + 8 j + (0, 2, 4, 6,
+//        1, 3, 5, 7), offset-binary (q + 8): nibbles (0, 4), (1, 5), (2, 6),
+//        (3, 7) decode to the fp16 pairs of tensor-memory columns 16 p + 4 j
+//        + 0..3 (k pairs (0,1), (2,3), (4,5), (6,7));
+//   int8 (4 parts): part p word j = bytes of k = 16 p + 4 j + 0..3,
+//        offset-binary (q + 128): columns 8 p + 2 j, 8 p + 2 j + 1.
+// Decoding uses the same exact fp16 operations as the tile layout, so both
+// layouts dequantize to identical weights.
+// ---------------------------------------------------------------------------
+constexpr int kLayoutTile = 0;
+constexpr int kLayoutRow = 1;
+constexpr int kRowBlock = 128;
 
 // An activation operand: either raw fp16 rows, or the un-normalised residual
 // sum of the previous layer with its RMSNorm still to apply:
@@ -121,6 +147,19 @@ cudaError_t launch_repack(const void* const* src, const half* const* src_scales,
 cudaError_t launch_dequant(const QTile& w, half* out, cudaStream_t st);
 cudaError_t launch_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
                         const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st);
+// Row layout: repack, dequantize and the tcgen05 GEMV (tc_gemv.cu).
+cudaError_t launch_repack_rows(const void* const* src, const half* const* src_scales, int n_src,
+                               const int* dst_src_row, const QTile& w, uint4* data, int k_pad, cudaStream_t st);
+cudaError_t launch_dequant_rows(const QTile& w, half* out, cudaStream_t st);
+cudaError_t launch_tc_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
+                           const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st);
+cudaError_t tc_gemv_init_attrs();
+// Dynamic shared memory a row-layout GEMV of `rows` activation rows needs.
+size_t tc_gemv_smem_bytes(const QTile& w, int rows);
+// Split-K partial floats a GEMV launch of w needs (either layout).
+size_t gemv_part_floats(const QTile& w);
+// CTAs along the output rows (argmax partials of a LOGITS launch).
+int gemv_out_blocks(const QTile& w);
 
 struct AttnArgs {
   const float* q = nullptr;  int ldq = 0;

@@ -71,9 +71,8 @@ extern "C" ALM_API int alm_qmatmul_noalloc(alm_ctx* ctx, const alm_qweight* w, c
   if (device < 0 || device >= kMaxDevices) return alm_internal_fail(ALM_ERR_ARG, "device index too large");
 
   // split-K needs: partial sums and one counter per CTA column
-  const size_t need = t.ksg > 1 ? static_cast<size_t>(t.ksg) * (t.n_tiles + 8) * alm::kWarp * 8 : 0;
-  const int ntc = 8 / t.ksw;
-  const size_t cols = static_cast<size_t>((t.n_tiles + ntc - 1) / ntc);
+  const size_t need = alm::gemv_part_floats(t);
+  const size_t cols = static_cast<size_t>(alm::gemv_out_blocks(t));
   if (need > kNoAllocPartFloats || cols > kNoAllocCounters) {
     g_msg = "weight needs " + std::to_string(need) + " partial floats / " + std::to_string(cols) +
             " counters; the fixed scratch holds " + std::to_string(kNoAllocPartFloats) + " / " +

@@ -3,31 +3,10 @@
 // against androidllm/quant.py:58-65; used to check the layout).
 #include "kernels.cuh"
 #include "qtile.cuh"
+#include "repack.cuh"
 
 namespace alm {
 namespace {
-
-struct SrcSet {
-  const uint8_t* data[3];
-  const half* scale[3];
-};
-
-// Signed code (or raw fp16 bits) of source row `row` (src index in the top
-// byte of `desc`) at column `col`; zero past the stored columns or for
-// padding rows (desc < 0).
-__device__ int fetch_code(const SrcSet& s, int desc, int col, int bits, int k_pad) {
-  if (desc < 0 || col >= k_pad) return 0;
-  const int si = desc >> 24;
-  const size_t row = static_cast<size_t>(desc & 0xffffff);
-  const uint8_t* p = s.data[si];
-  if (bits == 4) {
-    const uint8_t b = p[row * (k_pad / 2) + col / 2];
-    const int nib = (col & 1) ? (b >> 4) : (b & 0xf);
-    return nib >= 8 ? nib - 16 : nib;
-  }
-  if (bits == 8) return static_cast<int8_t>(p[row * k_pad + col]);
-  return reinterpret_cast<const uint16_t*>(p)[row * k_pad + col];
-}
 
 // One thread per (tile, kb, lane): assemble that lane's fragment data.
 __global__ void repack_kernel(SrcSet s, const int* __restrict__ dst_src_row, int bits, int n_tiles,

@@ -3,6 +3,7 @@
 #include <cuda_profiler_api.h>
 
 #include <algorithm>
+#include <functional>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -106,6 +107,34 @@ void choose_split(QTile& t, int n_sms) {
   while (t.ksw * t.kps > kMaxStageKb && t.ksw > 1) set_split(t, t.ksw / 2, t.ksg * 2);
 }
 
+// Row layout (tcgen05 GEMV): `wg` decoding warpgroups per CTA and `ksg` CTAs
+// along K.  Up to 16 decoding warps fit an SM (tensor memory: 128 / 256 / 512
+// columns for wg = 1 / 2 / 4), so wide matrices take one small CTA per 128
+// rows and narrow ones split K until about one CTA per SM is busy.
+void set_split_rows(QTile& t, int wg, int ksg) {
+  t.wg = wg;
+  t.ksw = 1;
+  t.kps = (t.k_blocks + ksg - 1) / ksg;
+  t.ksg = (t.k_blocks + t.kps - 1) / t.kps;
+}
+
+constexpr size_t kRowSmemBudget = 220 * 1024;
+
+void choose_split_rows(QTile& t, int n_sms) {
+  const int n_rb = t.n_rb, kb = t.k_blocks;
+  int wg = 4, ksg = 1;
+  if (n_rb >= 4 * n_sms) {
+    wg = 1;
+  } else if (n_rb >= 2 * n_sms) {
+    wg = 2;
+  } else if (n_rb < n_sms) {
+    ksg = std::max(1, std::min((n_sms + n_rb / 2) / n_rb, kb / 4));
+  }
+  set_split_rows(t, wg, ksg);
+  // activation staging for 16 rows beside the weight rings
+  while (tc_gemv_smem_bytes(t, kMaxRows) > kRowSmemBudget && t.kps > 1) set_split_rows(t, wg, t.ksg + 1);
+}
+
 }  // namespace
 
 // ----------------------------------------------------------------------------
@@ -117,6 +146,7 @@ struct alm_ctx {
   cudaStream_t stream = nullptr;
   bool pdl = true;       // programmatic dependent launch between forward kernels
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
+  int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
 };
 
 struct alm_qweight {
@@ -245,6 +275,15 @@ size_t src_bytes(int bits, int rows, int k_pad) {
                    : bits == 8 ? static_cast<size_t>(rows) * k_pad : static_cast<size_t>(rows) * k_pad * 2;
 }
 
+// With mode 1, weights at least this large take the row layout (tcgen05
+// kernel); smaller ones keep the mma.sync tile layout.
+constexpr size_t kRowMinBytes = 4u << 20;
+
+bool use_rows(const alm_ctx* ctx, int bits, int block, int n_rows, int in) {
+  if ((bits != 4 && bits != 8) || block % 64 != 0 || ctx->tc == 0) return false;
+  return ctx->tc == 2 || static_cast<size_t>(n_rows) * in * bits / 8 >= kRowMinBytes;
+}
+
 int check_format(int bits, int block, int in, int in_real) {
   ALM_REQ(bits == 4 || bits == 8 || bits == 16, "bits must be 4, 8 or 16");
   ALM_REQ(in > 0 && in_real > 0 && in_real <= in, "invalid in / in_real");
@@ -256,10 +295,12 @@ int check_format(int bits, int block, int in, int in_real) {
   return ALM_OK;
 }
 
-// Build one qtile weight from up to 3 sources with a destination row map
-// (dst row -> (src << 24) | src row, or -1).
-int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::vector<int>& dst_map,
-                  int n_rows, alm_qweight** out) {
+// Build one weight from up to 3 sources with a destination row map for the
+// chosen layout (dst row -> (src << 24) | src row, or -1).  `allow_rows`:
+// the consumer's epilogue exists in the row layout (every one but QKV).
+int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src,
+                  const std::function<std::vector<int>(int)>& map_of, int n_rows, bool allow_rows,
+                  alm_qweight** out) {
   const int bits = srcs[0].bits, block = srcs[0].block, in = srcs[0].in, in_real = srcs[0].in_real;
   for (int i = 0; i < n_src; ++i) {
     ALM_TRY(check_format(srcs[i].bits, srcs[i].block, srcs[i].in, srcs[i].in_real));
@@ -282,10 +323,24 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
   t.k_blocks = (in + 63) / 64;
   t.sb = bits == 16 ? 0 : (block == 32 ? 2 : 1);
   t.k_real = in_real;
-  choose_split(t, ctx->n_sms);
-
-  const int vec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
-  t.rec_u4 = vec * kWarp + t.sb * 2;   // codes + 8 half2 scales (32 B) per set
+  const bool rows = allow_rows && use_rows(ctx, bits, block, n_rows, in);
+  size_t n_rec = 0;
+  int n_counters = 0;
+  if (rows) {
+    t.layout = kLayoutRow;
+    t.n_rb = (n_rows + kRowBlock - 1) / kRowBlock;
+    t.rec_u4 = ((bits == 4 ? 2 : 4) * 512 + 64) / 16;   // codes + 32 fp16 scales
+    choose_split_rows(t, ctx->n_sms);
+    n_rec = static_cast<size_t>(t.n_rb) * 4 * t.k_blocks;
+    n_counters = t.n_rb;
+  } else {
+    choose_split(t, ctx->n_sms);
+    const int vec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
+    t.rec_u4 = vec * kWarp + t.sb * 2;   // codes + 8 half2 scales (32 B) per set
+    n_rec = static_cast<size_t>(t.n_tiles) * t.k_blocks;
+    n_counters = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+  }
+  const std::vector<int> dst_map = map_of(t.layout);
   std::vector<void*> tmp;
   auto cleanup = [&]() {
     for (void* p : tmp) cudaFree(p);
@@ -295,7 +350,7 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
   const half* dscale[3] = {nullptr, nullptr, nullptr};
   int* dmap = nullptr;
   do {
-    if ((rc = dev_alloc_t(&w->data, static_cast<size_t>(t.n_tiles) * t.k_blocks * t.rec_u4)) != ALM_OK) break;
+    if ((rc = dev_alloc_t(&w->data, n_rec * t.rec_u4)) != ALM_OK) break;
     for (int i = 0; i < n_src && rc == ALM_OK; ++i) {
       void* p = nullptr;
       const size_t nb = src_bytes(bits, srcs[i].out, in);
@@ -325,15 +380,15 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
       rc = fail(ALM_ERR_CUDA, "row map upload failed");
       break;
     }
-    cudaError_t e = launch_repack(dsrc, dscale, n_src, dmap, t, w->data, in, ctx->stream);
+    cudaError_t e = rows ? launch_repack_rows(dsrc, dscale, n_src, dmap, t, w->data, in, ctx->stream)
+                         : launch_repack(dsrc, dscale, n_src, dmap, t, w->data, in, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) {
       rc = fail(ALM_ERR_CUDA, std::string("repack: ") + cudaGetErrorString(e));
       break;
     }
-    const int grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
-    if ((rc = dev_alloc_t(&w->counters, grid_x)) != ALM_OK) break;
-    if (cudaMemset(w->counters, 0, grid_x * sizeof(unsigned)) != cudaSuccess) {
+    if ((rc = dev_alloc_t(&w->counters, n_counters)) != ALM_OK) break;
+    if (cudaMemset(w->counters, 0, n_counters * sizeof(unsigned)) != cudaSuccess) {
       rc = fail(ALM_ERR_CUDA, "counter init failed");
       break;
     }
@@ -349,17 +404,22 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src, const std::
   return ALM_OK;
 }
 
-std::vector<int> identity_map(int rows) {
-  std::vector<int> m((rows + 15) / 16 * 16, -1);
-  for (int r = 0; r < rows; ++r) m[r] = r;
-  return m;
+// Destination rows of a layout: tiles of 16 or blocks of 128.
+int padded_rows(int rows, int layout) {
+  const int r = layout == kLayoutRow ? kRowBlock : 16;
+  return (rows + r - 1) / r * r;
+}
+
+std::function<std::vector<int>(int)> identity_map(int rows) {
+  return [rows](int layout) {
+    std::vector<int> m(padded_rows(rows, layout), -1);
+    for (int r = 0; r < rows; ++r) m[r] = r;
+    return m;
+  };
 }
 
 // Split-K scratch large enough for weight w (floats).
-size_t split_need(const alm_qweight* w) {
-  if (!w || w->t.ksg <= 1) return 0;
-  return static_cast<size_t>(w->t.ksg) * (w->t.n_tiles + 8) * kWarp * 8;
-}
+size_t split_need(const alm_qweight* w) { return w ? gemv_part_floats(w->t) : 0; }
 
 int ensure_part(Work& ws, size_t need) {
   if (need <= ws.part_floats) return ALM_OK;
@@ -530,7 +590,7 @@ EmbedArgs embed_args(alm_model* m, int M) {
 int build_forward(alm_model* m) {
   const alm_model_config& c = m->cfg;
   std::vector<FwdLayer> host(c.layers);
-  size_t stage = gemv_stage_bytes(m->head->t, 1);
+  size_t stage = gemv_stage_bytes(m->head->t, kPersistRows);
   for (int li = 0; li < c.layers; ++li) {
     const Layer& L = m->layers[li];
     host[li].qkv = L.qkv->t;
@@ -539,7 +599,7 @@ int build_forward(alm_model* m) {
     host[li].down = L.down->t;
     host[li].n_in = L.n_in;
     host[li].n_post = L.n_post;
-    for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down}) stage = std::max(stage, gemv_stage_bytes(w->t, 1));
+    for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down}) stage = std::max(stage, gemv_stage_bytes(w->t, kPersistRows));
   }
   if (!m->fwd_layers) ALM_TRY(dev_alloc_t(&m->fwd_layers, static_cast<size_t>(c.layers)));
   ALM_CUDA(cudaMemcpy(m->fwd_layers, host.data(), host.size() * sizeof(FwdLayer), cudaMemcpyHostToDevice));
@@ -549,6 +609,11 @@ int build_forward(alm_model* m) {
   }
   m->fwd_grid = 0;
   m->fwd_smem = forward_smem_bytes(stage, c.head_dim, c.hidden);
+  // the persistent kernel runs the tile-layout GEMV only
+  if (m->head->t.layout != kLayoutTile) return ALM_OK;
+  for (const Layer& L : m->layers)
+    for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down})
+      if (w->t.layout != kLayoutTile) return ALM_OK;
   if (forward_barriers(c.layers, true) > kBarRound || c.head_dim % 16 || c.head_dim > 256) return ALM_OK;
   int per_sm = 0;
   if (forward_init_attrs(m->fwd_smem, &per_sm) != cudaSuccess) {
@@ -612,7 +677,7 @@ int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
 // Embedding (tokens already in ws.tokens, position in ws.pos) -> all layers ->
 // final norms -> head.
 int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
-  if (m->ctx->persist && m->fwd_grid > 0 && M <= 8) return enqueue_forward_persistent(m, kv, M, head);
+  if (m->ctx->persist && m->fwd_grid > 0 && M <= kPersistRows) return enqueue_forward_persistent(m, kv, M, head);
   Work& ws = m->ws;
   EmbedArgs ea;
   ea.table = m->embed_table;
@@ -751,6 +816,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
     c->pdl = !(e && e[0] == '1');
     const char* e2 = getenv("ALM_PERSIST");
     c->persist = e2 && e2[0] == '1';
+    const char* e3 = getenv("ALM_TC");
+    if (e3 && (e3[0] == '0' || e3[0] == '1' || e3[0] == '2')) c->tc = e3[0] - '0';
   }
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
@@ -772,6 +839,13 @@ int alm_ctx_destroy(alm_ctx* ctx) {
 int alm_ctx_set_persistent(alm_ctx* ctx, int enable) {
   ALM_REQ(ctx, "null context");
   ctx->persist = enable != 0;
+  return ALM_OK;
+}
+
+int alm_ctx_set_gemv_layout(alm_ctx* ctx, int mode) {
+  ALM_REQ(ctx, "null context");
+  ALM_REQ(mode >= 0 && mode <= 2, "mode must be 0 (tile layout), 1 (row layout for large weights) or 2 (row layout)");
+  ctx->tc = mode;
   return ALM_OK;
 }
 
@@ -815,18 +889,28 @@ int alm_qweight_upload(alm_ctx* ctx, const void* packed_host, const void* scale_
   ALM_REQ(out > 0, "out must be positive");
   DeviceGuard g(ctx->device);
   alm_proj_src s{packed_host, scale_host, bits, block, out, in, in_real};
-  return build_qweight(ctx, &s, 1, identity_map(out), out, w);
+  return build_qweight(ctx, &s, 1, identity_map(out), out, true, w);
 }
 
 int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg) {
   ALM_REQ(w, "null weight");
-  ALM_REQ((ksw == 1 || ksw == 2 || ksw == 4 || ksw == 8) && ksg >= 1 && ksw * ksg <= w->t.k_blocks,
-          "ksw must be 1, 2, 4 or 8 and ksw * ksg at most the number of 64-column blocks");
   DeviceGuard g(w->ctx->device);
   QTile t = w->t;
-  set_split(t, ksw, ksg);
-  ALM_REQ(t.ksw * t.kps <= 64, "per-CTA activation staging would exceed shared memory");
-  const int grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+  int grid_x = 0;
+  if (t.layout == kLayoutRow) {
+    // row layout: ksw = decoding warpgroups per CTA
+    ALM_REQ((ksw == 1 || ksw == 2 || ksw == 4) && ksg >= 1 && ksg <= t.k_blocks,
+            "row layout: ksw (warpgroups) must be 1, 2 or 4 and ksg at most the number of 64-column blocks");
+    set_split_rows(t, ksw, ksg);
+    ALM_REQ(tc_gemv_smem_bytes(t, kMaxRows) <= kRowSmemBudget, "per-CTA activation staging would exceed shared memory");
+    grid_x = t.n_rb;
+  } else {
+    ALM_REQ((ksw == 1 || ksw == 2 || ksw == 4 || ksw == 8) && ksg >= 1 && ksw * ksg <= t.k_blocks,
+            "ksw must be 1, 2, 4 or 8 and ksw * ksg at most the number of 64-column blocks");
+    set_split(t, ksw, ksg);
+    ALM_REQ(t.ksw * t.kps <= 64, "per-CTA activation staging would exceed shared memory");
+    grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+  }
   unsigned* counters = nullptr;
   ALM_TRY(dev_alloc_t(&counters, grid_x));
   ALM_CUDA(cudaMemset(counters, 0, grid_x * sizeof(unsigned)));
@@ -839,7 +923,7 @@ int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg) {
 
 int alm_qweight_get_split(const alm_qweight* w, int* ksw, int* ksg, int* kps) {
   ALM_REQ(w && ksw && ksg && kps, "null argument");
-  *ksw = w->t.ksw;
+  *ksw = w->t.layout == kLayoutRow ? w->t.wg : w->t.ksw;
   *ksg = w->t.ksg;
   *kps = w->t.kps;
   return ALM_OK;
@@ -860,7 +944,8 @@ int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host) 
   half* d = nullptr;
   const size_t n = static_cast<size_t>(w->out) * w->in_real;
   ALM_TRY(dev_alloc_t(&d, n));
-  cudaError_t e = launch_dequant(w->t, d, ctx->stream);
+  cudaError_t e = w->t.layout == kLayoutRow ? launch_dequant_rows(w->t, d, ctx->stream)
+                                             : launch_dequant(w->t, d, ctx->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(out_host, d, n * sizeof(half), cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   cudaFree(d);
@@ -997,7 +1082,7 @@ int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint1
   Layer& L = m->layers[li];
   // fused QKV: q and k rows permuted so tile rows g / g+8 are RoPE pairs
   // (d, d + head_dim/2) of one head; v rows in order.
-  std::vector<int> qkv_map(qd + 2 * kd, -1);
+  std::vector<int> qkv_map(padded_rows(qd + 2 * kd, kLayoutTile), -1);
   auto rope_rows = [&](int src, int n_heads, int dst0) {
     for (int h = 0; h < n_heads; ++h)
       for (int d = 0; d < hd; ++d) {
@@ -1010,17 +1095,23 @@ int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint1
   rope_rows(0, c.heads, 0);
   rope_rows(1, c.kv_heads, qd);
   for (int r = 0; r < kd; ++r) qkv_map[qd + kd + r] = (2 << 24) | r;
-  // fused gate/up: tile rows g = gate j, g + 8 = up j (j = 8 * tile + g)
-  std::vector<int> gu_map((2 * c.intermediate + 15) / 16 * 16, -1);
-  for (int j = 0; j < c.intermediate; ++j) {
-    gu_map[(j / 8) * 16 + j % 8] = (0 << 24) | j;
-    gu_map[(j / 8) * 16 + 8 + j % 8] = (1 << 24) | j;
-  }
+  // fused gate/up, tile layout: tile rows g = gate j, g + 8 = up j (j = 8 * tile + g);
+  // row layout: rows 0-15 of a 32-row group = gate j, rows 16-31 = up j (j = 16 * group + t)
+  const int inter = c.intermediate;
+  auto gu_map = [inter](int layout) {
+    std::vector<int> mp(padded_rows(2 * inter, layout), -1);
+    const int half_rows = layout == kLayoutRow ? 16 : 8;
+    for (int j = 0; j < inter; ++j) {
+      mp[(j / half_rows) * 2 * half_rows + j % half_rows] = (0 << 24) | j;
+      mp[(j / half_rows) * 2 * half_rows + half_rows + j % half_rows] = (1 << 24) | j;
+    }
+    return mp;
+  };
   alm_qweight *qkv = nullptr, *o = nullptr, *gu = nullptr, *dn = nullptr;
-  int rc = build_qweight(m->ctx, &p[0], 3, qkv_map, qd + 2 * kd, &qkv);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, &o);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[4], 2, gu_map, 2 * c.intermediate, &gu);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, &dn);
+  int rc = build_qweight(m->ctx, &p[0], 3, [&qkv_map](int) { return qkv_map; }, qd + 2 * kd, false, &qkv);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, true, &o);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[4], 2, gu_map, 2 * c.intermediate, true, &gu);
+  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, true, &dn);
   half *nin = nullptr, *npost = nullptr;
   if (rc == ALM_OK) rc = dev_alloc_t(&nin, c.hidden);
   if (rc == ALM_OK) rc = dev_alloc_t(&npost, c.hidden);
@@ -1089,7 +1180,7 @@ int alm_model_set_head(alm_model* m, const alm_proj_src* head) {
   ALM_REQ(head->out == m->cfg.vocab && head->in_real == m->cfg.hidden, "head must be (vocab, hidden)");
   DeviceGuard g(m->ctx->device);
   alm_qweight* w = nullptr;
-  ALM_TRY(build_qweight(m->ctx, head, 1, identity_map(head->out), head->out, &w));
+  ALM_TRY(build_qweight(m->ctx, head, 1, identity_map(head->out), head->out, true, &w));
   alm_qweight_free(m->head);
   m->head = w;
   m->finalized = false;
@@ -1117,7 +1208,7 @@ int alm_model_finalize(alm_model* m) {
     s.packed_host = host_tbl.data();
     s.scale_host = m->embed_bits != 16 ? host_scl.data() : nullptr;
     alm_qweight* w = nullptr;
-    ALM_TRY(build_qweight(m->ctx, &s, 1, identity_map(c.vocab), c.vocab, &w));
+    ALM_TRY(build_qweight(m->ctx, &s, 1, identity_map(c.vocab), c.vocab, true, &w));
     m->head = w;
   }
   Work& ws = m->ws;
@@ -1142,8 +1233,7 @@ int alm_model_finalize(alm_model* m) {
     ALM_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ws.pinned), 64 * sizeof(int)));
   }
   // per-CTA argmax partials of the head
-  const int ntc = 8 / m->head->t.ksw;
-  const int n_am = (m->head->t.n_tiles + ntc - 1) / ntc;
+  const int n_am = gemv_out_blocks(m->head->t);
   if (n_am > ws.n_am) {
     dev_free(ws.am_val);
     dev_free(ws.am_idx);

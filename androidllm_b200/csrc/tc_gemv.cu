@@ -1,0 +1,660 @@
+// Dequant-GEMV on the 5th-generation tensor cores: y(M, N) = x(M, K) . W(N, K)^T
+// for M <= 16 activation rows, W in the row-record layout (kernels.cuh).
+//
+// One CTA covers 128 weight rows (one tcgen05 MMA tile, M = 128) over its K
+// range, with `wg` decoding warpgroups and one issuing warp:
+//   * every decoding warp streams the records of its 32 rows (one tensor-
+//     memory lane quarter) through a ring of bulk copies (TMA engine,
+//     mbarrier completion, L2 evict-first), exactly like the tile-layout
+//     GEMV;
+//   * each thread owns one weight row: it decodes the row's 64 codes of a
+//     k-block to exact fp16 weights (the operations of the tile layout, so
+//     the weights equal androidllm's fp16(f32(q) * f32(scale))) and writes
+//     them to a tensor-memory A slot with one tcgen05.st (32 columns);
+//   * warpgroup g takes a contiguous run of the CTA's k-blocks and owns two A
+//     slots; after its four warps have stored a k-block, the issuing thread
+//     runs four tcgen05.mma (M 128, N 16, K 16) from that slot against the
+//     activations staged in shared memory, accumulating in tensor memory, and
+//     tcgen05.commit frees the slot when the MMAs have read it;
+//   * the MMAs run in a fixed order (round j of warpgroup 0, 1, ..., then
+//     round j + 1), and every output column depends only on its own
+//     activation row, so a pass of M rows reproduces M single-row passes
+//     bit for bit;
+//   * the accumulator is read back with tcgen05.ld (thread = row); K splits
+//     across CTAs are summed in split order by the last CTA of a row block;
+//     then the fused epilogues of the tile-layout GEMV (STORE, RESID,
+//     SWIGLU, LOGITS) run on the thread-per-row values.
+// The tensor core takes the contraction off the CUDA cores, which then only
+// decode: on B200 the legacy mma.sync path was the limit of the int4 GEMV.
+//
+// Activations are staged once per CTA as K-major "core matrices" of 8 rows x
+// 8 fp16: chunk q (8 columns) of row m at (q * xrows + m) * 16 bytes with
+// xrows = 8 for M <= 8 (rows 8..15 of an N = 16 MMA then read the next chunk:
+// finite values whose output columns are never stored) or 16.
+#include <algorithm>
+
+#include "act.cuh"
+#include "kernels.cuh"
+#include "repack.cuh"
+#include "tc.cuh"
+
+namespace alm {
+
+constexpr int kTcN = 16;              // MMA N: activation rows, padded
+constexpr int kTcMaxWg = 4;           // decoding warpgroups per CTA
+constexpr int kTcMaxThreads = 32 * (4 * kTcMaxWg + 1);
+constexpr int kTcRingSlots = 3;       // weight ring slots per decoding warp
+constexpr int kTcAPerWg = 2;          // tensor-memory A slots per warpgroup
+constexpr int kTcSlotCols = 32;       // A slot: one k-block of fp16 pairs
+constexpr int kTcAcc = 8;             // accumulators the MMAs rotate over
+constexpr size_t kTcMaxSmem = 225 * 1024;
+constexpr int kTcStageBatch = 4;
+
+template <int BITS>
+struct TcFmt;
+template <>
+struct TcFmt<4> { static constexpr int kParts = 2, kItems = 2; };
+template <>
+struct TcFmt<8> { static constexpr int kParts = 4, kItems = 1; };
+
+__host__ __device__ inline int tc_parts(int bits) { return bits == 4 ? 2 : 4; }
+__host__ __device__ inline int tc_items(int bits) { return bits == 4 ? 2 : 1; }
+__host__ __device__ inline int tc_rec_bytes(int bits) { return tc_parts(bits) * 512 + 64; }
+__host__ __device__ inline int tc_slot_bytes(int bits) { return tc_items(bits) * tc_rec_bytes(bits); }
+__host__ __device__ inline int tc_threads(int wg) { return 32 * (4 * wg + 1); }
+__host__ __device__ inline int tc_dcol(int wg) { return kTcAPerWg * wg * kTcSlotCols; }
+__host__ __device__ inline int tc_tmem_cols(int wg) {
+  int c = 32;
+  while (c < tc_dcol(wg) + kTcAcc * kTcN) c *= 2;
+  return c;
+}
+__host__ __device__ inline int tc_xrows(int rows) { return rows <= 8 ? 8 : 16; }
+__host__ __device__ inline size_t tc_stage_bytes(const QTile& w, int rows) {
+  const int nkb = w.kps < w.k_blocks ? w.kps : w.k_blocks;
+  return static_cast<size_t>(nkb) * 8 * tc_xrows(rows) * 16 + 128;
+}
+__host__ __device__ inline size_t tc_ring_bytes(const QTile& w) {
+  return static_cast<size_t>(4 * w.wg) * kTcRingSlots * tc_slot_bytes(w.bits);
+}
+size_t tc_gemv_smem_bytes(const QTile& w, int rows) { return tc_stage_bytes(w, rows) + tc_ring_bytes(w); }
+
+namespace {
+
+struct TcShared {
+  uint64_t full[kTcAPerWg * kTcMaxWg];    // A slot stored (4 warp arrivals)
+  uint64_t empty[kTcAPerWg * kTcMaxWg];   // A slot read by its MMAs (commit)
+  uint64_t dready;                        // every MMA done (commit)
+  uint64_t ring[4 * kTcMaxWg][kTcRingSlots];
+  uint32_t tmem;
+  int broken;                             // a bounded wait gave up: everyone stops waiting
+  int last;
+  float den_in[kMaxRows];
+  float den_res[kMaxRows];
+  float am_v[4][kMaxRows];
+  int am_i[4][kMaxRows];
+};
+
+// Bounded mbarrier wait that also gives up once another thread has.
+ALM_DEV bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* broken) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned i = 1; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*broken) return false;
+      if (global_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  *broken = 1;
+  return false;
+}
+
+// int4 part (32 codes of one row) -> 16 tensor-memory columns, scaled by s2.
+ALM_DEV void tc_decode4(const uint4& q, half2 s2, uint32_t* out) {
+  const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
+  const half2 off = u2h(0x64086408u);         // 1032 = 1024 + 8
+  const half2 sixteenth = u2h(0x2c002c00u);   // 1/16
+  const half2 off16 = u2h(0xd480d480u);       // -72 = -(64 + 8)
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t w = ws[j], w8 = w >> 8;
+    out[4 * j + 0] = h2u(__hmul2(__hsub2(u2h(and_or(w, 0x000f000fu, 0x64006400u)), off), s2));
+    out[4 * j + 1] = h2u(__hmul2(__hfma2(u2h(and_or(w, 0x00f000f0u, 0x64006400u)), sixteenth, off16), s2));
+    out[4 * j + 2] = h2u(__hmul2(__hsub2(u2h(and_or(w8, 0x000f000fu, 0x64006400u)), off), s2));
+    out[4 * j + 3] = h2u(__hmul2(__hfma2(u2h(and_or(w8, 0x00f000f0u, 0x64006400u)), sixteenth, off16), s2));
+  }
+}
+
+// int8 part (16 codes of one row) -> 8 tensor-memory columns.
+ALM_DEV void tc_decode8(const uint4& q, half2 s2, uint32_t* out) {
+  const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
+  const half2 off = u2h(0x64806480u);         // 1152 = 1024 + 128
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    out[2 * j] = h2u(__hmul2(__hsub2(u2h(prmt(ws[j], 0x64646464u, 0x4140u)), off), s2));
+    out[2 * j + 1] = h2u(__hmul2(__hsub2(u2h(prmt(ws[j], 0x64646464u, 0x4342u)), off), s2));
+  }
+}
+
+template <int BITS>
+ALM_DEV void tc_decode_record(const unsigned char* rec, int lane, uint32_t (&v)[32]) {
+  constexpr int P = TcFmt<BITS>::kParts;
+  uint4 q[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) q[p] = lds128(rec + p * 512 + lane * 16);
+  const half s = *reinterpret_cast<const half*>(rec + P * 512 + lane * 2);
+  const half2 s2 = __half2half2(s);
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    if constexpr (BITS == 4) tc_decode4(q[p], s2, v + 16 * p);
+    else tc_decode8(q[p], s2, v + 8 * p);
+  }
+}
+
+template <int BITS, int EPI>
+__global__ void __launch_bounds__(kTcMaxThreads, 1)
+    tc_gemv_kernel(const __grid_constant__ QTile w, const __grid_constant__ ActIn in, int M,
+                   const __grid_constant__ Epi epi, StepIO io, float* __restrict__ part) {
+  constexpr int IPS = TcFmt<BITS>::kItems;
+  constexpr int REC = TcFmt<BITS>::kParts * 512 + 64;
+  constexpr int SLOT = IPS * REC;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ TcShared sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_warps = blockDim.x >> 5;
+  const int wg = w.wg, n_dec = 4 * wg;
+  const bool decoder = warp < n_dec;
+  const int rb = blockIdx.x, ks = blockIdx.y;
+  const int cta_kb0 = ks * w.kps;
+  const int nkb = max(0, min(w.kps, w.k_blocks - cta_kb0));
+  const int per = (nkb + wg - 1) / wg;
+  const int xrows = tc_xrows(M);
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  unsigned char* rings = smem + tc_stage_bytes(w, M);
+
+  // ---- set-up: barriers, tensor memory ---------------------------------------
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcAPerWg * wg; ++i) {
+      mbar_init(&sh.full[i], 4);
+      mbar_init(&sh.empty[i], 1);
+    }
+    mbar_init(&sh.dready, 1);
+    sh.broken = 0;
+  }
+  if (decoder && lane == 0)
+    for (int i = 0; i < kTcRingSlots; ++i) mbar_init(&sh.ring[warp][i], 1);
+  if (lane == 0) fence_mbar_init();
+  if (warp == n_dec) tc_alloc(&sh.tmem, tc_tmem_cols(wg));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+
+  // ---- weight stream of this warp (independent of earlier kernels) -----------
+  const int g = warp >> 2, grp = warp & 3;
+  const int my0 = g * per;
+  const int cnt = decoder ? max(0, min(per, nkb - my0)) : 0;
+  const int n_chunks = (cnt + IPS - 1) / IPS;
+  const unsigned char* gsrc = reinterpret_cast<const unsigned char*>(
+      w.data + (static_cast<size_t>(rb * 4 + grp) * w.k_blocks + cta_kb0 + my0) * w.rec_u4);
+  unsigned char* wring = rings + static_cast<size_t>(decoder ? warp : 0) * kTcRingSlots * SLOT;
+  uint64_t* rbar = sh.ring[decoder ? warp : 0];
+  auto issue = [&](int c) {
+    const int slot = c % kTcRingSlots;
+    const uint32_t bytes = static_cast<uint32_t>(min(IPS, cnt - c * IPS) * REC);
+    mbar_expect_tx(&rbar[slot], bytes);
+    bulk_g2s(wring + slot * SLOT, gsrc + static_cast<size_t>(c) * IPS * REC, bytes, &rbar[slot], l2_evict_first());
+  };
+  int issued = 0;
+  if (decoder && lane == 0) {
+    for (int c = 0; c < n_chunks && c < kTcRingSlots; ++c) issue(c);
+    issued = min(n_chunks, kTcRingSlots);
+  }
+
+  grid_dep_wait();
+
+  // ---- deferred-norm denominators --------------------------------------------
+  for (int m = warp; m < M; m += n_warps) {
+    if (in.ss) {
+      const float d = row_denominator(in, m);
+      if (lane == 0) sh.den_in[m] = d;
+    }
+    if constexpr (EPI == EPI_RESID) {
+      if (epi.res.ss) {
+        const float d = row_denominator(epi.res, m);
+        if (lane == 0) sh.den_res[m] = d;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- activations -> shared memory (MMA B operand) --------------------------
+  {
+    const int per_row = nkb * 8;
+    const int n_stage = per_row * xrows;   // padding rows are zeroed
+    const bool deferred = in.ss != nullptr;
+    for (int base = 0; base < n_stage; base += blockDim.x * kTcStageBatch) {
+      uint4 raw[kTcStageBatch], wv[kTcStageBatch];
+#pragma unroll
+      for (int j = 0; j < kTcStageBatch; ++j) {
+        const int c = base + j * blockDim.x + threadIdx.x;
+        const int m = c % xrows, q = c / xrows;
+        const int col0 = cta_kb0 * 64 + q * 8;
+        const bool ok = c < n_stage && m < M;
+        raw[j] = ok ? load_row8(in, m, col0, w.k_real) : make_uint4(0, 0, 0, 0);
+        wv[j] = (ok && deferred) ? load_w8(in.w, col0, w.k_real, in.vec) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < kTcStageBatch; ++j) {
+        const int c = base + j * blockDim.x + threadIdx.x;
+        if (c >= n_stage) break;
+        const int m = c % xrows;
+        uint4 v = raw[j];
+        if (deferred && m < M) {
+          const float den = sh.den_in[m];
+          uint32_t words[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float a0 = norm_value(u4_half(raw[j], 2 * e), den, u4_half(wv[j], 2 * e));
+            const float a1 = norm_value(u4_half(raw[j], 2 * e + 1), den, u4_half(wv[j], 2 * e + 1));
+            words[e] = h2u(__floats2half2_rn(a0, a1));
+          }
+          v = make_uint4(words[0], words[1], words[2], words[3]);
+        }
+        xs[c] = v;   // c = q * xrows + m
+      }
+    }
+    if (threadIdx.x < 8) xs[n_stage + threadIdx.x] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();   // generic-proxy writes, read by the tensor core
+  }
+  __syncthreads();
+
+  // ---- decoding warps: records -> exact fp16 rows -> tensor memory -----------
+  if (decoder) {
+    const uint32_t lane_base = static_cast<uint32_t>(grp * 32) << 16;
+    int rslot = 0;
+    uint32_t rphase = 0;
+    int waited = 0, stored = 0;
+    bool ok = true;
+    for (int j = 0; j < cnt; ++j) {
+      const int jj = j % IPS, c = j / IPS;
+      if (jj == 0) {
+        ok = __all_sync(0xffffffffu, tc_wait(&rbar[rslot], rphase, &sh.broken));
+        if (!ok) break;
+        waited = c + 1;
+      }
+      uint32_t v[32];
+      tc_decode_record<BITS>(wring + rslot * SLOT + jj * REC, lane, v);
+      if (j > 0) {
+        // the previous k-block's store finished while this one was decoded
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.full[g + wg * ((j - 1) & 1)]);
+      }
+      const int aslot = g + wg * (j & 1);
+      const int use = j >> 1;
+      if (use >= 1) {
+        ok = __all_sync(0xffffffffu, tc_wait(&sh.empty[aslot], (use - 1) & 1, &sh.broken));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      __syncwarp();
+      tc_st32(tmem + lane_base + aslot * kTcSlotCols, v);
+      stored = j + 1;
+      if (jj == IPS - 1 || j == cnt - 1) {
+        // the ring slot's reads are complete (their values went through tcgen05.st)
+        if (lane == 0 && c + kTcRingSlots < n_chunks) {
+          fence_proxy_async_smem();
+          issue(c + kTcRingSlots);
+          ++issued;
+        }
+        if (++rslot == kTcRingSlots) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+      }
+    }
+    if (stored > 0) {
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&sh.full[g + wg * ((stored - 1) & 1)]);
+    }
+    if (!ok) {
+      // let every copy still in flight land before the CTA's shared memory is released
+      if (lane == 0 && io.err) atomicExch(io.err, 2);
+      issued = __shfl_sync(0xffffffffu, issued, 0);
+      for (int c = waited; c < issued; ++c) mbar_wait(&rbar[c % kTcRingSlots], (c / kTcRingSlots) & 1u);
+    }
+  } else if (lane == 0) {
+    // ---- issuing thread: MMAs in fixed order ----------------------------------
+    const uint32_t idesc = tc_idesc_f16(kRowBlock, kTcN);
+    const uint32_t dcol = tmem + tc_dcol(wg);
+    const uint32_t xbase = smem_addr(xs);
+    const uint32_t lbo = static_cast<uint32_t>(xrows) * 16;
+    bool ok = true;
+    int n_mma = 0;
+    for (int j = 0; j < per && ok; ++j)
+      for (int gg = 0; gg < wg; ++gg) {
+        const int cg = max(0, min(per, nkb - gg * per));
+        if (j >= cg) continue;
+        const int aslot = gg + wg * (j & 1);
+        if (!tc_wait(&sh.full[aslot], (j >> 1) & 1, &sh.broken)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int kbl = gg * per + j;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          // consecutive MMAs go to different accumulators so they do not wait on each other
+          const uint64_t bd = tc_sdesc(xbase + static_cast<uint32_t>((kbl * 8 + 2 * s) * xrows * 16), lbo, 128);
+          const int a = n_mma % kTcAcc;
+          tc_mma_ts(dcol + a * kTcN, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, n_mma >= kTcAcc);
+          ++n_mma;
+        }
+        tc_commit(&sh.empty[aslot]);
+      }
+    tc_commit(&sh.dready);
+    if (!ok && io.err) atomicExch(io.err, 2);
+  }
+
+  // ---- accumulator -> registers (thread = row) ---------------------------------
+  float acc[kTcN];
+#pragma unroll
+  for (int n = 0; n < kTcN; ++n) acc[n] = 0.f;
+  const int r_local = warp * 32 + lane;
+  const int row = rb * kRowBlock + r_local;
+  if (warp < 4) {
+    const bool ok = __all_sync(0xffffffffu, tc_wait(&sh.dready, 0, &sh.broken));
+    tc_fence_after();
+    __syncwarp();
+    // the accumulators that received MMAs, summed in a fixed order
+    const int n_acc = min(kTcAcc, 4 * nkb);
+    for (int a = 0; a < n_acc; ++a) {
+      uint32_t d[kTcN];
+      tc_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + tc_dcol(wg) + a * kTcN, d);
+      tc_wait_ld();
+#pragma unroll
+      for (int n = 0; n < kTcN; ++n) acc[n] = a == 0 ? __uint_as_float(d[n]) : fadd(acc[n], __uint_as_float(d[n]));
+    }
+    if (!ok && lane == 0 && io.err) atomicExch(io.err, 2);
+  }
+  grid_dep_launch();
+
+  // ---- K splits: partials, summed in split order by the last CTA --------------
+  bool do_epi = true;
+  if (w.ksg > 1) {
+    const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
+    if (warp < 4) {
+#pragma unroll
+      for (int m = 0; m < kTcN; ++m)
+        if (m < M) part[(static_cast<size_t>(ks) * kTcN + m) * rows_pad + row] = acc[m];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) sh.last = atomicAdd(&w.counters[rb], 1u) == static_cast<unsigned>(w.ksg - 1);
+    __syncthreads();
+    do_epi = sh.last != 0;
+    if (do_epi) {
+      __threadfence();
+      if (warp < 4) {
+#pragma unroll
+        for (int m = 0; m < kTcN; ++m) {
+          if (m >= M) continue;
+          float s = 0.f;
+          for (int sp = 0; sp < w.ksg; ++sp) s = fadd(s, __ldcg(part + (static_cast<size_t>(sp) * kTcN + m) * rows_pad + row));
+          acc[m] = s;
+        }
+      }
+      if (threadIdx.x == 0) atomicExch(&w.counters[rb], 0u);
+    }
+  }
+
+  // ---- fused epilogues (rounding points of androidllm/models/llama.py:96-146) --
+  if (do_epi && warp < 4) {
+    const bool valid = row < epi.n_out;
+    if constexpr (EPI == EPI_STORE) {
+#pragma unroll
+      for (int m = 0; m < kTcN; ++m)
+        if (m < M && valid) epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(acc[m]);
+    } else if constexpr (EPI == EPI_RESID) {
+      const ActIn& rs = epi.res;
+      const float rw = (rs.ss && valid) ? __half2float(__ldg(rs.w + row)) : 1.f;
+#pragma unroll
+      for (int m = 0; m < kTcN; ++m) {
+        if (m >= M) continue;
+        float sf = 0.f;
+        if (valid) {
+          const float rv = __half2float(__ldcg(rs.x + static_cast<size_t>(m) * rs.ld + row));
+          const float o = round_h(acc[m]);
+          const float res = rs.ss ? norm_value(rv, sh.den_res[m], rw) : rv;
+          const half s16 = __float2half_rn(fadd(res, o));
+          epi.out[static_cast<size_t>(m) * epi.ldo + row] = s16;
+          sf = __half2float(s16);
+        }
+        float sq = fmul(sf, sf);
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) sq = fadd(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+        const int tile = row >> 4;
+        if ((lane & 15) == 0 && tile < w.n_tiles) epi.ss_out[static_cast<size_t>(m) * w.n_tiles + tile] = sq;
+      }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      // lanes 0-15: gate rows j0 + t, lanes 16-31: up rows j0 + t
+      const int col = (rb * 4 + warp) * 16 + (lane & 15);
+#pragma unroll
+      for (int m = 0; m < kTcN; ++m) {
+        if (m >= M) continue;
+        const float v = round_h(acc[m]);
+        const float uv = __shfl_down_sync(0xffffffffu, v, 16);
+        if (lane < 16 && col < epi.n_out) {
+          const float sig = fdiv(1.f, fadd(1.f, expf(-v)));
+          epi.out[static_cast<size_t>(m) * epi.ldo + col] = __float2half_rn(fmul(fmul(v, sig), uv));
+        }
+      }
+    } else if constexpr (EPI == EPI_LOGITS) {
+#pragma unroll
+      for (int m = 0; m < kTcN; ++m) {
+        if (m >= M) continue;
+        float bv = kNegInf;
+        int bi = 0x7fffffff;
+        if (valid) {
+          const half l16 = __float2half_rn(acc[m]);
+          epi.out[static_cast<size_t>(m) * epi.ldo + row] = l16;
+          bv = __half2float(l16);
+          bi = row;
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          sh.am_v[warp][m] = bv;
+          sh.am_i[warp][m] = bi;
+        }
+      }
+    }
+  }
+  if constexpr (EPI == EPI_LOGITS) {
+    __syncthreads();
+    if (do_epi && threadIdx.x < M) {
+      const int m = threadIdx.x;
+      float bv = kNegInf;
+      int bi = 0x7fffffff;
+      for (int k = 0; k < 4; ++k)
+        if (better(sh.am_v[k][m], sh.am_i[k][m], bv, bi)) {
+          bv = sh.am_v[k][m];
+          bi = sh.am_i[k][m];
+        }
+      epi.am_val[static_cast<size_t>(m) * w.n_rb + rb] = bv;
+      epi.am_idx[static_cast<size_t>(m) * w.n_rb + rb] = bi;
+    }
+  }
+
+  // ---- tear-down -----------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == n_dec) {
+    __syncwarp();
+    tc_dealloc(tmem, tc_tmem_cols(wg));
+  }
+}
+
+// One thread per (record, row t): that row's codes and scale.
+__global__ void repack_rows_kernel(SrcSet s, const int* __restrict__ dst_src_row, int bits, int n_rb,
+                                   int k_blocks, int k_pad, int block, int src_nsb, int rec_u4,
+                                   uint4* __restrict__ out) {
+  const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long total = static_cast<long long>(n_rb) * 4 * k_blocks * kWarp;
+  if (gid >= total) return;
+  const int t = static_cast<int>(gid % kWarp);
+  const long long rec = gid / kWarp;
+  const int kb = static_cast<int>(rec % k_blocks);
+  const int row = static_cast<int>(rec / k_blocks) * kWarp + t;
+  const int desc = dst_src_row[row];
+  const int parts = bits == 4 ? 2 : 4;
+  uint4* dst = out + rec * rec_u4;
+  for (int p = 0; p < parts; ++p) {
+    uint32_t words[4];
+    for (int j = 0; j < 4; ++j) {
+      uint32_t wv = 0;
+      if (bits == 4) {
+        for (int i = 0; i < 8; ++i) {
+          const int k = kb * 64 + 32 * p + 8 * j + (i < 4 ? 2 * i : 2 * (i - 4) + 1);
+          wv |= static_cast<uint32_t>((fetch_code(s, desc, k, bits, k_pad) + 8) & 0xf) << (4 * i);
+        }
+      } else {
+        for (int b = 0; b < 4; ++b) {
+          const int k = kb * 64 + 16 * p + 4 * j + b;
+          wv |= static_cast<uint32_t>((fetch_code(s, desc, k, bits, k_pad) + 128) & 0xff) << (8 * b);
+        }
+      }
+      words[j] = wv;
+    }
+    dst[p * kWarp + t] = make_uint4(words[0], words[1], words[2], words[3]);
+  }
+  const int sbk = (kb * 64) / block;
+  const half sc = (desc < 0 || sbk >= src_nsb) ? __ushort_as_half(0)
+                                               : s.scale[desc >> 24][static_cast<size_t>(desc & 0xffffff) * src_nsb + sbk];
+  reinterpret_cast<half*>(dst + parts * kWarp)[t] = sc;
+}
+
+// Decode the row layout back to fp16 rows (out: n_rows x k_real).
+template <int BITS>
+__global__ void dequant_rows_kernel(QTile w, half* __restrict__ out) {
+  const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long total = static_cast<long long>(w.n_rb) * 4 * w.k_blocks * kWarp;
+  if (gid >= total) return;
+  const int t = static_cast<int>(gid % kWarp);
+  const long long rec = gid / kWarp;
+  const int kb = static_cast<int>(rec % w.k_blocks);
+  const int row = static_cast<int>(rec / w.k_blocks) * kWarp + t;
+  const unsigned char* rp = reinterpret_cast<const unsigned char*>(w.data + rec * w.rec_u4);
+  constexpr int P = TcFmt<BITS>::kParts;
+  uint4 q[P];
+  for (int p = 0; p < P; ++p) q[p] = reinterpret_cast<const uint4*>(rp)[p * kWarp + t];
+  const half2 s2 = __half2half2(reinterpret_cast<const half*>(rp + P * 512)[t]);
+  uint32_t v[32];
+  for (int p = 0; p < P; ++p) {
+    if constexpr (BITS == 4) tc_decode4(q[p], s2, v + 16 * p);
+    else tc_decode8(q[p], s2, v + 8 * p);
+  }
+  if (row >= w.n_rows) return;
+  half* o = out + static_cast<size_t>(row) * w.k_real;
+  for (int c = 0; c < 32; ++c) {
+    const int k = kb * 64 + 2 * c;
+    const half2 hv = u2h(v[c]);
+    if (k < w.k_real) o[k] = __low2half(hv);
+    if (k + 1 < w.k_real) o[k + 1] = __high2half(hv);
+  }
+}
+
+template <int BITS, int EPI>
+cudaError_t tc_launch_t(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
+                        const SplitScratch& scr, bool pdl, cudaStream_t st) {
+  const size_t smem = tc_gemv_smem_bytes(w, M);
+  if (smem > kTcMaxSmem || w.wg < 1 || w.wg > kTcMaxWg) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(w.n_rb, w.ksg, 1);
+  cfg.blockDim = dim3(tc_threads(w.wg), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, tc_gemv_kernel<BITS, EPI>, w, in, M, epi, io, scr.part);
+}
+
+template <int BITS>
+cudaError_t tc_dispatch(EpiKind kind, const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
+                        const SplitScratch& scr, bool pdl, cudaStream_t st) {
+  switch (kind) {
+    case EPI_STORE: return tc_launch_t<BITS, EPI_STORE>(w, in, M, epi, io, scr, pdl, st);
+    case EPI_RESID: return tc_launch_t<BITS, EPI_RESID>(w, in, M, epi, io, scr, pdl, st);
+    case EPI_SWIGLU: return tc_launch_t<BITS, EPI_SWIGLU>(w, in, M, epi, io, scr, pdl, st);
+    case EPI_LOGITS: return tc_launch_t<BITS, EPI_LOGITS>(w, in, M, epi, io, scr, pdl, st);
+    default: return cudaErrorNotSupported;   // QKV projections use the tile layout
+  }
+}
+
+template <int BITS>
+cudaError_t tc_set_attrs() {
+  const int v = static_cast<int>(kTcMaxSmem);
+  const auto a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+  cudaError_t e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_STORE>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_RESID>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_SWIGLU>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_LOGITS>, a, v);
+  return e;
+}
+
+}  // namespace
+
+cudaError_t tc_gemv_init_attrs() {
+  cudaError_t e = tc_set_attrs<4>();
+  if (e == cudaSuccess) e = tc_set_attrs<8>();
+  return e;
+}
+
+cudaError_t launch_tc_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
+                           const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st) {
+  if (M < 1 || M > kTcN || w.layout != kLayoutRow) return cudaErrorInvalidValue;
+  if (w.bits == 4) return tc_dispatch<4>(kind, w, in, M, epi, io, scr, pdl, st);
+  if (w.bits == 8) return tc_dispatch<8>(kind, w, in, M, epi, io, scr, pdl, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_repack_rows(const void* const* src, const half* const* src_scales, int n_src,
+                               const int* dst_src_row, const QTile& w, uint4* data, int k_pad, cudaStream_t st) {
+  if (n_src < 1 || n_src > 3 || (w.bits != 4 && w.bits != 8) || w.block % 64 != 0) return cudaErrorInvalidValue;
+  SrcSet s{};
+  for (int i = 0; i < n_src; ++i) {
+    s.data[i] = static_cast<const uint8_t*>(src[i]);
+    s.scale[i] = src_scales ? src_scales[i] : nullptr;
+  }
+  const long long total = static_cast<long long>(w.n_rb) * 4 * w.k_blocks * kWarp;
+  const int threads = 256;
+  repack_rows_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, st>>>(
+      s, dst_src_row, w.bits, w.n_rb, w.k_blocks, k_pad, w.block, k_pad / w.block, w.rec_u4, data);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_rows(const QTile& w, half* out, cudaStream_t st) {
+  const long long total = static_cast<long long>(w.n_rb) * 4 * w.k_blocks * kWarp;
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((total + threads - 1) / threads);
+  if (w.bits == 4) dequant_rows_kernel<4><<<blocks, threads, 0, st>>>(w, out);
+  else if (w.bits == 8) dequant_rows_kernel<8><<<blocks, threads, 0, st>>>(w, out);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+}  // namespace alm

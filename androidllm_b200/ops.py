@@ -40,6 +40,12 @@ class Context:
         per layer operation (the default); both give bit-identical results."""
         check(lib.alm_ctx_set_persistent(self.h, 1 if enable else 0))
 
+    def set_gemv_layout(self, mode):
+        """Layout of weights uploaded from now on: 0 = 16-row tiles (mma.sync
+        GEMV, the default), 1 = 128-row records (tcgen05 kernel) for weights of
+        4 MB or more, 2 = 128-row records wherever the format allows."""
+        check(lib.alm_ctx_set_gemv_layout(self.h, int(mode)))
+
     def close(self):
         if self.h:
             lib.alm_ctx_destroy(self.h)

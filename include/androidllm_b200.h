@@ -64,6 +64,15 @@ ALM_API int alm_ctx_sync(alm_ctx* ctx);
    variable ALM_PERSIST=1 turns the persistent kernel on at context creation).
    The results are bit-identical.  Graphs captured earlier keep their kernels. */
 ALM_API int alm_ctx_set_persistent(alm_ctx* ctx, int enable);
+/* Weight layout chosen by later uploads: 0 (the default) = 16-row tiles for
+   the mma.sync GEMV; 1 = 128-row records for the tcgen05 kernel for weights of
+   at least 4 MB, tiles otherwise; 2 = 128-row records wherever the format
+   allows (int4 / int8, 64-column blocks; never the fused QKV projection).
+   ALM_TC=0/1/2 sets it at context creation.  Dequantized weights are
+   identical in both layouts; GEMV results agree to fp32 summation order.
+   On B200 a tcgen05.mma costs about the same for N = 16 as for N = 256, so
+   the row layout pays off only for many activation rows (dense GEMM). */
+ALM_API int alm_ctx_set_gemv_layout(alm_ctx* ctx, int mode);
 /* Device memory helpers for hosts without their own device-memory library. */
 ALM_API int alm_dev_alloc(alm_ctx* ctx, size_t bytes, void** out_dev);
 ALM_API int alm_dev_free(alm_ctx* ctx, void* dev);
