@@ -197,7 +197,8 @@ ALM_DEV void gemv_phase_t(const FwdParams& P, GridSync& gs, uint32_t& seq, const
   gs.wait();
   while (vb < nvb) {
     seq += static_cast<uint32_t>(
-        gemv_run<BITS, 1, EPI>(w, in, P.M, epi, P.io, P.part, plan, ring, seq, fwd_stage(), s_fwd.g));
+        gemv_run<BITS, BITS == 16 ? 0 : 1, 1, EPI>(w, in, P.M, epi, P.io, P.part, plan, ring, seq, fwd_stage(),
+                                                   s_fwd.g));
     vb += gridDim.x;
     if (vb < nvb) {
       __syncthreads();

@@ -16,7 +16,7 @@ inline size_t gemv_smem_bytes(const QTile& w, int rows) {
   return ring_bytes(gemv_slot_bytes(w)) + gemv_stage_bytes(w, rows);
 }
 
-template <int BITS, int NT8, int EPI>
+template <int BITS, int SB, int NT8, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(QTile w, ActIn in, int M, Epi epi, StepIO io,
                                                             float* __restrict__ part) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -28,13 +28,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(QTile w, ActIn in
   gemv_issue_first<BITS>(ring, w, plan, 0);
   grid_dep_wait();
   uint4* xs = reinterpret_cast<uint4*>(smem + ring_bytes(slot_bytes));
-  gemv_run<BITS, NT8, EPI>(w, in, M, epi, io, part, plan, ring, 0, xs, sh);
+  gemv_run<BITS, SB, NT8, EPI>(w, in, M, epi, io, part, plan, ring, 0, xs, sh);
 }
 
 template <int BITS, int NT8, int EPI>
 cudaError_t launch_t(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                      const SplitScratch& scr, bool pdl, cudaStream_t st) {
-  auto kern = gemv_kernel<BITS, NT8, EPI>;
+  constexpr int SB1 = BITS == 16 ? 0 : 1;
+  constexpr int SB2 = BITS == 16 ? 0 : 2;
+  auto kern = w.sb == 2 ? gemv_kernel<BITS, SB2, NT8, EPI> : gemv_kernel<BITS, SB1, NT8, EPI>;
   const size_t smem = gemv_smem_bytes(w, M);
   if (smem > kGemvMaxSmem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
@@ -70,15 +72,23 @@ cudaError_t dispatch_nt(EpiKind kind, const QTile& w, const ActIn& in, int M, co
   return dispatch_epi<BITS, 2>(kind, w, in, M, epi, io, scr, pdl, st);
 }
 
-template <int BITS, int NT8>
-cudaError_t set_attrs_nt() {
+template <int BITS, int SB, int NT8>
+cudaError_t set_attrs_sb() {
   const int v = static_cast<int>(kGemvMaxSmem);
   const auto a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-  cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BITS, NT8, EPI_STORE>, a, v);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, NT8, EPI_QKV>, a, v);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, NT8, EPI_RESID>, a, v);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, NT8, EPI_SWIGLU>, a, v);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, NT8, EPI_LOGITS>, a, v);
+  cudaError_t e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_STORE>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_QKV>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_RESID>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_SWIGLU>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_LOGITS>, a, v);
+  return e;
+}
+
+template <int BITS, int NT8>
+cudaError_t set_attrs_nt() {
+  if constexpr (BITS == 16) return set_attrs_sb<16, 0, NT8>();
+  cudaError_t e = set_attrs_sb<BITS, 1, NT8>();
+  if (e == cudaSuccess) e = set_attrs_sb<BITS, 2, NT8>();
   return e;
 }
 

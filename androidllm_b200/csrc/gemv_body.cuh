@@ -174,14 +174,17 @@ ALM_DEV void gemv_issue_first(const Ring& r, const QTile& w, const GemvPlan& p, 
 
 // The rest of the virtual block after gemv_issue_first and after the inputs
 // are ready: norms, staging, the streamed main loop, reductions, epilogue.
+// SB: scale sets per record (0 for fp16, 1, or 2 for 32-column blocks), so
+// every offset inside a record is a compile-time constant.
 // xs: activation staging (gemv_stage_bytes).  Returns the chunks that went
 // through the warp's ring (the caller adds them to its seq).
-template <int BITS, int NT8, int EPI>
+template <int BITS, int SB, int NT8, int EPI>
 ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                      float* __restrict__ part, const GemvPlan& p, const Ring& ring, uint32_t seq,
                      uint4* __restrict__ xs, GemvShared<NT8>& sh) {
   constexpr int V = QTileTraits<BITS>::kVec;
   constexpr int IPS = Pipe<BITS>::kItems;
+  constexpr int REC = (V * kWarp + SB * 2) * 16;   // record bytes (w.rec_u4 * 16)
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int g = lane >> 2, t = lane & 3;
   const int ksw = w.ksw, ntc = p.ntc;
@@ -189,7 +192,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
   const bool tile_ok = p.tile_ok;
   const int kb0 = p.kb0, n = p.n, n_chunks = p.n_chunks;
   const int cta_kb0 = p.cta_kb0, cta_nkb = p.cta_nkb;
-  const int rec_bytes = w.rec_u4 * 16;
+  const int rec_bytes = REC;
   unsigned char* wring = ring.base + static_cast<size_t>(warp) * kSlots * ring.slot_bytes;
   uint64_t* bars = ring.bars + warp * kSlots;
 
@@ -267,7 +270,43 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
 #pragma unroll
   for (int nt = 0; nt < NT8; ++nt) xrow[nt] = xs + min(nt * 8 + g, M - 1) * 4 + t;
   const int xhalf = 4 * M;
-  const bool two_sets = w.sb == 2;
+  // one record: decode the lane's weights of a (tile, k-block) and feed 4 MMAs
+  auto record = [&](const unsigned char* rp, int kbl) {
+    uint4 cur[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) cur[v] = lds128(rp + v * 512 + lane * 16);
+    half2 sg_a = __float2half2_rn(1.f), sg8_a = sg_a, sg_b = sg_a, sg8_b = sg_a;
+    if constexpr (SB >= 1) {
+      const half2 sa = u2h(lds32(rp + V * 512 + g * 4));
+      sg_a = __low2half2(sa);
+      sg8_a = __high2half2(sa);
+      sg_b = sg_a;
+      sg8_b = sg8_a;
+    }
+    if constexpr (SB == 2) {
+      const half2 sb2 = u2h(lds32(rp + V * 512 + 32 + g * 4));
+      sg_b = __low2half2(sb2);
+      sg8_b = __high2half2(sb2);
+    }
+    uint4 xf[NT8][2];
+#pragma unroll
+    for (int nt = 0; nt < NT8; ++nt) {
+      xf[nt][0] = xrow[nt][(2 * kbl) * xhalf];
+      xf[nt][1] = xrow[nt][(2 * kbl + 1) * xhalf];
+    }
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t a0, a1, a2, a3;
+      decode_step<BITS>(cur, s, s >= 2 ? sg_b : sg_a, s >= 2 ? sg8_b : sg8_a, a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt) {
+        const uint4& X = xf[nt][s >> 1];
+        const uint32_t b0 = (s & 1) ? X.z : X.x;
+        const uint32_t b1 = (s & 1) ? X.w : X.y;
+        mma16816((s & 1) ? acc2[nt] : acc[nt], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  };
   int consumed = 0;
   bool stream_ok = true;
   int slot = static_cast<int>(seq % kSlots);
@@ -278,43 +317,15 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
       break;
     }
     const unsigned char* sp = wring + slot * ring.slot_bytes;
+    const int kbl0 = kb0 + c * IPS - cta_kb0;
     const int cnt = min(IPS, n - c * IPS);
+    if (cnt == IPS) {
 #pragma unroll
-    for (int j = 0; j < IPS; ++j) {
-      if (j < cnt) {
-        const unsigned char* rp = sp + j * rec_bytes;
-        uint4 cur[V];
+      for (int j = 0; j < IPS; ++j) record(sp + j * REC, kbl0 + j);
+    } else {
 #pragma unroll
-        for (int v = 0; v < V; ++v) cur[v] = lds128(rp + v * 512 + lane * 16);
-        half2 sg_a = __float2half2_rn(1.f), sg8_a = sg_a, sg_b = sg_a, sg8_b = sg_a;
-        if constexpr (BITS != 16) {
-          const half2 sa = u2h(lds32(rp + V * 512 + g * 4));
-          const half2 sb2 = two_sets ? u2h(lds32(rp + V * 512 + 32 + g * 4)) : sa;
-          sg_a = __low2half2(sa);
-          sg8_a = __high2half2(sa);
-          sg_b = __low2half2(sb2);
-          sg8_b = __high2half2(sb2);
-        }
-        const int kbl = kb0 + c * IPS + j - cta_kb0;
-        uint4 xf[NT8][2];
-#pragma unroll
-        for (int nt = 0; nt < NT8; ++nt) {
-          xf[nt][0] = xrow[nt][(2 * kbl) * xhalf];
-          xf[nt][1] = xrow[nt][(2 * kbl + 1) * xhalf];
-        }
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          uint32_t a0, a1, a2, a3;
-          decode_step<BITS>(cur, s, s >= 2 ? sg_b : sg_a, s >= 2 ? sg8_b : sg8_a, a0, a1, a2, a3);
-#pragma unroll
-          for (int nt = 0; nt < NT8; ++nt) {
-            const uint4& X = xf[nt][s >> 1];
-            const uint32_t b0 = (s & 1) ? X.z : X.x;
-            const uint32_t b1 = (s & 1) ? X.w : X.y;
-            mma16816((s & 1) ? acc2[nt] : acc[nt], a0, a1, a2, a3, b0, b1);
-          }
-        }
-      }
+      for (int j = 0; j < IPS; ++j)
+        if (j < cnt) record(sp + j * REC, kbl0 + j);
     }
     consumed = c + 1;
     __syncwarp();

@@ -609,11 +609,12 @@ int build_forward(alm_model* m) {
   }
   m->fwd_grid = 0;
   m->fwd_smem = forward_smem_bytes(stage, c.head_dim, c.hidden);
-  // the persistent kernel runs the tile-layout GEMV only
-  if (m->head->t.layout != kLayoutTile) return ALM_OK;
+  // the persistent kernel runs the tile-layout GEMV with 64-column scale blocks only
+  auto persistable = [](const alm_qweight* w) { return w->t.layout == kLayoutTile && w->t.sb != 2; };
+  if (!persistable(m->head)) return ALM_OK;
   for (const Layer& L : m->layers)
     for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down})
-      if (w->t.layout != kLayoutTile) return ALM_OK;
+      if (!persistable(w)) return ALM_OK;
   if (forward_barriers(c.layers, true) > kBarRound || c.head_dim % 16 || c.head_dim > 256) return ALM_OK;
   int per_sm = 0;
   if (forward_init_attrs(m->fwd_smem, &per_sm) != cudaSuccess) {
