@@ -105,9 +105,9 @@ cudaError_t gemv_init_attrs() {
   return e;
 }
 
-size_t gemv_part_floats(const QTile& w) {
+size_t gemv_part_floats(const QTile& w, int rows) {
+  if (w.layout == kLayoutRow) return tc_part_floats(w, rows);
   if (w.ksg <= 1) return 0;
-  if (w.layout == kLayoutRow) return static_cast<size_t>(w.ksg) * kMaxRows * w.n_rb * kRowBlock;
   return static_cast<size_t>(w.ksg) * (w.n_tiles + kGemvWarps) * kWarp * 8;
 }
 
@@ -115,16 +115,16 @@ int gemv_out_blocks(const QTile& w) { return w.layout == kLayoutRow ? w.n_rb : g
 
 cudaError_t launch_gemv(const QTile& w, const ActIn& in_, int M, EpiKind kind, const Epi& epi_,
                         const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st) {
-  if (M < 1 || M > kMaxRows) return cudaErrorInvalidValue;
+  if (M < 1 || M > (w.layout == kLayoutRow ? kMaxDenseRows : kMaxRows)) return cudaErrorInvalidValue;
   ActIn in = in_;
   set_vec(in);
   Epi epi = epi_;
   if (epi.res.x) set_vec(epi.res);
+  if (w.layout == kLayoutRow) return launch_tc_gemv(w, in, M, kind, epi, io, scr, pdl, st);
   if (w.ksg > 1) {
-    if (scr.part == nullptr || scr.part_floats < gemv_part_floats(w) || w.counters == nullptr)
+    if (scr.part == nullptr || scr.part_floats < gemv_part_floats(w, M) || w.counters == nullptr)
       return cudaErrorInvalidValue;
   }
-  if (w.layout == kLayoutRow) return launch_tc_gemv(w, in, M, kind, epi, io, scr, pdl, st);
   switch (w.bits) {
     case 4: return dispatch_nt<4>(kind, w, in, M, epi, io, scr, pdl, st);
     case 8: return dispatch_nt<8>(kind, w, in, M, epi, io, scr, pdl, st);

@@ -156,8 +156,12 @@ cudaError_t launch_tc_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind,
 cudaError_t tc_gemv_init_attrs();
 // Dynamic shared memory a row-layout GEMV of `rows` activation rows needs.
 size_t tc_gemv_smem_bytes(const QTile& w, int rows);
-// Split-K partial floats a GEMV launch of w needs (either layout).
-size_t gemv_part_floats(const QTile& w);
+// Split-K partial floats a GEMV launch of w over `rows` activation rows
+// needs (either layout; the row layout's dense path splits K by rows).
+size_t gemv_part_floats(const QTile& w, int rows = kMaxRows);
+size_t tc_part_floats(const QTile& w, int rows);
+// Activation rows one launch takes: 16, or 256 (STORE) for the row layout.
+constexpr int kMaxDenseRows = 256;
 // CTAs along the output rows (argmax partials of a LOGITS launch).
 int gemv_out_blocks(const QTile& w);
 

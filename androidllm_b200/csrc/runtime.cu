@@ -957,12 +957,13 @@ int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host) 
 int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m, uint16_t* y_dev,
                 int ldy) {
   ALM_REQ(ctx && w && x_dev && y_dev, "null argument");
-  ALM_REQ(m >= 1 && m <= kMaxRows, "m must be in 1..16");
+  ALM_REQ(m >= 1 && m <= (w->t.layout == kLayoutRow ? kMaxDenseRows : kMaxRows),
+          "m must be in 1..16 (1..256 for a row-layout weight)");
   ALM_REQ(ldx >= w->in_real && ldy >= w->out, "leading dimension too small");
   DeviceGuard g(ctx->device);
   static thread_local std::vector<std::pair<alm_ctx*, std::pair<float*, size_t>>> scratch;
   SplitScratch scr;
-  const size_t need = split_need(w);
+  const size_t need = gemv_part_floats(w->t, m);
   if (need) {
     std::pair<float*, size_t>* slot = nullptr;
     for (auto& p : scratch)
@@ -1761,12 +1762,14 @@ int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted) {
 int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint16_t* x_dev, int m,
                       uint16_t* y_dev, int iters, float* avg_us) {
   ALM_REQ(ctx && ws && n_w > 0 && x_dev && y_dev && avg_us, "null argument");
-  ALM_REQ(m >= 1 && m <= kMaxRows && iters >= 1, "m must be in 1..16");
+  ALM_REQ(iters >= 1, "iters must be positive");
   for (int i = 0; i < n_w; ++i)
     ALM_REQ(ws[i] && ws[i]->out == ws[0]->out && ws[i]->in_real == ws[0]->in_real, "weights must share a shape");
+  ALM_REQ(m >= 1 && m <= (ws[0]->t.layout == kLayoutRow ? kMaxDenseRows : kMaxRows),
+          "m must be in 1..16 (1..256 for row-layout weights)");
   DeviceGuard g(ctx->device);
   size_t need = 0;
-  for (int i = 0; i < n_w; ++i) need = std::max(need, split_need(ws[i]));
+  for (int i = 0; i < n_w; ++i) need = std::max(need, gemv_part_floats(ws[i]->t, m));
   float* part = nullptr;
   if (need) ALM_TRY(dev_alloc_t(&part, need));
   SplitScratch scr{part, need};

@@ -40,13 +40,13 @@
 
 namespace alm {
 
-constexpr int kTcN = 16;              // MMA N: activation rows, padded
+constexpr int kTcN = 16;              // MMA N of the fused GEMV: activation rows, padded
+constexpr int kTcMaxN = 256;          // MMA N of the dense path (STORE, up to 256 rows)
 constexpr int kTcMaxWg = 4;           // decoding warpgroups per CTA
 constexpr int kTcMaxThreads = 32 * (4 * kTcMaxWg + 1);
 constexpr int kTcRingSlots = 3;       // weight ring slots per decoding warp
 constexpr int kTcAPerWg = 2;          // tensor-memory A slots per warpgroup
 constexpr int kTcSlotCols = 32;       // A slot: one k-block of fp16 pairs
-constexpr int kTcAcc = 8;             // accumulators the MMAs rotate over
 constexpr size_t kTcMaxSmem = 225 * 1024;
 constexpr int kTcStageBatch = 4;
 
@@ -63,12 +63,15 @@ __host__ __device__ inline int tc_rec_bytes(int bits) { return tc_parts(bits) * 
 __host__ __device__ inline int tc_slot_bytes(int bits) { return tc_items(bits) * tc_rec_bytes(bits); }
 __host__ __device__ inline int tc_threads(int wg) { return 32 * (4 * wg + 1); }
 __host__ __device__ inline int tc_dcol(int wg) { return kTcAPerWg * wg * kTcSlotCols; }
-__host__ __device__ inline int tc_tmem_cols(int wg) {
+// MMA N for `rows` activation rows, and the rows staged per 8-column chunk
+// (8 for M <= 8: the MMA's rows 8..15 then read the next chunk).
+__host__ __device__ inline int tc_n(int rows) { return rows <= kTcN ? kTcN : (rows + 15) / 16 * 16; }
+__host__ __device__ inline int tc_xrows(int rows) { return rows <= 8 ? 8 : tc_n(rows); }
+__host__ __device__ inline int tc_tmem_cols(int wg, int rows) {
   int c = 32;
-  while (c < tc_dcol(wg) + kTcAcc * kTcN) c *= 2;
+  while (c < tc_dcol(wg) + tc_n(rows)) c *= 2;
   return c;
 }
-__host__ __device__ inline int tc_xrows(int rows) { return rows <= 8 ? 8 : 16; }
 __host__ __device__ inline size_t tc_stage_bytes(const QTile& w, int rows) {
   const int nkb = w.kps < w.k_blocks ? w.kps : w.k_blocks;
   return static_cast<size_t>(nkb) * 8 * tc_xrows(rows) * 16 + 128;
@@ -77,6 +80,27 @@ __host__ __device__ inline size_t tc_ring_bytes(const QTile& w) {
   return static_cast<size_t>(4 * w.wg) * kTcRingSlots * tc_slot_bytes(w.bits);
 }
 size_t tc_gemv_smem_bytes(const QTile& w, int rows) { return tc_stage_bytes(w, rows) + tc_ring_bytes(w); }
+
+// Launch shape for `rows` activation rows.  Up to 16 rows: the weight's own
+// split.  Dense (more rows): one decoding warpgroup (the MMAs bound the time)
+// and K split across CTAs so the staged activations fit in shared memory.
+QTile tc_launch_shape(const QTile& w, int rows) {
+  if (rows <= kTcN) return w;
+  QTile d = w;
+  d.wg = 1;
+  const size_t per_kb = static_cast<size_t>(8) * tc_xrows(rows) * 16;
+  const size_t budget = kTcMaxSmem - tc_ring_bytes(d) - 1024;
+  int kps = static_cast<int>(std::max<size_t>(1, std::min<size_t>(d.k_blocks, budget / per_kb)));
+  d.ksg = (d.k_blocks + kps - 1) / kps;
+  d.kps = (d.k_blocks + d.ksg - 1) / d.ksg;
+  return d;
+}
+
+size_t tc_part_floats(const QTile& w, int rows) {
+  const QTile d = tc_launch_shape(w, rows);
+  if (d.ksg <= 1) return 0;
+  return static_cast<size_t>(d.ksg) * tc_n(rows) * d.n_rb * kRowBlock;
+}
 
 namespace {
 
@@ -184,7 +208,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   if (decoder && lane == 0)
     for (int i = 0; i < kTcRingSlots; ++i) mbar_init(&sh.ring[warp][i], 1);
   if (lane == 0) fence_mbar_init();
-  if (warp == n_dec) tc_alloc(&sh.tmem, tc_tmem_cols(wg));
+  if (warp == n_dec) tc_alloc(&sh.tmem, tc_tmem_cols(wg, M));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -229,7 +253,27 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   __syncthreads();
 
   // ---- activations -> shared memory (MMA B operand) --------------------------
-  {
+  if (M > kTcN && in.ss == nullptr && in.vec) {
+    // dense path, raw rows: asynchronous 16-byte copies, coalesced along K
+    // (padding rows and columns past k_real read as zeros)
+    // a warp covers 8 rows x 4 chunks: 64 contiguous bytes of each row from
+    // global memory, 4 runs of 128 contiguous bytes in shared memory
+    const int per_row = nkb * 8;
+    const int n_stage = per_row * xrows;
+    for (int c = threadIdx.x; c < n_stage; c += blockDim.x) {
+      const int mi = c & 7, qi = (c >> 3) & 3, rest = c >> 5;
+      const int q = (rest % (per_row / 4)) * 4 + qi, m = (rest / (per_row / 4)) * 8 + mi;
+      const int col0 = cta_kb0 * 64 + q * 8;
+      const int valid = m < M ? max(0, min(8, w.k_real - col0)) : 0;
+      const half* src = in.x + static_cast<size_t>(valid ? m : 0) * in.ld + (valid ? col0 : 0);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(xs + q * xrows + m)), "l"(src),
+                   "r"(valid * 2)
+                   : "memory");
+    }
+    if (threadIdx.x < 8) xs[n_stage + threadIdx.x] = make_uint4(0, 0, 0, 0);
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+    fence_proxy_async_smem();
+  } else {
     const int per_row = nkb * 8;
     const int n_stage = per_row * xrows;   // padding rows are zeroed
     const bool deferred = in.ss != nullptr;
@@ -329,7 +373,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
     }
   } else if (lane == 0) {
     // ---- issuing thread: MMAs in fixed order ----------------------------------
-    const uint32_t idesc = tc_idesc_f16(kRowBlock, kTcN);
+    const uint32_t idesc = tc_idesc_f16(kRowBlock, tc_n(M));
     const uint32_t dcol = tmem + tc_dcol(wg);
     const uint32_t xbase = smem_addr(xs);
     const uint32_t lbo = static_cast<uint32_t>(xrows) * 16;
@@ -348,10 +392,8 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
         const int kbl = gg * per + j;
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
-          // consecutive MMAs go to different accumulators so they do not wait on each other
           const uint64_t bd = tc_sdesc(xbase + static_cast<uint32_t>((kbl * 8 + 2 * s) * xrows * 16), lbo, 128);
-          const int a = n_mma % kTcAcc;
-          tc_mma_ts(dcol + a * kTcN, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, n_mma >= kTcAcc);
+          tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, n_mma > 0);
           ++n_mma;
         }
         tc_commit(&sh.empty[aslot]);
@@ -366,26 +408,96 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   for (int n = 0; n < kTcN; ++n) acc[n] = 0.f;
   const int r_local = warp * 32 + lane;
   const int row = rb * kRowBlock + r_local;
+  const uint32_t dlane = tmem + (static_cast<uint32_t>(warp * 32) << 16) + tc_dcol(wg);
   if (warp < 4) {
     const bool ok = __all_sync(0xffffffffu, tc_wait(&sh.dready, 0, &sh.broken));
     tc_fence_after();
     __syncwarp();
-    // the accumulators that received MMAs, summed in a fixed order
-    const int n_acc = min(kTcAcc, 4 * nkb);
-    for (int a = 0; a < n_acc; ++a) {
+    if (M <= kTcN) {
       uint32_t d[kTcN];
-      tc_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + tc_dcol(wg) + a * kTcN, d);
+      tc_ld16(dlane, d);
       tc_wait_ld();
 #pragma unroll
-      for (int n = 0; n < kTcN; ++n) acc[n] = a == 0 ? __uint_as_float(d[n]) : fadd(acc[n], __uint_as_float(d[n]));
+      for (int n = 0; n < kTcN; ++n) acc[n] = __uint_as_float(d[n]);
     }
     if (!ok && lane == 0 && io.err) atomicExch(io.err, 2);
   }
   grid_dep_launch();
 
-  // ---- K splits: partials, summed in split order by the last CTA --------------
   bool do_epi = true;
-  if (w.ksg > 1) {
+  if (M > kTcN) {
+    // ---- dense path (STORE): 16 activation rows at a time ------------------------
+    const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
+    const int n_mma = tc_n(M);
+    const bool valid = row < epi.n_out;
+    // partials row-major: part[(split * rows_pad + row) * n_mma + m], so a
+    // thread moves its row's values as independent 16-byte accesses
+    if (warp < 4) {
+      for (int q = 0; q < n_mma / 16; ++q) {
+        uint32_t d[16];
+        tc_ld16(dlane + 16 * q, d);
+        tc_wait_ld();
+        if (w.ksg > 1) {
+          float4* dst = reinterpret_cast<float4*>(part + (static_cast<size_t>(ks) * rows_pad + row) * n_mma + 16 * q);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_float4(__uint_as_float(d[4 * i]), __uint_as_float(d[4 * i + 1]),
+                                 __uint_as_float(d[4 * i + 2]), __uint_as_float(d[4 * i + 3]));
+        } else {
+#pragma unroll
+          for (int mm = 0; mm < 16; ++mm) {
+            const int m = 16 * q + mm;
+            if (m < M && valid) epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(__uint_as_float(d[mm]));
+          }
+        }
+      }
+    }
+    if (w.ksg > 1) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) sh.last = atomicAdd(&w.counters[rb], 1u) == static_cast<unsigned>(w.ksg - 1);
+      __syncthreads();
+      if (sh.last) {
+        __threadfence();
+        if (warp < 4 && valid)
+          for (int q = 0; q < n_mma / 16; ++q) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            // splits summed in order; four splits' loads in flight at a time
+            for (int sp0 = 0; sp0 < w.ksg; sp0 += 4) {
+              float4 ld[4][4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int sp = sp0 + j;
+                const float4* src = reinterpret_cast<const float4*>(part + (static_cast<size_t>(sp < w.ksg ? sp : 0) * rows_pad + row) * n_mma + 16 * q);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) ld[j][i] = sp < w.ksg ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (sp0 + j >= w.ksg) break;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  v[4 * i] = fadd(v[4 * i], ld[j][i].x);
+                  v[4 * i + 1] = fadd(v[4 * i + 1], ld[j][i].y);
+                  v[4 * i + 2] = fadd(v[4 * i + 2], ld[j][i].z);
+                  v[4 * i + 3] = fadd(v[4 * i + 3], ld[j][i].w);
+                }
+              }
+            }
+#pragma unroll
+            for (int mm = 0; mm < 16; ++mm) {
+              const int m = 16 * q + mm;
+              if (m < M) epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(v[mm]);
+            }
+          }
+        if (threadIdx.x == 0) atomicExch(&w.counters[rb], 0u);
+      }
+    }
+    do_epi = false;
+  } else if (w.ksg > 1) {
+    // ---- K splits: partials, summed in split order by the last CTA --------------
     const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
     if (warp < 4) {
 #pragma unroll
@@ -502,7 +614,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   __syncthreads();
   if (warp == n_dec) {
     __syncwarp();
-    tc_dealloc(tmem, tc_tmem_cols(wg));
+    tc_dealloc(tmem, tc_tmem_cols(wg, M));
   }
 }
 
@@ -576,8 +688,11 @@ __global__ void dequant_rows_kernel(QTile w, half* __restrict__ out) {
 }
 
 template <int BITS, int EPI>
-cudaError_t tc_launch_t(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
+cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                         const SplitScratch& scr, bool pdl, cudaStream_t st) {
+  const QTile w = tc_launch_shape(w_, M);
+  if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
+    return cudaErrorInvalidValue;
   const size_t smem = tc_gemv_smem_bytes(w, M);
   if (smem > kTcMaxSmem || w.wg < 1 || w.wg > kTcMaxWg) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
@@ -626,7 +741,8 @@ cudaError_t tc_gemv_init_attrs() {
 
 cudaError_t launch_tc_gemv(const QTile& w, const ActIn& in, int M, EpiKind kind, const Epi& epi,
                            const StepIO& io, const SplitScratch& scr, bool pdl, cudaStream_t st) {
-  if (M < 1 || M > kTcN || w.layout != kLayoutRow) return cudaErrorInvalidValue;
+  if (M < 1 || w.layout != kLayoutRow) return cudaErrorInvalidValue;
+  if (M > (kind == EPI_STORE ? kTcMaxN : kTcN)) return cudaErrorInvalidValue;   // fused epilogues: <= 16 rows
   if (w.bits == 4) return tc_dispatch<4>(kind, w, in, M, epi, io, scr, pdl, st);
   if (w.bits == 8) return tc_dispatch<8>(kind, w, in, M, epi, io, scr, pdl, st);
   return cudaErrorInvalidValue;

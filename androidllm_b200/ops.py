@@ -149,7 +149,8 @@ class QWeight:
         return out
 
     def matmul(self, x):
-        """fp16(x (m, in_real) . W^T), m <= 16, fp32 accumulation."""
+        """fp16(x (m, in_real) . W^T), fp32 accumulation; m <= 16, or m <= 256
+        for a weight uploaded in the row layout (tcgen05 MMAs)."""
         x = _f16(x)
         m = x.shape[0]
         xb = DeviceBuffer(self.ctx, x.nbytes)

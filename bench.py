@@ -420,8 +420,10 @@ SWEEP_M = (1, 5, 8, 16, 40, 128)
 
 
 def run_sweep(args):
-    """GB/s of the dequant-GEMV per (N, K, bits, M), graph-replayed launches
-    cycling over weight copies larger than L2; one JSON line per case."""
+    """GB/s and TFLOP/s of the dequant matmul per (N, K, bits, M),
+    graph-replayed launches cycling over weight copies larger than L2; one
+    JSON line per case.  M <= 16: the fused dequant-GEMV on the tile layout
+    (mma.sync); M > 16: the row layout's dense path (tcgen05 MMAs, N = M)."""
     from androidllm_b200.ops import Context, QuantProj, QWeight, bench_qmatmul
     from androidllm_b200.quant import codes_for_storage, quantize_matrix
     ctx = Context(0)
@@ -438,21 +440,53 @@ def run_sweep(args):
             del w, q
             per = n * k * bits // 8
             copies = max(2, min(12, int(400e6 // per) + 1))
-            ws = [QWeight(ctx, proj) for _ in range(copies)]
-            for m in ms:
-                rec = {"n": n, "k": k, "bits": bits, "m": m}
-                if m > 16:
-                    rec["note"] = "M > 16 needs the dense tcgen05 path (not built)"
-                    print(json.dumps(rec), flush=True)
+            for layout, sel in ((0, [m for m in ms if m <= 16]), (2, [m for m in ms if m > 16])):
+                if not sel:
                     continue
-                x = rng.standard_normal((m, k)).astype(np.float16)
-                us = bench_qmatmul(ctx, ws, x, 200)
-                alg = gemv_bytes(n, k, m, bits)
-                gbs = alg / us / 1e3
-                rec.update({"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
-                            "tflops": round(2 * m * n * k / us / 1e6, 2), "split": list(ws[0].split())})
-                print(json.dumps(rec), flush=True)
-            del ws
+                ctx.set_gemv_layout(layout)
+                ws = [QWeight(ctx, proj) for _ in range(copies)]
+                for m in sel:
+                    x = rng.standard_normal((m, k)).astype(np.float16)
+                    us = bench_qmatmul(ctx, ws, x, 200 if m <= 16 else 40)
+                    alg = gemv_bytes(n, k, m, bits)
+                    gbs = alg / us / 1e3
+                    tflops = 2 * m * n * k / us / 1e6
+                    rec = {"n": n, "k": k, "bits": bits, "m": m, "us": round(us, 2), "gbs": round(gbs, 1),
+                           "frac": round(gbs / peaks["hbm_gbs"], 3), "tflops": round(tflops, 2),
+                           "tensor_frac": round(tflops / peaks["bf16_tflops"], 3),
+                           "path": "gemv mma.sync (tile layout)" if layout == 0 else "tcgen05 (row layout)",
+                           "split": list(ws[0].split())}
+                    print(json.dumps(rec), flush=True)
+                del ws
+            ctx.set_gemv_layout(0)
+    return 0
+
+
+def run_mma_rate(args):
+    """Tensor-core instruction rates on this GPU (JSON lines): mma.sync
+    m16n8k16 cycles per instruction per SM by warps per SM and accumulator
+    chains; tcgen05.mma (M 128, K 16) ns per instruction by N, operand source
+    (A in tensor memory: TS, shared memory: SS) and accumulators."""
+    import ctypes
+    from androidllm_b200._lib import check, lib
+    from androidllm_b200.ops import Context
+    ctx = Context(0)
+    r = ctypes.c_double()
+    for warps in (4, 8, 16, 32):
+        for chains in (1, 2, 4, 8):
+            check(lib.alm_bench_mma_rate(ctx.h, 0, warps, chains, ctypes.byref(r)))
+            print(json.dumps({"mma": "mma.sync.m16n8k16.f32.f16", "warps_per_sm": warps, "chains": chains,
+                              "cycles_per_mma_per_sm": round(r.value, 3),
+                              "mac_per_clk_per_sm": round(16 * 8 * 16 / r.value, 1)}), flush=True)
+    for kind, form in ((1, "TS"), (2, "SS")):
+        for n in (16, 64, 128, 256):
+            for na in (1, 8):
+                if na * n > 256:
+                    continue
+                check(lib.alm_bench_mma_rate(ctx.h, kind, n, na, ctypes.byref(r)))
+                print(json.dumps({"mma": "tcgen05.mma.kind::f16 M128 K16", "form": form, "n": n, "accumulators": na,
+                                  "ns_per_mma": round(r.value, 2),
+                                  "tmac_per_s_per_sm": round(128 * n * 16 / r.value / 1e3, 3)}), flush=True)
     return 0
 
 
@@ -561,10 +595,15 @@ def summarize_ncu(path):
         if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
             continue
         name = r[ki]
-        m = re.search(r"gemv_kernel<\(int\)(\d+), \(int\)(\d+), \(int\)(\d+)>|gemv_kernel<(\d+), (\d+), (\d+)>", name)
+        m = re.search(r"(tc_gemv_kernel|gemv_kernel)<([^>]*)>", name)
         if m:
-            g = [x for x in m.groups() if x is not None]
-            name = f"gemv_kernel<int{g[0]}, nt8={g[1]}, {epi.get(g[2], g[2])}>"
+            g = re.findall(r"\d+", m.group(2))
+            if m.group(1) == "tc_gemv_kernel" and len(g) == 2:
+                name = f"tc_gemv_kernel<int{g[0]}, {epi.get(g[1], g[1])}>"
+            elif len(g) == 4:   # gemv_kernel<bits, scale sets, n8 tiles, epilogue>
+                name = f"gemv_kernel<int{g[0]}, nt8={g[2]}, {epi.get(g[3], g[3])}>"
+            elif len(g) == 3:
+                name = f"gemv_kernel<int{g[0]}, nt8={g[1]}, {epi.get(g[2], g[2])}>"
         else:
             name = re.sub(r"\(.*", "", name).split("::")[-1]
         agg[name][0] += 1
@@ -608,11 +647,14 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
     ap.add_argument("--sweep-m", default=",".join(str(m) for m in SWEEP_M))
     ap.add_argument("--gemv", metavar="N,K,BITS,M", help="time one GEMV shape repeatedly (profiling target)")
+    ap.add_argument("--mma-rate", action="store_true", help="tensor-core instruction rates (JSON lines)")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args)
     if args.gemv:
         return run_gemv(args)
+    if args.mma_rate:
+        return run_mma_rate(args)
     if args.summarize_ncu:
         return summarize_ncu(args.summarize_ncu)
     if args.profile:

@@ -97,7 +97,8 @@ ALM_API int alm_qweight_get_split(const alm_qweight* w, int* ksw, int* ksg, int*
 /* Replaces androidllm/quant.py:58-65 dequantize_packed (sliced to in_real):
  * writes fp16 (out, in_real) to out_host; bit-exact. */
 ALM_API int alm_qweight_dequant(alm_ctx* ctx, const alm_qweight* w, uint16_t* out_host);
-/* y(m, out) = fp16(x(m, in_real) . W^T), fp32 accumulation, 1 <= m <= 16.
+/* y(m, out) = fp16(x(m, in_real) . W^T), fp32 accumulation, 1 <= m <= 16
+   (1 <= m <= 256 for a weight in the row layout: tcgen05 MMAs with N = m).
  * Device buffers; row strides in elements. */
 ALM_API int alm_qmatmul(alm_ctx* ctx, const alm_qweight* w, const uint16_t* x_dev, int ldx, int m,
                 uint16_t* y_dev, int ldy);
@@ -250,6 +251,14 @@ ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitt
 /* Start (1) or stop (0) the CUDA profiler's capture range, so a profiler
  * started with capture disabled records only the work in between. */
 ALM_API int alm_profiler_range(int start);
+/* Tensor-core instruction rates (no reference counterpart; they decide which
+ * MMA each matmul path uses).  kind 0: mma.sync m16n8k16 with n_or_warps
+ * warps per SM and acc_or_chains (1, 2, 4, 8) accumulator chains per warp,
+ * *result = cycles per instruction per SM.  kind 1 / 2: tcgen05.mma
+ * kind::f16 M = 128, K = 16, A from tensor memory / shared memory, N =
+ * n_or_warps, rotating over acc_or_chains accumulators, *result = ns per
+ * instruction per SM. */
+ALM_API int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains, double* result);
 /* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
  * n_w weights of one shape (so their total can exceed L2); *avg_us is the
  * mean device time of one launch. */

@@ -181,3 +181,21 @@ def test_rows_spec_greedy_equals_plain_greedy(models):
     assert acc + bonus == 128
     print("toy (row layout): %d of 128 greedy tokens equal the reference's before the first difference"
           % next((i for i, (a, b) in enumerate(zip(plain, g["plain"].tolist())) if a != b), 128))
+
+
+@pytest.mark.parametrize("bits,shape,m", [(4, (2048, 1536), 17), (4, (2048, 1536), 40), (8, (2048, 1536), 128),
+                                          (4, (2048, 1536), 256), (8, (1536, 8960), 40), (8, (1536, 8960), 128),
+                                          (4, (18944, 3584), 128), (8, (1000, 704), 33)])
+def test_tc_dense_matches_fp32_reference(ctx, bits, shape, m):
+    """More than 16 activation rows: tcgen05 MMAs with N = m (rounded up to
+    16), K split across CTAs so the staged rows fit in shared memory."""
+    rng = np.random.default_rng([bits, m, *shape, 3])
+    n, k = shape
+    packed, scale = random_codes(rng, n, k, bits, 64)
+    w = _upload(ctx, packed, scale, bits, 64, n, k)
+    deq = oquant.dequantize_packed(packed, scale, {"bits": bits, "block": 64, "out": n, "in": k})
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    got = w.matmul(x)
+    ref = ref_matmul(x, deq)
+    assert rel_err(got, ref) < 1e-2
+    assert np.mean(ulp_diff(got, ref) > 1) < 2e-3
