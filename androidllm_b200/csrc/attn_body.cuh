@@ -34,13 +34,18 @@ constexpr int kAttnWarps = kAttnThreads / kWarp;
 constexpr int kPvRows = 4;   // query rows per P.V block
 constexpr int kPvVld = 24;   // V slice row stride (halves): conflict-free
 constexpr int kPvPld = kPvSpan + 8;   // P row stride (halves)
+// one load phase per span: V vectors and score float4s within one pass of the block
+static_assert(kPvSpan * 2 <= kAttnThreads * 8 && kPvRows * kPvSpan / 4 <= kAttnThreads * 4,
+              "P.V span exceeds a single load phase");
 
+// Dynamic shared memory of each pass; both end with the page numbers of the
+// positions they read (one per position at most: page_size >= 1).
 __host__ __device__ inline size_t attn_scores_smem(int hd) {
-  return static_cast<size_t>(2 * kAttnRows + kAttnChunk) * (hd + 8) * sizeof(half);
+  return static_cast<size_t>(2 * kAttnRows + kAttnChunk) * (hd + 8) * sizeof(half) + kAttnChunk * sizeof(int);
 }
 __host__ __device__ inline size_t attn_pv_smem() {
   return static_cast<size_t>(kPvSpan) * kPvVld * sizeof(half) + static_cast<size_t>(kPvRows) * kPvPld * sizeof(half) +
-         static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float);
+         static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float) + (kPvSpan + 1) * sizeof(int);
 }
 __host__ __device__ inline int attn_row_groups(const AttnArgs& a) {
   return (a.M * (a.heads / a.kv_heads) + kAttnRows - 1) / kAttnRows;
@@ -62,9 +67,18 @@ ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
 }
 
-ALM_DEV const half* kv_row(const half* cache, const int* pt, int page_size, int kv_heads, int kvh,
+// Page numbers of the positions [p_begin, p_end) -> s_pg (read from global
+// memory once, so every K / V load needs one round trip, not two).
+ALM_DEV void stage_pages(const AttnArgs& a, int p_begin, int p_end, int* s_pg) {
+  const int pg0 = p_begin / a.page_size;
+  const int n_pg = (p_end - 1) / a.page_size - pg0 + 1;
+  for (int i = threadIdx.x; i < n_pg; i += kAttnThreads) s_pg[i] = __ldcg(a.page_table + pg0 + i);
+}
+
+// Row of position pos (pages of the staged range start at page pg0).
+ALM_DEV const half* kv_row(const half* cache, const int* s_pg, int pg0, int page_size, int kv_heads, int kvh,
                            int hd, int pos) {
-  const int page = pt[pos / page_size];
+  const int page = s_pg[pos / page_size - pg0];
   return cache + ((static_cast<size_t>(page) * kv_heads + kvh) * page_size + pos % page_size) * hd;
 }
 
@@ -75,6 +89,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   half* qhi = reinterpret_cast<half*>(smem_raw);
   half* qlo = qhi + kAttnRows * ld;
   half* ks = qlo + kAttnRows * ld;   // [64][ld]
+  int* s_pg = reinterpret_cast<int*>(ks + kAttnChunk * ld);
 
   const int pos0 = *a.pos;
   const int n_ctx = pos0 + a.M;
@@ -84,6 +99,8 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   const int n_rows = a.M * gq;
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const int pg0 = c0 / a.page_size;
+  stage_pages(a, c0, min(c0 + kAttnChunk, n_ctx), s_pg);
 
   // Q rows -> fp16 hi/lo (float4 loads, all issued before use)
   {
@@ -117,6 +134,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       }
     }
   }
+  __syncthreads();   // page numbers
   // K chunk (16-byte vectors, all issued before use)
   {
     const int vec_per_row = hd / 8;
@@ -129,7 +147,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
         const int p = c0 + i / vec_per_row;
         v[j] = make_uint4(0, 0, 0, 0);
         if (i < nv && p < n_ctx)
-          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, a.page_table, a.page_size, a.kv_heads, kvh,
+          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, s_pg, pg0, a.page_size, a.kv_heads, kvh,
                                                               hd, p)) + i % vec_per_row);
       }
 #pragma unroll
@@ -236,6 +254,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
   half* ps = vs + kPvSpan * kPvVld;                  // [kPvRows][kPvPld]
   float* s_acc = reinterpret_cast<float*>(ps + kPvRows * kPvPld);   // [kAttnWarps][kWarp][8]
+  int* s_pg = reinterpret_cast<int*>(s_acc + kAttnWarps * kWarp * 8);   // pages of the current span
 
   const int hd = a.head_dim;
   const int pos0 = *a.pos;
@@ -250,16 +269,30 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
 
+  // page numbers of the first span, read while the statistics are
+  stage_pages(a, 0, min(kPvSpan, n_ctx), s_pg);
+
   // row max / sum from the chunk statistics: one warp per row, lane l takes
   // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
-  // a row's last position contribute exact zeros)
+  // a row's last position contribute exact zeros).  The first 128 chunks'
+  // statistics are read once and kept in registers for both passes.
   {
     const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
     for (int i = warp; i < kPvRows; i += kAttnWarps) {
       const int rl = rl0 + i;
-      float mc[4], lc[4];
+      float mc0[4], lc0[4], mc[4], lc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = j * 32 + lane;
+        const float2 v = c < n_chunks ? __ldcg(reinterpret_cast<const float2*>(st + (c * kAttnRows + rl) * 2))
+                                      : make_float2(kNegInf, 0.f);
+        mc0[j] = v.x;
+        lc0[j] = v.y;
+      }
       float mx = kNegInf;
-      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc0[j]);
+      for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = base + j * 32 + lane;
@@ -271,7 +304,10 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       float l = 0.f;
-      for (int base = 0; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (mc0[j] != kNegInf) l = fadd(l, fmul(lc0[j], expf(mc0[j] - mx)));
+      for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = base + j * 32 + lane;
@@ -297,53 +333,56 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   for (int base = 0; base < n_ctx; base += kPvSpan) {
     const int span = min(kPvSpan, n_ctx - base);
     const int span_pad = (span + 15) & ~15;
-    // V slice: 16 dims (two 16 B vectors) per position
-    const int nv = span_pad * 2;
-    for (int b0 = 0; b0 < nv; b0 += kAttnThreads * 8) {
-      uint4 v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = b0 + j * kAttnThreads + tid;
-        const int p = base + (i >> 1);
-        v[j] = make_uint4(0, 0, 0, 0);
-        if (i < nv && p < n_ctx)
-          v[j] = __ldcg(reinterpret_cast<const uint4*>(
-                            kv_row(a.vcache, a.page_table, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
-                        (i & 1));
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = b0 + j * kAttnThreads + tid;
-        if (i >= nv) break;
-        *reinterpret_cast<uint4*>(vs + (i >> 1) * kPvVld + (i & 1) * 8) = v[j];
-      }
+    if (base > 0) {   // the first span's pages were staged with the statistics
+      stage_pages(a, base, base + span, s_pg);
+      __syncthreads();
     }
-    // P = fp16(exp(s - max) / sum) for this block's rows, 4 scores per load
+    const int pg0 = base / a.page_size;
+    // One load phase for the V slice (16 dims = two 16 B vectors per
+    // position: span_pad * 2 <= kAttnThreads * 8 vectors) and this block's
+    // scores (kPvRows * span_pad / 4 <= kAttnThreads * 4 float4s).
+    const int nv = span_pad * 2;
     const int per_row4 = span_pad / 4;
     const int np = kPvRows * per_row4;
-    for (int b0 = 0; b0 < np; b0 += kAttnThreads * 4) {
-      float4 sv[4];
+    uint4 v[8];
+    float4 sv[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = b0 + j * kAttnThreads + tid;
-        const int i_row = i / per_row4, p = base + (i % per_row4) * 4;
-        sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
-        if (i < np && r0 + i_row < n_rows)
-          sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
-      }
+    for (int j = 0; j < 8; ++j) {
+      const int i = j * kAttnThreads + tid;
+      const int p = base + (i >> 1);
+      v[j] = make_uint4(0, 0, 0, 0);
+      if (i < nv && p < n_ctx)
+        v[j] = __ldcg(reinterpret_cast<const uint4*>(
+                          kv_row(a.vcache, s_pg, pg0, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
+                      (i & 1));
+    }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = b0 + j * kAttnThreads + tid;
-        if (i >= np) break;
-        const int i_row = i / per_row4, pl = (i % per_row4) * 4;
-        const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+    for (int j = 0; j < 4; ++j) {
+      const int i = j * kAttnThreads + tid;
+      const int i_row = i / per_row4, p = base + (i % per_row4) * 4;
+      sv[j] = make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+      if (i < np && r0 + i_row < n_rows)
+        sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
+    }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int p = base + pl + e;
-          float pv = 0.f;
-          if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - sh.pm[i_row]), sh.pl[i_row]);
-          ps[i_row * kPvPld + pl + e] = __float2half_rn(pv);
-        }
+    for (int j = 0; j < 8; ++j) {
+      const int i = j * kAttnThreads + tid;
+      if (i >= nv) break;
+      *reinterpret_cast<uint4*>(vs + (i >> 1) * kPvVld + (i & 1) * 8) = v[j];
+    }
+    // P = fp16(exp(s - max) / sum) for this block's rows
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = j * kAttnThreads + tid;
+      if (i >= np) break;
+      const int i_row = i / per_row4, pl = (i % per_row4) * 4;
+      const float e4[4] = {sv[j].x, sv[j].y, sv[j].z, sv[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int p = base + pl + e;
+        float pv = 0.f;
+        if (p < n_ctx && e4[e] != kNegInf) pv = fdiv(expf(e4[e] - sh.pm[i_row]), sh.pl[i_row]);
+        ps[i_row * kPvPld + pl + e] = __float2half_rn(pv);
       }
     }
     __syncthreads();
