@@ -7,6 +7,8 @@ namespace {
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, float inv_sqrt_den) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
+  attn_scores_pages(a, blockIdx.x, smem_raw);   // the page table is not written by earlier kernels
+  __syncthreads();
   grid_dep_wait();
   attn_scores_body(a, inv_sqrt_den, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.x, smem_raw, sh);
   grid_dep_launch();
@@ -15,6 +17,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
 __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
+  attn_pv_pages(a, smem_raw);
+  __syncthreads();
   grid_dep_wait();
   attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh);
 }

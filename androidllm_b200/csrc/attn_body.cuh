@@ -37,6 +37,11 @@ constexpr int kPvPld = kPvSpan + 8;   // P row stride (halves)
 // one load phase per span: V vectors and score float4s within one pass of the block
 static_assert(kPvSpan * 2 <= kAttnThreads * 8 && kPvRows * kPvSpan / 4 <= kAttnThreads * 4,
               "P.V span exceeds a single load phase");
+// P.V: one warp per query row for the statistics
+static_assert(kPvRows <= kAttnWarps, "one warp per P.V row");
+// scores: q rows and the K chunk of head_dim <= 256 in one load phase
+static_assert(kAttnRows * 256 / 4 <= kAttnThreads * 4 && kAttnChunk * 256 / 8 <= kAttnThreads * 8,
+              "scores staging exceeds a single load phase");
 
 // Dynamic shared memory of each pass; both end with the page numbers of the
 // positions they read (one per position at most: page_size >= 1).
@@ -82,14 +87,28 @@ ALM_DEV const half* kv_row(const half* cache, const int* s_pg, int pg0, int page
   return cache + ((static_cast<size_t>(page) * kv_heads + kvh) * page_size + pos % page_size) * hd;
 }
 
+// Page numbers a scores block may read: its chunk's span of the cache
+// capacity.  The page table does not change while kernels run, so this runs
+// before the block waits for the kernels that produce q and K; the caller
+// synchronises the block before attn_scores_body.
+ALM_DEV int* attn_scores_pg(const AttnArgs& a, unsigned char* smem_raw) {
+  return reinterpret_cast<int*>(smem_raw + static_cast<size_t>(2 * kAttnRows + kAttnChunk) * (a.head_dim + 8) *
+                                               sizeof(half));
+}
+ALM_DEV void attn_scores_pages(const AttnArgs& a, int chunk, unsigned char* smem_raw) {
+  const int c0 = chunk * kAttnChunk;
+  if (c0 < a.max_ctx) stage_pages(a, c0, min(c0 + kAttnChunk, a.max_ctx), attn_scores_pg(a, smem_raw));
+}
+
 // Scores of (chunk, kv head, row group); n_chunks_max = the grid's chunk count.
+// Precondition: attn_scores_pages for this chunk, then a block barrier.
 ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, int kvh, int rg, int n_chunks_max,
                               unsigned char* smem_raw, AttnShared& sh) {
   const int hd = a.head_dim, ld = hd + 8;
   half* qhi = reinterpret_cast<half*>(smem_raw);
   half* qlo = qhi + kAttnRows * ld;
   half* ks = qlo + kAttnRows * ld;   // [64][ld]
-  int* s_pg = reinterpret_cast<int*>(ks + kAttnChunk * ld);
+  const int* s_pg = attn_scores_pg(a, smem_raw);
 
   const int pos0 = *a.pos;
   const int n_ctx = pos0 + a.M;
@@ -100,63 +119,51 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const int pg0 = c0 / a.page_size;
-  stage_pages(a, c0, min(c0 + kAttnChunk, n_ctx), s_pg);
 
-  // Q rows -> fp16 hi/lo (float4 loads, all issued before use)
-  {
-    const int per_row = hd / 4;
-    const int n4 = kAttnRows * per_row;
-    for (int base = 0; base < n4; base += kAttnThreads * 4) {
-      float4 v[4];
+  // Q rows (-> fp16 hi/lo) and the K chunk: every load issued before any is
+  // used (one round trip); hd <= 256 keeps each within one pass of the block
+  const int per_row = hd / 4, n4 = kAttnRows * per_row;
+  const int vec_per_row = hd / 8, nv = kAttnChunk * vec_per_row;
+  float4 qv[4];
+  uint4 kv8[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        const int rl = i / per_row, d4 = i % per_row;
-        const int r = rg * kAttnRows + rl;
-        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n4 && r < n_rows) {
-          const int m = r / gq, head = kvh * gq + r % gq;
-          v[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        if (i >= n4) break;
-        const int rl = i / per_row, d = (i % per_row) * 4;
-        const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const half h = __float2half_rn(vv[e]);
-          qhi[rl * ld + d + e] = h;
-          qlo[rl * ld + d + e] = __float2half_rn(vv[e] - __half2float(h));
-        }
-      }
+  for (int j = 0; j < 4; ++j) {
+    const int i = j * kAttnThreads + tid;
+    const int rl = i / per_row, d4 = i % per_row;
+    const int r = rg * kAttnRows + rl;
+    qv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4 && r < n_rows) {
+      const int m = r / gq, head = kvh * gq + r % gq;
+      qv[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
     }
   }
-  __syncthreads();   // page numbers
-  // K chunk (16-byte vectors, all issued before use)
-  {
-    const int vec_per_row = hd / 8;
-    const int nv = kAttnChunk * vec_per_row;
-    for (int base = 0; base < nv; base += kAttnThreads * 8) {
-      uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        const int p = c0 + i / vec_per_row;
-        v[j] = make_uint4(0, 0, 0, 0);
-        if (i < nv && p < n_ctx)
-          v[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, s_pg, pg0, a.page_size, a.kv_heads, kvh,
-                                                              hd, p)) + i % vec_per_row);
-      }
+  for (int j = 0; j < 8; ++j) {
+    const int i = j * kAttnThreads + tid;
+    const int p = c0 + i / vec_per_row;
+    kv8[j] = make_uint4(0, 0, 0, 0);
+    if (i < nv && p < n_ctx)
+      kv8[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, s_pg, pg0, a.page_size, a.kv_heads, kvh, hd, p)) +
+                      i % vec_per_row);
+  }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int i = base + j * kAttnThreads + tid;
-        if (i >= nv) break;
-        *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = v[j];
-      }
+  for (int j = 0; j < 4; ++j) {
+    const int i = j * kAttnThreads + tid;
+    if (i >= n4) break;
+    const int rl = i / per_row, d = (i % per_row) * 4;
+    const float vv[4] = {qv[j].x, qv[j].y, qv[j].z, qv[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const half h = __float2half_rn(vv[e]);
+      qhi[rl * ld + d + e] = h;
+      qlo[rl * ld + d + e] = __float2half_rn(vv[e] - __half2float(h));
     }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = j * kAttnThreads + tid;
+    if (i >= nv) break;
+    *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = kv8[j];
   }
   __syncthreads();
 
@@ -249,12 +256,24 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
 // per block keep the exp/divide work of forming P small; the rows ride in an
 // m16 tile (rows >= kPvRows are zero) so the product still runs on tensor
 // cores.
+ALM_DEV int* attn_pv_pg(unsigned char* smem_raw) {
+  return reinterpret_cast<int*>(smem_raw + static_cast<size_t>(kPvSpan) * kPvVld * sizeof(half) +
+                                static_cast<size_t>(kPvRows) * kPvPld * sizeof(half) +
+                                static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float));
+}
+// Page numbers of the first span of positions a P.V block may read (before
+// the block waits for the scores pass; the caller synchronises the block).
+ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw) {
+  stage_pages(a, 0, min(kPvSpan, a.max_ctx), attn_pv_pg(smem_raw));
+}
+
+// Precondition: attn_pv_pages, then a block barrier.
 ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, int grp, unsigned char* smem_raw,
                           AttnShared& sh) {
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
   half* ps = vs + kPvSpan * kPvVld;                  // [kPvRows][kPvPld]
   float* s_acc = reinterpret_cast<float*>(ps + kPvRows * kPvPld);   // [kAttnWarps][kWarp][8]
-  int* s_pg = reinterpret_cast<int*>(s_acc + kAttnWarps * kWarp * 8);   // pages of the current span
+  int* s_pg = attn_pv_pg(smem_raw);                  // pages of the current span
 
   const int hd = a.head_dim;
   const int pos0 = *a.pos;
@@ -268,84 +287,16 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
+  const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
 
-  // page numbers of the first span, read while the statistics are
-  stage_pages(a, 0, min(kPvSpan, n_ctx), s_pg);
-
-  // row max / sum from the chunk statistics: one warp per row, lane l takes
-  // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
-  // a row's last position contribute exact zeros).  The first 128 chunks'
-  // statistics are read once and kept in registers for both passes.
-  {
-    const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
-    for (int i = warp; i < kPvRows; i += kAttnWarps) {
-      const int rl = rl0 + i;
-      float mc0[4], lc0[4], mc[4], lc[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = j * 32 + lane;
-        const float2 v = c < n_chunks ? __ldcg(reinterpret_cast<const float2*>(st + (c * kAttnRows + rl) * 2))
-                                      : make_float2(kNegInf, 0.f);
-        mc0[j] = v.x;
-        lc0[j] = v.y;
-      }
-      float mx = kNegInf;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc0[j]);
-      for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = base + j * 32 + lane;
-          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc[j]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float l = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (mc0[j] != kNegInf) l = fadd(l, fmul(lc0[j], expf(mc0[j] - mx)));
-      for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = base + j * 32 + lane;
-          mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
-          lc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2 + 1) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (mc[j] != kNegInf) l = fadd(l, fmul(lc[j], expf(mc[j] - mx)));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
-      if (lane == 0) {
-        sh.pm[i] = mx;
-        sh.pl[i] = l;
-      }
-    }
-  }
-  __syncthreads();
-
-  const int g = lane >> 2, t = lane & 3;
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for (int base = 0; base < n_ctx; base += kPvSpan) {
-    const int span = min(kPvSpan, n_ctx - base);
-    const int span_pad = (span + 15) & ~15;
-    if (base > 0) {   // the first span's pages were staged with the statistics
-      stage_pages(a, base, base + span, s_pg);
-      __syncthreads();
-    }
+  // One load phase for a span: the V slice (16 dims = two 16 B vectors per
+  // position: span_pad * 2 <= kAttnThreads * 8 vectors) and this block's
+  // scores (kPvRows * span_pad / 4 <= kAttnThreads * 4 float4s).
+  uint4 v[8];
+  float4 sv[4];
+  auto load_span = [&](int base, int span_pad) {
     const int pg0 = base / a.page_size;
-    // One load phase for the V slice (16 dims = two 16 B vectors per
-    // position: span_pad * 2 <= kAttnThreads * 8 vectors) and this block's
-    // scores (kPvRows * span_pad / 4 <= kAttnThreads * 4 float4s).
-    const int nv = span_pad * 2;
-    const int per_row4 = span_pad / 4;
-    const int np = kPvRows * per_row4;
-    uint4 v[8];
-    float4 sv[4];
+    const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int i = j * kAttnThreads + tid;
@@ -364,6 +315,79 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       if (i < np && r0 + i_row < n_rows)
         sv[j] = __ldcg(reinterpret_cast<const float4*>(a.scores + (srow0 + i_row) * a.score_ld + p));
     }
+  };
+
+  // statistics of the first 128 chunks (one warp per row) in the same load
+  // phase as the first span's V slice and scores
+  float mc0[4], lc0[4];
+  if (warp < kPvRows) {
+    const int rl = rl0 + warp;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = j * 32 + lane;
+      const float2 f = c < n_chunks ? __ldcg(reinterpret_cast<const float2*>(st + (c * kAttnRows + rl) * 2))
+                                    : make_float2(kNegInf, 0.f);
+      mc0[j] = f.x;
+      lc0[j] = f.y;
+    }
+  }
+  load_span(0, (min(kPvSpan, n_ctx) + 15) & ~15);
+
+  // row max / sum from the chunk statistics: one warp per row, lane l takes
+  // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
+  // a row's last position contribute exact zeros)
+  if (warp < kPvRows) {
+    const int rl = rl0 + warp;
+    float mc[4], lc[4];
+    float mx = kNegInf;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc0[j]);
+    for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = base + j * 32 + lane;
+        mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mx = fmaxf(mx, mc[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float l = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (mc0[j] != kNegInf) l = fadd(l, fmul(lc0[j], expf(mc0[j] - mx)));
+    for (int base = 32 * 4; base < n_chunks; base += 32 * 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = base + j * 32 + lane;
+        mc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2) : kNegInf;
+        lc[j] = c < n_chunks ? __ldcg(st + (c * kAttnRows + rl) * 2 + 1) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (mc[j] != kNegInf) l = fadd(l, fmul(lc[j], expf(mc[j] - mx)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l = fadd(l, __shfl_xor_sync(0xffffffffu, l, o));
+    if (lane == 0) {
+      sh.pm[warp] = mx;
+      sh.pl[warp] = l;
+    }
+  }
+  __syncthreads();
+
+  const int g = lane >> 2, t = lane & 3;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int base = 0; base < n_ctx; base += kPvSpan) {
+    const int span = min(kPvSpan, n_ctx - base);
+    const int span_pad = (span + 15) & ~15;
+    if (base > 0) {   // the first span was loaded with the statistics
+      stage_pages(a, base, base + span, s_pg);
+      __syncthreads();
+      load_span(base, span_pad);
+    }
+    const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int i = j * kAttnThreads + tid;

@@ -274,15 +274,21 @@ ALM_DEV void attention_phases(const FwdParams& P, GridSync& gs, int li) {
   const int kvh = a.kv_heads;
   const int n_chunks = (*a.pos + a.M + kAttnChunk - 1) / kAttnChunk;   // chunks holding positions
   const int nvb1 = n_chunks * kvh * n_rg;
-  for (int vb = blockIdx.x; vb < nvb1; vb += gridDim.x)
+  for (int vb = blockIdx.x; vb < nvb1; vb += gridDim.x) {
+    attn_scores_pages(a, vb % n_chunks, s_dyn);
+    __syncthreads();
     attn_scores_body(a, P.sqrt_hd, vb % n_chunks, (vb / n_chunks) % kvh, vb / (n_chunks * kvh), ncm, s_dyn,
                      s_fwd.a);
+  }
   gs.arrive();
   gs.wait();
   const int nds = a.head_dim / 16, npg = attn_pv_groups(a);
   const int nvb2 = nds * kvh * npg;
-  for (int vb = blockIdx.x; vb < nvb2; vb += gridDim.x)
+  for (int vb = blockIdx.x; vb < nvb2; vb += gridDim.x) {
+    attn_pv_pages(a, s_dyn);
+    __syncthreads();
     attn_pv_body(a, ncm, vb % nds, (vb / nds) % kvh, vb / (nds * kvh), s_dyn, s_fwd.a);
+  }
   gs.arrive();
 }
 
