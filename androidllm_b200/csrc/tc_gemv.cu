@@ -96,10 +96,19 @@ QTile tc_launch_shape(const QTile& w, int rows) {
   return d;
 }
 
+// Launch shape of the dense path with streamed activations: the weight's own
+// K split, one decoding warpgroup.
+QTile tc_stream_shape(const QTile& w) {
+  QTile d = w;
+  d.wg = 1;
+  return d;
+}
+
 size_t tc_part_floats(const QTile& w, int rows) {
-  const QTile d = tc_launch_shape(w, rows);
-  if (d.ksg <= 1) return 0;
-  return static_cast<size_t>(d.ksg) * tc_n(rows) * d.n_rb * kRowBlock;
+  size_t need = 0;
+  for (const QTile& d : {tc_launch_shape(w, rows), rows > kTcN ? tc_stream_shape(w) : w})
+    if (d.ksg > 1) need = std::max(need, static_cast<size_t>(d.ksg) * tc_n(rows) * d.n_rb * kRowBlock);
+  return need;
 }
 
 namespace {
@@ -175,6 +184,178 @@ ALM_DEV void tc_decode_record(const unsigned char* rec, int lane, uint32_t (&v)[
   }
 }
 
+// One decoding warp's weight stream: its records through a ring of bulk
+// copies (TMA engine, mbarrier completion, L2 evict-first).
+template <int BITS>
+struct TcWeightStream {
+  static constexpr int IPS = TcFmt<BITS>::kItems;
+  static constexpr int REC = TcFmt<BITS>::kParts * 512 + 64;
+  static constexpr int SLOT = IPS * REC;
+  unsigned char* ring = nullptr;
+  uint64_t* bar = nullptr;
+  const unsigned char* src = nullptr;
+  int cnt = 0;        // records (k-blocks)
+  int n_chunks = 0;   // ring chunks of IPS records
+  // lane 0: chunk c into ring slot c % kTcRingSlots
+  ALM_DEV void issue(int c) const {
+    const int slot = c % kTcRingSlots;
+    const uint32_t bytes = static_cast<uint32_t>(min(IPS, cnt - c * IPS) * REC);
+    mbar_expect_tx(&bar[slot], bytes);
+    bulk_g2s(ring + slot * SLOT, src + static_cast<size_t>(c) * IPS * REC, bytes, &bar[slot], l2_evict_first());
+  }
+  // lane 0: the first chunks (weights do not depend on earlier kernels)
+  ALM_DEV int issue_first() const {
+    for (int c = 0; c < n_chunks && c < kTcRingSlots; ++c) issue(c);
+    return min(n_chunks, kTcRingSlots);
+  }
+};
+
+// A decoding warp: decode its j-th record to exact fp16 rows and store them
+// with tcgen05.st into A slot g + wg * (j & 1) (lanes of a_base); arrive on
+// full[slot] once stored, wait on empty[slot] (the MMAs that read the slot's
+// previous contents) before storing again.  The store of record j completes
+// while record j + 1 is decoded.  On a wait that gives up: report it and let
+// every copy in flight land before the CTA's shared memory is released.
+template <int BITS>
+ALM_DEV void tc_decode_warp(const TcWeightStream<BITS>& ws, int issued, uint32_t a_base, int g, int wg,
+                            uint64_t* full, uint64_t* empty, volatile int* broken, int lane, int* err) {
+  constexpr int IPS = TcWeightStream<BITS>::IPS, REC = TcWeightStream<BITS>::REC;
+  constexpr int SLOT = TcWeightStream<BITS>::SLOT;
+  int rslot = 0;
+  uint32_t rphase = 0;
+  int waited = 0, stored = 0;
+  bool ok = true;
+  for (int j = 0; j < ws.cnt; ++j) {
+    const int jj = j % IPS, c = j / IPS;
+    if (jj == 0) {
+      ok = __all_sync(0xffffffffu, tc_wait(&ws.bar[rslot], rphase, broken));
+      if (!ok) break;
+      waited = c + 1;
+    }
+    uint32_t v[32];
+    tc_decode_record<BITS>(ws.ring + rslot * SLOT + jj * REC, lane, v);
+    if (j > 0) {
+      // the previous k-block's store finished while this one was decoded
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[g + wg * ((j - 1) & 1)]);
+    }
+    const int aslot = g + wg * (j & 1);
+    const int use = j >> 1;
+    if (use >= 1) {
+      ok = __all_sync(0xffffffffu, tc_wait(&empty[aslot], (use - 1) & 1, broken));
+      if (!ok) break;
+      tc_fence_after();
+    }
+    __syncwarp();
+    tc_st32(a_base + aslot * kTcSlotCols, v);
+    stored = j + 1;
+    if (jj == IPS - 1 || j == ws.cnt - 1) {
+      // the ring slot's reads are complete (their values went through tcgen05.st)
+      if (lane == 0 && c + kTcRingSlots < ws.n_chunks) {
+        fence_proxy_async_smem();
+        ws.issue(c + kTcRingSlots);
+        ++issued;
+      }
+      if (++rslot == kTcRingSlots) {
+        rslot = 0;
+        rphase ^= 1u;
+      }
+    }
+  }
+  if (stored > 0) {
+    tc_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (ok && lane == 0) mbar_arrive(&full[g + wg * ((stored - 1) & 1)]);
+  }
+  if (!ok) {
+    if (lane == 0 && err) atomicExch(err, 2);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    for (int c = waited; c < issued; ++c) mbar_wait(&ws.bar[c % kTcRingSlots], (c / kTcRingSlots) & 1u);
+  }
+}
+
+// Dense store epilogue (more than 16 rows): the accumulator (N = tc_n(M)
+// columns at dlane) read 16 activation rows at a time; with K split across
+// CTAs, row-major partials part[(split * rows_pad + row) * n_mma + m] (a
+// thread moves its row's values as independent 16-byte accesses), summed in
+// split order by the last CTA of the row block.  All threads of the CTA call
+// it (block barriers); warps 0-3 hold the rows.
+ALM_DEV void tc_dense_store(const QTile& w, int rb, int ks, int M, uint32_t dlane, half* out, int ldo, int n_out,
+                            float* __restrict__ part, int* s_last) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = rb * kRowBlock + warp * 32 + lane;
+  const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
+  const int n_mma = tc_n(M);
+  const bool valid = row < n_out;
+  if (warp < 4) {
+    for (int q = 0; q < n_mma / 16; ++q) {
+      uint32_t d[16];
+      tc_ld16(dlane + 16 * q, d);
+      tc_wait_ld();
+      if (w.ksg > 1) {
+        float4* dst = reinterpret_cast<float4*>(part + (static_cast<size_t>(ks) * rows_pad + row) * n_mma + 16 * q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_float4(__uint_as_float(d[4 * i]), __uint_as_float(d[4 * i + 1]),
+                               __uint_as_float(d[4 * i + 2]), __uint_as_float(d[4 * i + 3]));
+      } else {
+#pragma unroll
+        for (int mm = 0; mm < 16; ++mm) {
+          const int m = 16 * q + mm;
+          if (m < M && valid) out[static_cast<size_t>(m) * ldo + row] = __float2half_rn(__uint_as_float(d[mm]));
+        }
+      }
+    }
+  }
+  if (w.ksg > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *s_last = atomicAdd(&w.counters[rb], 1u) == static_cast<unsigned>(w.ksg - 1);
+    __syncthreads();
+    if (*s_last) {
+      __threadfence();
+      if (warp < 4 && valid)
+        for (int q = 0; q < n_mma / 16; ++q) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          // splits summed in order; four splits' loads in flight at a time
+          for (int sp0 = 0; sp0 < w.ksg; sp0 += 4) {
+            float4 ld[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int sp = sp0 + j;
+              const float4* src = reinterpret_cast<const float4*>(
+                  part + (static_cast<size_t>(sp < w.ksg ? sp : 0) * rows_pad + row) * n_mma + 16 * q);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) ld[j][i] = sp < w.ksg ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (sp0 + j >= w.ksg) break;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                v[4 * i] = fadd(v[4 * i], ld[j][i].x);
+                v[4 * i + 1] = fadd(v[4 * i + 1], ld[j][i].y);
+                v[4 * i + 2] = fadd(v[4 * i + 2], ld[j][i].z);
+                v[4 * i + 3] = fadd(v[4 * i + 3], ld[j][i].w);
+              }
+            }
+          }
+#pragma unroll
+          for (int mm = 0; mm < 16; ++mm) {
+            const int m = 16 * q + mm;
+            if (m < M) out[static_cast<size_t>(m) * ldo + row] = __float2half_rn(v[mm]);
+          }
+        }
+      if (threadIdx.x == 0) atomicExch(&w.counters[rb], 0u);
+    }
+  }
+}
+
 template <int BITS, int EPI>
 __global__ void __launch_bounds__(kTcMaxThreads, 1)
     tc_gemv_kernel(const __grid_constant__ QTile w, const __grid_constant__ ActIn in, int M,
@@ -219,21 +400,15 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   const int my0 = g * per;
   const int cnt = decoder ? max(0, min(per, nkb - my0)) : 0;
   const int n_chunks = (cnt + IPS - 1) / IPS;
-  const unsigned char* gsrc = reinterpret_cast<const unsigned char*>(
+  TcWeightStream<BITS> ws;
+  ws.src = reinterpret_cast<const unsigned char*>(
       w.data + (static_cast<size_t>(rb * 4 + grp) * w.k_blocks + cta_kb0 + my0) * w.rec_u4);
-  unsigned char* wring = rings + static_cast<size_t>(decoder ? warp : 0) * kTcRingSlots * SLOT;
-  uint64_t* rbar = sh.ring[decoder ? warp : 0];
-  auto issue = [&](int c) {
-    const int slot = c % kTcRingSlots;
-    const uint32_t bytes = static_cast<uint32_t>(min(IPS, cnt - c * IPS) * REC);
-    mbar_expect_tx(&rbar[slot], bytes);
-    bulk_g2s(wring + slot * SLOT, gsrc + static_cast<size_t>(c) * IPS * REC, bytes, &rbar[slot], l2_evict_first());
-  };
+  ws.ring = rings + static_cast<size_t>(decoder ? warp : 0) * kTcRingSlots * SLOT;
+  ws.bar = sh.ring[decoder ? warp : 0];
+  ws.cnt = cnt;
+  ws.n_chunks = n_chunks;
   int issued = 0;
-  if (decoder && lane == 0) {
-    for (int c = 0; c < n_chunks && c < kTcRingSlots; ++c) issue(c);
-    issued = min(n_chunks, kTcRingSlots);
-  }
+  if (decoder && lane == 0) issued = ws.issue_first();
 
   grid_dep_wait();
 
@@ -315,62 +490,8 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 
   // ---- decoding warps: records -> exact fp16 rows -> tensor memory -----------
   if (decoder) {
-    const uint32_t lane_base = static_cast<uint32_t>(grp * 32) << 16;
-    int rslot = 0;
-    uint32_t rphase = 0;
-    int waited = 0, stored = 0;
-    bool ok = true;
-    for (int j = 0; j < cnt; ++j) {
-      const int jj = j % IPS, c = j / IPS;
-      if (jj == 0) {
-        ok = __all_sync(0xffffffffu, tc_wait(&rbar[rslot], rphase, &sh.broken));
-        if (!ok) break;
-        waited = c + 1;
-      }
-      uint32_t v[32];
-      tc_decode_record<BITS>(wring + rslot * SLOT + jj * REC, lane, v);
-      if (j > 0) {
-        // the previous k-block's store finished while this one was decoded
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.full[g + wg * ((j - 1) & 1)]);
-      }
-      const int aslot = g + wg * (j & 1);
-      const int use = j >> 1;
-      if (use >= 1) {
-        ok = __all_sync(0xffffffffu, tc_wait(&sh.empty[aslot], (use - 1) & 1, &sh.broken));
-        if (!ok) break;
-        tc_fence_after();
-      }
-      __syncwarp();
-      tc_st32(tmem + lane_base + aslot * kTcSlotCols, v);
-      stored = j + 1;
-      if (jj == IPS - 1 || j == cnt - 1) {
-        // the ring slot's reads are complete (their values went through tcgen05.st)
-        if (lane == 0 && c + kTcRingSlots < n_chunks) {
-          fence_proxy_async_smem();
-          issue(c + kTcRingSlots);
-          ++issued;
-        }
-        if (++rslot == kTcRingSlots) {
-          rslot = 0;
-          rphase ^= 1u;
-        }
-      }
-    }
-    if (stored > 0) {
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&sh.full[g + wg * ((stored - 1) & 1)]);
-    }
-    if (!ok) {
-      // let every copy still in flight land before the CTA's shared memory is released
-      if (lane == 0 && io.err) atomicExch(io.err, 2);
-      issued = __shfl_sync(0xffffffffu, issued, 0);
-      for (int c = waited; c < issued; ++c) mbar_wait(&rbar[c % kTcRingSlots], (c / kTcRingSlots) & 1u);
-    }
+    tc_decode_warp<BITS>(ws, issued, tmem + (static_cast<uint32_t>(grp * 32) << 16), g, wg, sh.full, sh.empty,
+                         &sh.broken, lane, io.err);
   } else if (lane == 0) {
     // ---- issuing thread: MMAs in fixed order ----------------------------------
     const uint32_t idesc = tc_idesc_f16(kRowBlock, tc_n(M));
@@ -426,75 +547,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 
   bool do_epi = true;
   if (M > kTcN) {
-    // ---- dense path (STORE): 16 activation rows at a time ------------------------
-    const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
-    const int n_mma = tc_n(M);
-    const bool valid = row < epi.n_out;
-    // partials row-major: part[(split * rows_pad + row) * n_mma + m], so a
-    // thread moves its row's values as independent 16-byte accesses
-    if (warp < 4) {
-      for (int q = 0; q < n_mma / 16; ++q) {
-        uint32_t d[16];
-        tc_ld16(dlane + 16 * q, d);
-        tc_wait_ld();
-        if (w.ksg > 1) {
-          float4* dst = reinterpret_cast<float4*>(part + (static_cast<size_t>(ks) * rows_pad + row) * n_mma + 16 * q);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_float4(__uint_as_float(d[4 * i]), __uint_as_float(d[4 * i + 1]),
-                                 __uint_as_float(d[4 * i + 2]), __uint_as_float(d[4 * i + 3]));
-        } else {
-#pragma unroll
-          for (int mm = 0; mm < 16; ++mm) {
-            const int m = 16 * q + mm;
-            if (m < M && valid) epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(__uint_as_float(d[mm]));
-          }
-        }
-      }
-    }
-    if (w.ksg > 1) {
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) sh.last = atomicAdd(&w.counters[rb], 1u) == static_cast<unsigned>(w.ksg - 1);
-      __syncthreads();
-      if (sh.last) {
-        __threadfence();
-        if (warp < 4 && valid)
-          for (int q = 0; q < n_mma / 16; ++q) {
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            // splits summed in order; four splits' loads in flight at a time
-            for (int sp0 = 0; sp0 < w.ksg; sp0 += 4) {
-              float4 ld[4][4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int sp = sp0 + j;
-                const float4* src = reinterpret_cast<const float4*>(part + (static_cast<size_t>(sp < w.ksg ? sp : 0) * rows_pad + row) * n_mma + 16 * q);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) ld[j][i] = sp < w.ksg ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                if (sp0 + j >= w.ksg) break;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  v[4 * i] = fadd(v[4 * i], ld[j][i].x);
-                  v[4 * i + 1] = fadd(v[4 * i + 1], ld[j][i].y);
-                  v[4 * i + 2] = fadd(v[4 * i + 2], ld[j][i].z);
-                  v[4 * i + 3] = fadd(v[4 * i + 3], ld[j][i].w);
-                }
-              }
-            }
-#pragma unroll
-            for (int mm = 0; mm < 16; ++mm) {
-              const int m = 16 * q + mm;
-              if (m < M) epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(v[mm]);
-            }
-          }
-        if (threadIdx.x == 0) atomicExch(&w.counters[rb], 0u);
-      }
-    }
+    tc_dense_store(w, rb, ks, M, dlane, epi.out, epi.ldo, epi.n_out, part, &sh.last);
     do_epi = false;
   } else if (w.ksg > 1) {
     // ---- K splits: partials, summed in split order by the last CTA --------------
@@ -618,6 +671,179 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dense path with streamed activations (more than 16 raw, 16-byte aligned
+// rows, STORE): like tc_gemv_kernel with one decoding warpgroup, but the
+// activations are not staged for the whole K range.  A producer warp copies
+// each k-block's rows (8 chunks x N rows x 16 B, the MMA's core-matrix
+// layout) into a ring of kTcXSlots slots with cp.async; each lane's copies of
+// k-block j are complete kTcXAhead k-blocks later (cp.async.wait_group), when
+// the lane fences the generic-proxy writes for the tensor core and arrives on
+// xfull[j % kTcXSlots].  The issuing thread waits for the decoded weights
+// and the activations of k-block j, runs its four MMAs and commits both
+// slots free.  No K split is needed for shared memory's sake.
+// ---------------------------------------------------------------------------
+constexpr int kTcXSlots = 6;
+constexpr int kTcXAhead = 4;   // cp.async groups in flight per producer lane
+constexpr int kTcGemmThreads = 32 * 6;   // 4 decoding warps, the issuing warp, the producer warp
+static_assert(kTcXAhead < kTcXSlots, "the producer must not wait on a slot it has not released");
+
+struct TcGemmShared {
+  uint64_t full[kTcAPerWg], empty[kTcAPerWg];
+  uint64_t xfull[kTcXSlots], xempty[kTcXSlots];
+  uint64_t dready;
+  uint64_t ring[4][kTcRingSlots];
+  uint32_t tmem;
+  int broken;
+  int last;
+};
+
+__host__ __device__ inline size_t tc_gemm_smem_bytes(int bits, int rows) {
+  return static_cast<size_t>(kTcXSlots) * tc_n(rows) * 128 + static_cast<size_t>(4) * kTcRingSlots * tc_slot_bytes(bits);
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kTcGemmThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ QTile w, const __grid_constant__ ActIn in, int M, half* __restrict__ out,
+                   int ldo, int n_out, StepIO io, float* __restrict__ part) {
+  constexpr int IPS = TcFmt<BITS>::kItems;
+  constexpr int kIssuer = 4, kProducer = 5;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ TcGemmShared sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rb = blockIdx.x, ks = blockIdx.y;
+  const int cta_kb0 = ks * w.kps;
+  const int nkb = max(0, min(w.kps, w.k_blocks - cta_kb0));
+  const int n_mma = tc_n(M);
+  const uint32_t xslot_bytes = static_cast<uint32_t>(n_mma) * 128;
+  unsigned char* xring = smem;
+  unsigned char* rings = smem + static_cast<size_t>(kTcXSlots) * xslot_bytes;
+
+  // ---- set-up ---------------------------------------------------------------------
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcAPerWg; ++i) {
+      mbar_init(&sh.full[i], 4);
+      mbar_init(&sh.empty[i], 1);
+    }
+    for (int i = 0; i < kTcXSlots; ++i) {
+      mbar_init(&sh.xfull[i], kWarp);
+      mbar_init(&sh.xempty[i], 1);
+    }
+    mbar_init(&sh.dready, 1);
+    sh.broken = 0;
+  }
+  if (warp < 4 && lane == 0)
+    for (int i = 0; i < kTcRingSlots; ++i) mbar_init(&sh.ring[warp][i], 1);
+  if (lane == 0) fence_mbar_init();
+  if (warp == kIssuer) tc_alloc(&sh.tmem, tc_tmem_cols(1, M));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+
+  TcWeightStream<BITS> ws;
+  int issued = 0;
+  if (warp < 4) {
+    ws.src = reinterpret_cast<const unsigned char*>(
+        w.data + (static_cast<size_t>(rb * 4 + warp) * w.k_blocks + cta_kb0) * w.rec_u4);
+    ws.ring = rings + static_cast<size_t>(warp) * kTcRingSlots * TcWeightStream<BITS>::SLOT;
+    ws.bar = sh.ring[warp];
+    ws.cnt = nkb;
+    ws.n_chunks = (nkb + IPS - 1) / IPS;
+    if (lane == 0) issued = ws.issue_first();
+  }
+
+  grid_dep_wait();
+
+  if (warp < 4) {
+    tc_decode_warp<BITS>(ws, issued, tmem + (static_cast<uint32_t>(warp * 32) << 16), 0, 1, sh.full, sh.empty,
+                         &sh.broken, lane, io.err);
+  } else if (warp == kProducer) {
+    // ---- activations: k-block j -> ring slot j % kTcXSlots ------------------------
+    const int per_kb = 8 * n_mma;   // 16-byte copies per k-block
+    bool ok = true;
+    int arrived = 0;
+    for (int j = 0; j < nkb; ++j) {
+      const int xs = j % kTcXSlots, use = j / kTcXSlots;
+      if (use >= 1) {
+        ok = __all_sync(0xffffffffu, tc_wait(&sh.xempty[xs], (use - 1) & 1, &sh.broken));
+        if (!ok) break;
+      }
+      unsigned char* dst = xring + static_cast<size_t>(xs) * xslot_bytes;
+      const int kcol = (cta_kb0 + j) * 64;
+      // a warp covers 8 rows x 4 chunks: 64 contiguous bytes of each row,
+      // 4 runs of 128 contiguous bytes in shared memory
+      for (int e = lane; e < per_kb; e += kWarp) {
+        const int mi = e & 7, qi = (e >> 3) & 3, rest = e >> 5;
+        const int q = (rest & 1) * 4 + qi, m = (rest >> 1) * 8 + mi;
+        const int col0 = kcol + q * 8;
+        const int valid = m < M ? max(0, min(8, w.k_real - col0)) : 0;
+        const half* src = in.x + static_cast<size_t>(valid ? m : 0) * in.ld + (valid ? col0 : 0);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst + (q * n_mma + m) * 16)),
+                     "l"(src), "r"(valid * 2)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (j >= kTcXAhead) {
+        // this lane's copies of k-block j - kTcXAhead are complete
+        asm volatile("cp.async.wait_group %0;" ::"n"(kTcXAhead) : "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        mbar_arrive(&sh.xfull[(j - kTcXAhead) % kTcXSlots]);
+        arrived = j - kTcXAhead + 1;
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (ok)
+      for (int j = arrived; j < nkb; ++j) mbar_arrive(&sh.xfull[j % kTcXSlots]);
+    else if (lane == 0 && io.err)
+      atomicExch(io.err, 2);
+  } else if (lane == 0) {
+    // ---- issuing thread ---------------------------------------------------------
+    const uint32_t idesc = tc_idesc_f16(kRowBlock, n_mma);
+    const uint32_t dcol = tmem + tc_dcol(1);
+    const uint32_t xbase = smem_addr(xring);
+    const uint32_t lbo = static_cast<uint32_t>(n_mma) * 16;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int aslot = j & 1, xs = j % kTcXSlots;
+      ok = tc_wait(&sh.full[aslot], (j >> 1) & 1, &sh.broken) &&
+           tc_wait(&sh.xfull[xs], (j / kTcXSlots) & 1, &sh.broken);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const uint64_t bd = tc_sdesc(xbase + xs * xslot_bytes + static_cast<uint32_t>(2 * s) * lbo, lbo, 128);
+        tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, j > 0 || s > 0);
+      }
+      tc_commit(&sh.empty[aslot]);
+      tc_commit(&sh.xempty[xs]);
+    }
+    tc_commit(&sh.dready);
+    if (!ok && io.err) atomicExch(io.err, 2);
+  }
+
+  // ---- accumulator -> output ---------------------------------------------------------
+  const uint32_t dlane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + tc_dcol(1);
+  if (warp < 4) {
+    const bool ok = __all_sync(0xffffffffu, tc_wait(&sh.dready, 0, &sh.broken));
+    tc_fence_after();
+    __syncwarp();
+    if (!ok && lane == 0 && io.err) atomicExch(io.err, 2);
+  }
+  grid_dep_launch();
+  tc_dense_store(w, rb, ks, M, dlane, out, ldo, n_out, part, &sh.last);
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kIssuer) {
+    __syncwarp();
+    tc_dealloc(tmem, tc_tmem_cols(1, M));
+  }
+}
+
 // One thread per (record, row t): that row's codes and scale.
 __global__ void repack_rows_kernel(SrcSet s, const int* __restrict__ dst_src_row, int bits, int n_rb,
                                    int k_blocks, int k_pad, int block, int src_nsb, int rec_u4,
@@ -690,6 +916,23 @@ __global__ void dequant_rows_kernel(QTile w, half* __restrict__ out) {
 template <int BITS, int EPI>
 cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                         const SplitScratch& scr, bool pdl, cudaStream_t st) {
+  if (EPI == EPI_STORE && M > kTcN && in.ss == nullptr && in.vec) {
+    // dense, raw aligned rows: activations streamed per k-block
+    const QTile w = tc_stream_shape(w_);
+    if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
+      return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(w.n_rb, w.ksg, 1);
+    cfg.blockDim = dim3(kTcGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = tc_gemm_smem_bytes(BITS, M);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS>, w, in, M, epi.out, epi.ldo, epi.n_out, io, scr.part);
+  }
   const QTile w = tc_launch_shape(w_, M);
   if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
     return cudaErrorInvalidValue;
@@ -728,6 +971,7 @@ cudaError_t tc_set_attrs() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_RESID>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_SWIGLU>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_LOGITS>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemm_kernel<BITS>, a, v);
   return e;
 }
 

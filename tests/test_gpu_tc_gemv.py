@@ -199,3 +199,26 @@ def test_tc_dense_matches_fp32_reference(ctx, bits, shape, m):
     ref = ref_matmul(x, deq)
     assert rel_err(got, ref) < 1e-2
     assert np.mean(ulp_diff(got, ref) > 1) < 2e-3
+
+
+@pytest.mark.parametrize("m", [24, 96])
+def test_tc_dense_unaligned_rows(ctx, m):
+    """Activation rows with a stride that is not a multiple of 8 halves take
+    the staged dense path (the streamed one needs 16-byte aligned rows); both
+    agree with the fp32 reference."""
+    from androidllm_b200._lib import check, lib
+    from androidllm_b200.ops import DeviceBuffer
+    rng = np.random.default_rng([m, 9])
+    n, k, ldx = 1024, 1536, 1539
+    packed, scale = random_codes(rng, n, k, 4, 64)
+    w = _upload(ctx, packed, scale, 4, 64, n, k)
+    deq = oquant.dequantize_packed(packed, scale, {"bits": 4, "block": 64, "out": n, "in": k})
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    xp = np.zeros((m, ldx), np.float16)
+    xp[:, :k] = x
+    xb, yb = DeviceBuffer(ctx, xp.nbytes), DeviceBuffer(ctx, m * n * 2)
+    xb.upload(xp)
+    check(lib.alm_qmatmul(ctx.h, w.h, xb.h, ldx, m, yb.h, n))
+    got = yb.download(np.empty((m, n), np.float16))
+    assert rel_err(got, ref_matmul(x, deq)) < 1e-2
+    assert np.array_equal(got.view(np.uint16), w.matmul(x).view(np.uint16)) or rel_err(got, w.matmul(x)) < 1e-2
