@@ -3,9 +3,9 @@
 //   * mma.sync m16n8k16 (f16 in, f32 accumulate, register operands): cycles
 //     per instruction per SM with W warps per SM and C independent
 //     accumulator chains per warp;
-//   * tcgen05.mma kind::f16, M = 128, K = 16, one issuing thread per SM: ns
-//     per instruction for a given N, A from tensor memory (TS) or shared
-//     memory (SS), rotating over NA accumulators.
+//   * tcgen05.mma kind::f16, M = 128, K = 16, one issuing thread per CTA and
+//     one or two CTAs per SM: ns per instruction per CTA for a given N, A from
+//     tensor memory (TS) or shared memory (SS), rotating over NA accumulators.
 // Operands are constants; only the issue and completion rates are measured.
 #include <vector>
 
@@ -46,18 +46,20 @@ __global__ void hmma_rate_kernel(int iters, float* sink, unsigned long long* cyc
 }
 
 // 16 KB of shared memory: A (128 x 16 fp16, K-major core matrices) at 0,
-// B (up to 256 x 16) at 4096.  Tensor memory: A in columns 0..7, the
-// accumulators from column 256 (na * n <= 256).
-__global__ void tc_rate_kernel(int ts, int n, int na, int iters, unsigned long long* ns, int* status) {
+// B (up to 256 x 16) at 4096.  Tensor memory: `cols` columns (512 / ctas
+// per SM), A in columns 0..7, issuer i's `na` accumulators of n columns from
+// column 32 + i * na * n.  Issuer i is lane 0 of warp i.
+__global__ void tc_rate_kernel(int ts, int n, int na, int iters, int cols, int issuers, unsigned long long* ns,
+                               int* status) {
   extern __shared__ __align__(1024) unsigned char sm[];
   __shared__ uint32_t tbase;
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bar[4];
   const int warp = threadIdx.x / 32;
   for (int i = threadIdx.x; i < 12288 / 2; i += blockDim.x) reinterpret_cast<uint16_t*>(sm)[i] = 0x3c00;
   fence_proxy_async_smem();
-  if (warp == 0) tc_alloc(&tbase, 512);
+  if (warp == 0) tc_alloc(&tbase, cols);
   if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -68,19 +70,20 @@ __global__ void tc_rate_kernel(int ts, int n, int na, int iters, unsigned long l
     uint32_t r[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) r[c] = 0x3c003c00u;
-    tc_st32(tc_addr(t, warp * 32, 0), r);
+    if (warp < 4) tc_st32(tc_addr(t, warp * 32, 0), r);   // columns 0..31: A
     tc_wait_st();
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (warp < issuers && (threadIdx.x & 31) == 0) {
     tc_fence_after();
     const uint32_t idesc = tc_idesc_f16(128, n);
     const uint64_t adesc = tc_sdesc(smem_addr(sm), 128 * 16, 128);
     const uint64_t bdesc = tc_sdesc(smem_addr(sm) + 4096, static_cast<uint32_t>(n) * 16, 128);
+    const uint32_t d0 = t + 32 + static_cast<uint32_t>(warp * na * n);
     const unsigned long long t0 = global_ns();
     for (int i = 0; i < iters; ++i) {
-      const uint32_t d = t + 256 + static_cast<uint32_t>((i % na) * n);
+      const uint32_t d = d0 + static_cast<uint32_t>((i % na) * n);
       if (ts) {
         tc_mma_ts(d, t, bdesc, idesc, i >= na);
       } else {
@@ -91,15 +94,15 @@ __global__ void tc_rate_kernel(int ts, int n, int na, int iters, unsigned long l
             : "memory");
       }
     }
-    tc_commit(&bar);
-    if (!mbar_wait(&bar, 0)) atomicExch(status, 1);
-    ns[blockIdx.x] = global_ns() - t0;
+    tc_commit(&bar[warp]);
+    if (!mbar_wait(&bar[warp], 0)) atomicExch(status, 1);
+    ns[blockIdx.x * issuers + warp] = global_ns() - t0;
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
-    tc_dealloc(t, 512);
+    tc_dealloc(t, cols);
   }
 }
 
@@ -108,6 +111,57 @@ __global__ void tc_rate_kernel(int ts, int n, int na, int iters, unsigned long l
 
 int alm_internal_fail(int code, const char* msg);
 int alm_internal_ctx(alm_ctx* ctx, int* device, cudaStream_t* stream);
+
+namespace {
+// ns per tcgen05.mma of each issuing thread; 0 or an ALM error code.
+int tc_rate(cudaStream_t st, int n_sms, int ts, int n, int na, int ctas_per_sm, int issuers, double* result) {
+  using namespace alm;
+  const int cols = 512 / ctas_per_sm, iters = 2048;
+  if ((ctas_per_sm != 1 && ctas_per_sm != 2 && ctas_per_sm != 4) || issuers < 1 || issuers > 4 || n < 16 ||
+      n > 256 || n % 16 || na < 1 || issuers * na * n > cols - 32)
+    return alm_internal_fail(ALM_ERR_ARG,
+                             "tcgen05 rate: N multiple of 16 in 16..256, 1/2/4 CTAs per SM, 1..4 issuers, "
+                             "issuers * accumulators * N <= 512 / ctas_per_sm - 32");
+  const size_t n_rec = static_cast<size_t>(ctas_per_sm) * n_sms * issuers;
+  int* status = nullptr;
+  unsigned long long* dv = nullptr;
+  if (cudaMalloc(&status, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&dv, n_rec * sizeof(unsigned long long)) != cudaSuccess) {
+    cudaFree(status);
+    return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
+  }
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384);
+  for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
+    tc_rate_kernel<<<ctas_per_sm * n_sms, 128, 16384, st>>>(ts, n, na, iters, cols, issuers, dv, status);
+    e = cudaStreamSynchronize(st);
+  }
+  std::vector<unsigned long long> h(n_rec);
+  int hs = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&hs, status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(h.data(), dv, n_rec * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  double t = 0;
+  for (auto v : h) t += static_cast<double>(v);
+  *result = t / static_cast<double>(n_rec) / iters;
+  if (e == cudaSuccess && hs) e = cudaErrorTimeout;
+  cudaFree(status);
+  cudaFree(dv);
+  if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
+  return 0;
+}
+}  // namespace
+
+int alm_bench_tc_rate(alm_ctx* ctx, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
+                      double* ns_per_mma) {
+  if (!ctx || !ns_per_mma) return alm_internal_fail(ALM_ERR_ARG, "null argument");
+  int device = 0;
+  cudaStream_t st = nullptr;
+  int rc = alm_internal_ctx(ctx, &device, &st);
+  if (rc) return rc;
+  int n_sms = 148;
+  cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
+  return tc_rate(st, n_sms, ts ? 1 : 0, n, accumulators, ctas_per_sm, issuers, ns_per_mma);
+}
 
 int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains, double* result) {
   using namespace alm;
@@ -118,64 +172,34 @@ int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains
   if (rc) return rc;
   int n_sms = 148;
   cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
-  void* buf = nullptr;        // mma.sync sink: one float per thread
-  int* status = nullptr;
-  unsigned long long* dv = nullptr;   // per-CTA cycles or nanoseconds
-  if (cudaMalloc(&buf, static_cast<size_t>(n_sms) * 1024 * sizeof(float)) != cudaSuccess ||
-      cudaMalloc(&status, sizeof(int)) != cudaSuccess ||
+  if (kind == 1 || kind == 2) return tc_rate(st, n_sms, kind == 1 ? 1 : 0, n_or_warps, acc_or_chains, 1, 1, result);
+  if (kind != 0) return alm_internal_fail(ALM_ERR_ARG, "kind 0 (mma.sync), 1 (tcgen05 TS) or 2 (tcgen05 SS)");
+  const int warps = n_or_warps, chains = acc_or_chains, iters = 4096;
+  if (warps < 1 || warps > 32 || (chains != 1 && chains != 2 && chains != 4 && chains != 8))
+    return alm_internal_fail(ALM_ERR_ARG, "mma.sync rate: 1..32 warps, 1/2/4/8 chains");
+  float* sink = nullptr;
+  unsigned long long* dv = nullptr;   // per-CTA cycles
+  if (cudaMalloc(&sink, static_cast<size_t>(n_sms) * 1024 * sizeof(float)) != cudaSuccess ||
       cudaMalloc(&dv, static_cast<size_t>(n_sms) * sizeof(unsigned long long)) != cudaSuccess) {
-    cudaFree(buf);
-    cudaFree(status);
+    cudaFree(sink);
     return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
   }
-  cudaMemsetAsync(status, 0, sizeof(int), st);
-  std::vector<unsigned long long> h(n_sms);
   cudaError_t e = cudaSuccess;
-  if (kind == 0) {
-    const int warps = n_or_warps, chains = acc_or_chains, iters = 4096;
-    if (warps < 1 || warps > 32 || (chains != 1 && chains != 2 && chains != 4 && chains != 8)) {
-      cudaFree(buf);
-      cudaFree(status);
-      cudaFree(dv);
-      return alm_internal_fail(ALM_ERR_ARG, "mma.sync rate: 1..32 warps, 1/2/4/8 chains");
+  for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
+    switch (chains) {
+      case 1: hmma_rate_kernel<1><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
+      case 2: hmma_rate_kernel<2><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
+      case 4: hmma_rate_kernel<4><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
+      default: hmma_rate_kernel<8><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
     }
-    for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
-      float* sink = static_cast<float*>(buf);
-      switch (chains) {
-        case 1: hmma_rate_kernel<1><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
-        case 2: hmma_rate_kernel<2><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
-        case 4: hmma_rate_kernel<4><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
-        default: hmma_rate_kernel<8><<<n_sms, warps * 32, 0, st>>>(iters, sink, dv); break;
-      }
-      e = cudaStreamSynchronize(st);
-    }
-    if (e == cudaSuccess) e = cudaMemcpy(h.data(), dv, n_sms * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-    double c = 0;
-    for (auto v : h) c += static_cast<double>(v);
-    *result = c / n_sms / (static_cast<double>(iters) * chains * warps);   // cycles per MMA per SM
-  } else {
-    const int n = n_or_warps, na = acc_or_chains, iters = 2048;
-    if ((kind != 1 && kind != 2) || n < 16 || n > 256 || n % 16 || na < 1 || na * n > 256) {
-      cudaFree(buf);
-      cudaFree(status);
-      cudaFree(dv);
-      return alm_internal_fail(ALM_ERR_ARG, "tcgen05 rate: kind 1 (TS) or 2 (SS), N multiple of 16 in 16..256, acc*N <= 256");
-    }
-    e = cudaFuncSetAttribute(tc_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384);
-    for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
-      tc_rate_kernel<<<n_sms, 128, 16384, st>>>(kind == 1 ? 1 : 0, n, na, iters, dv, status);
-      e = cudaStreamSynchronize(st);
-    }
-    int hs = 0;
-    if (e == cudaSuccess) e = cudaMemcpy(&hs, status, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemcpy(h.data(), dv, n_sms * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-    double t = 0;
-    for (auto v : h) t += static_cast<double>(v);
-    *result = t / n_sms / iters;   // ns per MMA
-    if (e == cudaSuccess && hs) e = cudaErrorTimeout;
+    e = cudaStreamSynchronize(st);
   }
-  cudaFree(buf);
-  cudaFree(status);
+  std::vector<unsigned long long> h(n_sms);
+  if (e == cudaSuccess) e = cudaMemcpy(h.data(), dv, n_sms * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  double c = 0;
+  for (auto v : h) c += static_cast<double>(v);
+  *result = c / n_sms / (static_cast<double>(iters) * chains * warps);   // cycles per MMA per SM
+  cudaFree(sink);
   cudaFree(dv);
   if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
   return 0;

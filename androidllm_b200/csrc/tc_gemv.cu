@@ -31,6 +31,8 @@
 // 8 fp16: chunk q (8 columns) of row m at (q * xrows + m) * 16 bytes with
 // xrows = 8 for M <= 8 (rows 8..15 of an N = 16 MMA then read the next chunk:
 // finite values whose output columns are never stored) or 16.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 #include "act.cuh"
@@ -211,12 +213,12 @@ struct TcWeightStream {
 };
 
 // A decoding warp: decode its j-th record to exact fp16 rows and store them
-// with tcgen05.st into A slot g + wg * (j & 1) (lanes of a_base); arrive on
+// with tcgen05.st into A slot g + wg * (j % NA) (lanes of a_base); arrive on
 // full[slot] once stored, wait on empty[slot] (the MMAs that read the slot's
 // previous contents) before storing again.  The store of record j completes
 // while record j + 1 is decoded.  On a wait that gives up: report it and let
 // every copy in flight land before the CTA's shared memory is released.
-template <int BITS>
+template <int BITS, int NA = kTcAPerWg>
 ALM_DEV void tc_decode_warp(const TcWeightStream<BITS>& ws, int issued, uint32_t a_base, int g, int wg,
                             uint64_t* full, uint64_t* empty, volatile int* broken, int lane, int* err) {
   constexpr int IPS = TcWeightStream<BITS>::IPS, REC = TcWeightStream<BITS>::REC;
@@ -239,10 +241,10 @@ ALM_DEV void tc_decode_warp(const TcWeightStream<BITS>& ws, int issued, uint32_t
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full[g + wg * ((j - 1) & 1)]);
+      if (lane == 0) mbar_arrive(&full[g + wg * ((j - 1) % NA)]);
     }
-    const int aslot = g + wg * (j & 1);
-    const int use = j >> 1;
+    const int aslot = g + wg * (j % NA);
+    const int use = j / NA;
     if (use >= 1) {
       ok = __all_sync(0xffffffffu, tc_wait(&empty[aslot], (use - 1) & 1, broken));
       if (!ok) break;
@@ -268,7 +270,7 @@ ALM_DEV void tc_decode_warp(const TcWeightStream<BITS>& ws, int issued, uint32_t
     tc_wait_st();
     tc_fence_before();
     __syncwarp();
-    if (ok && lane == 0) mbar_arrive(&full[g + wg * ((stored - 1) & 1)]);
+    if (ok && lane == 0) mbar_arrive(&full[g + wg * ((stored - 1) % NA)]);
   }
   if (!ok) {
     if (lane == 0 && err) atomicExch(err, 2);
@@ -672,25 +674,28 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Dense path with streamed activations (more than 16 raw, 16-byte aligned
-// rows, STORE): like tc_gemv_kernel with one decoding warpgroup, but the
-// activations are not staged for the whole K range.  A producer warp copies
-// each k-block's rows (8 chunks x N rows x 16 B, the MMA's core-matrix
-// layout) into a ring of kTcXSlots slots with cp.async; each lane's copies of
-// k-block j are complete kTcXAhead k-blocks later (cp.async.wait_group), when
-// the lane fences the generic-proxy writes for the tensor core and arrives on
-// xfull[j % kTcXSlots].  The issuing thread waits for the decoded weights
-// and the activations of k-block j, runs its four MMAs and commits both
-// slots free.  No K split is needed for shared memory's sake.
+// Dense path with TMA-streamed activations (more than 16 raw rows, 16-byte
+// aligned, STORE): one decoding warpgroup per 128-row block, but the
+// activations are not staged for the whole K range.
+//   * A producer thread copies each k-block's activations (64 columns x N
+//     rows) with one TMA tensor copy into a ring slot in the canonical
+//     K-major SWIZZLE_128B layout (row r at r * 128 bytes, its 16-byte chunk c
+//     at c ^ (r % 8)); rows past M and columns past k_real read as zeros.  It
+//     waits only for a slot to be released by the MMAs that read it.
+//   * The four decoding warps write k-block j to tensor-memory A slot
+//     j % kTcGemmA; kTcGemmA slots let the decode of the next k-blocks run
+//     while the MMAs of the previous ones complete.
+//   * The issuing thread waits for both operands of k-block j, runs its four
+//     MMAs (M 128, N = M rounded up to 16, K 16) and commits both slots free.
+// K is split across CTAs only as the weight's own split says.
 // ---------------------------------------------------------------------------
-constexpr int kTcXSlots = 6;
-constexpr int kTcXAhead = 4;   // cp.async groups in flight per producer lane
+constexpr int kTcGemmA = 4;              // tensor-memory A slots
+constexpr int kTcGemmMaxXSlots = 8;      // activation ring slots (fewer for N > 128)
 constexpr int kTcGemmThreads = 32 * 6;   // 4 decoding warps, the issuing warp, the producer warp
-static_assert(kTcXAhead < kTcXSlots, "the producer must not wait on a slot it has not released");
 
 struct TcGemmShared {
-  uint64_t full[kTcAPerWg], empty[kTcAPerWg];
-  uint64_t xfull[kTcXSlots], xempty[kTcXSlots];
+  uint64_t full[kTcGemmA], empty[kTcGemmA];
+  uint64_t xfull[kTcGemmMaxXSlots], xempty[kTcGemmMaxXSlots];
   uint64_t dready;
   uint64_t ring[4][kTcRingSlots];
   uint32_t tmem;
@@ -698,35 +703,69 @@ struct TcGemmShared {
   int last;
 };
 
+// Tensor memory: A slots in columns [0, 128), the accumulator from 128.
+__host__ __device__ constexpr int tc_gemm_dcol() { return kTcGemmA * kTcSlotCols; }
+__host__ __device__ inline int tc_gemm_tmem_cols(int rows) { return tc_n(rows) <= 128 ? 256 : 512; }
+__host__ __device__ inline size_t tc_gemm_ring_bytes(int bits) {
+  return static_cast<size_t>(4) * kTcRingSlots * tc_slot_bytes(bits);
+}
+__host__ __device__ inline int tc_gemm_xslots(int bits, int rows) {
+  const size_t slot = static_cast<size_t>(tc_n(rows)) * 128;
+  const size_t n = (kTcMaxSmem - 1024 - tc_gemm_ring_bytes(bits)) / slot;
+  return static_cast<int>(n < kTcGemmMaxXSlots ? n : kTcGemmMaxXSlots);
+}
+// 1024 bytes of slack put the swizzled slots on a 1024-byte boundary.
 __host__ __device__ inline size_t tc_gemm_smem_bytes(int bits, int rows) {
-  return static_cast<size_t>(kTcXSlots) * tc_n(rows) * 128 + static_cast<size_t>(4) * kTcRingSlots * tc_slot_bytes(bits);
+  return 1024 + static_cast<size_t>(tc_gemm_xslots(bits, rows)) * tc_n(rows) * 128 + tc_gemm_ring_bytes(bits);
+}
+
+// Shared-memory descriptor of a K-major SWIZZLE_128B operand: 8-row groups
+// 1024 bytes apart; the leading byte offset is unused by this layout.  A K16
+// step inside the 128-byte swizzle span advances the start by 32 bytes.
+ALM_DEV uint64_t tc_sdesc_sw128(uint32_t smem_byte_addr) {
+  uint64_t d = static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1) << 16;            // LBO 16 bytes (unused)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;    // SBO
+  d |= static_cast<uint64_t>(1) << 46;            // descriptor version of sm_100
+  d |= static_cast<uint64_t>(2) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+ALM_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
 }
 
 template <int BITS>
 __global__ void __launch_bounds__(kTcGemmThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ QTile w, const __grid_constant__ ActIn in, int M, half* __restrict__ out,
-                   int ldo, int n_out, StepIO io, float* __restrict__ part) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ QTile w, int M,
+                   half* __restrict__ out, int ldo, int n_out, StepIO io, float* __restrict__ part) {
   constexpr int IPS = TcFmt<BITS>::kItems;
   constexpr int kIssuer = 4, kProducer = 5;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ TcGemmShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rb = blockIdx.x, ks = blockIdx.y;
   const int cta_kb0 = ks * w.kps;
   const int nkb = max(0, min(w.kps, w.k_blocks - cta_kb0));
   const int n_mma = tc_n(M);
+  const int n_xs = tc_gemm_xslots(BITS, M);
+  const int tcols = tc_gemm_tmem_cols(M);
   const uint32_t xslot_bytes = static_cast<uint32_t>(n_mma) * 128;
-  unsigned char* xring = smem;
-  unsigned char* rings = smem + static_cast<size_t>(kTcXSlots) * xslot_bytes;
+  unsigned char* xring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  unsigned char* rings = xring + static_cast<size_t>(n_xs) * xslot_bytes;
 
   // ---- set-up ---------------------------------------------------------------------
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcAPerWg; ++i) {
+    for (int i = 0; i < kTcGemmA; ++i) {
       mbar_init(&sh.full[i], 4);
       mbar_init(&sh.empty[i], 1);
     }
-    for (int i = 0; i < kTcXSlots; ++i) {
-      mbar_init(&sh.xfull[i], kWarp);
+    for (int i = 0; i < n_xs; ++i) {
+      mbar_init(&sh.xfull[i], 1);
       mbar_init(&sh.xempty[i], 1);
     }
     mbar_init(&sh.dready, 1);
@@ -734,8 +773,10 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
   }
   if (warp < 4 && lane == 0)
     for (int i = 0; i < kTcRingSlots; ++i) mbar_init(&sh.ring[warp][i], 1);
+  if (warp == kProducer && lane == 0)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
   if (lane == 0) fence_mbar_init();
-  if (warp == kIssuer) tc_alloc(&sh.tmem, tc_tmem_cols(1, M));
+  if (warp == kIssuer) tc_alloc(&sh.tmem, tcols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -756,77 +797,54 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
   grid_dep_wait();
 
   if (warp < 4) {
-    tc_decode_warp<BITS>(ws, issued, tmem + (static_cast<uint32_t>(warp * 32) << 16), 0, 1, sh.full, sh.empty,
-                         &sh.broken, lane, io.err);
+    tc_decode_warp<BITS, kTcGemmA>(ws, issued, tmem + (static_cast<uint32_t>(warp * 32) << 16), 0, 1, sh.full,
+                                   sh.empty, &sh.broken, lane, io.err);
   } else if (warp == kProducer) {
-    // ---- activations: k-block j -> ring slot j % kTcXSlots ------------------------
-    const int per_kb = 8 * n_mma;   // 16-byte copies per k-block
-    bool ok = true;
-    int arrived = 0;
-    for (int j = 0; j < nkb; ++j) {
-      const int xs = j % kTcXSlots, use = j / kTcXSlots;
-      if (use >= 1) {
-        ok = __all_sync(0xffffffffu, tc_wait(&sh.xempty[xs], (use - 1) & 1, &sh.broken));
-        if (!ok) break;
+    // ---- activations: k-block j -> ring slot j % n_xs -------------------------------
+    if (lane == 0) {
+      bool ok = true;
+      int sent = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int xs = j % n_xs, use = j / n_xs;
+        if (use >= 1 && !(ok = tc_wait(&sh.xempty[xs], (use - 1) & 1, &sh.broken))) break;
+        mbar_expect_tx(&sh.xfull[xs], xslot_bytes);
+        tma_load_2d(xring + static_cast<size_t>(xs) * xslot_bytes, &xmap, (cta_kb0 + j) * 64, 0, &sh.xfull[xs]);
+        sent = j + 1;
       }
-      unsigned char* dst = xring + static_cast<size_t>(xs) * xslot_bytes;
-      const int kcol = (cta_kb0 + j) * 64;
-      // a warp covers 8 rows x 4 chunks: 64 contiguous bytes of each row,
-      // 4 runs of 128 contiguous bytes in shared memory
-      for (int e = lane; e < per_kb; e += kWarp) {
-        const int mi = e & 7, qi = (e >> 3) & 3, rest = e >> 5;
-        const int q = (rest & 1) * 4 + qi, m = (rest >> 1) * 8 + mi;
-        const int col0 = kcol + q * 8;
-        const int valid = m < M ? max(0, min(8, w.k_real - col0)) : 0;
-        const half* src = in.x + static_cast<size_t>(valid ? m : 0) * in.ld + (valid ? col0 : 0);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst + (q * n_mma + m) * 16)),
-                     "l"(src), "r"(valid * 2)
-                     : "memory");
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      if (j >= kTcXAhead) {
-        // this lane's copies of k-block j - kTcXAhead are complete
-        asm volatile("cp.async.wait_group %0;" ::"n"(kTcXAhead) : "memory");
-        fence_proxy_async_smem();
-        __syncwarp();
-        mbar_arrive(&sh.xfull[(j - kTcXAhead) % kTcXSlots]);
-        arrived = j - kTcXAhead + 1;
+      if (!ok) {
+        if (io.err) atomicExch(io.err, 2);
+        // the copies still in flight land before the CTA's shared memory goes
+        for (int j = max(0, sent - n_xs); j < sent; ++j) mbar_wait(&sh.xfull[j % n_xs], (j / n_xs) & 1);
       }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (ok)
-      for (int j = arrived; j < nkb; ++j) mbar_arrive(&sh.xfull[j % kTcXSlots]);
-    else if (lane == 0 && io.err)
-      atomicExch(io.err, 2);
   } else if (lane == 0) {
     // ---- issuing thread ---------------------------------------------------------
     const uint32_t idesc = tc_idesc_f16(kRowBlock, n_mma);
-    const uint32_t dcol = tmem + tc_dcol(1);
+    const uint32_t dcol = tmem + tc_gemm_dcol();
     const uint32_t xbase = smem_addr(xring);
-    const uint32_t lbo = static_cast<uint32_t>(n_mma) * 16;
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
-      const int aslot = j & 1, xs = j % kTcXSlots;
-      ok = tc_wait(&sh.full[aslot], (j >> 1) & 1, &sh.broken) &&
-           tc_wait(&sh.xfull[xs], (j / kTcXSlots) & 1, &sh.broken);
+    for (int j = 0; j < nkb; ++j) {
+      const int aslot = j % kTcGemmA, xs = j % n_xs;
+      ok = tc_wait(&sh.full[aslot], (j / kTcGemmA) & 1, &sh.broken) &&
+           tc_wait(&sh.xfull[xs], (j / n_xs) & 1, &sh.broken);
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const uint64_t bd = tc_sdesc(xbase + xs * xslot_bytes + static_cast<uint32_t>(2 * s) * lbo, lbo, 128);
-        tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, j > 0 || s > 0);
-      }
+      for (int s = 0; s < 4; ++s)
+        tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s,
+                  tc_sdesc_sw128(xbase + xs * xslot_bytes + 32u * static_cast<uint32_t>(s)), idesc, j > 0 || s > 0);
       tc_commit(&sh.empty[aslot]);
       tc_commit(&sh.xempty[xs]);
     }
     tc_commit(&sh.dready);
-    if (!ok && io.err) atomicExch(io.err, 2);
+    if (!ok) {
+      if (io.err) atomicExch(io.err, 2);
+      mbar_wait(&sh.dready, 0);   // the MMAs issued so far finish before tensor memory is freed
+    }
   }
 
   // ---- accumulator -> output ---------------------------------------------------------
-  const uint32_t dlane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + tc_dcol(1);
+  const uint32_t dlane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + tc_gemm_dcol();
   if (warp < 4) {
     const bool ok = __all_sync(0xffffffffu, tc_wait(&sh.dready, 0, &sh.broken));
     tc_fence_after();
@@ -840,7 +858,7 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
   __syncthreads();
   if (warp == kIssuer) {
     __syncwarp();
-    tc_dealloc(tmem, tc_tmem_cols(1, M));
+    tc_dealloc(tmem, tcols);
   }
 }
 
@@ -913,11 +931,40 @@ __global__ void dequant_rows_kernel(QTile w, half* __restrict__ out) {
   }
 }
 
+// cuTensorMapEncodeTiled from the driver (resolved once; null if absent).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor map of M activation rows (k_real fp16 columns, row stride ld) read
+// as 64-column x N-row boxes in the SWIZZLE_128B K-major layout; elements
+// outside the matrix read as zeros.
+bool tc_encode_xmap(CUtensorMap* map, const half* x, int ld, int M, int k_real) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_real), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(half)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(tc_n(M))};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<half*>(x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BITS, int EPI>
 cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                         const SplitScratch& scr, bool pdl, cudaStream_t st) {
-  if (EPI == EPI_STORE && M > kTcN && in.ss == nullptr && in.vec) {
-    // dense, raw aligned rows: activations streamed per k-block
+  CUtensorMap xmap;
+  if (EPI == EPI_STORE && M > kTcN && in.ss == nullptr && in.vec && tc_encode_xmap(&xmap, in.x, in.ld, M, w_.k_real)) {
+    // dense, raw aligned rows: activations streamed per k-block by the TMA engine
     const QTile w = tc_stream_shape(w_);
     if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
       return cudaErrorInvalidValue;
@@ -931,7 +978,7 @@ cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS>, w, in, M, epi.out, epi.ldo, epi.n_out, io, scr.part);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part);
   }
   const QTile w = tc_launch_shape(w_, M);
   if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))

@@ -487,6 +487,17 @@ def run_mma_rate(args):
                 print(json.dumps({"mma": "tcgen05.mma.kind::f16 M128 K16", "form": form, "n": n, "accumulators": na,
                                   "ns_per_mma": round(r.value, 2),
                                   "tmac_per_s_per_sm": round(128 * n * 16 / r.value / 1e3, 3)}), flush=True)
+    # several issuing threads per SM: CTAs per SM x issuers per CTA (A in tensor memory)
+    for cps in (1, 2, 4):
+        for iss in (1, 2, 4):
+            for n in (16, 32, 64, 128, 256):
+                if iss * n > 512 // cps - 32:
+                    continue
+                check(lib.alm_bench_tc_rate(ctx.h, 1, n, 1, cps, iss, ctypes.byref(r)))
+                print(json.dumps({"mma": "tcgen05.mma.kind::f16 M128 K16", "form": "TS", "ctas_per_sm": cps,
+                                  "issuers_per_cta": iss, "n": n, "ns_per_mma": round(r.value, 2),
+                                  "tmac_per_s_per_sm": round(cps * iss * 128 * n * 16 / r.value / 1e3, 3)}),
+                      flush=True)
     return 0
 
 
@@ -495,6 +506,8 @@ def run_gemv(args):
     from androidllm_b200.ops import Context, QuantProj, QWeight, bench_qmatmul
     n, k, bits, m = (int(v) for v in args.gemv.split(","))
     ctx = Context(0)
+    if m > 16:
+        ctx.set_gemv_layout(2)   # more than 16 rows: the row layout's dense tcgen05 path
     rng = np.random.default_rng(0)
     q = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8) if bits == 4 else \
         rng.integers(-127, 128, size=(n, k), dtype=np.int8)

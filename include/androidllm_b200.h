@@ -256,9 +256,17 @@ ALM_API int alm_profiler_range(int start);
  * warps per SM and acc_or_chains (1, 2, 4, 8) accumulator chains per warp,
  * *result = cycles per instruction per SM.  kind 1 / 2: tcgen05.mma
  * kind::f16 M = 128, K = 16, A from tensor memory / shared memory, N =
- * n_or_warps, rotating over acc_or_chains accumulators, *result = ns per
- * instruction per SM. */
+ * n_or_warps, rotating over acc_or_chains accumulators, one CTA per SM,
+ * *result = ns per instruction. */
 ALM_API int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains, double* result);
+
+/* tcgen05.mma kind::f16 (M = 128, K = 16) issue rate with several issuers
+ * per SM: ctas_per_sm (1, 2, 4) CTAs on every SM, each with `issuers` (1..4)
+ * issuing threads in different warps, each rotating over `accumulators`
+ * accumulators of N = n columns (A from tensor memory if ts, else shared
+ * memory).  *ns_per_mma = ns per instruction of one issuing thread. */
+ALM_API int alm_bench_tc_rate(alm_ctx* ctx, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
+                              double* ns_per_mma);
 /* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
  * n_w weights of one shape (so their total can exceed L2); *avg_us is the
  * mean device time of one launch. */
