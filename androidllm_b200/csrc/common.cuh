@@ -35,6 +35,9 @@ ALM_DEV uint32_t ld_nc_u32(const void* p) {
 // hanging (a copy of valid memory completes in microseconds).
 constexpr unsigned kSpinLimit = 1u << 24;
 constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;
+// A waiting thread is suspended in hardware until the phase completes or at
+// most this long, so that waiting warps take no issue slots from working ones.
+constexpr uint32_t kSuspendNs = 20000;
 
 ALM_DEV unsigned long long global_ns() {
   unsigned long long t;
@@ -76,13 +79,24 @@ ALM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// As mbar_try_wait, suspending the thread until the phase completes or
+// kSuspendNs have passed.
+ALM_DEV bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase of `parity`; false if the limit ran out.
 ALM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (unsigned i = 1; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
   }
   return false;
 }

@@ -2,7 +2,8 @@
 // for M <= 16 activation rows, W in the row-record layout (kernels.cuh).
 //
 // One CTA covers 128 weight rows (one tcgen05 MMA tile, M = 128) over its K
-// range, with `wg` decoding warpgroups and one issuing warp:
+// range, with `wg` warpgroups, each of four decoding warps and one issuing
+// warp:
 //   * every decoding warp streams the records of its 32 rows (one tensor-
 //     memory lane quarter) through a ring of bulk copies (TMA engine,
 //     mbarrier completion, L2 evict-first), exactly like the tile-layout
@@ -11,15 +12,18 @@
 //     k-block to exact fp16 weights (the operations of the tile layout, so
 //     the weights equal androidllm's fp16(f32(q) * f32(scale))) and writes
 //     them to a tensor-memory A slot with one tcgen05.st (32 columns);
-//   * warpgroup g takes a contiguous run of the CTA's k-blocks and owns two A
-//     slots; after its four warps have stored a k-block, the issuing thread
+//   * warpgroup g takes a contiguous run of the CTA's k-blocks and owns three
+//     A slots; after its four warps have stored a k-block, its issuing thread
 //     runs four tcgen05.mma (M 128, N 16, K 16) from that slot against the
-//     activations staged in shared memory, accumulating in tensor memory, and
-//     tcgen05.commit frees the slot when the MMAs have read it;
-//   * the MMAs run in a fixed order (round j of warpgroup 0, 1, ..., then
-//     round j + 1), and every output column depends only on its own
-//     activation row, so a pass of M rows reproduces M single-row passes
-//     bit for bit;
+//     activations staged in shared memory, accumulating in the warpgroup's
+//     own tensor-memory accumulator, and tcgen05.commit frees the slot when
+//     the MMAs have read it.  An issuing thread completes about one MMA per
+//     110 ns whatever N is, and issuing threads run concurrently, so each
+//     warpgroup issues its own;
+//   * each accumulator sums its k-blocks in order, the accumulators are added
+//     in warpgroup order, and every output column depends only on its own
+//     activation row, so a pass of M rows reproduces M single-row passes bit
+//     for bit;
 //   * the accumulator is read back with tcgen05.ld (thread = row); K splits
 //     across CTAs are summed in split order by the last CTA of a row block;
 //     then the fused epilogues of the tile-layout GEMV (STORE, RESID,
@@ -45,9 +49,9 @@ namespace alm {
 constexpr int kTcN = 16;              // MMA N of the fused GEMV: activation rows, padded
 constexpr int kTcMaxN = 256;          // MMA N of the dense path (STORE, up to 256 rows)
 constexpr int kTcMaxWg = 4;           // decoding warpgroups per CTA
-constexpr int kTcMaxThreads = 32 * (4 * kTcMaxWg + 1);
+constexpr int kTcMaxThreads = 32 * 5 * kTcMaxWg;   // per warpgroup: 4 decoding warps + 1 issuing warp
 constexpr int kTcRingSlots = 3;       // weight ring slots per decoding warp
-constexpr int kTcAPerWg = 2;          // tensor-memory A slots per warpgroup
+constexpr int kTcAPerWg = 3;          // tensor-memory A slots per warpgroup
 constexpr int kTcSlotCols = 32;       // A slot: one k-block of fp16 pairs
 constexpr size_t kTcMaxSmem = 225 * 1024;
 constexpr int kTcStageBatch = 4;
@@ -63,15 +67,16 @@ __host__ __device__ inline int tc_parts(int bits) { return bits == 4 ? 2 : 4; }
 __host__ __device__ inline int tc_items(int bits) { return bits == 4 ? 2 : 1; }
 __host__ __device__ inline int tc_rec_bytes(int bits) { return tc_parts(bits) * 512 + 64; }
 __host__ __device__ inline int tc_slot_bytes(int bits) { return tc_items(bits) * tc_rec_bytes(bits); }
-__host__ __device__ inline int tc_threads(int wg) { return 32 * (4 * wg + 1); }
+__host__ __device__ inline int tc_threads(int wg) { return 32 * 5 * wg; }
 __host__ __device__ inline int tc_dcol(int wg) { return kTcAPerWg * wg * kTcSlotCols; }
 // MMA N for `rows` activation rows, and the rows staged per 8-column chunk
 // (8 for M <= 8: the MMA's rows 8..15 then read the next chunk).
 __host__ __device__ inline int tc_n(int rows) { return rows <= kTcN ? kTcN : (rows + 15) / 16 * 16; }
 __host__ __device__ inline int tc_xrows(int rows) { return rows <= 8 ? 8 : tc_n(rows); }
+// A slots, then one accumulator of tc_n(rows) columns per warpgroup.
 __host__ __device__ inline int tc_tmem_cols(int wg, int rows) {
   int c = 32;
-  while (c < tc_dcol(wg) + tc_n(rows)) c *= 2;
+  while (c < tc_dcol(wg) + wg * tc_n(rows)) c *= 2;
   return c;
 }
 __host__ __device__ inline size_t tc_stage_bytes(const QTile& w, int rows) {
@@ -118,7 +123,7 @@ namespace {
 struct TcShared {
   uint64_t full[kTcAPerWg * kTcMaxWg];    // A slot stored (4 warp arrivals)
   uint64_t empty[kTcAPerWg * kTcMaxWg];   // A slot read by its MMAs (commit)
-  uint64_t dready;                        // every MMA done (commit)
+  uint64_t dready;                        // every MMA done (one commit per issuing thread)
   uint64_t ring[4 * kTcMaxWg][kTcRingSlots];
   uint32_t tmem;
   int broken;                             // a bounded wait gave up: everyone stops waiting
@@ -134,11 +139,9 @@ ALM_DEV bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* broken) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (unsigned i = 1; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*broken) return false;
-      if (global_ns() - t0 > kWaitLimitNs) break;
-    }
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if (*broken) return false;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   *broken = 1;
   return false;
@@ -279,14 +282,15 @@ ALM_DEV void tc_decode_warp(const TcWeightStream<BITS>& ws, int issued, uint32_t
   }
 }
 
-// Dense store epilogue (more than 16 rows): the accumulator (N = tc_n(M)
-// columns at dlane) read 16 activation rows at a time; with K split across
+// Dense store epilogue (more than 16 rows): the n_acc accumulators (N =
+// tc_n(M) columns each, from dlane) read 16 activation rows at a time and
+// added in accumulator order; with K split across
 // CTAs, row-major partials part[(split * rows_pad + row) * n_mma + m] (a
 // thread moves its row's values as independent 16-byte accesses), summed in
 // split order by the last CTA of the row block.  All threads of the CTA call
 // it (block barriers); warps 0-3 hold the rows.
-ALM_DEV void tc_dense_store(const QTile& w, int rb, int ks, int M, uint32_t dlane, half* out, int ldo, int n_out,
-                            float* __restrict__ part, int* s_last) {
+ALM_DEV void tc_dense_store(const QTile& w, int rb, int ks, int M, uint32_t dlane, int n_acc, half* out, int ldo,
+                            int n_out, float* __restrict__ part, int* s_last) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = rb * kRowBlock + warp * 32 + lane;
   const size_t rows_pad = static_cast<size_t>(w.n_rb) * kRowBlock;
@@ -297,6 +301,13 @@ ALM_DEV void tc_dense_store(const QTile& w, int rb, int ks, int M, uint32_t dlan
       uint32_t d[16];
       tc_ld16(dlane + 16 * q, d);
       tc_wait_ld();
+      for (int a = 1; a < n_acc; ++a) {
+        uint32_t e[16];
+        tc_ld16(dlane + a * n_mma + 16 * q, e);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[i] = __float_as_uint(fadd(__uint_as_float(d[i]), __uint_as_float(e[i])));
+      }
       if (w.ksg > 1) {
         float4* dst = reinterpret_cast<float4*>(part + (static_cast<size_t>(ks) * rows_pad + row) * n_mma + 16 * q);
 #pragma unroll
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
       mbar_init(&sh.full[i], 4);
       mbar_init(&sh.empty[i], 1);
     }
-    mbar_init(&sh.dready, 1);
+    mbar_init(&sh.dready, wg);
     sh.broken = 0;
   }
   if (decoder && lane == 0)
@@ -495,34 +506,31 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
     tc_decode_warp<BITS>(ws, issued, tmem + (static_cast<uint32_t>(grp * 32) << 16), g, wg, sh.full, sh.empty,
                          &sh.broken, lane, io.err);
   } else if (lane == 0) {
-    // ---- issuing thread: MMAs in fixed order ----------------------------------
+    // ---- issuing thread of warpgroup gi: its k-blocks in order, own accumulator --
+    const int gi = warp - n_dec;
+    const int cg = max(0, min(per, nkb - gi * per));
     const uint32_t idesc = tc_idesc_f16(kRowBlock, tc_n(M));
-    const uint32_t dcol = tmem + tc_dcol(wg);
+    const uint32_t dcol = tmem + tc_dcol(wg) + gi * tc_n(M);
     const uint32_t xbase = smem_addr(xs);
     const uint32_t lbo = static_cast<uint32_t>(xrows) * 16;
     bool ok = true;
-    int n_mma = 0;
-    for (int j = 0; j < per && ok; ++j)
-      for (int gg = 0; gg < wg; ++gg) {
-        const int cg = max(0, min(per, nkb - gg * per));
-        if (j >= cg) continue;
-        const int aslot = gg + wg * (j & 1);
-        if (!tc_wait(&sh.full[aslot], (j >> 1) & 1, &sh.broken)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const int kbl = gg * per + j;
+    for (int j = 0; j < cg; ++j) {
+      const int aslot = gi + wg * (j % kTcAPerWg);
+      if (!(ok = tc_wait(&sh.full[aslot], (j / kTcAPerWg) & 1, &sh.broken))) break;
+      tc_fence_after();
+      const int kbl = gi * per + j;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const uint64_t bd = tc_sdesc(xbase + static_cast<uint32_t>((kbl * 8 + 2 * s) * xrows * 16), lbo, 128);
-          tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, n_mma > 0);
-          ++n_mma;
-        }
-        tc_commit(&sh.empty[aslot]);
+      for (int s = 0; s < 4; ++s) {
+        const uint64_t bd = tc_sdesc(xbase + static_cast<uint32_t>((kbl * 8 + 2 * s) * xrows * 16), lbo, 128);
+        tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s, bd, idesc, j > 0 || s > 0);
       }
+      tc_commit(&sh.empty[aslot]);
+    }
     tc_commit(&sh.dready);
-    if (!ok && io.err) atomicExch(io.err, 2);
+    if (!ok) {
+      if (io.err) atomicExch(io.err, 2);
+      mbar_wait(&sh.dready, 0);   // the MMAs issued so far finish before tensor memory is freed
+    }
   }
 
   // ---- accumulator -> registers (thread = row) ---------------------------------
@@ -537,11 +545,14 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
     tc_fence_after();
     __syncwarp();
     if (M <= kTcN) {
-      uint32_t d[kTcN];
-      tc_ld16(dlane, d);
-      tc_wait_ld();
+      // warpgroup accumulators summed in warpgroup order (those with k-blocks)
+      for (int gi = 0; gi < wg && gi * per < nkb; ++gi) {
+        uint32_t d[kTcN];
+        tc_ld16(dlane + gi * kTcN, d);
+        tc_wait_ld();
 #pragma unroll
-      for (int n = 0; n < kTcN; ++n) acc[n] = __uint_as_float(d[n]);
+        for (int n = 0; n < kTcN; ++n) acc[n] = gi == 0 ? __uint_as_float(d[n]) : fadd(acc[n], __uint_as_float(d[n]));
+      }
     }
     if (!ok && lane == 0 && io.err) atomicExch(io.err, 2);
   }
@@ -549,7 +560,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 
   bool do_epi = true;
   if (M > kTcN) {
-    tc_dense_store(w, rb, ks, M, dlane, epi.out, epi.ldo, epi.n_out, part, &sh.last);
+    tc_dense_store(w, rb, ks, M, dlane, 1, epi.out, epi.ldo, epi.n_out, part, &sh.last);
     do_epi = false;
   } else if (w.ksg > 1) {
     // ---- K splits: partials, summed in split order by the last CTA --------------
@@ -685,13 +696,20 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 //   * The four decoding warps write k-block j to tensor-memory A slot
 //     j % kTcGemmA; kTcGemmA slots let the decode of the next k-blocks run
 //     while the MMAs of the previous ones complete.
-//   * The issuing thread waits for both operands of k-block j, runs its four
-//     MMAs (M 128, N = M rounded up to 16, K 16) and commits both slots free.
+//   * n_iss issuing threads take the k-blocks in turn (thread i: j = i,
+//     i + n_iss, ...), each into its own tensor-memory accumulator: one
+//     issuing thread completes about one MMA per 110 ns for any N, and the
+//     SM's tensor pipe is full when the concurrent MMAs add up to N = 256, so
+//     n_iss = 4, 2 or 1 as 256 / N allows (a template parameter).  An issuing thread waits for both operands of
+//     its k-block, runs the four MMAs (M 128, N = M rounded up to 16, K 16)
+//     and commits both slots free.  The accumulators are added in issuer
+//     order by the epilogue.
 // K is split across CTAs only as the weight's own split says.
 // ---------------------------------------------------------------------------
 constexpr int kTcGemmA = 4;              // tensor-memory A slots
 constexpr int kTcGemmMaxXSlots = 8;      // activation ring slots (fewer for N > 128)
-constexpr int kTcGemmThreads = 32 * 6;   // 4 decoding warps, the issuing warp, the producer warp
+constexpr int kTcGemmMaxIss = 4;         // issuing threads (one per warp)
+constexpr int kTcGemmThreads = 32 * (4 + kTcGemmMaxIss + 1);   // at most: decoding, issuing, producer warps
 
 struct TcGemmShared {
   uint64_t full[kTcGemmA], empty[kTcGemmA];
@@ -700,12 +718,20 @@ struct TcGemmShared {
   uint64_t ring[4][kTcRingSlots];
   uint32_t tmem;
   int broken;
-  int last;
 };
 
-// Tensor memory: A slots in columns [0, 128), the accumulator from 128.
+// 1, 2 or 4 issuing threads, so that their MMAs add up to at most N = 256.
+__host__ __device__ inline int tc_gemm_issuers(int rows) {
+  const int n = 256 / tc_n(rows);
+  return n >= 4 ? 4 : n >= 2 ? 2 : 1;
+}
+// Tensor memory: A slots in columns [0, 128), then the issuers' accumulators.
 __host__ __device__ constexpr int tc_gemm_dcol() { return kTcGemmA * kTcSlotCols; }
-__host__ __device__ inline int tc_gemm_tmem_cols(int rows) { return tc_n(rows) <= 128 ? 256 : 512; }
+__host__ __device__ inline int tc_gemm_tmem_cols(int rows, int n_iss) {
+  int c = 32;
+  while (c < tc_gemm_dcol() + n_iss * tc_n(rows)) c *= 2;
+  return c;
+}
 __host__ __device__ inline size_t tc_gemm_ring_bytes(int bits) {
   return static_cast<size_t>(4) * kTcRingSlots * tc_slot_bytes(bits);
 }
@@ -739,12 +765,69 @@ ALM_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint
       : "memory");
 }
 
-template <int BITS>
+// Streamed dense epilogue (warps 0-3, thread = row): the n_acc accumulators
+// (N = tc_n(M) columns each, from dlane) added in accumulator order; one K
+// split stores fp16 outputs, several store fp32 partials
+// part[(ks * N + m) * rows_pad + row] (lanes along rows), summed in split
+// order by tc_split_reduce_kernel.
+ALM_DEV void tc_gemm_store(int rb, int ks, int ksg, int n_rb, int M, uint32_t dlane, int n_acc, half* out, int ldo,
+                           int n_out, float* __restrict__ part) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = rb * kRowBlock + warp * 32 + lane;
+  const size_t rows_pad = static_cast<size_t>(n_rb) * kRowBlock;
+  const int n_mma = tc_n(M);
+  for (int q = 0; q < n_mma / 16; ++q) {
+    uint32_t d[16];
+    tc_ld16(dlane + 16 * q, d);
+    tc_wait_ld();
+    for (int a = 1; a < n_acc; ++a) {
+      uint32_t e[16];
+      tc_ld16(dlane + a * n_mma + 16 * q, e);
+      tc_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d[i] = __float_as_uint(fadd(__uint_as_float(d[i]), __uint_as_float(e[i])));
+    }
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) {
+      const int m = 16 * q + mm;
+      if (m >= M) break;
+      if (ksg > 1)
+        part[(static_cast<size_t>(ks) * n_mma + m) * rows_pad + row] = __uint_as_float(d[mm]);
+      else if (row < n_out)
+        out[static_cast<size_t>(m) * ldo + row] = __float2half_rn(__uint_as_float(d[mm]));
+    }
+  }
+}
+
+// out[m][row] = fp16(sum of the K splits' partials in split order); one
+// thread per (row, m), lanes along rows.
+__global__ void __launch_bounds__(256) tc_split_reduce_kernel(const float* __restrict__ part, int ksg, int n_mma,
+                                                              int n_rb, int M, int n_out, half* __restrict__ out,
+                                                              int ldo) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int row = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (row >= n_out || m >= M) return;
+  const size_t rows_pad = static_cast<size_t>(n_rb) * kRowBlock;
+  const size_t stride = static_cast<size_t>(n_mma) * rows_pad;
+  const float* p = part + static_cast<size_t>(m) * rows_pad + row;
+  float sum = 0.f;
+  int sp = 0;
+  for (; sp + 4 <= ksg; sp += 4) {
+    const float v0 = __ldcg(p + sp * stride), v1 = __ldcg(p + (sp + 1) * stride);
+    const float v2 = __ldcg(p + (sp + 2) * stride), v3 = __ldcg(p + (sp + 3) * stride);
+    sum = fadd(fadd(fadd(fadd(sum, v0), v1), v2), v3);
+  }
+  for (; sp < ksg; ++sp) sum = fadd(sum, __ldcg(p + sp * stride));
+  out[static_cast<size_t>(m) * ldo + row] = __float2half_rn(sum);
+}
+
+template <int BITS, int NISS>
 __global__ void __launch_bounds__(kTcGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ QTile w, int M,
                    half* __restrict__ out, int ldo, int n_out, StepIO io, float* __restrict__ part) {
   constexpr int IPS = TcFmt<BITS>::kItems;
-  constexpr int kIssuer = 4, kProducer = 5;
+  constexpr int kIssuer = 4, kProducer = 4 + NISS;   // blockDim = 32 * (4 + NISS + 1)
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ TcGemmShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -753,7 +836,8 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
   const int nkb = max(0, min(w.kps, w.k_blocks - cta_kb0));
   const int n_mma = tc_n(M);
   const int n_xs = tc_gemm_xslots(BITS, M);
-  const int tcols = tc_gemm_tmem_cols(M);
+  constexpr int n_iss = NISS;   // tc_gemm_issuers(M) or fewer
+  const int tcols = tc_gemm_tmem_cols(M, n_iss);
   const uint32_t xslot_bytes = static_cast<uint32_t>(n_mma) * 128;
   unsigned char* xring = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   unsigned char* rings = xring + static_cast<size_t>(n_xs) * xslot_bytes;
@@ -768,7 +852,7 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
       mbar_init(&sh.xfull[i], 1);
       mbar_init(&sh.xempty[i], 1);
     }
-    mbar_init(&sh.dready, 1);
+    mbar_init(&sh.dready, n_iss);
     sh.broken = 0;
   }
   if (warp < 4 && lane == 0)
@@ -817,13 +901,14 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
         for (int j = max(0, sent - n_xs); j < sent; ++j) mbar_wait(&sh.xfull[j % n_xs], (j / n_xs) & 1);
       }
     }
-  } else if (lane == 0) {
-    // ---- issuing thread ---------------------------------------------------------
+  } else if (warp - kIssuer < n_iss && lane == 0) {
+    // ---- issuing thread i: k-blocks i, i + n_iss, ... into accumulator i ----------
+    const int iss = warp - kIssuer;
     const uint32_t idesc = tc_idesc_f16(kRowBlock, n_mma);
-    const uint32_t dcol = tmem + tc_gemm_dcol();
+    const uint32_t dcol = tmem + tc_gemm_dcol() + iss * n_mma;
     const uint32_t xbase = smem_addr(xring);
     bool ok = true;
-    for (int j = 0; j < nkb; ++j) {
+    for (int j = iss; j < nkb; j += n_iss) {
       const int aslot = j % kTcGemmA, xs = j % n_xs;
       ok = tc_wait(&sh.full[aslot], (j / kTcGemmA) & 1, &sh.broken) &&
            tc_wait(&sh.xfull[xs], (j / n_xs) & 1, &sh.broken);
@@ -832,7 +917,7 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
 #pragma unroll
       for (int s = 0; s < 4; ++s)
         tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s,
-                  tc_sdesc_sw128(xbase + xs * xslot_bytes + 32u * static_cast<uint32_t>(s)), idesc, j > 0 || s > 0);
+                  tc_sdesc_sw128(xbase + xs * xslot_bytes + 32u * static_cast<uint32_t>(s)), idesc, j > iss || s > 0);
       tc_commit(&sh.empty[aslot]);
       tc_commit(&sh.xempty[xs]);
     }
@@ -852,7 +937,7 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
     if (!ok && lane == 0 && io.err) atomicExch(io.err, 2);
   }
   grid_dep_launch();
-  tc_dense_store(w, rb, ks, M, dlane, out, ldo, n_out, part, &sh.last);
+  if (warp < 4) tc_gemm_store(rb, ks, w.ksg, w.n_rb, M, dlane, min(n_iss, nkb), out, ldo, n_out, part);
 
   tc_fence_before();
   __syncthreads();
@@ -966,11 +1051,9 @@ cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi,
   if (EPI == EPI_STORE && M > kTcN && in.ss == nullptr && in.vec && tc_encode_xmap(&xmap, in.x, in.ld, M, w_.k_real)) {
     // dense, raw aligned rows: activations streamed per k-block by the TMA engine
     const QTile w = tc_stream_shape(w_);
-    if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
-      return cudaErrorInvalidValue;
+    if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M))) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(w.n_rb, w.ksg, 1);
-    cfg.blockDim = dim3(kTcGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = tc_gemm_smem_bytes(BITS, M);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -978,7 +1061,19 @@ cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part);
+    const int n_iss = tc_gemm_issuers(M);
+    cfg.blockDim = dim3(32 * (4 + n_iss + 1), 1, 1);
+    cudaError_t e =
+        n_iss == 4   ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS, 4>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part)
+        : n_iss == 2 ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS, 2>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part)
+                     : cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS, 1>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part);
+    if (e != cudaSuccess || w.ksg == 1) return e;
+    // K splits: partials summed in split order across the whole GPU
+    cfg.gridDim = dim3((epi.n_out + 255) / 256, M, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, tc_split_reduce_kernel, static_cast<const float*>(scr.part), w.ksg, tc_n(M),
+                              w.n_rb, M, epi.n_out, epi.out, epi.ldo);
   }
   const QTile w = tc_launch_shape(w_, M);
   if (w.ksg > 1 && (scr.part == nullptr || scr.part_floats < tc_part_floats(w_, M) || w.counters == nullptr))
@@ -1018,7 +1113,9 @@ cudaError_t tc_set_attrs() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_RESID>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_SWIGLU>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemv_kernel<BITS, EPI_LOGITS>, a, v);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemm_kernel<BITS>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemm_kernel<BITS, 1>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemm_kernel<BITS, 2>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_gemm_kernel<BITS, 4>, a, v);
   return e;
 }
 

@@ -430,7 +430,9 @@ def run_sweep(args):
     peaks = load_peaks()
     rng = np.random.default_rng(3)
     ms = [int(x) for x in args.sweep_m.split(",")]
-    for n, k in SWEEP_SHAPES:
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.sweep_shapes.split(",")] if args.sweep_shapes \
+        else SWEEP_SHAPES
+    for n, k in shapes:
         for bits in (4, 8):
             # quantize one N(0, 0.02) matrix with the format's own quantizer,
             # then copy it so the rotation exceeds the 126 MB L2
@@ -440,7 +442,9 @@ def run_sweep(args):
             del w, q
             per = n * k * bits // 8
             copies = max(2, min(12, int(400e6 // per) + 1))
-            for layout, sel in ((0, [m for m in ms if m <= 16]), (2, [m for m in ms if m > 16])):
+            plan = ((2, ms),) if args.sweep_layout == "row" else \
+                ((0, [m for m in ms if m <= 16]), (2, [m for m in ms if m > 16]))
+            for layout, sel in plan:
                 if not sel:
                     continue
                 ctx.set_gemv_layout(layout)
@@ -506,8 +510,8 @@ def run_gemv(args):
     from androidllm_b200.ops import Context, QuantProj, QWeight, bench_qmatmul
     n, k, bits, m = (int(v) for v in args.gemv.split(","))
     ctx = Context(0)
-    if m > 16:
-        ctx.set_gemv_layout(2)   # more than 16 rows: the row layout's dense tcgen05 path
+    if m > 16 or args.sweep_layout == "row":
+        ctx.set_gemv_layout(2)   # the row layout (tcgen05); always for more than 16 rows
     rng = np.random.default_rng(0)
     q = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8) if bits == 4 else \
         rng.integers(-127, 128, size=(n, k), dtype=np.int8)
@@ -659,6 +663,9 @@ def main():
                     help="run N traced persistent forwards per model and print the phase timeline")
     ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
     ap.add_argument("--sweep-m", default=",".join(str(m) for m in SWEEP_M))
+    ap.add_argument("--sweep-shapes", default="", metavar="NxK,...", help="sweep only these weight shapes")
+    ap.add_argument("--sweep-layout", choices=("auto", "row"), default="auto",
+                    help="auto: tile layout (mma.sync) up to 16 rows, row layout (tcgen05) above; row: row layout for all")
     ap.add_argument("--gemv", metavar="N,K,BITS,M", help="time one GEMV shape repeatedly (profiling target)")
     ap.add_argument("--mma-rate", action="store_true", help="tensor-core instruction rates (JSON lines)")
     args = ap.parse_args()

@@ -185,10 +185,13 @@ def test_rows_spec_greedy_equals_plain_greedy(models):
 
 @pytest.mark.parametrize("bits,shape,m", [(4, (2048, 1536), 17), (4, (2048, 1536), 40), (8, (2048, 1536), 128),
                                           (4, (2048, 1536), 256), (8, (1536, 8960), 40), (8, (1536, 8960), 128),
-                                          (4, (18944, 3584), 128), (8, (1000, 704), 33)])
+                                          (4, (18944, 3584), 128), (8, (1000, 704), 33), (4, (40000, 1536), 40),
+                                          (8, (40000, 1536), 256)])
 def test_tc_dense_matches_fp32_reference(ctx, bits, shape, m):
     """More than 16 activation rows: tcgen05 MMAs with N = m (rounded up to
-    16), K split across CTAs so the staged rows fit in shared memory."""
+    16) against activations streamed per k-block; 1, 2 or 4 issuing threads
+    (fewer on grids of several waves), K splits summed by a separate
+    kernel."""
     rng = np.random.default_rng([bits, m, *shape, 3])
     n, k = shape
     packed, scale = random_codes(rng, n, k, bits, 64)
