@@ -693,39 +693,56 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 //     K-major SWIZZLE_128B layout (row r at r * 128 bytes, its 16-byte chunk c
 //     at c ^ (r % 8)); rows past M and columns past k_real read as zeros.  It
 //     waits only for a slot to be released by the MMAs that read it.
-//   * The four decoding warps write k-block j to tensor-memory A slot
-//     j % kTcGemmA; kTcGemmA slots let the decode of the next k-blocks run
-//     while the MMAs of the previous ones complete.
+//   * Two warpgroups of four decoding warps take the two halves of the
+//     CTA's k-blocks (each warp its 32-row lane quarter, its own weight
+//     stream); warpgroup h writes its j-th k-block to tensor-memory A slot
+//     h + 2 * (j % 3), so three k-blocks per warpgroup are decoded while the
+//     MMAs of earlier ones complete.  Producer and issuing threads walk the
+//     k-blocks in one interleaved sequence (h0 j0, h1 j0, h0 j1, ...).
 //   * n_iss issuing threads take the k-blocks in turn (thread i: j = i,
 //     i + n_iss, ...), each into its own tensor-memory accumulator: one
 //     issuing thread completes about one MMA per 110 ns for any N, and the
 //     SM's tensor pipe is full when the concurrent MMAs add up to N = 256, so
-//     n_iss = 4, 2 or 1 as 256 / N allows (a template parameter).  An issuing thread waits for both operands of
-//     its k-block, runs the four MMAs (M 128, N = M rounded up to 16, K 16)
-//     and commits both slots free.  The accumulators are added in issuer
-//     order by the epilogue.
+//     n_iss = 4, 2 or 1 as 256 / N allows (a template parameter).  An
+//     issuing thread waits for both operands of its k-block, runs the four
+//     MMAs (M 128, N = M rounded up to 16, K 16) and commits both slots
+//     free.  The accumulators are added in issuer order by the epilogue.
 // K is split across CTAs only as the weight's own split says.
 // ---------------------------------------------------------------------------
-constexpr int kTcGemmA = 4;              // tensor-memory A slots
+constexpr int kTcGemmDec = 8;            // decoding warps (two warpgroups)
+constexpr int kTcGemmAPerWg = 3;         // tensor-memory A slots per decoding warpgroup
+constexpr int kTcGemmA = 2 * kTcGemmAPerWg;
 constexpr int kTcGemmMaxXSlots = 8;      // activation ring slots (fewer for N > 128)
 constexpr int kTcGemmMaxIss = 4;         // issuing threads (one per warp)
-constexpr int kTcGemmThreads = 32 * (4 + kTcGemmMaxIss + 1);   // at most: decoding, issuing, producer warps
+constexpr int kTcGemmThreads = 32 * (kTcGemmDec + kTcGemmMaxIss + 1);   // at most: decoding, issuing, producer
 
 struct TcGemmShared {
   uint64_t full[kTcGemmA], empty[kTcGemmA];
   uint64_t xfull[kTcGemmMaxXSlots], xempty[kTcGemmMaxXSlots];
   uint64_t dready;
-  uint64_t ring[4][kTcRingSlots];
+  uint64_t ring[kTcGemmDec][kTcRingSlots];
   uint32_t tmem;
   int broken;
 };
+
+// Position q of the interleaved k-block sequence -> (warpgroup h, its j-th
+// k-block); warpgroup 1 has cnt1 k-blocks, warpgroup 0 cnt1 or cnt1 + 1.
+ALM_DEV void tc_gemm_pos(int q, int cnt1, int& h, int& j) {
+  if (q < 2 * cnt1) {
+    h = q & 1;
+    j = q >> 1;
+  } else {
+    h = 0;
+    j = q - cnt1;
+  }
+}
 
 // 1, 2 or 4 issuing threads, so that their MMAs add up to at most N = 256.
 __host__ __device__ inline int tc_gemm_issuers(int rows) {
   const int n = 256 / tc_n(rows);
   return n >= 4 ? 4 : n >= 2 ? 2 : 1;
 }
-// Tensor memory: A slots in columns [0, 128), then the issuers' accumulators.
+// Tensor memory: A slots in columns [0, 192), then the issuers' accumulators.
 __host__ __device__ constexpr int tc_gemm_dcol() { return kTcGemmA * kTcSlotCols; }
 __host__ __device__ inline int tc_gemm_tmem_cols(int rows, int n_iss) {
   int c = 32;
@@ -733,7 +750,7 @@ __host__ __device__ inline int tc_gemm_tmem_cols(int rows, int n_iss) {
   return c;
 }
 __host__ __device__ inline size_t tc_gemm_ring_bytes(int bits) {
-  return static_cast<size_t>(4) * kTcRingSlots * tc_slot_bytes(bits);
+  return static_cast<size_t>(kTcGemmDec) * kTcRingSlots * tc_slot_bytes(bits);
 }
 __host__ __device__ inline int tc_gemm_xslots(int bits, int rows) {
   const size_t slot = static_cast<size_t>(tc_n(rows)) * 128;
@@ -827,13 +844,14 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ QTile w, int M,
                    half* __restrict__ out, int ldo, int n_out, StepIO io, float* __restrict__ part) {
   constexpr int IPS = TcFmt<BITS>::kItems;
-  constexpr int kIssuer = 4, kProducer = 4 + NISS;   // blockDim = 32 * (4 + NISS + 1)
+  constexpr int kIssuer = kTcGemmDec, kProducer = kTcGemmDec + NISS;   // blockDim = 32 * (8 + NISS + 1)
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ TcGemmShared sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rb = blockIdx.x, ks = blockIdx.y;
   const int cta_kb0 = ks * w.kps;
   const int nkb = max(0, min(w.kps, w.k_blocks - cta_kb0));
+  const int half0 = (nkb + 1) / 2, cnt1 = nkb - half0;   // k-blocks of warpgroups 0 and 1
   const int n_mma = tc_n(M);
   const int n_xs = tc_gemm_xslots(BITS, M);
   constexpr int n_iss = NISS;   // tc_gemm_issuers(M) or fewer
@@ -855,7 +873,7 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
     mbar_init(&sh.dready, n_iss);
     sh.broken = 0;
   }
-  if (warp < 4 && lane == 0)
+  if (warp < kTcGemmDec && lane == 0)
     for (int i = 0; i < kTcRingSlots; ++i) mbar_init(&sh.ring[warp][i], 1);
   if (warp == kProducer && lane == 0)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
@@ -866,34 +884,39 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sh.tmem;
 
+  const int dh = warp >> 2, quarter = warp & 3;   // decoding warps: warpgroup, lane quarter
   TcWeightStream<BITS> ws;
   int issued = 0;
-  if (warp < 4) {
+  if (warp < kTcGemmDec) {
+    const int kb_off = dh ? half0 : 0;
     ws.src = reinterpret_cast<const unsigned char*>(
-        w.data + (static_cast<size_t>(rb * 4 + warp) * w.k_blocks + cta_kb0) * w.rec_u4);
+        w.data + (static_cast<size_t>(rb * 4 + quarter) * w.k_blocks + cta_kb0 + kb_off) * w.rec_u4);
     ws.ring = rings + static_cast<size_t>(warp) * kTcRingSlots * TcWeightStream<BITS>::SLOT;
     ws.bar = sh.ring[warp];
-    ws.cnt = nkb;
-    ws.n_chunks = (nkb + IPS - 1) / IPS;
+    ws.cnt = dh ? cnt1 : half0;
+    ws.n_chunks = (ws.cnt + IPS - 1) / IPS;
     if (lane == 0) issued = ws.issue_first();
   }
 
   grid_dep_wait();
 
-  if (warp < 4) {
-    tc_decode_warp<BITS, kTcGemmA>(ws, issued, tmem + (static_cast<uint32_t>(warp * 32) << 16), 0, 1, sh.full,
-                                   sh.empty, &sh.broken, lane, io.err);
+  if (warp < kTcGemmDec) {
+    tc_decode_warp<BITS, kTcGemmAPerWg>(ws, issued, tmem + (static_cast<uint32_t>(quarter * 32) << 16), dh, 2,
+                                        sh.full, sh.empty, &sh.broken, lane, io.err);
   } else if (warp == kProducer) {
     // ---- activations: k-block j -> ring slot j % n_xs -------------------------------
     if (lane == 0) {
       bool ok = true;
       int sent = 0;
-      for (int j = 0; j < nkb; ++j) {
-        const int xs = j % n_xs, use = j / n_xs;
+      for (int q = 0; q < nkb; ++q) {
+        const int xs = q % n_xs, use = q / n_xs;
         if (use >= 1 && !(ok = tc_wait(&sh.xempty[xs], (use - 1) & 1, &sh.broken))) break;
+        int h, j;
+        tc_gemm_pos(q, cnt1, h, j);
         mbar_expect_tx(&sh.xfull[xs], xslot_bytes);
-        tma_load_2d(xring + static_cast<size_t>(xs) * xslot_bytes, &xmap, (cta_kb0 + j) * 64, 0, &sh.xfull[xs]);
-        sent = j + 1;
+        tma_load_2d(xring + static_cast<size_t>(xs) * xslot_bytes, &xmap, (cta_kb0 + (h ? half0 : 0) + j) * 64, 0,
+                    &sh.xfull[xs]);
+        sent = q + 1;
       }
       if (!ok) {
         if (io.err) atomicExch(io.err, 2);
@@ -908,16 +931,18 @@ __global__ void __launch_bounds__(kTcGemmThreads, 1)
     const uint32_t dcol = tmem + tc_gemm_dcol() + iss * n_mma;
     const uint32_t xbase = smem_addr(xring);
     bool ok = true;
-    for (int j = iss; j < nkb; j += n_iss) {
-      const int aslot = j % kTcGemmA, xs = j % n_xs;
-      ok = tc_wait(&sh.full[aslot], (j / kTcGemmA) & 1, &sh.broken) &&
-           tc_wait(&sh.xfull[xs], (j / n_xs) & 1, &sh.broken);
+    for (int q = iss; q < nkb; q += n_iss) {
+      int h, j;
+      tc_gemm_pos(q, cnt1, h, j);
+      const int aslot = h + 2 * (j % kTcGemmAPerWg), xs = q % n_xs;
+      ok = tc_wait(&sh.full[aslot], (j / kTcGemmAPerWg) & 1, &sh.broken) &&
+           tc_wait(&sh.xfull[xs], (q / n_xs) & 1, &sh.broken);
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
       for (int s = 0; s < 4; ++s)
         tc_mma_ts(dcol, tmem + aslot * kTcSlotCols + 8 * s,
-                  tc_sdesc_sw128(xbase + xs * xslot_bytes + 32u * static_cast<uint32_t>(s)), idesc, j > iss || s > 0);
+                  tc_sdesc_sw128(xbase + xs * xslot_bytes + 32u * static_cast<uint32_t>(s)), idesc, q > iss || s > 0);
       tc_commit(&sh.empty[aslot]);
       tc_commit(&sh.xempty[xs]);
     }
@@ -1062,7 +1087,7 @@ cudaError_t tc_launch_t(const QTile& w_, const ActIn& in, int M, const Epi& epi,
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     const int n_iss = tc_gemm_issuers(M);
-    cfg.blockDim = dim3(32 * (4 + n_iss + 1), 1, 1);
+    cfg.blockDim = dim3(32 * (kTcGemmDec + n_iss + 1), 1, 1);
     cudaError_t e =
         n_iss == 4   ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS, 4>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part)
         : n_iss == 2 ? cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BITS, 2>, xmap, w, M, epi.out, epi.ldo, epi.n_out, io, scr.part)
