@@ -225,3 +225,19 @@ def test_tc_dense_unaligned_rows(ctx, m):
     got = yb.download(np.empty((m, n), np.float16))
     assert rel_err(got, ref_matmul(x, deq)) < 1e-2
     assert np.array_equal(got.view(np.uint16), w.matmul(x).view(np.uint16)) or rel_err(got, w.matmul(x)) < 1e-2
+
+
+@pytest.mark.parametrize("bits,m", [(4, 40), (8, 256)])
+def test_tc_dense_padded_k(ctx, bits, m):
+    """in_real < in: the activation tensor map reads zeros past in_real, so
+    the padded weight columns add nothing."""
+    rng = np.random.default_rng([bits, m, 11])
+    n, k, k_real = 2048, 704, 688
+    packed, scale = random_codes(rng, n, k, bits, 64)
+    w = _upload(ctx, packed, scale, bits, 64, n, k, k_real)
+    deq = oquant.dequantize_packed(packed, scale, {"bits": bits, "block": 64, "out": n, "in": k})[:, :k_real]
+    x = rng.standard_normal((m, k_real)).astype(np.float16)
+    got = w.matmul(x)
+    ref = ref_matmul(x, deq)
+    assert rel_err(got, ref) < 1e-2
+    assert np.mean(ulp_diff(got, ref) > 1) < 2e-3
