@@ -28,7 +28,7 @@ ALM_DEV uint32_t ld_nc_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------
-// bulk copies (TMA engine, no multicast) into shared memory with mbarriers
+// bulk copies (TMA engine, each CTA its own copy) into shared memory with mbarriers
 // ---------------------------------------------------------------------------
 // Limits of every mbarrier wait: after this many polls, or this much time on
 // the global timer, the waiter gives up and reports an error instead of
