@@ -106,6 +106,15 @@ __global__ void tc_rate_kernel(int ts, int n, int na, int iters, int cols, int i
   }
 }
 
+// An empty dependent kernel: wait for the previous grid, touch one word, let
+// the next grid start.  A chain of these measures the per-launch floor of a
+// CUDA graph with programmatic dependent launch.
+__global__ void nop_chain_kernel(unsigned* word) {
+  grid_dep_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) *word += 1;
+  grid_dep_launch();
+}
+
 }  // namespace
 }  // namespace alm
 
@@ -201,6 +210,57 @@ int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains
   *result = c / n_sms / (static_cast<double>(iters) * chains * warps);   // cycles per MMA per SM
   cudaFree(sink);
   cudaFree(dv);
+  if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
+  return 0;
+}
+
+int alm_bench_launch_floor(alm_ctx* ctx, int n_ctas, int pdl, double* us_per_launch) {
+  using namespace alm;
+  if (!ctx || !us_per_launch || n_ctas < 1 || n_ctas > 4096) return alm_internal_fail(ALM_ERR_ARG, "bad argument");
+  int device = 0;
+  cudaStream_t st = nullptr;
+  int rc = alm_internal_ctx(ctx, &device, &st);
+  if (rc) return rc;
+  constexpr int kChain = 200, kReps = 20;
+  unsigned* word = nullptr;
+  if (cudaMalloc(&word, sizeof(unsigned)) != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaError_t e = cudaMemsetAsync(word, 0, sizeof(unsigned), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_ctas, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t le = cudaSuccess;
+    for (int i = 0; i < kChain && le == cudaSuccess; ++i) le = cudaLaunchKernelEx(&cfg, nop_chain_kernel, word);
+    e = cudaStreamEndCapture(st, &graph);
+    if (e == cudaSuccess) e = le;
+  }
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e1);
+  for (int w = 0; w < 3 && e == cudaSuccess; ++w) e = cudaGraphLaunch(exec, st);
+  if (e == cudaSuccess) e = cudaEventRecord(e0, st);
+  for (int r = 0; r < kReps && e == cudaSuccess; ++r) e = cudaGraphLaunch(exec, st);
+  if (e == cudaSuccess) e = cudaEventRecord(e1, st);
+  if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+  float ms = 0.f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  *us_per_launch = static_cast<double>(ms) * 1000.0 / (kChain * kReps);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFree(word);
   if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
   return 0;
 }

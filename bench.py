@@ -470,7 +470,9 @@ def run_mma_rate(args):
     """Tensor-core instruction rates on this GPU (JSON lines): mma.sync
     m16n8k16 cycles per instruction per SM by warps per SM and accumulator
     chains; tcgen05.mma (M 128, K 16) ns per instruction by N, operand source
-    (A in tensor memory: TS, shared memory: SS) and accumulators."""
+    (A in tensor memory: TS, shared memory: SS), accumulators and issuing
+    threads per SM; then the per-launch floor of a CUDA graph of empty
+    dependent kernels."""
     import ctypes
     from androidllm_b200._lib import check, lib
     from androidllm_b200.ops import Context
@@ -502,6 +504,12 @@ def run_mma_rate(args):
                                   "issuers_per_cta": iss, "n": n, "ns_per_mma": round(r.value, 2),
                                   "tmac_per_s_per_sm": round(cps * iss * 128 * n * 16 / r.value / 1e3, 3)}),
                       flush=True)
+    # per-launch floor of a CUDA graph: chains of empty dependent kernels
+    for pdl in (1, 0):
+        for n_ctas in (1, 148, 296, 1184):
+            check(lib.alm_bench_launch_floor(ctx.h, n_ctas, pdl, ctypes.byref(r)))
+            print(json.dumps({"launch_floor": "empty dependent kernels in a CUDA graph", "pdl": bool(pdl),
+                              "ctas": n_ctas, "threads": 256, "us_per_launch": round(r.value, 3)}), flush=True)
     return 0
 
 

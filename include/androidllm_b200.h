@@ -267,6 +267,11 @@ ALM_API int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_o
  * memory).  *ns_per_mma = ns per instruction of one issuing thread. */
 ALM_API int alm_bench_tc_rate(alm_ctx* ctx, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
                               double* ns_per_mma);
+
+/* Per-launch floor of a CUDA graph: a chain of 200 empty dependent kernels of
+ * n_ctas CTAs x 256 threads (with programmatic dependent launch if pdl),
+ * replayed 20 times; *us_per_launch = device time per launch. */
+ALM_API int alm_bench_launch_floor(alm_ctx* ctx, int n_ctas, int pdl, double* us_per_launch);
 /* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
  * n_w weights of one shape (so their total can exceed L2); *avg_us is the
  * mean device time of one launch. */
