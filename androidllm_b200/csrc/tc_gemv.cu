@@ -686,8 +686,8 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Dense path with TMA-streamed activations (more than 16 raw rows, 16-byte
-// aligned, STORE): one decoding warpgroup per 128-row block, but the
-// activations are not staged for the whole K range.
+// aligned, STORE): one CTA per 128-row block and K split, the activations
+// streamed per k-block instead of staged for the whole K range.
 //   * A producer thread copies each k-block's activations (64 columns x N
 //     rows) with one TMA tensor copy into a ring slot in the canonical
 //     K-major SWIZZLE_128B layout (row r at r * 128 bytes, its 16-byte chunk c
@@ -699,15 +699,16 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
 //     h + 2 * (j % 3), so three k-blocks per warpgroup are decoded while the
 //     MMAs of earlier ones complete.  Producer and issuing threads walk the
 //     k-blocks in one interleaved sequence (h0 j0, h1 j0, h0 j1, ...).
-//   * n_iss issuing threads take the k-blocks in turn (thread i: j = i,
-//     i + n_iss, ...), each into its own tensor-memory accumulator: one
+//   * n_iss issuing threads take the sequence positions in turn (thread i:
+//     q = i, i + n_iss, ...), each into its own tensor-memory accumulator: one
 //     issuing thread completes about one MMA per 110 ns for any N, and the
 //     SM's tensor pipe is full when the concurrent MMAs add up to N = 256, so
 //     n_iss = 4, 2 or 1 as 256 / N allows (a template parameter).  An
 //     issuing thread waits for both operands of its k-block, runs the four
 //     MMAs (M 128, N = M rounded up to 16, K 16) and commits both slots
 //     free.  The accumulators are added in issuer order by the epilogue.
-// K is split across CTAs only as the weight's own split says.
+// K is split across CTAs only as the weight's own split says; the splits'
+// fp32 partials are summed in split order by tc_split_reduce_kernel.
 // ---------------------------------------------------------------------------
 constexpr int kTcGemmDec = 8;            // decoding warps (two warpgroups)
 constexpr int kTcGemmAPerWg = 3;         // tensor-memory A slots per decoding warpgroup
