@@ -620,10 +620,12 @@ def summarize_ncu(path):
         if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
             continue
         name = r[ki]
-        m = re.search(r"(tc_gemv_kernel|gemv_kernel)<([^>]*)>", name)
+        m = re.search(r"(tc_gemm_kernel|tc_gemv_kernel|gemv_kernel)<([^>]*)>", name)
         if m:
             g = re.findall(r"\d+", m.group(2))
-            if m.group(1) == "tc_gemv_kernel" and len(g) == 2:
+            if m.group(1) == "tc_gemm_kernel" and len(g) == 2:   # dense path: bits, issuing threads
+                name = f"tc_gemm_kernel<int{g[0]}, {g[1]} issuer{'s' if g[1] != '1' else ''}>"
+            elif m.group(1) == "tc_gemv_kernel" and len(g) == 2:
                 name = f"tc_gemv_kernel<int{g[0]}, {epi.get(g[1], g[1])}>"
             elif len(g) == 4:   # gemv_kernel<bits, scale sets, n8 tiles, epilogue>
                 name = f"gemv_kernel<int{g[0]}, nt8={g[2]}, {epi.get(g[3], g[3])}>"
