@@ -47,9 +47,6 @@ SIGNATURES = {
     "alm_ctx_sync": [_P],
     "alm_ctx_set_persistent": [_P, _I],
     "alm_ctx_set_gemv_layout": [_P, _I],
-    "alm_bench_mma_rate": [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_double)],
-    "alm_bench_tc_rate": [_P, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_double)],
-    "alm_bench_launch_floor": [_P, _I, _I, ctypes.POINTER(ctypes.c_double)],
     "alm_dev_alloc": [_P, ctypes.c_size_t, _PP],
     "alm_dev_free": [_P, _P],
     "alm_copy_h2d": [_P, _P, _P, ctypes.c_size_t],

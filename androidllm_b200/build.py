@@ -3,7 +3,9 @@
     python -m androidllm_b200.build [--verbose]
 
 The library is a single shared object with a plain C ABI
-(include/androidllm_b200.h); it links only the CUDA runtime.
+(include/androidllm_b200.h); it links only the CUDA runtime.  The measurement
+probes (probes/*.cu: tensor-core instruction rates, the graph launch floor)
+build into a separate libalm_probes.so that only `bench.py --mma-rate` loads.
 """
 import argparse
 import glob
@@ -14,6 +16,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libandroidllm_b200.so")
+PROBES_LIB = os.path.join(HERE, "libalm_probes.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 FLAGS = [
@@ -29,16 +32,23 @@ def sources():
     return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
 
 
+def probe_sources():
+    return sorted(glob.glob(os.path.join(HERE, "probes", "*.cu")))
+
+
 def headers():
     return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh")) +
                   glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def up_to_date():
-    if not os.path.exists(LIB):
-        return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(f) <= t for f in sources() + headers() + [__file__])
+    for lib, srcs in ((LIB, sources()), (PROBES_LIB, probe_sources())):
+        if not os.path.exists(lib):
+            return False
+        t = os.path.getmtime(lib)
+        if not all(os.path.getmtime(f) <= t for f in srcs + headers() + [__file__]):
+            return False
+    return True
 
 
 def _run(cmd, verbose):
@@ -61,16 +71,17 @@ def build(force=False, verbose=False, ptxas_info=False):
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     extra = ["-Xptxas=-v"] if ptxas_info else []
-    jobs, objs = [], []
-    for src in sources():
+    jobs, objs, probe_objs = [], [], []
+    for src in sources() + probe_sources():
         obj = os.path.join(objdir, os.path.basename(src) + ".o")
-        objs.append(obj)
+        (probe_objs if src in probe_sources() else objs).append(obj)
         jobs.append(_run([NVCC, *extra, *FLAGS, "-c", src, "-o", obj], verbose))
     errs = [_finish(p) for p in jobs]
     if ptxas_info or verbose:
         print("".join(errs), file=sys.stderr)
-    _finish(_run([NVCC, *FLAGS, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart"], verbose))
-    os.replace(LIB + ".tmp", LIB)
+    for lib, o in ((LIB, objs), (PROBES_LIB, probe_objs)):
+        _finish(_run([NVCC, *FLAGS, "-shared", "-o", lib + ".tmp", *o, "-lcudart"], verbose))
+        os.replace(lib + ".tmp", lib)
     return LIB
 
 

@@ -81,6 +81,14 @@ extern "C" ALM_API int alm_qmatmul_noalloc(alm_ctx* ctx, const alm_qweight* w, c
   }
 
   // once per device, with that device current: resolve the array's address
+  int prev_device = -1;
+  if (cudaGetDevice(&prev_device) != cudaSuccess) prev_device = -1;
+  struct Restore {
+    int d;
+    ~Restore() {
+      if (d >= 0) cudaSetDevice(d);
+    }
+  } restore{prev_device};
   if (cudaSetDevice(device) != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, "cudaSetDevice failed");
   void* base = nullptr;
   {

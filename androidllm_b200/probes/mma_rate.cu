@@ -1,5 +1,7 @@
-// Tensor-core instruction rates on this GPU, measured by the library itself
-// (bench.py --mma-rate): they decide which MMA each matmul path uses.
+// Measurement probes, built as a separate library (libalm_probes.so) that
+// the product library does not contain or export; `bench.py --mma-rate`
+// loads it.  Tensor-core instruction rates on this GPU decide which MMA each
+// matmul path uses:
 //   * mma.sync m16n8k16 (f16 in, f32 accumulate, register operands): cycles
 //     per instruction per SM with W warps per SM and C independent
 //     accumulator chains per warp;
@@ -9,8 +11,9 @@
 // Operands are constants; only the issue and completion rates are measured.
 #include <vector>
 
-#include "../../include/androidllm_b200.h"
-#include "tc.cuh"
+#include <string>
+
+#include "../csrc/tc.cuh"
 
 namespace alm {
 namespace {
@@ -118,18 +121,34 @@ __global__ void nop_chain_kernel(unsigned* word) {
 }  // namespace
 }  // namespace alm
 
-int alm_internal_fail(int code, const char* msg);
-int alm_internal_ctx(alm_ctx* ctx, int* device, cudaStream_t* stream);
-
 namespace {
+thread_local std::string g_probe_err;
+int probe_fail(const char* msg) {
+  g_probe_err = msg;
+  return 1;
+}
+// A stream on `device` for one probe call.
+struct ProbeStream {
+  cudaStream_t st = nullptr;
+  int n_sms = 148;
+  cudaError_t e = cudaSuccess;
+  explicit ProbeStream(int device) {
+    e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
+  }
+  ~ProbeStream() {
+    if (st) cudaStreamDestroy(st);
+  }
+};
 // ns per tcgen05.mma of each issuing thread; 0 or an ALM error code.
 int tc_rate(cudaStream_t st, int n_sms, int ts, int n, int na, int ctas_per_sm, int issuers, double* result) {
   using namespace alm;
   const int cols = 512 / ctas_per_sm, iters = 2048;
   if ((ctas_per_sm != 1 && ctas_per_sm != 2 && ctas_per_sm != 4) || issuers < 1 || issuers > 4 || n < 16 ||
       n > 256 || n % 16 || na < 1 || issuers * na * n > cols - 32)
-    return alm_internal_fail(ALM_ERR_ARG,
-                             "tcgen05 rate: N multiple of 16 in 16..256, 1/2/4 CTAs per SM, 1..4 issuers, "
+    return probe_fail(
+        "tcgen05 rate: N multiple of 16 in 16..256, 1/2/4 CTAs per SM, 1..4 issuers, "
                              "issuers * accumulators * N <= 512 / ctas_per_sm - 32");
   const size_t n_rec = static_cast<size_t>(ctas_per_sm) * n_sms * issuers;
   int* status = nullptr;
@@ -137,7 +156,7 @@ int tc_rate(cudaStream_t st, int n_sms, int ts, int n, int na, int ctas_per_sm, 
   if (cudaMalloc(&status, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&dv, n_rec * sizeof(unsigned long long)) != cudaSuccess) {
     cudaFree(status);
-    return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
+    return probe_fail("allocation failed");
   }
   cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), st);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(tc_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384);
@@ -155,43 +174,50 @@ int tc_rate(cudaStream_t st, int n_sms, int ts, int n, int na, int ctas_per_sm, 
   if (e == cudaSuccess && hs) e = cudaErrorTimeout;
   cudaFree(status);
   cudaFree(dv);
-  if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) return probe_fail(cudaGetErrorString(e));
   return 0;
 }
 }  // namespace
 
-int alm_bench_tc_rate(alm_ctx* ctx, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
-                      double* ns_per_mma) {
-  if (!ctx || !ns_per_mma) return alm_internal_fail(ALM_ERR_ARG, "null argument");
-  int device = 0;
-  cudaStream_t st = nullptr;
-  int rc = alm_internal_ctx(ctx, &device, &st);
-  if (rc) return rc;
-  int n_sms = 148;
-  cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
-  return tc_rate(st, n_sms, ts ? 1 : 0, n, accumulators, ctas_per_sm, issuers, ns_per_mma);
+#define PROBE_API extern "C" __attribute__((visibility("default")))
+
+PROBE_API const char* probe_last_error(void) { return g_probe_err.c_str(); }
+
+// tcgen05.mma kind::f16 (M = 128, K = 16) issue rate: ctas_per_sm CTAs on
+// every SM, each with `issuers` issuing threads rotating over `accumulators`
+// accumulators of N = n columns (A from tensor memory if ts, else shared
+// memory).  *ns_per_mma = ns per instruction of one issuing thread.
+PROBE_API int probe_tc_rate(int device, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
+                            double* ns_per_mma) {
+  if (!ns_per_mma) return probe_fail("null argument");
+  ProbeStream ps(device);
+  if (ps.e != cudaSuccess) return probe_fail(cudaGetErrorString(ps.e));
+  return tc_rate(ps.st, ps.n_sms, ts ? 1 : 0, n, accumulators, ctas_per_sm, issuers, ns_per_mma);
 }
 
-int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains, double* result) {
+// kind 0: mma.sync m16n8k16 with n_or_warps warps per SM and acc_or_chains
+// (1, 2, 4, 8) accumulator chains per warp, *result = cycles per instruction
+// per SM.  kind 1 / 2: tcgen05.mma, A from tensor memory / shared memory, N =
+// n_or_warps, rotating over acc_or_chains accumulators, one CTA per SM,
+// *result = ns per instruction.
+PROBE_API int probe_mma_rate(int device, int kind, int n_or_warps, int acc_or_chains, double* result) {
   using namespace alm;
-  if (!ctx || !result) return alm_internal_fail(ALM_ERR_ARG, "null argument");
-  int device = 0;
-  cudaStream_t st = nullptr;
-  int rc = alm_internal_ctx(ctx, &device, &st);
-  if (rc) return rc;
-  int n_sms = 148;
-  cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device);
+  if (!result) return probe_fail("null argument");
+  ProbeStream ps(device);
+  if (ps.e != cudaSuccess) return probe_fail(cudaGetErrorString(ps.e));
+  cudaStream_t st = ps.st;
+  const int n_sms = ps.n_sms;
   if (kind == 1 || kind == 2) return tc_rate(st, n_sms, kind == 1 ? 1 : 0, n_or_warps, acc_or_chains, 1, 1, result);
-  if (kind != 0) return alm_internal_fail(ALM_ERR_ARG, "kind 0 (mma.sync), 1 (tcgen05 TS) or 2 (tcgen05 SS)");
+  if (kind != 0) return probe_fail("kind 0 (mma.sync), 1 (tcgen05 TS) or 2 (tcgen05 SS)");
   const int warps = n_or_warps, chains = acc_or_chains, iters = 4096;
   if (warps < 1 || warps > 32 || (chains != 1 && chains != 2 && chains != 4 && chains != 8))
-    return alm_internal_fail(ALM_ERR_ARG, "mma.sync rate: 1..32 warps, 1/2/4/8 chains");
+    return probe_fail("mma.sync rate: 1..32 warps, 1/2/4/8 chains");
   float* sink = nullptr;
   unsigned long long* dv = nullptr;   // per-CTA cycles
   if (cudaMalloc(&sink, static_cast<size_t>(n_sms) * 1024 * sizeof(float)) != cudaSuccess ||
       cudaMalloc(&dv, static_cast<size_t>(n_sms) * sizeof(unsigned long long)) != cudaSuccess) {
     cudaFree(sink);
-    return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
+    return probe_fail("allocation failed");
   }
   cudaError_t e = cudaSuccess;
   for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
@@ -210,20 +236,22 @@ int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains
   *result = c / n_sms / (static_cast<double>(iters) * chains * warps);   // cycles per MMA per SM
   cudaFree(sink);
   cudaFree(dv);
-  if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) return probe_fail(cudaGetErrorString(e));
   return 0;
 }
 
-int alm_bench_launch_floor(alm_ctx* ctx, int n_ctas, int pdl, double* us_per_launch) {
+// Per-launch floor of a CUDA graph: a chain of 200 empty dependent kernels of
+// n_ctas CTAs x 256 threads (with programmatic dependent launch if pdl),
+// replayed 20 times; *us_per_launch = device time per launch.
+PROBE_API int probe_launch_floor(int device, int n_ctas, int pdl, double* us_per_launch) {
   using namespace alm;
-  if (!ctx || !us_per_launch || n_ctas < 1 || n_ctas > 4096) return alm_internal_fail(ALM_ERR_ARG, "bad argument");
-  int device = 0;
-  cudaStream_t st = nullptr;
-  int rc = alm_internal_ctx(ctx, &device, &st);
-  if (rc) return rc;
+  if (!us_per_launch || n_ctas < 1 || n_ctas > 4096) return probe_fail("bad argument");
+  ProbeStream ps(device);
+  if (ps.e != cudaSuccess) return probe_fail(cudaGetErrorString(ps.e));
+  cudaStream_t st = ps.st;
   constexpr int kChain = 200, kReps = 20;
   unsigned* word = nullptr;
-  if (cudaMalloc(&word, sizeof(unsigned)) != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, "allocation failed");
+  if (cudaMalloc(&word, sizeof(unsigned)) != cudaSuccess) return probe_fail("allocation failed");
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
@@ -261,6 +289,6 @@ int alm_bench_launch_floor(alm_ctx* ctx, int n_ctas, int pdl, double* us_per_lau
   if (e0) cudaEventDestroy(e0);
   if (e1) cudaEventDestroy(e1);
   cudaFree(word);
-  if (e != cudaSuccess) return alm_internal_fail(ALM_ERR_CUDA, cudaGetErrorString(e));
+  if (e != cudaSuccess) return probe_fail(cudaGetErrorString(e));
   return 0;
 }

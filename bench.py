@@ -472,15 +472,21 @@ def run_mma_rate(args):
     chains; tcgen05.mma (M 128, K 16) ns per instruction by N, operand source
     (A in tensor memory: TS, shared memory: SS), accumulators and issuing
     threads per SM; then the per-launch floor of a CUDA graph of empty
-    dependent kernels."""
+    dependent kernels.  The probe kernels live in libalm_probes.so, apart
+    from the product library."""
     import ctypes
-    from androidllm_b200._lib import check, lib
-    from androidllm_b200.ops import Context
-    ctx = Context(0)
+    from androidllm_b200.build import PROBES_LIB
+    plib = ctypes.CDLL(PROBES_LIB)
+    plib.probe_last_error.restype = ctypes.c_char_p
     r = ctypes.c_double()
+
+    def check(rc):
+        if rc:
+            raise RuntimeError(plib.probe_last_error().decode())
+
     for warps in (4, 8, 16, 32):
         for chains in (1, 2, 4, 8):
-            check(lib.alm_bench_mma_rate(ctx.h, 0, warps, chains, ctypes.byref(r)))
+            check(plib.probe_mma_rate(0, 0, warps, chains, ctypes.byref(r)))
             print(json.dumps({"mma": "mma.sync.m16n8k16.f32.f16", "warps_per_sm": warps, "chains": chains,
                               "cycles_per_mma_per_sm": round(r.value, 3),
                               "mac_per_clk_per_sm": round(16 * 8 * 16 / r.value, 1)}), flush=True)
@@ -489,7 +495,7 @@ def run_mma_rate(args):
             for na in (1, 8):
                 if na * n > 256:
                     continue
-                check(lib.alm_bench_mma_rate(ctx.h, kind, n, na, ctypes.byref(r)))
+                check(plib.probe_mma_rate(0, kind, n, na, ctypes.byref(r)))
                 print(json.dumps({"mma": "tcgen05.mma.kind::f16 M128 K16", "form": form, "n": n, "accumulators": na,
                                   "ns_per_mma": round(r.value, 2),
                                   "tmac_per_s_per_sm": round(128 * n * 16 / r.value / 1e3, 3)}), flush=True)
@@ -499,7 +505,7 @@ def run_mma_rate(args):
             for n in (16, 32, 64, 128, 256):
                 if iss * n > 512 // cps - 32:
                     continue
-                check(lib.alm_bench_tc_rate(ctx.h, 1, n, 1, cps, iss, ctypes.byref(r)))
+                check(plib.probe_tc_rate(0, 1, n, 1, cps, iss, ctypes.byref(r)))
                 print(json.dumps({"mma": "tcgen05.mma.kind::f16 M128 K16", "form": "TS", "ctas_per_sm": cps,
                                   "issuers_per_cta": iss, "n": n, "ns_per_mma": round(r.value, 2),
                                   "tmac_per_s_per_sm": round(cps * iss * 128 * n * 16 / r.value / 1e3, 3)}),
@@ -507,7 +513,7 @@ def run_mma_rate(args):
     # per-launch floor of a CUDA graph: chains of empty dependent kernels
     for pdl in (1, 0):
         for n_ctas in (1, 148, 296, 1184):
-            check(lib.alm_bench_launch_floor(ctx.h, n_ctas, pdl, ctypes.byref(r)))
+            check(plib.probe_launch_floor(0, n_ctas, pdl, ctypes.byref(r)))
             print(json.dumps({"launch_floor": "empty dependent kernels in a CUDA graph", "pdl": bool(pdl),
                               "ctas": n_ctas, "threads": 256, "us_per_launch": round(r.value, 3)}), flush=True)
     return 0

@@ -251,27 +251,6 @@ ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitt
 /* Start (1) or stop (0) the CUDA profiler's capture range, so a profiler
  * started with capture disabled records only the work in between. */
 ALM_API int alm_profiler_range(int start);
-/* Tensor-core instruction rates (no reference counterpart; they decide which
- * MMA each matmul path uses).  kind 0: mma.sync m16n8k16 with n_or_warps
- * warps per SM and acc_or_chains (1, 2, 4, 8) accumulator chains per warp,
- * *result = cycles per instruction per SM.  kind 1 / 2: tcgen05.mma
- * kind::f16 M = 128, K = 16, A from tensor memory / shared memory, N =
- * n_or_warps, rotating over acc_or_chains accumulators, one CTA per SM,
- * *result = ns per instruction. */
-ALM_API int alm_bench_mma_rate(alm_ctx* ctx, int kind, int n_or_warps, int acc_or_chains, double* result);
-
-/* tcgen05.mma kind::f16 (M = 128, K = 16) issue rate with several issuers
- * per SM: ctas_per_sm (1, 2, 4) CTAs on every SM, each with `issuers` (1..4)
- * issuing threads in different warps, each rotating over `accumulators`
- * accumulators of N = n columns (A from tensor memory if ts, else shared
- * memory).  *ns_per_mma = ns per instruction of one issuing thread. */
-ALM_API int alm_bench_tc_rate(alm_ctx* ctx, int ts, int n, int accumulators, int ctas_per_sm, int issuers,
-                              double* ns_per_mma);
-
-/* Per-launch floor of a CUDA graph: a chain of 200 empty dependent kernels of
- * n_ctas CTAs x 256 threads (with programmatic dependent launch if pdl),
- * replayed 20 times; *us_per_launch = device time per launch. */
-ALM_API int alm_bench_launch_floor(alm_ctx* ctx, int n_ctas, int pdl, double* us_per_launch);
 /* Time `iters` launches of the dequant-GEMV (x_dev: m rows) cycling through
  * n_w weights of one shape (so their total can exceed L2); *avg_us is the
  * mean device time of one launch. */

@@ -1,10 +1,10 @@
 """Generate the golden fixtures in this directory by running the androidllm
 reference itself (numpy path) on seeded inputs.
 
-Run from the repository root, in a container that has the reference checked
-out at /root/reference:
+Run from the repository root, with the path of an androidllm checkout (or
+the environment variable ANDROIDLLM_REFERENCE set to it):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <androidllm checkout> [--only qwen]
 
 It writes:
   quant.npz     reference quantize/pack/dequant outputs for seeded matrices,
@@ -26,6 +26,15 @@ It writes:
                 logits.
   sampling.npz  reference sampler picks for seeded logits and a grid of
                 (temperature, top_p, min_p), with the uniform each pick used.
+  qwen.npz      the benchmark's layer shapes: 2-layer Qwen2.5-1.5B-shaped target
+                (head_dim 128, 12/2 heads, FFN 8960, int4 attention / int8
+                MLP, tied int8 per-row 151936 head) and 2-layer Qwen2.5-0.5B-
+                shaped draft (head_dim 64, 14/2 heads, FFN 4864, int4), with
+                the KV cache of positions 0..775 filled from seeded fp16
+                values: layer states of 1-row decode and 5-row verify passes
+                at positions 511-771, and argmax / top-2 margin / sha256 /
+                sampled entries of the logits.  --only qwen regenerates just
+                this file (the reference takes a few minutes at these shapes).
 
 The reference never travels with this repository: only the fixtures do.
 """
@@ -44,6 +53,10 @@ sys.path.insert(0, ROOT)
 
 from androidllm_b200 import shard as my_shard  # noqa: E402
 from androidllm_b200 import synth  # noqa: E402
+
+sys.path.insert(0, HERE)
+from qwen_cases import (QWEN_CASES, QWEN_FILL, QWEN_MODELS, qwen_case_tokens,  # noqa: E402
+                        qwen_kv_fill, qwen_logit_index)
 
 TOY_PROMPT_SEED = 123
 TOY_SEED = 1
@@ -226,10 +239,58 @@ def run_toy(LayerStreamingEngine, toy, draft, out_path):
           "distinct", len(set(plain)), "min margin", float(plain_margins.min()))
 
 
+def run_qwen(LayerStreamingEngine, tmp, out_path):
+    """Reference layer_forward / logits at the benchmark's shapes over a
+    seeded KV cache (the reference has no batched pass: a 5-row verify case is
+    5 consecutive single-row forwards, each row through every layer)."""
+    out = {}
+    for name, canon, seed, kw in QWEN_MODELS:
+        d = os.path.join(tmp, name)
+        out[f"{name}_files"] = np.array(json.dumps(write_ref_model(sys.modules["androidllm.shard"], canon, seed,
+                                                                    kw, d)))
+        e = LayerStreamingEngine(d, keep_layers=canon["layers"])
+        model = e.model
+        layers = [e._load_layer_raw(i) for i in range(canon["layers"])]
+        fills = [qwen_kv_fill(canon, seed, li) for li in range(canon["layers"])]
+        idx = qwen_logit_index(canon["vocab"])
+        states, am, mg, hashes, samples = [], [], [], [], []
+        for ci, (rows, pos0) in enumerate(QWEN_CASES):
+            kv = model.prepare_kv(QWEN_FILL + 8)
+            for li, (k, v) in enumerate(fills):
+                kv[li][0][:QWEN_FILL] = k
+                kv[li][1][:QWEN_FILL] = v
+            toks = qwen_case_tokens(canon, seed, ci)[:rows]
+            st = np.zeros((5, canon["layers"], canon["hidden"]), np.float16)
+            for r, tok in enumerate(toks):
+                x = model.embed[tok].reshape(1, -1)
+                for li in range(canon["layers"]):
+                    x = model.layer_forward(x, layers[li], kv[li], pos0 + r)
+                    st[r, li] = np.asarray(x, np.float16).reshape(-1)
+                lg = np.asarray(model.logits(x), np.float32).reshape(-1).astype(np.float16)
+                srt = np.sort(lg.astype(np.float32))
+                am.append(int(np.argmax(lg)))
+                mg.append(float(srt[-1] - srt[-2]))
+                hashes.append(hashlib.sha256(lg.tobytes()).hexdigest())
+                samples.append(lg[idx])
+            states.append(st)
+            print(name, "case", ci, rows, pos0, "argmax", am[-rows:], flush=True)
+        out[f"{name}_states"] = np.stack(states)
+        out[f"{name}_argmax"] = np.array(am, np.int64)
+        out[f"{name}_margin"] = np.array(mg, np.float32)
+        out[f"{name}_hash"] = np.array(hashes)
+        out[f"{name}_sample"] = np.stack(samples)
+    out["cases"] = np.array(QWEN_CASES, np.int64)
+    np.savez_compressed(out_path, **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ANDROIDLLM_REFERENCE"),
+                    help="androidllm checkout (default: $ANDROIDLLM_REFERENCE)")
+    ap.add_argument("--only", choices=["qwen"], help="regenerate one fixture file only")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or ANDROIDLLM_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     os.environ["ANDROIDLLM_PREFIX_KV"] = "0"
     from androidllm import engine as ref_engine
@@ -248,6 +309,12 @@ def main():
                 c.finalize(n)
 
     LayerStreamingEngine._finalize_kv = _finalize_kv
+
+    if args.only == "qwen":
+        with tempfile.TemporaryDirectory() as tmp:
+            run_qwen(LayerStreamingEngine, tmp, os.path.join(HERE, "qwen.npz"))
+        print("qwen fixture written")
+        return
 
     np.savez_compressed(os.path.join(HERE, "quant.npz"), **quant_cases(ref_quant))
     np.savez_compressed(os.path.join(HERE, "sampling.npz"), **sampling_cases(ref_engine))
