@@ -589,6 +589,12 @@ EmbedArgs embed_args(alm_model* m, int M) {
 // resident, and forwards then use the standalone kernels).
 int build_forward(alm_model* m) {
   const alm_model_config& c = m->cfg;
+  m->fwd_grid = 0;
+  // a model may be finalized before its layers are set (the drop-in
+  // LlamaModel uploads each layer dict on first use): no persistent kernel
+  // until every layer is present
+  for (const Layer& L : m->layers)
+    if (!L.qkv) return ALM_OK;
   std::vector<FwdLayer> host(c.layers);
   size_t stage = gemv_stage_bytes(m->head->t, kPersistRows);
   for (int li = 0; li < c.layers; ++li) {
