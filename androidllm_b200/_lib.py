@@ -88,6 +88,7 @@ SIGNATURES = {
     "alm_model_sample": [_P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],
     "alm_profiler_range": [_I],
     "alm_spec_bench": [_P, _I, ctypes.POINTER(ctypes.c_float), _PI32],
+    "alm_spec_profile": [_P, _I, _P, _P, _P, _PI32],
     "alm_bench_qmatmul": [_P, _PP, _I, _P, _I, _P, _I, ctypes.POINTER(ctypes.c_float)],
 }
 _RESTYPE = {"alm_last_error": ctypes.c_char_p}

@@ -50,6 +50,7 @@ cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
   c1.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&c1, attn_scores_kernel, a, den);
   if (e != cudaSuccess) return e;
+  prof_mark(3 /* ALM_OP_ATTN_SCORES */, a.M);
 
   cudaLaunchConfig_t c2 = c1;
   c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a));

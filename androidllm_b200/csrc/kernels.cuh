@@ -183,6 +183,13 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
 
+// Per-launch profile of a speculative step (alm_spec_profile): while a
+// profiled step is being captured, prof_mark records a timing event after
+// each kernel launch, tagged with the launch's operation (ALM_OP_* of the
+// public header) and activation rows; outside a profiled capture it does
+// nothing.
+void prof_mark(int op, int rows);
+
 // embedding gather: x0[m] = dequant(embed[token_m])
 struct EmbedArgs {
   const void* table = nullptr;   // int4 packed / int8 / fp16 rows

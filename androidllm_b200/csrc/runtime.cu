@@ -454,6 +454,38 @@ int ensure_attn(alm_model* m, int max_ctx) {
 // --------------------------------------------------------------------------
 // forward enqueue (no host synchronisation)
 // --------------------------------------------------------------------------
+// ---- per-launch profile of a captured step (alm_spec_profile) ----------------
+struct LaunchProfile {
+  cudaStream_t st = nullptr;
+  int role = 0;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> op, rows;
+  cudaError_t err = cudaSuccess;
+};
+thread_local LaunchProfile* g_prof = nullptr;
+
+void prof_role(int role) {
+  if (g_prof) g_prof->role = role;
+}
+
+}  // namespace
+
+namespace alm {
+void prof_mark(int op, int rows) {
+  LaunchProfile* p = g_prof;
+  if (!p || p->err != cudaSuccess) return;
+  cudaEvent_t e = nullptr;
+  p->err = cudaEventCreate(&e);
+  if (p->err != cudaSuccess) return;
+  p->ev.push_back(e);
+  p->op.push_back(op + 100 * p->role);
+  p->rows.push_back(rows);
+  p->err = cudaEventRecordWithFlags(e, p->st, cudaEventRecordExternal);
+}
+}  // namespace alm
+
+namespace {
+
 SplitScratch scratch_of(alm_model* m) { return SplitScratch{m->ws.part, m->ws.part_floats}; }
 
 int n_h_tiles(const alm_model* m) { return (m->cfg.hidden + 15) / 16; }
@@ -504,6 +536,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   e.head_dim = c.head_dim;
   e.rope = m->rope;
   ALM_LAUNCH(launch_gemv(L.qkv->t, in, M, EPI_QKV, e, io, scr, pdl, st));
+  prof_mark(ALM_OP_QKV, M);
 
   AttnArgs a;
   a.q = ws.q;
@@ -524,6 +557,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.ctx = ws.ctx;
   a.ldc = qdim;
   ALM_LAUNCH(launch_attention(a, pdl, st));
+  prof_mark(ALM_OP_ATTN_PV, M);
 
   Epi eo;
   eo.out = ws.s1;
@@ -532,6 +566,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   eo.res = in;
   eo.ss_out = ws.ss1;
   ALM_LAUNCH(launch_gemv(L.o->t, raw_in(ws.ctx, qdim, qdim), M, EPI_RESID, eo, io, scr, pdl, st));
+  prof_mark(ALM_OP_O, M);
 
   const ActIn n1 = deferred_in(m, ws.s1, ws.ss1, L.n_in);
   Epi eg;
@@ -539,6 +574,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   eg.ldo = c.intermediate;
   eg.n_out = c.intermediate;
   ALM_LAUNCH(launch_gemv(L.gu->t, n1, M, EPI_SWIGLU, eg, io, scr, pdl, st));
+  prof_mark(ALM_OP_GATE_UP, M);
 
   Epi ed;
   ed.out = ws.s2;
@@ -548,6 +584,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   ed.ss_out = ws.ss2;
   ALM_LAUNCH(launch_gemv(L.down->t, raw_in(ws.h, c.intermediate, c.intermediate), M, EPI_RESID, ed, io, scr,
                          pdl, st));
+  prof_mark(ALM_OP_DOWN, M);
   return ALM_OK;
 }
 
@@ -562,7 +599,9 @@ int enqueue_head(alm_model* m, int M, bool pdl) {
   e.am_idx = ws.am_idx;
   const ActIn in = raw_in(ws.xn, m->cfg.hidden, m->cfg.hidden);
   ALM_LAUNCH(launch_gemv(m->head->t, in, M, EPI_LOGITS, e, StepIO{ws.pos, ws.err}, scratch_of(m), pdl, m->ctx->stream));
+  prof_mark(ALM_OP_HEAD, M);
   ALM_LAUNCH(launch_argmax_final(ws.am_val, ws.am_idx, ws.n_am, M, ws.argmax, pdl, m->ctx->stream));
+  prof_mark(ALM_OP_ARGMAX, M);
   return ALM_OK;
 }
 
@@ -700,6 +739,7 @@ int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
   ea.M = M;
   ea.err = ws.err;
   ALM_LAUNCH(launch_embed(ea, pdl, m->ctx->stream));
+  prof_mark(ALM_OP_EMBED, M);
   ActIn in = raw_in(ws.x0, m->cfg.hidden, m->cfg.hidden);
   for (int li = 0; li < m->cfg.layers; ++li) {
     ALM_TRY(enqueue_layer(m, li, kv, M, in, pdl));
@@ -707,6 +747,7 @@ int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
   }
   if (!head) return ALM_OK;
   ALM_LAUNCH(launch_rownorm(in, M, m->final_norm, m->cfg.rms_eps, ws.xn, m->cfg.hidden, pdl, m->ctx->stream));
+  prof_mark(ALM_OP_FINAL_NORM, M);
   return enqueue_head(m, M, pdl);
 }
 
@@ -1511,21 +1552,33 @@ static int enqueue_spec_step(alm_spec* s) {
   cudaStream_t st = t->ctx->stream;
   const bool sampled = s->temperature > 0.f;
   for (int i = 0; i < s->k; ++i) {
+    prof_role(0);
     ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
+    prof_mark(ALM_OP_SPEC_PREP, 1);
+    prof_role(1);
     ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
     // draft candidate i: the draft's sample, draw k-step offset i
-    if (sampled)
+    if (sampled) {
       ALM_CUDA(launch_sample(sample_args(d, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, i), 1,
                              false, st));
+      prof_mark(ALM_OP_SAMPLE, 1);
+    }
   }
+  prof_role(0);
   ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
+  prof_mark(ALM_OP_SPEC_PREP, s->k + 1);
+  prof_role(2);
   ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
   // target row j: the target's sample with draw k + j
-  if (sampled)
+  if (sampled) {
     ALM_CUDA(launch_sample(sample_args(t, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, s->k),
                            s->k + 1, false, st));
+    prof_mark(ALM_OP_SAMPLE, s->k + 1);
+  }
+  prof_role(0);
   ALM_CUDA(launch_spec_accept_greedy(s->state, s->cand, t->ws.argmax, s->k, s->out_tokens, s->out_acc,
                                      s->cap_tokens, s->cap_steps, sampled ? 1 : 0, st));
+  prof_mark(ALM_OP_SPEC_ACCEPT, s->k + 1);
   return ALM_OK;
 }
 
@@ -1763,6 +1816,68 @@ int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted) {
   ALM_CUDA(cudaMemcpy(st4, s->state, sizeof(st4), cudaMemcpyDeviceToHost));
   *n_emitted = st4[2];
   return ALM_OK;
+}
+
+int alm_spec_profile(alm_spec* s, int cap, int32_t* ops_host, int32_t* rows_host, float* us_host,
+                     int32_t* n_out) {
+  ALM_REQ(s && ops_host && rows_host && us_host && n_out && cap > 0, "null argument");
+  DeviceGuard g(s->target->ctx->device);
+  alm_ctx* c = s->target->ctx;
+  cudaStream_t st = c->stream;
+  int cur[8];
+  ALM_CUDA(cudaMemcpy(cur, s->state, sizeof(cur), cudaMemcpyDeviceToHost));
+  ALM_REQ(cur[1] + 2 * (s->k + 1) + s->k < s->tkv->max_len && cur[1] + 2 * (s->k + 1) + s->k < s->dkv->max_len,
+          "speculative steps would overflow the kv cache");
+  ALM_TRY(check_uniforms(s, 1));
+  // per-operation launches, no programmatic dependent launch: every kernel
+  // runs alone between its two events
+  const bool pdl = c->pdl, persist = c->persist;
+  c->pdl = false;
+  c->persist = false;
+  LaunchProfile prof;
+  prof.st = st;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int rc = ALM_OK;
+  if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    rc = fail(ALM_ERR_CUDA, "graph capture failed to start");
+  } else {
+    g_prof = &prof;
+    prof_mark(ALM_OP_BEGIN, 0);
+    rc = enqueue_spec_step(s);
+    g_prof = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc == ALM_OK && prof.err != cudaSuccess) rc = fail(ALM_ERR_CUDA, cudaGetErrorString(prof.err));
+    if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+  }
+  c->pdl = pdl;
+  c->persist = persist;
+  if (rc == ALM_OK && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "instantiate of the profiled step failed");
+  // two replays (the second one timed), each from the saved state
+  for (int rep = 0; rep < 2 && rc == ALM_OK; ++rep) {
+    if (cudaMemcpyAsync(s->state, cur, sizeof(cur), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaGraphLaunch(exec, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "replay of the profiled step failed");
+  }
+  const int n = static_cast<int>(prof.ev.size()) - 1;
+  if (rc == ALM_OK && n > cap) rc = fail(ALM_ERR_ARG, "profile capacity too small: " + std::to_string(n) + " launches");
+  for (int i = 0; rc == ALM_OK && i < n; ++i) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, prof.ev[i], prof.ev[i + 1]) != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, "event timing of the profiled step failed");
+      break;
+    }
+    ops_host[i] = prof.op[i + 1];
+    rows_host[i] = prof.rows[i + 1];
+    us_host[i] = ms * 1000.f;
+  }
+  if (rc == ALM_OK) *n_out = n;
+  cudaMemcpy(s->state, cur, sizeof(cur), cudaMemcpyHostToDevice);
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
+  for (cudaEvent_t e : prof.ev) cudaEventDestroy(e);
+  return rc;
 }
 
 int alm_bench_qmatmul(alm_ctx* ctx, alm_qweight* const* ws, int n_w, const uint16_t* x_dev, int m,

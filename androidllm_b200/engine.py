@@ -186,6 +186,7 @@ class LayerStreamingEngine:
             for k in ("draft_tokens", "spec_accepted", "spec_bonus", "spec_steps"):
                 self.stats.setdefault(k, 0)
         # prefill: kv[0..n-2] filled, token = id at position n-1 (engine.py:346-354)
+        t_pre = time.perf_counter()
         self._prefill(kv, prompt_ids[:-1], 0)
         token = prompt_ids[-1]
         pos = len(prompt_ids) - 1
@@ -195,6 +196,7 @@ class LayerStreamingEngine:
             self.draft._prefill(dkv, prompt_ids, 0)
             dec = self._spec_decoder()
             dec.begin(token, pos)
+        t_pre = time.perf_counter() - t_pre
         generated = []
         steps = 0
         t_dec = time.perf_counter()
@@ -241,7 +243,7 @@ class LayerStreamingEngine:
                 self.stats["tokens_served"] += 1
                 if callback:
                     callback(token)
-        self.last_decode = {"seconds": time.perf_counter() - t_dec, "tokens": len(generated),
+        self.last_decode = {"seconds": time.perf_counter() - t_dec, "prefill_seconds": t_pre, "tokens": len(generated),
                             "steps": steps}
         self._kv_len = pos
         return generated

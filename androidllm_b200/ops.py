@@ -12,6 +12,9 @@ from . import safetensors
 from ._lib import ModelConfig, ProjSrc, check, lib, ptr
 
 PROJ_BASES = ("q", "k", "v", "o", "gate", "up", "down")   # androidllm/shard.py:111
+# ALM_OP_* codes of include/androidllm_b200.h, in order
+OP_NAMES = ("begin", "embed", "qkv", "attn_scores", "attn_pv", "o", "gate_up", "down", "final_norm", "head",
+            "argmax", "spec_prep", "spec_accept", "sample")
 
 # At interpreter exit the order of finalizers is arbitrary (a context could go
 # before the models on it); the process teardown frees device memory anyway.
@@ -464,6 +467,19 @@ class SpecDecoder:
         ms, n = ctypes.c_float(), ctypes.c_int32()
         check(lib.alm_spec_bench(self.h, int(n_steps), ctypes.byref(ms), ctypes.byref(n)))
         return ms.value, n.value
+
+    def profile(self, cap=4096):
+        """Device time of every kernel launch of one step from the current
+        state (alm_spec_profile): a list of (role, op, rows, us), role
+        "draft" / "target" / "spec", op the ALM_OP_* name."""
+        ops = np.empty(cap, np.int32)
+        rows = np.empty(cap, np.int32)
+        us = np.empty(cap, np.float32)
+        n = ctypes.c_int32()
+        check(lib.alm_spec_profile(self.h, cap, ptr(ops), ptr(rows), ptr(us), ctypes.byref(n)))
+        roles = {0: "spec", 1: "draft", 2: "target"}
+        return [(roles[int(o) // 100], OP_NAMES[int(o) % 100], int(r), float(u))
+                for o, r, u in zip(ops[: n.value], rows[: n.value], us[: n.value])]
 
     def kernel_count(self):
         n = ctypes.c_int32()

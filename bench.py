@@ -101,6 +101,68 @@ def forward_weight_bytes(man):
     return total
 
 
+def _proj_bytes(man, bases, m):
+    """Algorithmic bytes of one fused GEMV over the projections ``bases`` of
+    layer 0 (weights + scales + m input rows + m output rows)."""
+    q = [man["quant"]["layers"]["0"][b] for b in bases]
+    n = sum(p["out"] for p in q)
+    k = q[0]["in"]
+    w = sum(p["out"] * p["in"] * p["bits"] // 8 + p["out"] * (p["in"] // p["block"]) * 2 for p in q)
+    return w + m * k * 2 + m * n * 2, n, k, q[0]["bits"]
+
+
+def _head_bytes(man, m):
+    c = man["config"]
+    hq = man.get("lm_head_quant") or man.get("embed_quant") or {}
+    bits = hq.get("bits", 16)
+    w = c["vocab"] * c["hidden"] * bits // 8 + (c["vocab"] * (c["hidden"] // hq["block"]) * 2 if hq else 0)
+    return w + m * c["hidden"] * 2 + m * c["vocab"] * 2, bits
+
+
+_GEMV_OPS = {"qkv": (("q", "k", "v"), "qkv+rope+kv write"), "o": (("o",), "resid"),
+             "gate_up": (("gate", "up"), "swiglu"), "down": (("down",), "resid")}
+
+
+def step_profile_groups(prof, tman, dman, pos, k):
+    """Group alm_spec_profile launches by (model, operation): launches, device
+    time, share of the step, and achieved GB/s from the algorithmic bytes of
+    each launch (GEMV: weights + scales + activations; attention: the K or V
+    rows of the context it reads; the rest: none counted)."""
+    groups, total, fwd = {}, 0.0, -1
+    for role, op, rows, us in prof:
+        total += us
+        man = dman if role == "draft" else tman
+        if role == "draft" and op == "embed":
+            fwd += 1
+        nbytes, desc = 0, op
+        if role in ("draft", "target") and op in _GEMV_OPS:
+            bases, epi = _GEMV_OPS[op]
+            nbytes, n, kk, bits = _proj_bytes(man, bases, rows)
+            desc = f"{op}: gemv_kernel<int{bits}, {epi}> {n}x{kk}, M={rows}"
+        elif role in ("draft", "target") and op == "head":
+            nbytes, bits = _head_bytes(man, rows)
+            c = man["config"]
+            desc = f"head: gemv_kernel<int{bits}, logits> {c['vocab']}x{c['hidden']}, M={rows}"
+        elif op in ("attn_scores", "attn_pv"):
+            c = man["config"]
+            ctx = pos + (fwd + 1 if role == "draft" else k + 1)
+            nbytes = c["kv_heads"] * ctx * c["head_dim"] * 2
+            desc = f"{op}_kernel hd={c['head_dim']} group={c['heads'] // c['kv_heads']} ctx~{ctx}, M={rows}"
+        key = f"{role}.{op}"
+        g = groups.setdefault(key, {"key": key, "kernel": f"{role} {desc}", "launches": 0, "us": 0.0, "bytes": 0})
+        g["launches"] += 1
+        g["us"] += us
+        g["bytes"] += nbytes
+    out = []
+    for g in groups.values():
+        g["us_per_launch"] = round(g["us"] / g["launches"], 2)
+        g["share"] = round(g["us"] / total, 4)
+        g["gbs"] = round(g["bytes"] / (g["us"] * 1e3), 1) if g["us"] > 0 else 0.0
+        g["bytes_per_launch"] = g["bytes"] // g["launches"]
+        out.append(g)
+    return sorted(out, key=lambda g: -g["us"])
+
+
 # --------------------------------------------------------------------------
 # clocks during the timed region
 # --------------------------------------------------------------------------
@@ -121,7 +183,7 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.device), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-i", str(self.device), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         return self
@@ -156,36 +218,67 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # CPU baseline: the oracle port of the reference numpy path (bounded sample)
 # --------------------------------------------------------------------------
+def host_description():
+    """nproc and the CPU model of this host (the CPU baseline's machine)."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model}
+
+
 class CpuSample:
     """Times the reference numpy computation (oracle restatement of
-    androidllm/models/llama.py) for the workload's shapes: one target layer,
-    one draft layer (each at position PROMPT_LEN) and a 1/layers slice of each
-    LM head per sample, then extrapolates the time of one speculative step."""
+    androidllm/models/llama.py and quant.py) for the workload's shapes: one
+    target layer, one draft layer (each at position PROMPT_LEN) and a
+    1/layers slice of each LM head per sample, plus the per-layer dequant
+    that the reference's default streaming engine repeats for every layer of
+    every token (androidllm/engine.py:160-174), then extrapolates the time of
+    one speculative step for resident and for streamed weights."""
 
     def __init__(self, workload):
         from androidllm_b200 import synth
-        from oracle import llama
-        tname, _, dname, _ = WORKLOADS[workload]
+        from oracle import llama, quant
+        tname, tkw, dname, dkw = WORKLOADS[workload]
         self.llama = llama
+        self.quant = quant
         self.tc = dict(synth.CANONS[tname])
         self.dc = dict(synth.CANONS[dname or tname], layers=2 if dname is None else synth.CANONS[dname]["layers"])
         rng = np.random.default_rng(0)
-        self.t = self._setup(self.tc, rng)
-        self.d = self._setup(self.dc, rng)
+        self.t = self._setup(self.tc, tkw, rng)
+        self.d = self._setup(self.dc, dkw or tkw, rng)
 
-    def _setup(self, c, rng):
+    def _setup(self, c, kw, rng):
         h, hd, nh, nkv, i = c["hidden"], c["head_dim"], c["heads"], c["kv_heads"], c["intermediate"]
         mk = lambda *s: (rng.standard_normal(s, dtype=np.float32) * 0.02).astype(np.float16)  # noqa: E731
-        layer = {"q": mk(nh * hd, h), "k": mk(nkv * hd, h), "v": mk(nkv * hd, h), "o": mk(h, nh * hd),
-                 "gate": mk(i, h), "up": mk(i, h), "down": mk(h, i),
-                 "n_in": np.ones(h, np.float16), "n_post": np.ones(h, np.float16)}
+        shapes = {"q": (nh * hd, h), "k": (nkv * hd, h), "v": (nkv * hd, h), "o": (h, nh * hd),
+                  "gate": (i, h), "up": (i, h), "down": (h, i)}
+        layer = {b: mk(*sh) for b, sh in shapes.items()}
+        layer["n_in"] = np.ones(h, np.float16)
+        layer["n_post"] = np.ones(h, np.float16)
+        # the shard-format codes of one layer, dequantized per token when streaming
+        packed = {}
+        for b, (o, k) in shapes.items():
+            bits = kw["attn_bits"] if b in ("q", "k", "v", "o") else kw["mlp_bits"]
+            blk = kw["block"]
+            if bits == 4:
+                codes = rng.integers(0, 256, size=(o, k // 2), dtype=np.uint8)
+            else:
+                codes = rng.integers(-127, 128, size=(o, k), dtype=np.int8)
+            packed[b] = (codes, (np.abs(rng.standard_normal((o, k // blk))) * 0.003).astype(np.float16),
+                         {"bits": bits, "block": blk, "out": o, "in": k})
         canon = dict(c, max_len=PROMPT_LEN + 8)
         model = self.llama.OracleModel(canon, None, np.ones(h, np.float16), None)
         kv = (mk(PROMPT_LEN + 8, nkv, hd) * 50, mk(PROMPT_LEN + 8, nkv, hd) * 50)
         n_slice = -(-c["vocab"] // c["layers"])
         head_slice = mk(n_slice, h)
         x = (rng.standard_normal((1, h)).astype(np.float16))
-        return {"c": c, "layer": layer, "model": model, "kv": kv, "head": head_slice, "x": x}
+        return {"c": c, "layer": layer, "packed": packed, "model": model, "kv": kv, "head": head_slice, "x": x}
 
     def _one(self, s):
         t0 = time.perf_counter()
@@ -194,42 +287,50 @@ class CpuSample:
         h = self.llama.rms_norm(s["x"], s["model"].final_norm)
         self.llama.matmul_f16(h.astype(np.float16), s["head"])
         t2 = time.perf_counter()
-        # per full token: layers x layer time + layers x (1/layers of the head)
-        return s["c"]["layers"] * ((t1 - t0) + (t2 - t1))
+        for codes, scale, meta in s["packed"].values():
+            self.quant.dequantize_packed(codes, scale, meta)
+        t3 = time.perf_counter()
+        # per full token: layers x (layer time [+ its dequant]) + layers x (1/layers of the head)
+        n = s["c"]["layers"]
+        return n * ((t1 - t0) + (t2 - t1)), n * (t3 - t2)
 
     def step(self, tokens_per_step, k=SPEC_K):
         """Seconds of one reference speculative step (androidllm/engine.py:288-320):
-        k draft tokens, then one target token per emitted token."""
-        t_target = self._one(self.t)
-        t_draft = self._one(self.d)
-        return k * t_draft + tokens_per_step * t_target, t_target, t_draft
+        k draft tokens, then one target token per emitted token; resident
+        weights, and the extra per-token dequant of the streaming engine."""
+        t_target, dq_target = self._one(self.t)
+        t_draft, dq_draft = self._one(self.d)
+        resident = k * t_draft + tokens_per_step * t_target
+        streaming = resident + k * dq_draft + tokens_per_step * dq_target
+        return resident, streaming, t_target, t_draft
 
 
 def cpu_baseline(workload, tokens_per_step, samples):
     s = CpuSample(workload)
     s.step(tokens_per_step)       # warm-up
-    times = []
-    t0 = time.perf_counter()
-    tt = td = 0.0
+    res, stream, walls = [], [], []
     for _ in range(samples):
-        st, a, b = s.step(tokens_per_step)
-        times.append(st)
-        tt += a
-        td += b
-    wall = time.perf_counter() - t0
-    step_s = statistics.mean(times)
+        t0 = time.perf_counter()
+        a, b, _, _ = s.step(tokens_per_step)
+        walls.append(time.perf_counter() - t0)
+        res.append(a)
+        stream.append(b)
+    host = host_description()
     return {
-        "value": tokens_per_step / step_s,
+        "value": tokens_per_step / statistics.mean(res),
         "unit": "tokens/s",
         "cores": 1,
         "kind": "port",
-        "sample": (f"{samples} samples of one target layer + one draft layer at position {PROMPT_LEN} "
-                   f"and a 1/layers slice of each fp16 LM head (numpy fp16 matmul, 1 thread), "
-                   f"extrapolated to a full step of {SPEC_K} draft tokens + {tokens_per_step:.2f} target "
-                   f"tokens with resident dequantized weights (the reference's default streaming engine "
-                   f"also dequantizes every layer per token); {wall:.1f}s of CPU work"),
-        "target_token_s": tt / samples,
-        "draft_token_s": td / samples,
+        "value_streaming": tokens_per_step / statistics.mean(stream),
+        "host": host,
+        "sample": (f"{samples} samples of one target layer + one draft layer at position {PROMPT_LEN}, "
+                   f"a 1/layers slice of each fp16 LM head, and one layer's dequantize_packed of each model "
+                   f"(numpy, 1 thread: numpy's fp16 matmul has no BLAS path and the reference decodes one "
+                   f"sequence; host has {host['nproc']} threads, {host['cpu_model']}), extrapolated to a full "
+                   f"step of {SPEC_K} draft tokens + {tokens_per_step:.2f} target tokens; value = resident "
+                   f"dequantized weights, value_streaming = the reference's default streaming engine, which "
+                   f"also dequantizes every layer for every token; {sum(walls):.1f}s of CPU work"),
+        "sample_s": statistics.mean(walls),
     }
 
 
@@ -239,16 +340,20 @@ def run_reference(args):
         return 0
     tokens_per_step = 1.0
     t0 = time.perf_counter()
-    # each sample is ~0.3 s of numpy work at the 1.5B shapes; cap the count so
+    # each sample is ~0.5 s of numpy work at the 1.5B shapes; cap the count so
     # the arm ends within a few minutes whatever --steps is
     cb = cpu_baseline(args.workload, tokens_per_step, min(REF_MAX_SAMPLES, max(1, args.steps)))
     line = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * tokens_per_step / cb["value"], "higher_is_better": True,
+        # a step of this arm is one bounded sample (see cpu_baseline.sample);
+        # the full speculative step it stands for is extrapolated
+        "ms_per_step": round(1000.0 * cb["sample_s"], 3),
+        "ms_per_full_step_extrapolated": round(1000.0 * tokens_per_step / cb["value"], 1),
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": workload_config(args, world),
-        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "value_streaming", "host")},
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
     }
@@ -269,13 +374,13 @@ def workload_config(args, world):
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
-def _profiled_traffic(name):
-    """DRAM bytes per launch of the roofline kernel from its committed ncu
-    summary (profiles/), or None."""
-    path = os.path.join(ROOT, "profiles", name)
+def _profiled_traffic(key):
+    """DRAM bytes per launch of a step operation (``draft.down`` and so on)
+    from the committed ncu summary profiles/step_kernel_dram.json, or None."""
+    path = os.path.join(ROOT, "profiles", "step_kernel_dram.json")
     try:
         with open(path) as f:
-            return json.load(f)["dram_bytes_per_launch"]
+            return json.load(f)[key]["dram_bytes_per_launch"]
     except (OSError, KeyError, ValueError):
         return None
 
@@ -318,41 +423,49 @@ def run_ours(args):
     out = eng.generate(prompt, max_new_tokens=EPISODE_TOKENS, temperature=0)
     dec = eng.last_decode
     e2e = {"value": len(out) / dec["seconds"], "unit": "tokens/s",
+           "scope": "decode steps of generate() (the prompt's prefill is timed separately: prefill_ms)",
+           "prefill_ms": round(dec["prefill_seconds"] * 1000.0, 2),
            # per step: the (token, pos) state in (16 B), the state + emitted
            # tokens + accepted count out
            "h2d_bytes_per_step": 16,
            "d2h_bytes_per_step": 16 + 4 * (len(out) / max(1, dec["steps"])) + 4,
            "steps": dec["steps"], "tokens": len(out)}
 
-    # device-resident throughput: episodes of up to EPISODE_TOKENS steps from
-    # the post-prompt state, graph replays timed with CUDA events
+    # device-resident throughput.  Warm-up: one whole episode from the
+    # post-prompt state (positions 511..767 and the tokens at them).  Timed:
+    # exactly --steps speculative steps whose start positions are spread
+    # evenly over the episode, each a replay of the step graph timed with
+    # CUDA events on the decoder's stream, so attention sees the episode's
+    # context lengths 512-768 in proportion.
     spec = eng._spec_decoder()
     state0 = (prompt[-1], PROMPT_LEN - 1)
     eng._target_kv().cache.zero()
     eng._prefill(eng._kv, prompt[:-1], 0)
     eng._draft_kv().cache.zero()
     eng.draft._prefill(eng.draft._kv, prompt, 0)
-
-    def episodes(n_steps):
-        ms_tot, tok_tot, left = 0.0, 0, n_steps
-        while left > 0:
-            n = min(left, EPISODE_TOKENS)
-            spec.begin(*state0)
-            ms, tok = spec.bench(n)
-            ms_tot += ms
-            tok_tot += tok
-            left -= n
-        return ms_tot, tok_tot
-
-    episodes(max(3, args.warmup))
+    clk = ClockSampler(local).__enter__()          # sampled from the warm-up on
+    spec.begin(*state0)
+    stream = [prompt[-1]]
+    while len(stream) <= EPISODE_TOKENS:
+        emitted, _ = spec.run(1)
+        stream += emitted
+    for _ in range(max(0, args.warmup - 1)):
+        spec.begin(*state0)
+        spec.bench(min(EPISODE_TOKENS, 64))
+    starts = [PROMPT_LEN - 1 + (i * EPISODE_TOKENS) // args.steps for i in range(args.steps)]
     if dist is not None:
         import torch
         dist.barrier()
         torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_wall = time.perf_counter()
-        ms, tokens = episodes(args.steps)
-        t_wall = time.perf_counter() - t_wall
+    t_wall = time.perf_counter()
+    ms, tokens = 0.0, 0
+    for p0 in starts:
+        spec.begin(stream[p0 - (PROMPT_LEN - 1)], p0)
+        m1, n1 = spec.bench(1)
+        ms += m1
+        tokens += n1
+    t_wall = time.perf_counter() - t_wall
+    clk.__exit__(None, None, None)
     if dist is not None:
         import torch
         torch.cuda.synchronize()
@@ -363,27 +476,21 @@ def run_ours(args):
     value = tokens_all / (ms_max / 1000.0)
     ms_per_step = ms_max / args.steps
 
-    # roofline of the dominant kernel: the fused gate/up dequant-GEMV of the
-    # target verify pass (int8, N = 2 x 8960, K = 1536, M = k+1 = 5), timed in
-    # isolation over rotating weight copies larger than L2
-    c = eng.canon
-    n_gu, k_gu, m = 2 * c["intermediate"], c["hidden"], SPEC_K + 1
-    rng = np.random.default_rng(7)
-    copies = []
-    for i in range(6):
-        q = rng.integers(-127, 128, size=(n_gu, k_gu), dtype=np.int8)
-        s = (np.abs(rng.standard_normal((n_gu, k_gu // 64))) * 0.003 + 1e-4).astype(np.float16)
-        copies.append(QWeight(eng.ctx, QuantProj(q, s, 8, 64, n_gu, k_gu)))
-    x = rng.standard_normal((m, k_gu)).astype(np.float16)
-    us = bench_qmatmul(eng.ctx, copies, x, 600)
-    alg = gemv_bytes(n_gu, k_gu, m, 8)
+    # per-launch device times of one step at the middle of the episode
+    # (alm_spec_profile: the step re-captured with a timing event after every
+    # kernel); the operation with the largest share is the roofline kernel
+    mid = PROMPT_LEN - 1 + EPISODE_TOKENS // 2
+    spec.begin(stream[mid - (PROMPT_LEN - 1)], mid)
+    prof = spec.profile()
     peaks = load_peaks()
-    achieved = alg / (us * 1e-6) / 1e9
-    roofline = {"kernel": "gemv_kernel<8,1,*> fused gate/up, int8, N=17920 K=1536 M=5",
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 3),
-                "peak_source": peaks["source"], "algorithmic_bytes": alg, "avg_launch_us": round(us, 2),
-                "traffic": _profiled_traffic("gemv_int8_17920x1536_m5_dram.json")}
+    groups = step_profile_groups(prof, eng.manifest, eng.draft.manifest, mid, SPEC_K)
+    top = groups[0]
+    roofline = {"kernel": top["kernel"], "bound": "hbm", "achieved": top["gbs"], "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(top["gbs"] / peaks["hbm_gbs"], 3),
+                "peak_source": peaks["source"], "algorithmic_bytes": top["bytes_per_launch"],
+                "avg_launch_us": top["us_per_launch"], "launches_per_step": top["launches"],
+                "share_of_step": top["share"],
+                "traffic": _profiled_traffic(top["key"])}
     step_bytes = SPEC_K * forward_weight_bytes(eng.draft.manifest) + forward_weight_bytes(eng.manifest)
     step_roof = step_bytes / (ms_per_step * 1e-3) / 1e9
 
@@ -391,9 +498,16 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic", "config": workload_config(args, world),
+        "data": "synthetic", "config": dict(workload_config(args, world),
+                                            positions_timed=[starts[0], starts[-1]]),
         "e2e": {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()},
         "roofline": roofline,
+        "step_profile": {"position": mid, "launches": len(prof),
+                         "sum_us": round(sum(r[3] for r in prof), 1),
+                         "note": "per-launch device times of one step re-captured with an event after every "
+                                 "kernel (no programmatic dependent launch); shares of that sum",
+                         "top": [{k: g[k] for k in ("kernel", "launches", "us_per_launch", "share", "gbs")}
+                                 for g in groups[:8]]},
         "step_roofline": {"weight_bytes_per_step": step_bytes, "achieved_gbs": round(step_roof, 1),
                           "frac": round(step_roof / peaks["hbm_gbs"], 3)},
         "tokens_per_step": round(tokens_all / (args.steps * world), 3),

@@ -248,6 +248,25 @@ ALM_API int alm_spec_uniforms_used(alm_spec* s, int32_t* used);
  * events on the context's stream: *ms = device time, *n_emitted = tokens.
  * The state advances as in alm_spec_run. */
 ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted);
+/* Operations of a speculative step, as alm_spec_profile reports them
+ * (op + 100 * role; role 1 = draft forward, 2 = target verify forward,
+ * 0 = the step's own bookkeeping). */
+enum {
+  ALM_OP_BEGIN = 0, ALM_OP_EMBED = 1, ALM_OP_QKV = 2, ALM_OP_ATTN_SCORES = 3, ALM_OP_ATTN_PV = 4,
+  ALM_OP_O = 5, ALM_OP_GATE_UP = 6, ALM_OP_DOWN = 7, ALM_OP_FINAL_NORM = 8, ALM_OP_HEAD = 9,
+  ALM_OP_ARGMAX = 10, ALM_OP_SPEC_PREP = 11, ALM_OP_SPEC_ACCEPT = 12, ALM_OP_SAMPLE = 13
+};
+/* Device time of every kernel launch of one speculative step (profiling; no
+ * counterpart in the reference).  The step is captured once more with a
+ * timing event after each launch and without programmatic dependent launch,
+ * replayed from the current state (which is restored afterwards), and
+ * timed on the context's stream: launch i ran from event i to event i+1.
+ * ops_host / rows_host / us_host (capacity cap) receive each launch's
+ * operation code (see above), activation rows and microseconds; *n_out
+ * their count.  Kernels back to back without overlap: the shares, not the
+ * sum, are what compare with the step graph. */
+ALM_API int alm_spec_profile(alm_spec* s, int cap, int32_t* ops_host, int32_t* rows_host, float* us_host,
+                             int32_t* n_out);
 /* Start (1) or stop (0) the CUDA profiler's capture range, so a profiler
  * started with capture disabled records only the work in between. */
 ALM_API int alm_profiler_range(int start);
