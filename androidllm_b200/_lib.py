@@ -83,6 +83,9 @@ SIGNATURES = {
     "alm_spec_kernel_count": [_P, _PI32],
     "alm_spec_set_sampling": [_P, ctypes.c_float, ctypes.c_float, ctypes.c_float],
     "alm_spec_set_uniforms": [_P, _P, _I],
+    "alm_spec_set_rejection": [_P, _I],
+    "alm_probs": [_P, _P, _I, _I, ctypes.c_float, ctypes.c_float, _P],
+    "alm_accept": [_P, _P, _P, _P, _I, _I, ctypes.c_float, ctypes.c_float, _P, _P, _PI32],
     "alm_spec_uniforms_used": [_P, _PI32],
     "alm_sample": [_P, _P, _I, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],
     "alm_model_sample": [_P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],

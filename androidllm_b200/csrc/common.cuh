@@ -170,6 +170,27 @@ ALM_DEV float fsub(float a, float b) { return __fsub_rn(a, b); }
 ALM_DEV float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 ALM_DEV float round_h(float a) { return __half2float(__float2half_rn(a)); }
 
+// exp(x) for fp32 x <= 0 from correctly rounded fp32 operations only.
+ALM_DEV float rexp(float x) {
+  const float log2e = __uint_as_float(0x3fb8aa3bu);
+  const float ln2_hi = __uint_as_float(0x3f317200u);   // fp32(ln 2) with its low 9 mantissa bits cleared
+  const float ln2_lo = __uint_as_float(0x35bfbe8eu);   // fp32(ln 2 - ln2_hi)
+  const float k = rintf(fmul(x, log2e));
+  const float r = fsub(fsub(x, fmul(k, ln2_hi)), fmul(k, ln2_lo));
+  // 1/7!, 1/6!, ..., 1/1!, 1/0! in Horner order
+  const uint32_t c[8] = {0x39500d01u, 0x3ab60b61u, 0x3c088889u, 0x3d2aaaabu,
+                         0x3e2aaaabu, 0x3f000000u, 0x3f800000u, 0x3f800000u};
+  float acc = __uint_as_float(c[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) acc = fadd(fmul(acc, r), __uint_as_float(c[i]));
+  // exact scaling by 2^k: for x >= -87, k >= -126 so 2^k is a normal fp32 and
+  // one correctly rounded multiply equals ldexp
+  const int ki = static_cast<int>(k);
+  const float scale = __int_as_float((ki + 127) << 23);
+  return x < __uint_as_float(0xc2ae0000u) ? 0.f : fmul(acc, scale);   // below -87: 0
+}
+
+
 ALM_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

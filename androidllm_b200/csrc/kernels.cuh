@@ -183,6 +183,49 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
 
+// ---- speculative rejection sampling (accept.cu) ----------------------------
+constexpr int kAccMaxChunks = 4096;   // rows of up to 4096 * 256 entries
+
+// Rows of softmax((l - max) / t), min-p filtered when 0 < min_p < 1.
+struct ProbsArgs {
+  const half* logits = nullptr;  int ld = 0;
+  float* probs = nullptr;        int ldp = 0;
+  int vocab = 0;
+  float t = 1.f;                 // fp32(max(temperature, 1e-9))
+  float min_p = 0.f;
+};
+// One inverse-CDF draw from a probability row with draw u[*cursor + u_offset].
+struct DrawArgs {
+  const float* probs = nullptr;
+  int vocab = 0;
+  const double* u = nullptr;
+  const int* cursor = nullptr;   // nullable: 0
+  int u_offset = 0;
+  int* out = nullptr;
+};
+// min(1, p/q) acceptance of k candidates; draws u[*cursor + u_offset + i]
+// (accept i) and u[*cursor + u_offset + k] (resample).  Outputs: tokens
+// (k + 1, the accepted prefix then the resampled / bonus token) and n_acc,
+// and, with state, the speculative step's state / ring update.
+struct AcceptArgs {
+  const float* p = nullptr;  int ldp = 0;
+  const float* q = nullptr;  int ldq = 0;
+  const int* cand = nullptr;
+  int k = 0, vocab = 0;
+  const double* u = nullptr;
+  const int* cursor = nullptr;
+  int u_offset = 0;
+  int* tokens = nullptr;
+  int* n_acc = nullptr;
+  int* state = nullptr;
+  int* ring = nullptr;
+  int* ring_acc = nullptr;
+  int cap_tokens = 0, cap_steps = 0, cursor_advance = 0;
+};
+cudaError_t launch_probs(const ProbsArgs& a, int rows, cudaStream_t st);
+cudaError_t launch_draw(const DrawArgs& a, cudaStream_t st);
+cudaError_t launch_accept(const AcceptArgs& a, cudaStream_t st);
+
 // Per-launch profile of a speculative step (alm_spec_profile): while a
 // profiled step is being captured, prof_mark records a timing event after
 // each kernel launch, tagged with the launch's operation (ALM_OP_* of the

@@ -210,6 +210,20 @@ void dev_free(void* p) {
   if (p) cudaFree(p);
 }
 
+// Device copies of a standalone call's inputs and outputs (freed on return).
+struct DevBufs {
+  std::vector<void*> ptrs;
+  ~DevBufs() {
+    for (void* p : ptrs) cudaFree(p);
+  }
+  template <typename T>
+  int get(T** p, size_t count) {
+    ALM_TRY(dev_alloc_t(p, count));
+    ptrs.push_back(*p);
+    return ALM_OK;
+  }
+};
+
 }  // namespace
 
 struct alm_model {
@@ -259,6 +273,9 @@ struct alm_spec {
   float top_p = 1.f, min_p = 0.f;
   double* uniforms = nullptr;  // device stream of uniform draws; state[4] = next unused
   int n_uniforms = 0, cap_uniforms = 0;
+  // min(1, p/q) rejection sampling instead of the reference's rule (T > 0)
+  bool rejection = false;
+  float* probs = nullptr;      // (k + 1) target rows then k draft rows of vocab fp32
 };
 
 namespace {
@@ -1500,6 +1517,93 @@ int alm_sample(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, f
   return rc;
 }
 
+int alm_probs(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature, float min_p,
+              float* probs_host) {
+  ALM_REQ(ctx && logits_host && probs_host, "null argument");
+  ALM_REQ(rows >= 1 && vocab >= 1 && vocab <= kAccMaxChunks * 256, "rows >= 1 and 1 <= vocab <= 1048576");
+  ALM_REQ(temperature > 0.f, "temperature must be positive");
+  ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
+  DeviceGuard g(ctx->device);
+  const size_t n = static_cast<size_t>(rows) * vocab;
+  DevBufs b;
+  half* lg = nullptr;
+  float* pr = nullptr;
+  ALM_TRY(b.get(&lg, n));
+  ALM_TRY(b.get(&pr, n));
+  ALM_CUDA(cudaMemcpyAsync(lg, logits_host, n * sizeof(half), cudaMemcpyHostToDevice, ctx->stream));
+  ProbsArgs a;
+  a.logits = lg;
+  a.ld = vocab;
+  a.probs = pr;
+  a.ldp = vocab;
+  a.vocab = vocab;
+  a.t = std::max(temperature, 1e-9f);
+  a.min_p = min_p;
+  ALM_CUDA(launch_probs(a, rows, ctx->stream));
+  ALM_CUDA(cudaMemcpyAsync(probs_host, pr, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  ALM_CUDA(cudaStreamSynchronize(ctx->stream));
+  return ALM_OK;
+}
+
+int alm_accept(alm_ctx* ctx, const uint16_t* target_logits_host, const float* draft_probs_host,
+               const int32_t* draft_tokens_host, int k, int vocab, float temperature, float min_p,
+               const double* uniforms_host, int32_t* out_tokens_host, int32_t* n_accepted_host) {
+  ALM_REQ(ctx && target_logits_host && draft_probs_host && draft_tokens_host && uniforms_host && out_tokens_host &&
+              n_accepted_host,
+          "null argument");
+  ALM_REQ(k >= 1 && k <= 31, "k must be in 1..31");
+  ALM_REQ(vocab >= 1 && vocab <= kAccMaxChunks * 256, "vocab must be in 1..1048576");
+  ALM_REQ(temperature > 0.f, "temperature must be positive");
+  ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
+  for (int i = 0; i < k; ++i) ALM_REQ(draft_tokens_host[i] >= 0 && draft_tokens_host[i] < vocab, "draft token out of range");
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const size_t vp = static_cast<size_t>(k + 1) * vocab, vq = static_cast<size_t>(k) * vocab;
+  DevBufs b;
+  half* lg = nullptr;
+  float *p = nullptr, *q = nullptr;
+  int *cand = nullptr, *tok = nullptr;
+  double* u = nullptr;
+  ALM_TRY(b.get(&lg, vp));
+  ALM_TRY(b.get(&p, vp));
+  ALM_TRY(b.get(&q, vq));
+  ALM_TRY(b.get(&cand, static_cast<size_t>(k)));
+  ALM_TRY(b.get(&tok, static_cast<size_t>(k + 2)));
+  ALM_TRY(b.get(&u, static_cast<size_t>(k + 1)));
+  ALM_CUDA(cudaMemcpyAsync(lg, target_logits_host, vp * sizeof(half), cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaMemcpyAsync(q, draft_probs_host, vq * sizeof(float), cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaMemcpyAsync(cand, draft_tokens_host, k * sizeof(int), cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaMemcpyAsync(u, uniforms_host, (k + 1) * sizeof(double), cudaMemcpyHostToDevice, st));
+  ProbsArgs pa;
+  pa.logits = lg;
+  pa.ld = vocab;
+  pa.probs = p;
+  pa.ldp = vocab;
+  pa.vocab = vocab;
+  pa.t = std::max(temperature, 1e-9f);
+  pa.min_p = min_p;
+  ALM_CUDA(launch_probs(pa, k + 1, st));
+  AcceptArgs aa;
+  aa.p = p;
+  aa.ldp = vocab;
+  aa.q = q;
+  aa.ldq = vocab;
+  aa.cand = cand;
+  aa.k = k;
+  aa.vocab = vocab;
+  aa.u = u;
+  aa.tokens = tok;
+  aa.n_acc = tok + k + 1;
+  ALM_CUDA(launch_accept(aa, st));
+  int host[33];
+  ALM_CUDA(cudaMemcpyAsync(host, tok, (k + 2) * sizeof(int), cudaMemcpyDeviceToHost, st));
+  ALM_CUDA(cudaStreamSynchronize(st));
+  const int n = host[k + 1];
+  for (int i = 0; i <= n; ++i) out_tokens_host[i] = host[i];
+  *n_accepted_host = n;
+  return ALM_OK;
+}
+
 int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
                      const double* uniforms_host, int32_t* out_host) {
   ALM_TRY(check_ready(m));
@@ -1546,7 +1650,83 @@ int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, 
 }
 
 // ---- speculative decoding -----------------------------------------------------------
+// The speculative step with min(1, p/q) rejection sampling: every draft
+// candidate is an inverse-CDF draw from the draft's softmax row q_i (draw i),
+// the verify rows' softmax rows p_0..p_k go to the acceptance kernel with
+// draws k..2k (accept i, then the resample); the cursor advances 2k + 1.
+static int enqueue_spec_step_rejection(alm_spec* s) {
+  alm_model* d = s->draft;
+  alm_model* t = s->target;
+  cudaStream_t st = t->ctx->stream;
+  const int V = t->cfg.vocab;
+  float* p_rows = s->probs;
+  float* q_rows = s->probs + static_cast<size_t>(s->k + 1) * V;
+  for (int i = 0; i < s->k; ++i) {
+    prof_role(0);
+    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
+    prof_mark(ALM_OP_SPEC_PREP, 1);
+    prof_role(1);
+    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
+    ProbsArgs pa;
+    pa.logits = d->ws.logits;
+    pa.ld = V;
+    pa.probs = q_rows + static_cast<size_t>(i) * V;
+    pa.ldp = V;
+    pa.vocab = V;
+    pa.t = s->temperature;
+    pa.min_p = s->min_p;
+    ALM_CUDA(launch_probs(pa, 1, st));
+    prof_mark(ALM_OP_SAMPLE, 1);
+    DrawArgs da;
+    da.probs = pa.probs;
+    da.vocab = V;
+    da.u = s->uniforms;
+    da.cursor = s->state + 4;
+    da.u_offset = i;
+    da.out = d->ws.argmax;
+    ALM_CUDA(launch_draw(da, st));
+    prof_mark(ALM_OP_SAMPLE, 1);
+  }
+  prof_role(0);
+  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
+  prof_mark(ALM_OP_SPEC_PREP, s->k + 1);
+  prof_role(2);
+  ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
+  ProbsArgs pa;
+  pa.logits = t->ws.logits;
+  pa.ld = V;
+  pa.probs = p_rows;
+  pa.ldp = V;
+  pa.vocab = V;
+  pa.t = s->temperature;
+  pa.min_p = s->min_p;
+  ALM_CUDA(launch_probs(pa, s->k + 1, st));
+  prof_mark(ALM_OP_SAMPLE, s->k + 1);
+  prof_role(0);
+  AcceptArgs aa;
+  aa.p = p_rows;
+  aa.ldp = V;
+  aa.q = q_rows;
+  aa.ldq = V;
+  aa.cand = s->cand;
+  aa.k = s->k;
+  aa.vocab = V;
+  aa.u = s->uniforms;
+  aa.cursor = s->state + 4;
+  aa.u_offset = s->k;
+  aa.state = s->state;
+  aa.ring = s->out_tokens;
+  aa.ring_acc = s->out_acc;
+  aa.cap_tokens = s->cap_tokens;
+  aa.cap_steps = s->cap_steps;
+  aa.cursor_advance = 2 * s->k + 1;
+  ALM_CUDA(launch_accept(aa, st));
+  prof_mark(ALM_OP_SPEC_ACCEPT, s->k + 1);
+  return ALM_OK;
+}
+
 static int enqueue_spec_step(alm_spec* s) {
+  if (s->rejection && s->temperature > 0.f) return enqueue_spec_step_rejection(s);
   alm_model* d = s->draft;
   alm_model* t = s->target;
   cudaStream_t st = t->ctx->stream;
@@ -1588,6 +1768,8 @@ static int capture_spec_graph(alm_spec* s) {
     ALM_TRY(ensure_sample_scratch(s->target));
     ALM_TRY(ensure_sample_scratch(s->draft));
   }
+  if (s->rejection && !s->probs)
+    ALM_TRY(dev_alloc_t(&s->probs, static_cast<size_t>(2 * s->k + 1) * s->target->cfg.vocab));
   if (s->graph) {
     cudaGraphExecDestroy(s->graph);
     s->graph = nullptr;
@@ -1665,6 +1847,7 @@ int alm_spec_destroy(alm_spec* s) {
   dev_free(s->out_tokens);
   dev_free(s->out_acc);
   dev_free(s->uniforms);
+  dev_free(s->probs);
   if (s->pinned) cudaFreeHost(s->pinned);
   delete s;
   return ALM_OK;
@@ -1714,6 +1897,15 @@ int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min
   s->temperature = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
   s->top_p = top_p;
   s->min_p = min_p;
+  return capture_spec_graph(s);
+}
+
+int alm_spec_set_rejection(alm_spec* s, int enable) {
+  ALM_REQ(s, "null spec");
+  DeviceGuard g(s->target->ctx->device);
+  ALM_REQ(s->target->cfg.vocab <= kAccMaxChunks * 256, "vocabulary too large for the acceptance kernel");
+  ALM_CUDA(cudaStreamSynchronize(s->target->ctx->stream));
+  s->rejection = enable != 0;
   return capture_spec_graph(s);
 }
 

@@ -40,26 +40,6 @@ constexpr unsigned long long kMassMask = kCountOne - 1;
 
 ALM_DEV float bits_f(uint32_t u) { return __uint_as_float(u); }
 
-// exp(x) for fp32 x <= 0 from correctly rounded fp32 operations only.
-ALM_DEV float rexp(float x) {
-  const float log2e = bits_f(0x3fb8aa3bu);
-  const float ln2_hi = bits_f(0x3f317200u);   // fp32(ln 2) with its low 9 mantissa bits cleared
-  const float ln2_lo = bits_f(0x35bfbe8eu);   // fp32(ln 2 - ln2_hi)
-  const float k = rintf(fmul(x, log2e));
-  const float r = fsub(fsub(x, fmul(k, ln2_hi)), fmul(k, ln2_lo));
-  // 1/7!, 1/6!, ..., 1/1!, 1/0! in Horner order
-  const uint32_t c[8] = {0x39500d01u, 0x3ab60b61u, 0x3c088889u, 0x3d2aaaabu,
-                         0x3e2aaaabu, 0x3f000000u, 0x3f800000u, 0x3f800000u};
-  float acc = bits_f(c[0]);
-#pragma unroll
-  for (int i = 1; i < 8; ++i) acc = fadd(fmul(acc, r), bits_f(c[i]));
-  // exact scaling by 2^k: for x >= -87, k >= -126 so 2^k is a normal fp32 and
-  // one correctly rounded multiply equals ldexp
-  const int ki = static_cast<int>(k);
-  const float scale = __int_as_float((ki + 127) << 23);
-  return x < bits_f(0xc2ae0000u) ? 0.f : fmul(acc, scale);   // below -87: 0
-}
-
 // floor(p * 2^52) for 0 <= p <= 1, from the fp32 bits (exact: a shift of the
 // 24-bit significand).
 ALM_DEV unsigned long long mass_of(float p) {

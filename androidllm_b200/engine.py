@@ -19,7 +19,10 @@ streaming was a phone's RAM; a B200 holds the model many times over):
   rejection; a plain step takes one draw.
 
 ``seed`` (not in the reference, whose generator is unseeded) makes the
-stream reproducible.  Out of the path and not carried over: prompt-prefix KV
+stream reproducible.  ``accept_rule="rejection"`` (not in the reference)
+accepts sampled candidates by speculative rejection sampling instead: u <
+min(1, p/q), the residual max(0, p - q) resampled at the first rejection,
+2k + 1 draws per step (``alm_spec_set_rejection``).  Out of the path and not carried over: prompt-prefix KV
 reuse, layer skipping, throttling, grammar masking (grammar disables
 speculation in the reference too) and the tokenizer.
 """
@@ -37,7 +40,11 @@ PREFILL_ROWS = 16
 
 
 class LayerStreamingEngine:
-    def __init__(self, model_dir, keep_layers=0, draft_dir=None, spec_k=0, device=0, seed=None, _ctx=None):
+    def __init__(self, model_dir, keep_layers=0, draft_dir=None, spec_k=0, device=0, seed=None,
+                 accept_rule="reference", _ctx=None):
+        if accept_rule not in ("reference", "rejection"):
+            raise ValueError("accept_rule must be 'reference' or 'rejection'")
+        self.accept_rule = accept_rule
         self.model_dir = model_dir
         self.manifest = load_manifest(model_dir)
         canon = self.manifest["config"]
@@ -136,6 +143,7 @@ class LayerStreamingEngine:
     def _feed_spec(self, dec, temperature, top_p, min_p):
         """Sampling settings and enough draws for one speculative step."""
         dec.set_sampling(temperature, top_p, min_p)
+        dec.set_rejection(self.accept_rule == "rejection" and temperature > 0)
         if temperature > 0:
             need = 2 * self.spec_k + 1
             if dec._uniforms is not self._u or self._u_host_moved or self._u.size - self._u_used < need:

@@ -190,6 +190,35 @@ def sample(ctx, logits, temperature, top_p=1.0, min_p=0.0, uniforms=None):
     return out
 
 
+def probs(ctx, logits, temperature, min_p=0.0):
+    """alm_probs: softmax(l / T) rows (min-p filtered) with the rejection
+    sampler's fixed arithmetic, fp32 (rows, vocab)."""
+    lg = _f16(np.atleast_2d(logits))
+    out = np.empty(lg.shape, np.float32)
+    check(lib.alm_probs(ctx.h, ptr(lg), lg.shape[0], lg.shape[1], float(temperature), float(min_p), ptr(out)))
+    return out
+
+
+def accept(ctx, target_logits, draft_probs, draft_tokens, temperature, uniforms, min_p=0.0):
+    """alm_accept: min(1, p/q) acceptance of k draft tokens against k + 1
+    target logit rows; uniforms = k acceptance draws then the resample draw.
+    Returns (emitted tokens, number accepted)."""
+    lg = _f16(np.atleast_2d(target_logits))
+    q = np.ascontiguousarray(np.atleast_2d(draft_probs), dtype=np.float32)
+    tok = np.ascontiguousarray(draft_tokens, dtype=np.int32).reshape(-1)
+    k = tok.size
+    if lg.shape[0] != k + 1 or q.shape != (k, lg.shape[1]):
+        raise ValueError("target_logits (k + 1, vocab), draft_probs (k, vocab), draft_tokens (k,)")
+    u = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(-1)
+    if u.size != k + 1:
+        raise ValueError("k + 1 uniform draws: k acceptance draws and the resample draw")
+    out = np.empty(k + 1, np.int32)
+    n = ctypes.c_int32()
+    check(lib.alm_accept(ctx.h, ptr(lg), ptr(q), ptr(tok), k, lg.shape[1], float(temperature), float(min_p),
+                         ptr(u), ptr(out), ctypes.byref(n)))
+    return out[: n.value + 1].tolist(), n.value
+
+
 def bench_qmatmul(ctx, weights, x, iters):
     """Mean device time (us) of one dequant-GEMV launch, cycling through
     ``weights`` (QWeight of one shape) so their total can exceed L2."""
@@ -450,6 +479,14 @@ class SpecDecoder:
         if key != self._sampling:
             check(lib.alm_spec_set_sampling(self.h, key[0], key[1], key[2]))
             self._sampling = key
+
+    def set_rejection(self, enable):
+        """Sampling steps accept by min(1, p/q) rejection sampling (True) or
+        by the reference's rule (False, the default)."""
+        enable = bool(enable)
+        if enable != getattr(self, "_rejection", False):
+            check(lib.alm_spec_set_rejection(self.h, 1 if enable else 0))
+            self._rejection = enable
 
     def set_uniforms(self, uniforms):
         """Load the uniform draws the sampling steps consume (cursor reset)."""

@@ -191,6 +191,27 @@ ALM_API int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, floa
  * are deterministic. */
 ALM_API int alm_sample(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature,
                  float top_p, float min_p, const double* uniforms_host, int32_t* out_host);
+/* softmax(l / T) of rows of fp16 logits (rows, vocab) -> fp32 probs_host,
+ * min-p filtered when 0 < min_p < 1, with fixed arithmetic (rexp, sums in
+ * 256-element chunks, sequential) so results are reproducible bit for bit.
+ * The distribution the rejection sampler works on (no reference counterpart;
+ * the reference's engine.py:29-36 computes the same softmax in numpy). */
+ALM_API int alm_probs(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature, float min_p,
+                      float* probs_host);
+/* Speculative rejection sampling of k draft candidates (SURVEY's accept
+ * boundary; no reference counterpart, the reference accepts by its own rule,
+ * engine.py:306-320): p = alm_probs of the k + 1 target logit rows
+ * target_logits_host (k + 1, vocab), q = draft_probs_host (k, vocab) the
+ * distributions the candidates draft_tokens_host (k) were drawn from.
+ * Candidate i is accepted iff fp32(uniforms[i]) * q_i(x_i) < p_i(x_i); at the
+ * first rejection the token is drawn from max(0, p_i - q_i) (or p_i if that
+ * has no positive entry) by inverse CDF at uniforms[k]; after k accepts the
+ * bonus token is drawn from p_k the same way.  out_tokens_host (capacity
+ * k + 1) receives the accepted candidates and the drawn token,
+ * *n_accepted_host the number accepted (tokens emitted = n + 1). */
+ALM_API int alm_accept(alm_ctx* ctx, const uint16_t* target_logits_host, const float* draft_probs_host,
+                       const int32_t* draft_tokens_host, int k, int vocab, float temperature, float min_p,
+                       const double* uniforms_host, int32_t* out_tokens_host, int32_t* n_accepted_host);
 /* alm_sample on the first `rows` rows of the model's last computed logits
  * (alm_forward with a head) without copying them to the host. */
 ALM_API int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
@@ -235,6 +256,17 @@ ALM_API int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels);
  * (alm_sample's rule), accepted while they agree.  temperature <= 0 restores
  * the greedy step.  Re-captures the step graph. */
 ALM_API int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min_p);
+/* Sampling steps with min(1, p/q) rejection sampling (enable = 1) instead
+ * of the reference's rule (engine.py:306-320, the default): each draft
+ * candidate is drawn from the draft's softmax(l / T) row (min-p filtered;
+ * top-p is not applied in this mode, since the rule needs the distributions
+ * the candidates were drawn from), candidate i is accepted iff
+ * u_i * q_i(x) < p_i(x), the first rejected row is resampled from
+ * max(0, p - q), and after k accepts a bonus token is drawn from the last
+ * target row.  A step consumes exactly 2k + 1 draws: k candidate draws, k
+ * acceptance draws, one resample draw.  No reference counterpart: the
+ * reference has no rejection sampler.  Re-captures the step graph. */
+ALM_API int alm_spec_set_rejection(alm_spec* s, int enable);
 /* Load the stream of uniform draws in [0, 1) the sampling steps consume in
  * the reference's order (the k draft samples, then one per target row up to
  * the first rejection); resets the cursor to the stream's start.  A run of n
