@@ -165,7 +165,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
     if (i >= nv) break;
     *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = kv8[j];
   }
-  __syncthreads();
+  body_sync();
 
   // warps 0-3: positions c0 + 16 w .. c0 + 16 w + 15 (two n8 tiles); all
   // warps take part in the staging above and in the block barriers below
@@ -214,13 +214,13 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       if (t == 0) sh.red[warp][g + 8 * h] = rmax[h];
     }
   }
-  __syncthreads();
+  body_sync();
   if (tid < kAttnRows) {
     float mx = kNegInf;
     for (int w2 = 0; w2 < kScoreWarps; ++w2) mx = fmaxf(mx, sh.red[w2][tid]);
     sh.mx[tid] = mx;
   }
-  __syncthreads();
+  body_sync();
   float rsum[2] = {0.f, 0.f};
   if (mw) {
 #pragma unroll
@@ -232,7 +232,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
         rsum[e >> 1] = fadd(rsum[e >> 1], ex);
       }
   }
-  __syncthreads();
+  body_sync();
   if (mw) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -241,7 +241,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       if (t == 0) sh.red[warp][g + 8 * h] = rsum[h];
     }
   }
-  __syncthreads();
+  body_sync();
   if (tid < kAttnRows) {
     float l = 0.f;
     for (int w2 = 0; w2 < kScoreWarps; ++w2) l = fadd(l, sh.red[w2][tid]);
@@ -249,7 +249,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
     st[0] = sh.mx[tid];
     st[1] = l;
   }
-  __syncthreads();   // shared memory is reused by the caller's next block
+  body_sync();   // shared memory is reused by the caller's next block
 }
 
 // P.V for (16-dim slice, kv head, group of kPvRows query rows).  Few rows
@@ -375,7 +375,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       sh.pl[warp] = l;
     }
   }
-  __syncthreads();
+  body_sync();
 
   const int g = lane >> 2, t = lane & 3;
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -384,7 +384,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     const int span_pad = (span + 15) & ~15;
     if (base > 0) {   // the first span was loaded with the statistics
       stage_pages(a, base, base + span, s_pg);
-      __syncthreads();
+      body_sync();
       load_span(base, span_pad);
     }
     const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
@@ -409,7 +409,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
         ps[i_row * kPvPld + pl + e] = __float2half_rn(pv);
       }
     }
-    __syncthreads();
+    body_sync();
     for (int kk = warp; kk < span_pad / 16; kk += kAttnWarps) {
       // A: rows g < kPvRows hold P, rows g+8 and g >= kPvRows are zero
       uint32_t a0 = 0, a2 = 0;
@@ -425,14 +425,14 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       mma16816(acc[0], a0, 0u, a2, 0u, b0, b1);
       mma16816(acc[1], a0, 0u, a2, 0u, b2, b3);
     }
-    __syncthreads();
+    body_sync();
   }
 
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) s_acc[(warp * kWarp + lane) * 8 + nt * 4 + e] = acc[nt][e];
-  __syncthreads();
+  body_sync();
   grid_dep_launch();
   if (warp == 0 && g < kPvRows) {
 #pragma unroll
@@ -449,7 +449,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
         }
       }
   }
-  __syncthreads();   // shared memory is reused by the caller's next block
+  body_sync();   // shared memory is reused by the caller's next block
 }
 
 }  // namespace alm

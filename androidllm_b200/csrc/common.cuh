@@ -105,6 +105,17 @@ ALM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
 ALM_DEV uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 ALM_DEV uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Barrier of the 256 threads that run a shared device body (attention, row
+// and embedding bodies): the whole block in kernels of 256 threads, warps
+// 0-7 (named barrier 1) in kernels that add a weight-producer warp.
+ALM_DEV void body_sync() {
+  if (blockDim.x == 256) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  }
+}
+
 // Argmax order: larger value first, then the smaller index.
 ALM_DEV bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
 

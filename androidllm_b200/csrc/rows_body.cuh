@@ -46,10 +46,10 @@ ALM_DEV float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fadd(v, __shfl_xor_sync(0xffffffffu, v, o));
   if (lane == 0) red[warp] = v;
-  __syncthreads();
+  body_sync();
   float s = 0.f;
   for (int w = 0; w < kRowThreads / kWarp; ++w) s = fadd(s, red[w]);
-  __syncthreads();
+  body_sync();
   return s;
 }
 
@@ -69,7 +69,7 @@ ALM_DEV void rownorm_body(const ActIn& in, const half* w2, float eps2, half* out
     const float d = row_denominator(in, m);
     if (threadIdx.x == 0) sh.den = d;
   }
-  __syncthreads();
+  body_sync();
   const float den = in.ss ? sh.den : 1.f;
   float sq = 0.f;
   const int n8 = (H + 7) / 8;
@@ -96,7 +96,7 @@ ALM_DEV void rownorm_body(const ActIn& in, const half* w2, float eps2, half* out
       }
     }
   }
-  __syncthreads();
+  body_sync();
   half* o = out + static_cast<size_t>(m) * ldo;
   if (w2 == nullptr) {
     for (int k = threadIdx.x; k < H; k += kRowThreads) o[k] = xrow[k];
@@ -106,7 +106,7 @@ ALM_DEV void rownorm_body(const ActIn& in, const half* w2, float eps2, half* out
     for (int k = threadIdx.x; k < H; k += kRowThreads)
       o[k] = __float2half_rn(fmul(fdiv(__half2float(xrow[k]), den2), __half2float(__ldg(w2 + k))));
   }
-  __syncthreads();   // xrow is reused by the caller's next block
+  body_sync();   // xrow is reused by the caller's next block
 }
 
 ALM_DEV void argmax_final_body(const float* am_val, const int* am_idx, int n_part, int* out, int m,
@@ -130,16 +130,16 @@ ALM_DEV void argmax_final_body(const float* am_val, const int* am_idx, int n_par
   }
   sv[threadIdx.x] = bv;
   si[threadIdx.x] = bi;
-  __syncthreads();
+  body_sync();
   for (int s = kRowThreads / 2; s > 0; s >>= 1) {
     if (threadIdx.x < s && better(sv[threadIdx.x + s], si[threadIdx.x + s], sv[threadIdx.x], si[threadIdx.x])) {
       sv[threadIdx.x] = sv[threadIdx.x + s];
       si[threadIdx.x] = si[threadIdx.x + s];
     }
-    __syncthreads();
+    body_sync();
   }
   if (threadIdx.x == 0) out[m] = si[0] == 0x7fffffff ? 0 : si[0];
-  __syncthreads();
+  body_sync();
 }
 
 }  // namespace alm

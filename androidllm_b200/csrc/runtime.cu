@@ -10,6 +10,7 @@
 
 #include "../../include/androidllm_b200.h"
 #include "common.cuh"
+#include "cluster_fwd.cuh"
 #include "forward.cuh"
 #include "gemv_body.cuh"
 #include "kernels.cuh"
@@ -146,6 +147,7 @@ struct alm_ctx {
   cudaStream_t stream = nullptr;
   bool pdl = true;       // programmatic dependent launch between forward kernels
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
+  bool cluster = true;   // single-row forwards of small models as one cluster kernel
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
 };
 
@@ -243,6 +245,9 @@ struct alm_model {
   unsigned long long* fwd_bar = nullptr;    // device grid-barrier counter
   size_t fwd_smem = 0;
   int fwd_grid = 0;                         // 0: not available for this model
+  // cluster forward kernel (single-row forwards)
+  size_t cf_smem = 0;
+  bool cf_ok = false;
 };
 
 struct alm_kv {
@@ -687,8 +692,7 @@ int build_forward(alm_model* m) {
   return ALM_OK;
 }
 
-int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
-                               unsigned long long* trace = nullptr) {
+FwdParams forward_params(alm_model* m, alm_kv* kv, int M, bool head) {
   const alm_model_config& c = m->cfg;
   Work& ws = m->ws;
   FwdParams p;
@@ -732,8 +736,42 @@ int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
   p.argmax = ws.argmax;
   p.io = StepIO{ws.pos, ws.err};
   p.bar = m->fwd_bar;
+  return p;
+}
+
+int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
+                               unsigned long long* trace = nullptr) {
+  FwdParams p = forward_params(m, kv, M, head);
   p.trace = trace;
   ALM_LAUNCH(launch_forward(p, m->fwd_grid, m->fwd_smem, m->ctx->stream));
+  return ALM_OK;
+}
+
+// Whether the model's single-row forwards can run as the cluster kernel, and
+// its shared memory.  Needs the device layer table of build_forward.
+int build_cluster_fwd(alm_model* m) {
+  m->cf_ok = false;
+  if (!m->fwd_layers) return ALM_OK;
+  const alm_model_config& c = m->cfg;
+  if (c.head_dim % 16 || c.head_dim > 256 || c.heads % c.kv_heads) return ALM_OK;
+  int max_kb = 0;
+  for (const Layer& L : m->layers) {
+    if (!L.qkv) return ALM_OK;
+    for (const alm_qweight* w : {L.qkv, L.o, L.gu, L.down}) {
+      if (!cluster_fwd_weight_ok(w->t)) return ALM_OK;
+      max_kb = std::max(max_kb, w->t.k_blocks);
+    }
+  }
+  const size_t smem = cluster_fwd_smem_bytes(max_kb, c.head_dim);
+  if (smem > 227 * 1024 - 16 * 1024) return ALM_OK;   // static shared memory stays below the rest
+  int n_clusters = 0;
+  if (cluster_fwd_init(smem, &n_clusters) != cudaSuccess) {
+    cudaGetLastError();
+    return ALM_OK;
+  }
+  if (n_clusters < 1) return ALM_OK;
+  m->cf_smem = smem;
+  m->cf_ok = true;
   return ALM_OK;
 }
 
@@ -742,6 +780,17 @@ int enqueue_forward_persistent(alm_model* m, alm_kv* kv, int M, bool head,
 int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
   if (m->ctx->persist && m->fwd_grid > 0 && M <= kPersistRows) return enqueue_forward_persistent(m, kv, M, head);
   Work& ws = m->ws;
+  if (M == 1 && m->ctx->cluster && m->cf_ok) {
+    // embedding and every layer in one cluster launch, then the final norm
+    // and the head over the whole GPU
+    ALM_LAUNCH(launch_cluster_fwd(forward_params(m, kv, 1, false), m->cf_smem, pdl, m->ctx->stream));
+    prof_mark(ALM_OP_LAYERS, M);
+    if (!head) return ALM_OK;
+    const ActIn fin = deferred_in(m, ws.s2, ws.ss2, m->layers[m->cfg.layers - 1].n_post);
+    ALM_LAUNCH(launch_rownorm(fin, M, m->final_norm, m->cfg.rms_eps, ws.xn, m->cfg.hidden, pdl, m->ctx->stream));
+    prof_mark(ALM_OP_FINAL_NORM, M);
+    return enqueue_head(m, M, pdl);
+  }
   EmbedArgs ea;
   ea.table = m->embed_table;
   ea.scale = m->embed_scale;
@@ -881,6 +930,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
     c->pdl = !(e && e[0] == '1');
     const char* e2 = getenv("ALM_PERSIST");
     c->persist = e2 && e2[0] == '1';
+    const char* e4 = getenv("ALM_CLUSTER");
+    c->cluster = !(e4 && e4[0] == '0');
     const char* e3 = getenv("ALM_TC");
     if (e3 && (e3[0] == '0' || e3[0] == '1' || e3[0] == '2')) c->tc = e3[0] - '0';
   }
@@ -904,6 +955,18 @@ int alm_ctx_destroy(alm_ctx* ctx) {
 int alm_ctx_set_persistent(alm_ctx* ctx, int enable) {
   ALM_REQ(ctx, "null context");
   ctx->persist = enable != 0;
+  return ALM_OK;
+}
+
+int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable) {
+  ALM_REQ(ctx, "null context");
+  ctx->cluster = enable != 0;
+  return ALM_OK;
+}
+
+int alm_model_cluster_forward(const alm_model* m, int* uses_cluster) {
+  ALM_REQ(m && uses_cluster, "null argument");
+  *uses_cluster = (m->cf_ok && m->ctx->cluster) ? 1 : 0;
   return ALM_OK;
 }
 
@@ -1314,6 +1377,7 @@ int alm_model_finalize(alm_model* m) {
     need = std::max({need, split_need(L.qkv), split_need(L.o), split_need(L.gu), split_need(L.down)});
   ALM_TRY(ensure_part(ws, need));
   ALM_TRY(build_forward(m));
+  ALM_TRY(build_cluster_fwd(m));
   m->finalized = true;
   return ALM_OK;
 }

@@ -14,7 +14,7 @@ from ._lib import ModelConfig, ProjSrc, check, lib, ptr
 PROJ_BASES = ("q", "k", "v", "o", "gate", "up", "down")   # androidllm/shard.py:111
 # ALM_OP_* codes of include/androidllm_b200.h, in order
 OP_NAMES = ("begin", "embed", "qkv", "attn_scores", "attn_pv", "o", "gate_up", "down", "final_norm", "head",
-            "argmax", "spec_prep", "spec_accept", "sample")
+            "argmax", "spec_prep", "spec_accept", "sample", "layers")
 
 # At interpreter exit the order of finalizers is arbitrary (a context could go
 # before the models on it); the process teardown frees device memory anyway.
@@ -42,6 +42,11 @@ class Context:
         """Run forwards of <= 8 rows as one persistent kernel or as one launch
         per layer operation (the default); both give bit-identical results."""
         check(lib.alm_ctx_set_persistent(self.h, 1 if enable else 0))
+
+    def set_cluster_forward(self, enable):
+        """Single-row forwards of small models as one 16-CTA cluster kernel
+        (the default) or as one launch per layer operation."""
+        check(lib.alm_ctx_set_cluster_forward(self.h, 1 if enable else 0))
 
     def set_gemv_layout(self, mode):
         """Layout of weights uploaded from now on: 0 = 16-row tiles (mma.sync
@@ -299,6 +304,12 @@ class DeviceModel:
 
     def finalize(self):
         check(lib.alm_model_finalize(self.h))
+
+    def uses_cluster_forward(self):
+        """Whether single-row forwards run as the 16-CTA cluster kernel."""
+        v = ctypes.c_int32()
+        check(lib.alm_model_cluster_forward(self.h, ctypes.byref(v)))
+        return bool(v.value)
 
     @classmethod
     def from_dir(cls, ctx, model_dir, layers=None):

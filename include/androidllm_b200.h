@@ -64,6 +64,13 @@ ALM_API int alm_ctx_sync(alm_ctx* ctx);
    variable ALM_PERSIST=1 turns the persistent kernel on at context creation).
    The results are bit-identical.  Graphs captured earlier keep their kernels. */
 ALM_API int alm_ctx_set_persistent(alm_ctx* ctx, int enable);
+/* Single-row forwards (decode steps, the speculative draft) of models whose
+   projections fit it run the embedding and every layer as one launch of one
+   16-CTA thread-block cluster (enable = 1, the default; ALM_CLUSTER=0 at
+   context creation turns it off), or as one launch per layer operation
+   (enable = 0).  Results agree to the last bits of fp32 sums (a different K
+   split), deterministically.  Graphs captured earlier keep their kernels. */
+ALM_API int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable);
 /* Weight layout chosen by later uploads: 0 (the default) = 16-row tiles for
    the mma.sync GEMV; 1 = 128-row records for the tcgen05 kernel for weights of
    at least 4 MB, tiles otherwise; 2 = 128-row records wherever the format
@@ -152,6 +159,9 @@ ALM_API int alm_model_set_final_norm(alm_model* m, const uint16_t* w_host);
 /* Untied LM head (vocab, hidden) in shard format; without it the head is the
  * embedding table (tied, androidllm/models/llama.py:145). */
 ALM_API int alm_model_set_head(alm_model* m, const alm_proj_src* head);
+/* *uses_cluster = 1 when the model's single-row forwards run as the cluster
+   kernel (alm_ctx_set_cluster_forward enabled and every projection fits it). */
+ALM_API int alm_model_cluster_forward(const alm_model* m, int* uses_cluster);
 /* Validate and allocate work buffers; required before any forward. */
 ALM_API int alm_model_finalize(alm_model* m);
 
@@ -286,7 +296,8 @@ ALM_API int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitt
 enum {
   ALM_OP_BEGIN = 0, ALM_OP_EMBED = 1, ALM_OP_QKV = 2, ALM_OP_ATTN_SCORES = 3, ALM_OP_ATTN_PV = 4,
   ALM_OP_O = 5, ALM_OP_GATE_UP = 6, ALM_OP_DOWN = 7, ALM_OP_FINAL_NORM = 8, ALM_OP_HEAD = 9,
-  ALM_OP_ARGMAX = 10, ALM_OP_SPEC_PREP = 11, ALM_OP_SPEC_ACCEPT = 12, ALM_OP_SAMPLE = 13
+  ALM_OP_ARGMAX = 10, ALM_OP_SPEC_PREP = 11, ALM_OP_SPEC_ACCEPT = 12, ALM_OP_SAMPLE = 13,
+  ALM_OP_LAYERS = 14   /* embedding and every layer as one cluster kernel */
 };
 /* Device time of every kernel launch of one speculative step (profiling; no
  * counterpart in the reference).  The step is captured once more with a
