@@ -80,13 +80,17 @@ ALM_DEV void mbar_arrive_remote(uint64_t* bar, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(bar)), "r"(rank));
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
-ALM_DEV bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+// Non-blocking test of a phase with cluster-scope acquire.  The phase sync
+// polls with it instead of a suspending try_wait: a thread suspended on a
+// barrier is not woken promptly by arrivals from other CTAs (measured: a
+// sync then costs up to the whole suspend-time hint).
+ALM_DEV bool mbar_test_acq_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+      : "r"(smem_addr(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -97,9 +101,26 @@ ALM_DEV void cf_fail(const FwdParams& P) {
   s_cf.broken = 1;
   if (P.io.err) atomicExch(P.io.err, 4);
 }
+// Bounded wait for a phase of one of the CTA's ring barriers, polling with a
+// short back-off (no hardware suspension, for the reason above).
+ALM_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 ALM_DEV bool cf_wait(uint64_t* bar, uint32_t parity, const FwdParams& P) {
   if (s_cf.broken) return false;
-  if (mbar_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (unsigned i = 0; i < (1u << 30); ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if (i >= 16) __nanosleep(32);
+    if ((i & 63) == 63 && global_ns() - t0 > kWaitLimitNs) break;
+  }
   cf_fail(P);
   return false;
 }
@@ -119,16 +140,17 @@ ALM_DEV void cf_sync(uint32_t& n, const FwdParams& P) {
       const uint32_t parity = (n >> 1) & 1u;
       const unsigned long long t0 = global_ns();
       bool ok = false;
-      for (unsigned i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait_acq_cluster(bar, parity)) {
+      for (unsigned i = 0; i < (1u << 30); ++i) {
+        if (mbar_test_acq_cluster(bar, parity)) {
           ok = true;
           break;
         }
-        if (global_ns() - t0 > kWaitLimitNs) break;
+        if ((i & 255) == 255 && global_ns() - t0 > kWaitLimitNs) break;
       }
       if (!ok) cf_fail(P);
     }
   }
+  if (P.trace && threadIdx.x == 0 && cluster_rank() == 0) P.trace[n] = global_ns();
   cons_sync();
   ++n;
 }
@@ -169,7 +191,11 @@ ALM_DEV void cf_produce(const FwdParams& P, int cta) {
   // chunks' full phases (earlier ones were consumed before their slots were
   // reused)
   const uint32_t first = c > static_cast<uint32_t>(kCfSlots) ? c - kCfSlots : 0u;
-  for (uint32_t d = first; d < c; ++d) mbar_wait(&s_cf.full[d % kCfSlots], (d / kCfSlots) & 1u);
+  for (uint32_t d = first; d < c; ++d) {
+    const unsigned long long t0 = global_ns();
+    while (!mbar_test(&s_cf.full[d % kCfSlots], (d / kCfSlots) & 1u) && global_ns() - t0 < kWaitLimitNs)
+      __nanosleep(32);
+  }
 }
 
 // ---- decoding warps: one GEMV phase ----------------------------------------------

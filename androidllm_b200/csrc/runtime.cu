@@ -872,6 +872,7 @@ int sync_and_check(alm_model* m) {
     cudaMemset(m->ws.err, 0, sizeof(int));
     if (err == 2) return fail(ALM_ERR_CUDA, "a device-side wait gave up (weight stream did not arrive)");
     if (err == 3) return fail(ALM_ERR_CUDA, "a device-side wait gave up (grid barrier of the persistent forward)");
+    if (err == 4) return fail(ALM_ERR_CUDA, "a device-side wait gave up (cluster forward)");
     return fail(ALM_ERR_TOKEN, "token id outside the vocabulary");
   }
   return ALM_OK;
@@ -1511,8 +1512,35 @@ int alm_forward_trace(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int 
   ALM_REQ(tokens_host && trace_host && n_barriers && n_ctas, "null argument");
   ALM_TRY(check_layers(m));
   ALM_REQ(rows >= 1 && rows <= 8, "rows must be in 1..8");
-  if (m->fwd_grid <= 0) return fail(ALM_ERR_STATE, "persistent forward kernel unavailable for this model");
   DeviceGuard g(m->ctx->device);
+  if (rows == 1 && m->cf_ok && m->ctx->cluster) {
+    // cluster forward: when CTA 0 left each phase sync (embedding, then six
+    // per layer), one entry per sync
+    ALM_TRY(check_kv(m, kv, rows, pos0));
+    const int nb = 1 + 6 * m->cfg.layers;
+    ALM_REQ(cap >= nb, "trace buffer too small");
+    unsigned long long* dtrace = nullptr;
+    ALM_TRY(dev_alloc_t(&dtrace, static_cast<size_t>(nb)));
+    cudaStream_t st = m->ctx->stream;
+    int rc = set_pos(m, pos0);
+    if (rc == ALM_OK && cudaMemcpyAsync(m->ws.tokens, tokens_host, sizeof(int), cudaMemcpyHostToDevice, st) !=
+                            cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "token upload failed");
+    FwdParams p = forward_params(m, kv, 1, false);
+    p.trace = dtrace;
+    if (rc == ALM_OK && launch_cluster_fwd(p, m->cf_smem, false, st) != cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "cluster forward launch failed");
+    if (rc == ALM_OK) rc = sync_and_check(m);
+    if (rc == ALM_OK && cudaMemcpy(trace_host, dtrace, nb * sizeof(unsigned long long), cudaMemcpyDeviceToHost) !=
+                            cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "trace download failed");
+    dev_free(dtrace);
+    if (rc != ALM_OK) return rc;
+    *n_barriers = nb;
+    *n_ctas = 1;
+    return ALM_OK;
+  }
+  if (m->fwd_grid <= 0) return fail(ALM_ERR_STATE, "persistent forward kernel unavailable for this model");
   ALM_TRY(check_kv(m, kv, rows, pos0));
   const int nb = forward_barriers(m->cfg.layers, true);
   const size_t n = static_cast<size_t>(nb) * (m->fwd_grid + 1);

@@ -388,6 +388,20 @@ class DeviceModel:
         nb, nc = nb.value, nc.value
         return buf[: nb * nc].reshape(nb, nc), buf[nb * nc: nb * nc + nb]
 
+    def cluster_trace(self, kv, token, pos0):
+        """One single-row cluster forward (no head) recording when CTA 0 left
+        each phase sync; returns the global-timer nanoseconds of the
+        embedding's sync and of the six syncs of every layer."""
+        tok = np.ascontiguousarray([token], dtype=np.int32)
+        nb_max = 1 + 6 * self.canon["layers"]
+        buf = np.zeros(nb_max, np.uint64)
+        nb, nc = ctypes.c_int(), ctypes.c_int()
+        check(lib.alm_forward_trace(self.h, kv.h, ptr(tok), 1, int(pos0), ptr(buf), nb_max,
+                                    ctypes.byref(nb), ctypes.byref(nc)))
+        if nc.value != 1:
+            raise RuntimeError("the model does not run the cluster forward")
+        return buf[: nb.value].astype(np.int64)
+
     def close(self):
         if self.h:
             lib.alm_model_destroy(self.h)

@@ -724,6 +724,31 @@ def run_trace_forward(args):
     return 0
 
 
+def run_trace_cluster(args):
+    """Per-phase timeline of the single-row cluster forward of the draft
+    (sync times of CTA 0) at position 600: median microseconds per phase."""
+    from androidllm_b200.ops import Context, DeviceKV, DeviceModel
+    _, ddir = prepare_models(args.workload)
+    ctx = Context(0)
+    m = DeviceModel.from_dir(ctx, ddir)
+    kv = DeviceKV(m, 1024)
+    toks = np.random.default_rng(5).integers(0, m.canon["vocab"], 608).tolist()
+    for i in range(0, 592, 16):
+        m.forward(kv, toks[i:i + 16], i, logits=False, argmax=False)
+    runs = [m.cluster_trace(kv, toks[600], 600) for _ in range(args.trace_cluster)]
+    names = ["qkv", "scores", "pv", "o", "gate_up", "down"]
+    per = {n: [] for n in names}
+    total = []
+    for t in runs:
+        d = np.diff(t)
+        total.append((t[-1] - t[0]) / 1e3)
+        for i, v in enumerate(d):
+            per[names[i % 6]].append(v / 1e3)
+    print(json.dumps({"model": "draft", "layers": m.canon["layers"], "layers_us": round(float(np.median(total)), 1),
+                      "per_layer_us": {n: round(float(np.median(v)), 2) for n, v in per.items()}}), flush=True)
+    return 0
+
+
 def summarize_ncu(path):
     """Aggregate an ncu --csv launch list (gpu__time_duration.sum) by kernel."""
     import collections
@@ -791,6 +816,8 @@ def main():
     ap.add_argument("--top-p", type=float, default=0.9, help="--profile: nucleus of the sampling steps")
     ap.add_argument("--trace-forward", type=int, default=0, metavar="N",
                     help="run N traced persistent forwards per model and print the phase timeline")
+    ap.add_argument("--trace-cluster", type=int, default=0, metavar="N",
+                    help="run N traced single-row cluster forwards of the draft and print the phase timeline")
     ap.add_argument("--sweep", action="store_true", help="isolated quantized-matmul sweep (JSON lines)")
     ap.add_argument("--sweep-m", default=",".join(str(m) for m in SWEEP_M))
     ap.add_argument("--sweep-shapes", default="", metavar="NxK,...", help="sweep only these weight shapes")
@@ -811,6 +838,8 @@ def main():
         return run_profile(args)
     if args.trace_forward:
         return run_trace_forward(args)
+    if args.trace_cluster:
+        return run_trace_cluster(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

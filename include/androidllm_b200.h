@@ -232,7 +232,9 @@ ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, in
                 float* logits_host, int32_t* argmax_host);
 /* Profiling (no counterpart in the reference): alm_forward with the head,
  * run as the persistent forward kernel (rows <= 8), recording global-timer
- * nanoseconds.  trace_host receives n_barriers * n_ctas arrival times
+ * nanoseconds; for rows = 1 of a model on the cluster forward, the cluster
+ * kernel alone, with *n_ctas = 1 and one time per phase sync (when CTA 0 left
+ * it: the embedding, then six per layer).  trace_host receives n_barriers * n_ctas arrival times
  * (barrier-major: when each CTA finished a phase) followed by n_barriers
  * times at which CTA 0 passed each barrier; cap is its length in entries.
  * Fails with ALM_ERR_STATE when the persistent kernel is unavailable. */
