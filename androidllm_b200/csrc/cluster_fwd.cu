@@ -95,6 +95,19 @@ ALM_DEV bool mbar_test_acq_cluster(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Profiling trace (alm_forward_trace): CTA 0 records (label << 48 | global
+// ns) at points of its phases into the first half of P.trace (count in
+// trace[0]) and its producer lane into the second half (count at trace[half]).
+__shared__ int s_cf_tn, s_cf_tp;
+ALM_DEV void cf_mark(const FwdParams& P, int label, bool producer = false) {
+  if (!P.trace || cluster_rank() != 0) return;
+  const int half = P.trace_cap / 2;
+  int& n = producer ? s_cf_tp : s_cf_tn;
+  unsigned long long* base = P.trace + (producer ? half : 0);
+  if (n + 1 < half) base[1 + n++] = (static_cast<unsigned long long>(label) << 48) | (global_ns() & 0xffffffffffffull);
+  base[0] = static_cast<unsigned long long>(n);
+}
+
 // A wait that gave up: remember it (later waits of this CTA are skipped) and
 // report it to the host.
 ALM_DEV void cf_fail(const FwdParams& P) {
@@ -150,7 +163,7 @@ ALM_DEV void cf_sync(uint32_t& n, const FwdParams& P) {
       if (!ok) cf_fail(P);
     }
   }
-  if (P.trace && threadIdx.x == 0 && cluster_rank() == 0) P.trace[n] = global_ns();
+  if (threadIdx.x == 0) cf_mark(P, 6);
   cons_sync();
   ++n;
 }
@@ -172,6 +185,7 @@ ALM_DEV void cf_produce(const FwdParams& P, int cta) {
     const QTile* ws[4] = {&L.qkv, &L.o, &L.gu, &L.down};
     for (int ph = 0; ph < 4 && ok; ++ph) {
       const CfPlan pl = cf_plan(*ws[ph], cta);
+      cf_mark(P, 16 + ph, true);
       for (int k = 0; k < pl.n_chunks; ++k, ++c) {
         const uint32_t slot = c % kCfSlots, use = c / kCfSlots;
         if (use > 0 && !cf_wait(&s_cf.empty[slot], (use - 1) & 1u, P)) {
@@ -185,6 +199,7 @@ ALM_DEV void cf_produce(const FwdParams& P, int cta) {
         bulk_g2s(s_cf_dyn + static_cast<size_t>(slot) * kCfSlotBytes,
                  pl.base + static_cast<size_t>(k) * pl.R * pl.rec_bytes, bytes, &s_cf.full[slot], pol);
       }
+      cf_mark(P, 32 + ph, true);
     }
   }
   // every issued copy lands before the CTA can leave: the last kCfSlots
@@ -424,13 +439,18 @@ ALM_DEV void cf_gemv_t(const QTile& w, const ActIn& in, const Epi& epi, uint32_t
     }
   }
   cons_sync();
+  if (threadIdx.x == 0) cf_mark(P, 1);
   uint4* xs = reinterpret_cast<uint4*>(cf_work());
   cf_stage(w, in, xs);
   cons_sync();
+  if (threadIdx.x == 0) cf_mark(P, 2);
   cf_items<BITS, SB>(w, pl, cbase, xs, P);
+  if (threadIdx.x == 0) cf_mark(P, 3);
   cbase += static_cast<uint32_t>(pl.n_chunks);
   cons_sync();
+  if (threadIdx.x == 0) cf_mark(P, 4);
   cf_epilogue<EPI>(w, pl, epi, P);
+  if (threadIdx.x == 0) cf_mark(P, 5);
   cf_sync(n_sync, P);
 }
 
@@ -528,6 +548,7 @@ ALM_DEV void cf_layer(const FwdParams& P, int li, uint32_t& cbase, uint32_t& n_s
       attn_scores_body(a, P.sqrt_hd, vb % n_chunks, (vb / n_chunks) % kvh, vb / (n_chunks * kvh), ncm, work,
                        s_cf.attn);
     }
+    if (threadIdx.x == 0) cf_mark(P, 7);
     cf_sync(n_sync, P);
     const int nds = a.head_dim / 16, npg = attn_pv_groups(a);
     const int nvb2 = nds * kvh * npg;
@@ -536,6 +557,7 @@ ALM_DEV void cf_layer(const FwdParams& P, int li, uint32_t& cbase, uint32_t& n_s
       cons_sync();
       attn_pv_body(a, ncm, vb % nds, (vb / nds) % kvh, vb / (nds * kvh), work, s_cf.attn);
     }
+    if (threadIdx.x == 0) cf_mark(P, 8);
     cf_sync(n_sync, P);
   }
   const ActIn n1 = cf_deferred(P, P.s1, P.ss1, L.n_in);
@@ -576,6 +598,8 @@ __global__ void __launch_bounds__(kCfThreads, 1) cluster_fwd_kernel(const __grid
     mbar_init(&s_cf.sync[0], kCfCtas);
     mbar_init(&s_cf.sync[1], kCfCtas);
     s_cf.broken = 0;
+    s_cf_tn = 0;
+    s_cf_tp = 0;
     fence_mbar_init();
   }
   // every CTA's barriers are initialised before any remote arrival

@@ -59,6 +59,7 @@ struct FwdParams {
   // Optional phase trace (global timer, ns): arrival time of every CTA at
   // every barrier, [barrier][cta], then the time CTA 0 left each barrier.
   unsigned long long* trace = nullptr;
+  int trace_cap = 0;   // entries of trace (cluster forward)
 };
 
 __host__ __device__ int forward_barriers(int n_layers, bool head);

@@ -147,7 +147,7 @@ struct alm_ctx {
   cudaStream_t stream = nullptr;
   bool pdl = true;       // programmatic dependent launch between forward kernels
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
-  bool cluster = true;   // single-row forwards of small models as one cluster kernel
+  bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
 };
 
@@ -932,7 +932,7 @@ int alm_ctx_create(int device, alm_ctx** out) {
     const char* e2 = getenv("ALM_PERSIST");
     c->persist = e2 && e2[0] == '1';
     const char* e4 = getenv("ALM_CLUSTER");
-    c->cluster = !(e4 && e4[0] == '0');
+    c->cluster = e4 && e4[0] == '1';
     const char* e3 = getenv("ALM_TC");
     if (e3 && (e3[0] == '0' || e3[0] == '1' || e3[0] == '2')) c->tc = e3[0] - '0';
   }
@@ -1514,29 +1514,32 @@ int alm_forward_trace(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int 
   ALM_REQ(rows >= 1 && rows <= 8, "rows must be in 1..8");
   DeviceGuard g(m->ctx->device);
   if (rows == 1 && m->cf_ok && m->ctx->cluster) {
-    // cluster forward: when CTA 0 left each phase sync (embedding, then six
-    // per layer), one entry per sync
+    // cluster forward: trace_host[0] = n, then n entries (label << 48 |
+    // global ns) of CTA 0's decoding threads; from cap / 2 the same for its
+    // weight producer
     ALM_TRY(check_kv(m, kv, rows, pos0));
-    const int nb = 1 + 6 * m->cfg.layers;
-    ALM_REQ(cap >= nb, "trace buffer too small");
+    ALM_REQ(cap >= 64, "trace buffer too small");
     unsigned long long* dtrace = nullptr;
-    ALM_TRY(dev_alloc_t(&dtrace, static_cast<size_t>(nb)));
+    ALM_TRY(dev_alloc_t(&dtrace, static_cast<size_t>(cap)));
     cudaStream_t st = m->ctx->stream;
     int rc = set_pos(m, pos0);
+    if (rc == ALM_OK && cudaMemsetAsync(dtrace, 0, static_cast<size_t>(cap) * 8, st) != cudaSuccess)
+      rc = fail(ALM_ERR_CUDA, "trace clear failed");
     if (rc == ALM_OK && cudaMemcpyAsync(m->ws.tokens, tokens_host, sizeof(int), cudaMemcpyHostToDevice, st) !=
                             cudaSuccess)
       rc = fail(ALM_ERR_CUDA, "token upload failed");
     FwdParams p = forward_params(m, kv, 1, false);
     p.trace = dtrace;
+    p.trace_cap = cap;
     if (rc == ALM_OK && launch_cluster_fwd(p, m->cf_smem, false, st) != cudaSuccess)
       rc = fail(ALM_ERR_CUDA, "cluster forward launch failed");
     if (rc == ALM_OK) rc = sync_and_check(m);
-    if (rc == ALM_OK && cudaMemcpy(trace_host, dtrace, nb * sizeof(unsigned long long), cudaMemcpyDeviceToHost) !=
+    if (rc == ALM_OK && cudaMemcpy(trace_host, dtrace, static_cast<size_t>(cap) * 8, cudaMemcpyDeviceToHost) !=
                             cudaSuccess)
       rc = fail(ALM_ERR_CUDA, "trace download failed");
     dev_free(dtrace);
     if (rc != ALM_OK) return rc;
-    *n_barriers = nb;
+    *n_barriers = cap;
     *n_ctas = 1;
     return ALM_OK;
   }

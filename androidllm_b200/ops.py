@@ -45,7 +45,8 @@ class Context:
 
     def set_cluster_forward(self, enable):
         """Single-row forwards of small models as one 16-CTA cluster kernel
-        (the default) or as one launch per layer operation."""
+        (opt-in, bit-identical, slower on B200 at the draft's shape) or as one
+        launch per layer operation (the default)."""
         check(lib.alm_ctx_set_cluster_forward(self.h, 1 if enable else 0))
 
     def set_gemv_layout(self, mode):
@@ -388,19 +389,22 @@ class DeviceModel:
         nb, nc = nb.value, nc.value
         return buf[: nb * nc].reshape(nb, nc), buf[nb * nc: nb * nc + nb]
 
-    def cluster_trace(self, kv, token, pos0):
-        """One single-row cluster forward (no head) recording when CTA 0 left
-        each phase sync; returns the global-timer nanoseconds of the
-        embedding's sync and of the six syncs of every layer."""
+    def cluster_trace(self, kv, token, pos0, cap=1 << 16):
+        """One single-row cluster forward (no head) with CTA 0's trace points:
+        returns (decoder points, producer points), each a list of (label,
+        global-timer ns)."""
         tok = np.ascontiguousarray([token], dtype=np.int32)
-        nb_max = 1 + 6 * self.canon["layers"]
-        buf = np.zeros(nb_max, np.uint64)
+        buf = np.zeros(cap, np.uint64)
         nb, nc = ctypes.c_int(), ctypes.c_int()
-        check(lib.alm_forward_trace(self.h, kv.h, ptr(tok), 1, int(pos0), ptr(buf), nb_max,
+        check(lib.alm_forward_trace(self.h, kv.h, ptr(tok), 1, int(pos0), ptr(buf), cap,
                                     ctypes.byref(nb), ctypes.byref(nc)))
         if nc.value != 1:
             raise RuntimeError("the model does not run the cluster forward")
-        return buf[: nb.value].astype(np.int64)
+
+        def points(b):
+            n = int(b[0])
+            return [(int(v) >> 48, int(v) & 0xffffffffffff) for v in b[1:1 + n]]
+        return points(buf[: cap // 2]), points(buf[cap // 2:])
 
     def close(self):
         if self.h:

@@ -736,16 +736,20 @@ def run_trace_cluster(args):
     for i in range(0, 592, 16):
         m.forward(kv, toks[i:i + 16], i, logits=False, argmax=False)
     runs = [m.cluster_trace(kv, toks[600], 600) for _ in range(args.trace_cluster)]
-    names = ["qkv", "scores", "pv", "o", "gate_up", "down"]
-    per = {n: [] for n in names}
-    total = []
-    for t in runs:
-        d = np.diff(t)
-        total.append((t[-1] - t[0]) / 1e3)
-        for i, v in enumerate(d):
-            per[names[i % 6]].append(v / 1e3)
-    print(json.dumps({"model": "draft", "layers": m.canon["layers"], "layers_us": round(float(np.median(total)), 1),
-                      "per_layer_us": {n: round(float(np.median(v)), 2) for n, v in per.items()}}), flush=True)
+    dec, prod = runs[-1]
+    t0 = dec[0][1]
+    # per GEMV phase: staging, items (first warp), items (all), epilogue, sync
+    names = {1: "start", 2: "staged", 3: "items_w0", 4: "items_all", 5: "epilogue", 6: "sync",
+             7: "scores", 8: "pv"}
+    layer = []
+    prev = t0
+    for lab, t in dec[: 60]:
+        layer.append((names.get(lab, str(lab)), round((t - prev) / 1e3, 2)))
+        prev = t
+    totals = [(d[-1][1] - d[0][1]) / 1e3 for d, _ in runs]
+    pr = [(lab, round((t - t0) / 1e3, 2)) for lab, t in prod[: 24]]
+    print(json.dumps({"model": "draft", "layers": m.canon["layers"], "total_us": round(float(np.median(totals)), 1),
+                      "first_points_us_since_previous": layer, "producer_points_us_since_start": pr}), flush=True)
     return 0
 
 

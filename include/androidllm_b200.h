@@ -66,10 +66,12 @@ ALM_API int alm_ctx_sync(alm_ctx* ctx);
 ALM_API int alm_ctx_set_persistent(alm_ctx* ctx, int enable);
 /* Single-row forwards (decode steps, the speculative draft) of models whose
    projections fit it run the embedding and every layer as one launch of one
-   16-CTA thread-block cluster (enable = 1, the default; ALM_CLUSTER=0 at
-   context creation turns it off), or as one launch per layer operation
-   (enable = 0).  Results agree to the last bits of fp32 sums (a different K
-   split), deterministically.  Graphs captured earlier keep their kernels. */
+   16-CTA thread-block cluster (enable = 1; ALM_CLUSTER=1 at context creation
+   turns it on), or as one launch per layer operation (enable = 0, the
+   default).  The results are bit-identical.  Measured on B200 at the
+   Qwen2.5-0.5B draft shape it is slower (2.8 ms against 0.87 ms per
+   forward): 16 SMs cannot decode int4 weights as fast as the whole GPU.
+   Graphs captured earlier keep their kernels. */
 ALM_API int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable);
 /* Weight layout chosen by later uploads: 0 (the default) = 16-row tiles for
    the mma.sync GEMV; 1 = 128-row records for the tcgen05 kernel for weights of
@@ -233,8 +235,12 @@ ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, in
 /* Profiling (no counterpart in the reference): alm_forward with the head,
  * run as the persistent forward kernel (rows <= 8), recording global-timer
  * nanoseconds; for rows = 1 of a model on the cluster forward, the cluster
- * kernel alone, with *n_ctas = 1 and one time per phase sync (when CTA 0 left
- * it: the embedding, then six per layer).  trace_host receives n_barriers * n_ctas arrival times
+ * kernel alone, with *n_ctas = 1: trace_host[0] = n, then n points of CTA 0's
+ * decoding threads (label << 48 | global-timer ns: 1 phase start, 2 input
+ * staged, 3 first warp's items done, 4 all items done, 5 epilogue done,
+ * 6 phase sync passed, 7 scores done, 8 P.V done), and from cap / 2 the
+ * same for its weight producer (16 + p / 32 + p: first / last chunk of
+ * projection p issued).  trace_host receives n_barriers * n_ctas arrival times
  * (barrier-major: when each CTA finished a phase) followed by n_barriers
  * times at which CTA 0 passed each barrier; cap is its length in entries.
  * Fails with ALM_ERR_STATE when the persistent kernel is unavailable. */

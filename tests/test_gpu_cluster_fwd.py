@@ -21,8 +21,9 @@ pytestmark = pytest.mark.gpu
 def ctx():
     from androidllm_b200.ops import Context
     c = Context(0)
-    yield c
     c.set_cluster_forward(True)
+    yield c
+    c.set_cluster_forward(False)
 
 
 def _both(ctx, m, make_kv, steps):
