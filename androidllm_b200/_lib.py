@@ -48,6 +48,8 @@ SIGNATURES = {
     "alm_ctx_set_persistent": [_P, _I],
     "alm_ctx_set_gemv_layout": [_P, _I],
     "alm_ctx_set_cluster_forward": [_P, _I],
+    "alm_nccl_unique_id": [_P],
+    "alm_ctx_init_tp": [_P, _I, _I, _P],
     "alm_dev_alloc": [_P, ctypes.c_size_t, _PP],
     "alm_dev_free": [_P, _P],
     "alm_copy_h2d": [_P, _P, _P, ctypes.c_size_t],
@@ -68,6 +70,7 @@ SIGNATURES = {
     "alm_model_set_head": [_P, ctypes.POINTER(ProjSrc)],
     "alm_model_finalize": [_P],
     "alm_model_cluster_forward": [_P, _PI32],
+    "alm_model_set_tp": [_P, _I, _I],
     "alm_kv_create": [_P, _P, _I, _I, _PP],
     "alm_kv_destroy": [_P],
     "alm_kv_zero": [_P],

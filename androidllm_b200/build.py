@@ -3,7 +3,8 @@
     python -m androidllm_b200.build [--verbose]
 
 The library is a single shared object with a plain C ABI
-(include/androidllm_b200.h); it links only the CUDA runtime.  The measurement
+(include/androidllm_b200.h); it links only the CUDA runtime (NCCL, for
+tensor parallelism, is opened at run time).  The measurement
 probes (probes/*.cu: tensor-core instruction rates, the graph launch floor)
 build into a separate libalm_probes.so that only `bench.py --mma-rate` loads.
 """
@@ -80,7 +81,7 @@ def build(force=False, verbose=False, ptxas_info=False):
     if ptxas_info or verbose:
         print("".join(errs), file=sys.stderr)
     for lib, o in ((LIB, objs), (PROBES_LIB, probe_objs)):
-        _finish(_run([NVCC, *FLAGS, "-shared", "-o", lib + ".tmp", *o, "-lcudart"], verbose))
+        _finish(_run([NVCC, *FLAGS, "-shared", "-o", lib + ".tmp", *o, "-lcudart", "-ldl"], verbose))
         os.replace(lib + ".tmp", lib)
     return LIB
 

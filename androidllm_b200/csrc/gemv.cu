@@ -61,6 +61,7 @@ cudaError_t dispatch_epi(EpiKind kind, const QTile& w, const ActIn& in, int M, c
     case EPI_RESID: return launch_t<BITS, NT8, EPI_RESID>(w, in, M, epi, io, scr, pdl, st);
     case EPI_SWIGLU: return launch_t<BITS, NT8, EPI_SWIGLU>(w, in, M, epi, io, scr, pdl, st);
     case EPI_LOGITS: return launch_t<BITS, NT8, EPI_LOGITS>(w, in, M, epi, io, scr, pdl, st);
+    case EPI_STORE32: return launch_t<BITS, NT8, EPI_STORE32>(w, in, M, epi, io, scr, pdl, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -81,6 +82,7 @@ cudaError_t set_attrs_sb() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_RESID>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_SWIGLU>, a, v);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_LOGITS>, a, v);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<BITS, SB, NT8, EPI_STORE32>, a, v);
   return e;
 }
 

@@ -29,7 +29,7 @@
 // output element is summed in the same order for any M: a verify pass of k+1
 // rows produces exactly the values of k+1 single-row passes.
 //
-// Epilogues (fused): STORE fp16; QKV = fp16 round, RoPE in fp32, K/V written
+// Epilogues (fused): STORE fp16; STORE32 fp32 sums (tensor-parallel partials); QKV = fp16 round, RoPE in fp32, K/V written
 // to the paged cache; RESID = fp16 residual add plus per-tile sums of
 // squares for the next RMSNorm; SWIGLU on interleaved gate/up rows; LOGITS =
 // fp16 logits plus per-block argmax partials.  The rounding points follow
@@ -421,6 +421,18 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
             const int m = nt * 8 + 2 * t + j, row = tile * 16 + g + 8 * r;
             if (m < M && row < epi.n_out)
               epi.out[static_cast<size_t>(m) * epi.ldo + row] = __float2half_rn(acc[nt][2 * r + j]);
+          }
+    }
+  } else if constexpr (EPI == EPI_STORE32) {
+    if (owner) {
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = nt * 8 + 2 * t + j, row = tile * 16 + g + 8 * r;
+            if (m < M && row < epi.n_out) epi.out32[static_cast<size_t>(m) * epi.ldo + row] = acc[nt][2 * r + j];
           }
     }
   } else if constexpr (EPI == EPI_QKV) {

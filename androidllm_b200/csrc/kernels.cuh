@@ -101,10 +101,11 @@ __host__ __device__ inline void set_vec(ActIn& a) {
   a.vec = ok ? 1 : 0;
 }
 
-enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+enum EpiKind : int { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_STORE32 = 5 };
 
 struct Epi {
   half* out = nullptr;   // STORE / RESID / SWIGLU / LOGITS output rows
+  float* out32 = nullptr;  // STORE32: fp32 sums before rounding (tensor-parallel partials)
   int ldo = 0;
   int n_out = 0;         // valid output columns (rows of W, or I for SwiGLU)
   // QKV: q (fp32) and the paged K/V cache of one layer
@@ -272,5 +273,21 @@ cudaError_t launch_sample(const SampleArgs& a, int rows, bool pdl, cudaStream_t 
 // argmax over CTA partials -> tokens (M)
 cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_part, int M,
                                 int* out, bool pdl, cudaStream_t st);
+
+// ---- tensor parallelism (rows.cu) ------------------------------------------
+// After the all-reduce of a row-split projection's fp32 partials o32 (M, H):
+// out = fp16(res + fp16(o)) with res's deferred norm applied, and per
+// 16-column tile sums of squares of out (the RESID epilogue's arithmetic).
+cudaError_t launch_tp_resid(const ActIn& res, const float* o32, int M, int H, half* out, float* ss_out, bool pdl,
+                            cudaStream_t st);
+// Local argmax of each row from the head GEMV's per-CTA partials, as
+// (value bits, global index = local index + offset) pairs.
+cudaError_t launch_tp_argmax_local(const float* am_val, const int* am_idx, int n_part, int M, int offset,
+                                   int* pairs, bool pdl, cudaStream_t st);
+// Best of the all-gathered pairs (world, M, 2) of every row -> out[m].
+cudaError_t launch_tp_argmax_pick(const int* pairs, int world, int M, int* out, bool pdl, cudaStream_t st);
+// All-gathered local logits (world, M, v_local) -> rows (M, world * v_local).
+cudaError_t launch_tp_logits_reorder(const half* gathered, int world, int M, int v_local, half* out, bool pdl,
+                                     cudaStream_t st);
 
 }  // namespace alm

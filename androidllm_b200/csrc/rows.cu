@@ -26,6 +26,86 @@ __global__ void __launch_bounds__(kRowThreads) argmax_final_kernel(const float* 
   argmax_final_body(am_val, am_idx, n_part, out, blockIdx.x, sh);
 }
 
+// One row per block: out = fp16(res + fp16(o32)) and the tile sums of squares
+// in the RESID epilogue's order (per 16-column tile, lane g of 8 adds the
+// squares of columns g and g + 8, then a butterfly over g).
+__global__ void __launch_bounds__(kRowThreads) tp_resid_kernel(ActIn res, const float* o32, int H, half* out,
+                                                               float* ss_out) {
+  __shared__ float s_den;
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  if (res.ss && threadIdx.x < kWarp) {
+    const float d = row_denominator(res, m);
+    if (threadIdx.x == 0) s_den = d;
+  }
+  body_sync();
+  const int n_tiles = (H + 15) / 16;
+  for (int base = 0; base < n_tiles * 8; base += kRowThreads) {
+    const int e = base + static_cast<int>(threadIdx.x);
+    const bool live = e < n_tiles * 8;
+    const int tile = e / 8, g = e % 8;
+    float sq = 0.f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int col = tile * 16 + g + 8 * r;
+      if (live && col < H) {
+        const float rv = __half2float(__ldcg(res.x + static_cast<size_t>(m) * res.ld + col));
+        const float rval = res.ss ? norm_value(rv, s_den, __half2float(__ldg(res.w + col))) : rv;
+        const float o = round_h(__ldcg(o32 + static_cast<size_t>(m) * H + col));
+        const half s16 = __float2half_rn(fadd(rval, o));
+        out[static_cast<size_t>(m) * H + col] = s16;
+        const float sf = __half2float(s16);
+        sq = r == 0 ? fmul(sf, sf) : fadd(sq, fmul(sf, sf));
+      }
+    }
+    sq = fadd(sq, __shfl_xor_sync(0xffffffffu, sq, 1));
+    sq = fadd(sq, __shfl_xor_sync(0xffffffffu, sq, 2));
+    sq = fadd(sq, __shfl_xor_sync(0xffffffffu, sq, 4));
+    if (live && g == 0) ss_out[static_cast<size_t>(m) * n_tiles + tile] = sq;
+  }
+  grid_dep_launch();
+}
+
+__global__ void __launch_bounds__(kRowThreads) tp_argmax_local_kernel(const float* am_val, const int* am_idx,
+                                                                      int n_part, int offset, int* pairs) {
+  __shared__ RowShared sh;
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  float bv;
+  int bi;
+  argmax_reduce_body(am_val, am_idx, n_part, m, sh, bv, bi);
+  if (threadIdx.x == 0) {
+    pairs[2 * m] = __float_as_int(bv);
+    pairs[2 * m + 1] = bi == 0x7fffffff ? 0x7fffffff : bi + offset;
+  }
+}
+
+__global__ void __launch_bounds__(kWarp) tp_argmax_pick_kernel(const int* pairs, int world, int M, int* out) {
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  float bv = kNegInf;
+  int bi = 0x7fffffff;
+  for (int r = 0; r < world; ++r) {
+    const float v = __int_as_float(__ldcg(pairs + (static_cast<size_t>(r) * M + m) * 2));
+    const int i = __ldcg(pairs + (static_cast<size_t>(r) * M + m) * 2 + 1);
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  out[m] = bi == 0x7fffffff ? 0 : bi;
+}
+
+__global__ void __launch_bounds__(kRowThreads) tp_logits_reorder_kernel(const half* gathered, int world, int M,
+                                                                        int v_local, half* out) {
+  grid_dep_wait();
+  const int m = blockIdx.y, r = blockIdx.z;
+  const half* src = gathered + (static_cast<size_t>(r) * M + m) * v_local;
+  half* dst = out + static_cast<size_t>(m) * world * v_local + static_cast<size_t>(r) * v_local;
+  for (int i = blockIdx.x * kRowThreads + threadIdx.x; i < v_local; i += gridDim.x * kRowThreads) dst[i] = src[i];
+}
+
 cudaLaunchConfig_t row_cfg(int M, size_t smem, bool pdl, cudaStream_t st, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t c = {};
   c.gridDim = dim3(M);
@@ -67,6 +147,37 @@ cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_pa
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
   return cudaLaunchKernelEx(&c, argmax_final_kernel, am_val, am_idx, n_part, out);
+}
+
+cudaError_t launch_tp_resid(const ActIn& res_, const float* o32, int M, int H, half* out, float* ss_out, bool pdl,
+                            cudaStream_t st) {
+  ActIn res = res_;
+  set_vec(res);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  return cudaLaunchKernelEx(&c, tp_resid_kernel, res, o32, H, out, ss_out);
+}
+
+cudaError_t launch_tp_argmax_local(const float* am_val, const int* am_idx, int n_part, int M, int offset,
+                                   int* pairs, bool pdl, cudaStream_t st) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  return cudaLaunchKernelEx(&c, tp_argmax_local_kernel, am_val, am_idx, n_part, offset, pairs);
+}
+
+cudaError_t launch_tp_argmax_pick(const int* pairs, int world, int M, int* out, bool pdl, cudaStream_t st) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  c.blockDim = dim3(kWarp);
+  return cudaLaunchKernelEx(&c, tp_argmax_pick_kernel, pairs, world, M, out);
+}
+
+cudaError_t launch_tp_logits_reorder(const half* gathered, int world, int M, int v_local, half* out, bool pdl,
+                                     cudaStream_t st) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  c.gridDim = dim3((v_local + kRowThreads * 8 - 1) / (kRowThreads * 8), M, world);
+  return cudaLaunchKernelEx(&c, tp_logits_reorder_kernel, gathered, world, M, v_local, out);
 }
 
 }  // namespace alm

@@ -109,8 +109,10 @@ ALM_DEV void rownorm_body(const ActIn& in, const half* w2, float eps2, half* out
   body_sync();   // xrow is reused by the caller's next block
 }
 
-ALM_DEV void argmax_final_body(const float* am_val, const int* am_idx, int n_part, int* out, int m,
-                               RowShared& sh) {
+// Best (value, index) of row m's per-CTA argmax partials (larger value, then
+// smaller index); every thread gets the pair.
+ALM_DEV void argmax_reduce_body(const float* am_val, const int* am_idx, int n_part, int m, RowShared& sh,
+                                float& best_v, int& best_i) {
   float* sv = sh.sv;
   int* si = sh.si;
   float bv = kNegInf;
@@ -138,8 +140,17 @@ ALM_DEV void argmax_final_body(const float* am_val, const int* am_idx, int n_par
     }
     body_sync();
   }
-  if (threadIdx.x == 0) out[m] = si[0] == 0x7fffffff ? 0 : si[0];
+  best_v = sv[0];
+  best_i = si[0];
   body_sync();
+}
+
+ALM_DEV void argmax_final_body(const float* am_val, const int* am_idx, int n_part, int* out, int m,
+                               RowShared& sh) {
+  float bv;
+  int bi;
+  argmax_reduce_body(am_val, am_idx, n_part, m, sh, bv, bi);
+  if (threadIdx.x == 0) out[m] = bi == 0x7fffffff ? 0 : bi;
 }
 
 }  // namespace alm

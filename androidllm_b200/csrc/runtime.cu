@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "cluster_fwd.cuh"
 #include "forward.cuh"
+#include "tp.cuh"
 #include "gemv_body.cuh"
 #include "kernels.cuh"
 
@@ -149,6 +150,9 @@ struct alm_ctx {
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
   bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
+  // tensor parallelism: NCCL communicator of this rank (alm_ctx_init_tp)
+  void* tp_comm = nullptr;
+  int tp_rank = 0, tp_world = 1;
 };
 
 struct alm_qweight {
@@ -194,6 +198,11 @@ struct Work {
   float* sample_scratch = nullptr;   // kMaxRows * vocab fp32 for the sampler
   float* scores = nullptr;
   float* stats = nullptr;
+  // tensor parallelism
+  float* o32 = nullptr;        // (kMaxRows, hidden) fp32 partials of the row-split projections
+  int* tp_pairs = nullptr;     // (kMaxRows, 2) local argmax, then (world, kMaxRows, 2) gathered
+  half* logits_local = nullptr;  // (kMaxRows, vocab_local) this rank's vocabulary slice
+  half* logits_gather = nullptr; // (world, kMaxRows, vocab_local)
   int attn_ctx = 0;       // capacity of the attention scratch (positions)
   int score_ld = 0;       // row stride of the score scratch
   int* pinned = nullptr;  // host staging for small copies
@@ -248,6 +257,11 @@ struct alm_model {
   // cluster forward kernel (single-row forwards)
   size_t cf_smem = 0;
   bool cf_ok = false;
+  // tensor parallelism: this model is the rank's shard (local heads, FFN
+  // slice, head rows [vocab_offset, vocab_offset + vocab_local))
+  bool tp = false;
+  int vocab_offset = 0, vocab_local = 0;
+  bool tp_need_logits = false;   // gather the full logits after the head
 };
 
 struct alm_kv {
@@ -537,6 +551,26 @@ ActIn deferred_in(const alm_model* m, const half* s, const float* ss, const half
     if (e_ != cudaSuccess) return fail(ALM_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
+// A row-split projection of a tensor-parallel shard: this rank's fp32
+// partial sums over its K slice, an all-reduce (sum) over the ranks, then
+// out = fp16(res + fp16(sum)) with the sums of squares of the next norm.
+int enqueue_tp_rowsplit(alm_model* m, const alm_qweight* w, const ActIn& in, int M, const ActIn& res, half* out,
+                        float* ss_out, bool pdl) {
+  Work& ws = m->ws;
+  cudaStream_t st = m->ctx->stream;
+  const int H = m->cfg.hidden;
+  Epi e;
+  e.out32 = ws.o32;
+  e.ldo = H;
+  e.n_out = H;
+  ALM_LAUNCH(launch_gemv(w->t, in, M, EPI_STORE32, e, StepIO{ws.pos, ws.err}, scratch_of(m), pdl, st));
+  std::string err;
+  if (tp_allreduce_sum_f32(m->ctx->tp_comm, ws.o32, static_cast<size_t>(M) * H, st, &err))
+    return fail(ALM_ERR_CUDA, err);
+  ALM_LAUNCH(launch_tp_resid(res, ws.o32, M, H, out, ss_out, false, st));
+  return ALM_OK;
+}
+
 int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool pdl) {
   const alm_model_config& c = m->cfg;
   Layer& L = m->layers[li];
@@ -581,14 +615,20 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   ALM_LAUNCH(launch_attention(a, pdl, st));
   prof_mark(ALM_OP_ATTN_PV, M);
 
-  Epi eo;
-  eo.out = ws.s1;
-  eo.ldo = c.hidden;
-  eo.n_out = c.hidden;
-  eo.res = in;
-  eo.ss_out = ws.ss1;
-  ALM_LAUNCH(launch_gemv(L.o->t, raw_in(ws.ctx, qdim, qdim), M, EPI_RESID, eo, io, scr, pdl, st));
-  prof_mark(ALM_OP_O, M);
+  if (m->tp) {
+    // row-split O: fp32 partials, sum over ranks, then residual and norm partials
+    ALM_TRY(enqueue_tp_rowsplit(m, L.o, raw_in(ws.ctx, qdim, qdim), M, in, ws.s1, ws.ss1, pdl));
+    prof_mark(ALM_OP_O, M);
+  } else {
+    Epi eo;
+    eo.out = ws.s1;
+    eo.ldo = c.hidden;
+    eo.n_out = c.hidden;
+    eo.res = in;
+    eo.ss_out = ws.ss1;
+    ALM_LAUNCH(launch_gemv(L.o->t, raw_in(ws.ctx, qdim, qdim), M, EPI_RESID, eo, io, scr, pdl, st));
+    prof_mark(ALM_OP_O, M);
+  }
 
   const ActIn n1 = deferred_in(m, ws.s1, ws.ss1, L.n_in);
   Epi eg;
@@ -598,6 +638,11 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   ALM_LAUNCH(launch_gemv(L.gu->t, n1, M, EPI_SWIGLU, eg, io, scr, pdl, st));
   prof_mark(ALM_OP_GATE_UP, M);
 
+  if (m->tp) {
+    ALM_TRY(enqueue_tp_rowsplit(m, L.down, raw_in(ws.h, c.intermediate, c.intermediate), M, n1, ws.s2, ws.ss2, pdl));
+    prof_mark(ALM_OP_DOWN, M);
+    return ALM_OK;
+  }
   Epi ed;
   ed.out = ws.s2;
   ed.ldo = c.hidden;
@@ -611,7 +656,39 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
 }
 
 // Head on normalised rows `x` (M, hidden) already in ws.xn.
+int enqueue_head_tp(alm_model* m, int M, bool pdl) {
+  Work& ws = m->ws;
+  cudaStream_t st = m->ctx->stream;
+  const int world = m->ctx->tp_world;
+  Epi e;
+  e.out = ws.logits_local;
+  e.ldo = m->vocab_local;
+  e.n_out = m->vocab_local;
+  e.am_val = ws.am_val;
+  e.am_idx = ws.am_idx;
+  const ActIn in = raw_in(ws.xn, m->cfg.hidden, m->cfg.hidden);
+  ALM_LAUNCH(launch_gemv(m->head->t, in, M, EPI_LOGITS, e, StepIO{ws.pos, ws.err}, scratch_of(m), pdl, st));
+  prof_mark(ALM_OP_HEAD, M);
+  // (value, global index) of each rank's best, gathered; the best of them
+  int* send = ws.tp_pairs;
+  int* recv = ws.tp_pairs + 2 * kMaxRows;
+  ALM_LAUNCH(launch_tp_argmax_local(ws.am_val, ws.am_idx, ws.n_am, M, m->vocab_offset, send, pdl, st));
+  std::string err;
+  if (tp_allgather(m->ctx->tp_comm, send, recv, static_cast<size_t>(M) * 2 * sizeof(int), st, &err))
+    return fail(ALM_ERR_CUDA, err);
+  ALM_LAUNCH(launch_tp_argmax_pick(recv, world, M, ws.argmax, false, st));
+  prof_mark(ALM_OP_ARGMAX, M);
+  if (m->tp_need_logits) {
+    if (tp_allgather(m->ctx->tp_comm, ws.logits_local, ws.logits_gather,
+                     static_cast<size_t>(M) * m->vocab_local * sizeof(half), st, &err))
+      return fail(ALM_ERR_CUDA, err);
+    ALM_LAUNCH(launch_tp_logits_reorder(ws.logits_gather, world, M, m->vocab_local, ws.logits, false, st));
+  }
+  return ALM_OK;
+}
+
 int enqueue_head(alm_model* m, int M, bool pdl) {
+  if (m->tp) return enqueue_head_tp(m, M, pdl);
   Work& ws = m->ws;
   Epi e;
   e.out = ws.logits;
@@ -948,8 +1025,30 @@ int alm_ctx_destroy(alm_ctx* ctx) {
   if (!ctx) return ALM_OK;
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  tp_comm_destroy(ctx->tp_comm);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
+  return ALM_OK;
+}
+
+int alm_nccl_unique_id(uint8_t* id_out) {
+  ALM_REQ(id_out, "null argument");
+  std::string err;
+  if (tp_unique_id(id_out, &err)) return fail(ALM_ERR_STATE, err);
+  return ALM_OK;
+}
+
+int alm_ctx_init_tp(alm_ctx* ctx, int rank, int world, const uint8_t* id) {
+  ALM_REQ(ctx && id, "null argument");
+  ALM_REQ(world >= 1 && rank >= 0 && rank < world, "rank must be in 0..world-1");
+  ALM_REQ(!ctx->tp_comm, "tensor parallelism already initialised on this context");
+  DeviceGuard g(ctx->device);
+  std::string err;
+  void* comm = nullptr;
+  if (tp_comm_init(rank, world, id, &comm, &err)) return fail(ALM_ERR_STATE, err);
+  ctx->tp_comm = comm;
+  ctx->tp_rank = rank;
+  ctx->tp_world = world;
   return ALM_OK;
 }
 
@@ -1187,7 +1286,8 @@ int alm_model_destroy(alm_model* m) {
   for (void* p : {(void*)w.tokens, (void*)w.pos, (void*)w.err, (void*)w.x0, (void*)w.s1, (void*)w.s2,
                   (void*)w.ss1, (void*)w.ss2, (void*)w.q, (void*)w.ctx, (void*)w.h, (void*)w.xn, (void*)w.xout,
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
-                  (void*)w.scores, (void*)w.stats, (void*)w.sample_scratch})
+                  (void*)w.scores, (void*)w.stats, (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
+                  (void*)w.logits_local, (void*)w.logits_gather})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
   dev_free(m->fwd_layers);
@@ -1307,12 +1407,28 @@ int alm_model_set_final_norm(alm_model* m, const uint16_t* w_host) {
 
 int alm_model_set_head(alm_model* m, const alm_proj_src* head) {
   ALM_REQ(m && head, "null argument");
-  ALM_REQ(head->out == m->cfg.vocab && head->in_real == m->cfg.hidden, "head must be (vocab, hidden)");
+  ALM_REQ(head->out == (m->tp ? m->vocab_local : m->cfg.vocab) && head->in_real == m->cfg.hidden,
+          "head must be (vocab, hidden), or (vocab_local, hidden) for a tensor-parallel shard");
   DeviceGuard g(m->ctx->device);
   alm_qweight* w = nullptr;
   ALM_TRY(build_qweight(m->ctx, head, 1, identity_map(head->out), head->out, true, &w));
   alm_qweight_free(m->head);
   m->head = w;
+  m->finalized = false;
+  return ALM_OK;
+}
+
+int alm_model_set_tp(alm_model* m, int vocab_offset, int vocab_local) {
+  ALM_REQ(m, "null model");
+  ALM_REQ(m->ctx->tp_comm, "tensor parallelism not initialised on the context (alm_ctx_init_tp)");
+  ALM_REQ(vocab_local >= 1 && vocab_offset >= 0 && vocab_offset + vocab_local <= m->cfg.vocab,
+          "vocabulary slice out of range");
+  ALM_REQ(vocab_local * m->ctx->tp_world == m->cfg.vocab,
+          "the vocabulary must split evenly over the ranks (vocab_local * world == vocab)");
+  ALM_REQ(!m->head, "alm_model_set_tp comes before alm_model_set_head");
+  m->tp = true;
+  m->vocab_offset = vocab_offset;
+  m->vocab_local = vocab_local;
   m->finalized = false;
   return ALM_OK;
 }
@@ -1323,6 +1439,8 @@ int alm_model_finalize(alm_model* m) {
   const alm_model_config& c = m->cfg;
   if (!m->embed_table) return fail(ALM_ERR_STATE, "embedding not set");
   if (!m->final_norm) return fail(ALM_ERR_STATE, "final norm not set");
+  if (m->tp && !m->head)
+    return fail(ALM_ERR_STATE, "a tensor-parallel shard needs its head rows (alm_model_set_head)");
   if (!m->head) {
     // tied head: the embedding table in the tile layout
     alm_proj_src s{m->embed_table, m->embed_scale, m->embed_bits, m->embed_block, c.vocab, c.hidden, c.hidden};
@@ -1362,6 +1480,13 @@ int alm_model_finalize(alm_model* m) {
     ALM_TRY(dev_alloc_t(&ws.argmax, kMaxRows));
     ALM_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ws.pinned), 64 * sizeof(int)));
   }
+  if (m->tp && !ws.o32) {
+    const int world = m->ctx->tp_world;
+    ALM_TRY(dev_alloc_t(&ws.o32, static_cast<size_t>(kMaxRows) * c.hidden));
+    ALM_TRY(dev_alloc_t(&ws.tp_pairs, static_cast<size_t>(2 * kMaxRows) * (world + 1)));
+    ALM_TRY(dev_alloc_t(&ws.logits_local, static_cast<size_t>(kMaxRows) * m->vocab_local));
+    ALM_TRY(dev_alloc_t(&ws.logits_gather, static_cast<size_t>(kMaxRows) * m->vocab_local * world));
+  }
   // per-CTA argmax partials of the head
   const int n_am = gemv_out_blocks(m->head->t);
   if (n_am > ws.n_am) {
@@ -1379,6 +1504,10 @@ int alm_model_finalize(alm_model* m) {
   ALM_TRY(ensure_part(ws, need));
   ALM_TRY(build_forward(m));
   ALM_TRY(build_cluster_fwd(m));
+  if (m->tp) {   // the single-launch forwards have no collectives
+    m->fwd_grid = 0;
+    m->cf_ok = false;
+  }
   m->finalized = true;
   return ALM_OK;
 }
@@ -1501,7 +1630,10 @@ int alm_head_logits(alm_model* m, const uint16_t* x_host, int rows, float* logit
                            cudaMemcpyHostToDevice, st));
   ALM_CUDA(launch_rownorm(raw_in(m->ws.x0, m->cfg.hidden, m->cfg.hidden), rows, m->final_norm, m->cfg.rms_eps,
                           m->ws.xn, m->cfg.hidden, m->ctx->pdl, st));
-  ALM_TRY(enqueue_head(m, rows, m->ctx->pdl));
+  m->tp_need_logits = logits_host != nullptr;
+  const int rc = enqueue_head(m, rows, m->ctx->pdl);
+  m->tp_need_logits = false;
+  ALM_TRY(rc);
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
 }
@@ -1739,7 +1871,10 @@ int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, 
   ALM_TRY(set_pos(m, pos0));
   ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host, rows * sizeof(int), cudaMemcpyHostToDevice, st));
   const bool head = logits_host != nullptr || argmax_host != nullptr;
-  ALM_TRY(enqueue_forward(m, kv, rows, head, m->ctx->pdl));
+  m->tp_need_logits = logits_host != nullptr;
+  const int rc = enqueue_forward(m, kv, rows, head, m->ctx->pdl);
+  m->tp_need_logits = false;
+  ALM_TRY(rc);
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
 }
@@ -1874,7 +2009,10 @@ static int capture_spec_graph(alm_spec* s) {
   cudaGraph_t graph = nullptr;
   if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
     return fail(ALM_ERR_CUDA, "graph capture failed to start");
+  // the sampler reads the target's full logits rows
+  s->target->tp_need_logits = s->temperature > 0.f;
   int rc = enqueue_spec_step(s);
+  s->target->tp_need_logits = false;
   cudaError_t e = cudaStreamEndCapture(st, &graph);
   if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
   if (rc == ALM_OK) {

@@ -42,8 +42,15 @@ WORKLOADS = {
     # name: (target canon, target bits, draft canon, draft bits)
     "qwen2.5-1.5b": ("qwen2.5-1.5b", dict(attn_bits=4, mlp_bits=8, block=64, embed_bits=8),
                      "qwen2.5-0.5b", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=8)),
+    # tensor parallel over the GPUs of the run (k = 6, 2048-token prompt);
+    # the draft is the 0.5B shape with the 7B vocabulary, replicated per rank
+    "qwen2.5-7b": ("qwen2.5-7b", dict(attn_bits=4, mlp_bits=8, block=64, embed_bits=8),
+                   "qwen2.5-0.5b-v152064", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=8)),
     "toy": ("toy", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=0), None, None),
 }
+TP_WORKLOAD = "qwen2.5-7b"
+TP_SPEC_K = 6
+TP_PROMPT_LEN = 2048
 
 
 def dist_env():
@@ -54,9 +61,16 @@ def dist_env():
 # --------------------------------------------------------------------------
 # models
 # --------------------------------------------------------------------------
+def canon_of(name):
+    from androidllm_b200 import synth
+    if name == "qwen2.5-0.5b-v152064":
+        return dict(synth.CANONS["qwen2.5-0.5b"], vocab=152064, name="qwen2.5-0.5b-synth-v152064")
+    return dict(synth.CANONS[name])
+
+
 def ensure_model(canon_name, kw, seed):
-    from androidllm_b200 import shard, synth
-    canon = dict(synth.CANONS[canon_name])
+    from androidllm_b200 import shard
+    canon = canon_of(canon_name)
     tag = f"{canon_name}-s{seed}-a{kw['attn_bits']}m{kw['mlp_bits']}e{kw['embed_bits']}"
     out = os.path.join(CACHE, tag)
     if not os.path.exists(os.path.join(out, ".complete")):
@@ -247,8 +261,8 @@ class CpuSample:
         tname, tkw, dname, dkw = WORKLOADS[workload]
         self.llama = llama
         self.quant = quant
-        self.tc = dict(synth.CANONS[tname])
-        self.dc = dict(synth.CANONS[dname or tname], layers=2 if dname is None else synth.CANONS[dname]["layers"])
+        self.tc = canon_of(tname)
+        self.dc = dict(canon_of(dname or tname), layers=2 if dname is None else canon_of(dname)["layers"])
         rng = np.random.default_rng(0)
         self.t = self._setup(self.tc, tkw, rng)
         self.d = self._setup(self.dc, dkw or tkw, rng)
@@ -305,13 +319,13 @@ class CpuSample:
         return resident, streaming, t_target, t_draft
 
 
-def cpu_baseline(workload, tokens_per_step, samples):
+def cpu_baseline(workload, tokens_per_step, samples, k=SPEC_K):
     s = CpuSample(workload)
-    s.step(tokens_per_step)       # warm-up
+    s.step(tokens_per_step, k)       # warm-up
     res, stream, walls = [], [], []
     for _ in range(samples):
         t0 = time.perf_counter()
-        a, b, _, _ = s.step(tokens_per_step)
+        a, b, _, _ = s.step(tokens_per_step, k)
         walls.append(time.perf_counter() - t0)
         res.append(a)
         stream.append(b)
@@ -327,7 +341,7 @@ def cpu_baseline(workload, tokens_per_step, samples):
                    f"a 1/layers slice of each fp16 LM head, and one layer's dequantize_packed of each model "
                    f"(numpy, 1 thread: numpy's fp16 matmul has no BLAS path and the reference decodes one "
                    f"sequence; host has {host['nproc']} threads, {host['cpu_model']}), extrapolated to a full "
-                   f"step of {SPEC_K} draft tokens + {tokens_per_step:.2f} target tokens; value = resident "
+                   f"step of {k} draft tokens + {tokens_per_step:.2f} target tokens; value = resident "
                    f"dequantized weights, value_streaming = the reference's default streaming engine, which "
                    f"also dequantizes every layer for every token; {sum(walls):.1f}s of CPU work"),
         "sample_s": statistics.mean(walls),
@@ -340,20 +354,27 @@ def run_reference(args):
         return 0
     tokens_per_step = 1.0
     t0 = time.perf_counter()
-    # each sample is ~0.5 s of numpy work at the 1.5B shapes; cap the count so
+    tp = args.workload == TP_WORKLOAD or world > 1
+    workload = TP_WORKLOAD if tp else args.workload
+    k = TP_SPEC_K if tp else SPEC_K
+    # each sample is ~0.5 s (1.5B) / ~2 s (7B) of numpy work; cap the count so
     # the arm ends within a few minutes whatever --steps is
-    cb = cpu_baseline(args.workload, tokens_per_step, min(REF_MAX_SAMPLES, max(1, args.steps)))
+    cb = cpu_baseline(workload, tokens_per_step, min(REF_MAX_SAMPLES if not tp else 24, max(1, args.steps)), k)
+    metric = "spec-decode tokens/sec (k=6) at Qwen2.5-7B, tensor parallel" if tp else METRIC
     line = {
-        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+        "impl": "reference", "metric": metric, "value": cb["value"], "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         # a step of this arm is one bounded sample (see cpu_baseline.sample);
         # the full speculative step it stands for is extrapolated
         "ms_per_step": round(1000.0 * cb["sample_s"], 3),
         "ms_per_full_step_extrapolated": round(1000.0 * tokens_per_step / cb["value"], 1),
         "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": workload_config(args, world),
-        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "value_streaming", "host")},
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(args, world) if not tp else
+        {"workload": f"qwen2.5-7b spec-decode (the reference runs one process on the host; the GPU arm is "
+                     f"tensor parallel x{world})", "k": TP_SPEC_K, "batch": 1, "prompt_len": TP_PROMPT_LEN,
+         "episode_tokens": EPISODE_TOKENS, "temperature": 0},
+        "cpu_baseline": {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample", "value_streaming", "host")},
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
     }
@@ -517,11 +538,131 @@ def run_ours(args):
     }
     if rank == 0 and not args.no_cpu_baseline:
         cb = cpu_baseline(args.workload, tokens_per_step=line["tokens_per_step"], samples=args.cpu_samples)
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "value_streaming",
+                                                    "host")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     spec.close()
     if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+# --------------------------------------------------------------------------
+# tensor-parallel arm: the Qwen2.5-7B-shaped target split over the ranks
+# --------------------------------------------------------------------------
+def run_tp(args):
+    """Speculative decoding (k = 6, greedy) of the Qwen2.5-7B-shaped target
+    (int4 attention / int8 MLP / int8 head, block 64) split over the ranks
+    by tensor parallelism (heads, FFN and vocabulary; NCCL all-reduce after o
+    and down, all-gathered head argmax), with the 0.5B-shaped int4 draft
+    replicated on every rank.  2048-token prompt, 256-token episodes; exactly
+    --steps steps timed, their start positions spread over the episode."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from androidllm_b200 import tp
+    from androidllm_b200.ops import Context, DeviceKV, DeviceModel, SpecDecoder
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    if rank == 0:
+        tdir, ddir = prepare_models(TP_WORKLOAD)
+    if world > 1:
+        dist.barrier()
+    tdir, ddir = prepare_models(TP_WORKLOAD)
+    ctx = Context(local)
+    if world > 1:
+        uid = [tp.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp.init_context_tp(ctx, rank, world, uid[0])
+        t = tp.device_model_tp(ctx, tdir, rank, world)
+    else:
+        t = DeviceModel.from_dir(ctx, tdir)
+    d = DeviceModel.from_dir(ctx, ddir)
+    cap = TP_PROMPT_LEN + EPISODE_TOKENS + 2 * (TP_SPEC_K + 1) + 16
+    tkv, dkv = DeviceKV(t, cap), DeviceKV(d, cap)
+    prompt = np.random.default_rng(321).integers(0, t.canon["vocab"], TP_PROMPT_LEN).tolist()
+    t0 = time.perf_counter()
+    for i in range(0, TP_PROMPT_LEN - 1, 16):
+        t.forward(tkv, prompt[:-1][i:i + 16], i, logits=False, argmax=False)
+    for i in range(0, TP_PROMPT_LEN, 16):
+        d.forward(dkv, prompt[i:i + 16], i, logits=False, argmax=False)
+    prefill_s = time.perf_counter() - t0
+    s = SpecDecoder(t, d, tkv, dkv, TP_SPEC_K)
+    p0 = TP_PROMPT_LEN - 1
+    clk = ClockSampler(local).__enter__()
+    # warm-up: one episode (fills the caches over the episode's positions)
+    s.begin(prompt[-1], p0)
+    stream = [prompt[-1]]
+    t_e2e = time.perf_counter()
+    n_e2e = 0
+    while len(stream) <= EPISODE_TOKENS:
+        emitted, _ = s.run(1)
+        stream += emitted
+        n_e2e += 1
+    t_e2e = time.perf_counter() - t_e2e
+    for _ in range(max(0, args.warmup - 1)):
+        s.begin(prompt[-1], p0)
+        s.bench(32)
+    starts = [p0 + (i * EPISODE_TOKENS) // args.steps for i in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms, tokens = 0.0, 0
+    for st in starts:
+        s.begin(stream[st - p0], st)
+        m1, n1 = s.bench(1)
+        ms += m1
+        tokens += n1
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    if world > 1:
+        ms_max, _ = combine_ranks(dist, ms, tokens, "cuda")
+    else:
+        ms_max = ms
+    # every rank emits the same tokens: the job's tokens are one rank's
+    value = tokens / (ms_max / 1000.0)
+    ms_per_step = ms_max / args.steps
+    mid = p0 + EPISODE_TOKENS // 2
+    s.begin(stream[mid - p0], mid)
+    prof = s.profile()
+    peaks = load_peaks()
+    per_rank_bytes = TP_SPEC_K * forward_weight_bytes(d.manifest) + forward_weight_bytes(t.manifest) // world
+    line = {
+        "metric": "spec-decode tokens/sec (k=6) at Qwen2.5-7B, tensor parallel", "value": round(value, 2),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"qwen2.5-7b spec-decode, tensor parallel x{world} (draft qwen2.5-0.5b shape, "
+                               f"int4, replicated)",
+                   "target": "qwen2.5-7b: int4 attention, int8 MLP, int8 head, block 64",
+                   "draft": "qwen2.5-0.5b: int4, vocabulary 152064", "k": TP_SPEC_K, "batch": 1,
+                   "prompt_len": TP_PROMPT_LEN, "episode_tokens": EPISODE_TOKENS, "temperature": 0,
+                   "parallelism": f"tp{world}", "positions_timed": [starts[0], starts[-1]],
+                   "l2": "weights (>= 1 GB streamed per step per rank) exceed the 126 MB L2; no flush needed"},
+        "e2e": {"value": round((len(stream) - 1) / t_e2e, 3), "unit": "tokens/s",
+                "scope": "SpecDecoder.run(1) per step from the host (state in, emitted tokens out)",
+                "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16 + 4 * (TP_SPEC_K + 1) + 4,
+                "steps": n_e2e, "tokens": len(stream) - 1, "prefill_s": round(prefill_s, 2)},
+        "step_roofline": {"weight_bytes_per_step_per_rank": per_rank_bytes,
+                          "achieved_gbs_per_rank": round(per_rank_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+                          "frac": round(per_rank_bytes / (ms_per_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)},
+        "step_profile": {"position": mid, "launches": len(prof), "sum_us": round(sum(r[3] for r in prof), 1),
+                         "top": [{k: g[k] for k in ("kernel", "launches", "us_per_launch", "share")}
+                                 for g in step_profile_groups(prof, t.manifest, d.manifest, mid, TP_SPEC_K)[:6]]},
+        "tokens_per_step": round(tokens / args.steps, 3),
+        "gpu_launches": s.kernel_count() * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    s.close()
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
@@ -848,6 +989,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == TP_WORKLOAD or dist_env()[1] > 1:
+        return run_tp(args)
     return run_ours(args)
 
 

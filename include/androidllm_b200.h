@@ -82,6 +82,14 @@ ALM_API int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable);
    On B200 a tcgen05.mma costs about the same for N = 16 as for N = 256, so
    the row layout pays off only for many activation rows (dense GEMM). */
 ALM_API int alm_ctx_set_gemv_layout(alm_ctx* ctx, int mode);
+/* Tensor parallelism (SURVEY e: larger models split over the GPUs of one
+ * node; no reference counterpart, the reference runs whole matrices in one
+ * process, androidllm/models/llama.py:97-127).  One process per GPU; rank 0
+ * makes an NCCL unique id (128 bytes) that the host hands to every rank,
+ * and each rank joins with alm_ctx_init_tp on its context.  NCCL is opened
+ * at run time (libnccl.so.2); the collectives run on the context's stream. */
+ALM_API int alm_nccl_unique_id(uint8_t* id_out);
+ALM_API int alm_ctx_init_tp(alm_ctx* ctx, int rank, int world, const uint8_t* id);
 /* Device memory helpers for hosts without their own device-memory library. */
 ALM_API int alm_dev_alloc(alm_ctx* ctx, size_t bytes, void** out_dev);
 ALM_API int alm_dev_free(alm_ctx* ctx, void* dev);
@@ -161,6 +169,20 @@ ALM_API int alm_model_set_final_norm(alm_model* m, const uint16_t* w_host);
 /* Untied LM head (vocab, hidden) in shard format; without it the head is the
  * embedding table (tied, androidllm/models/llama.py:145). */
 ALM_API int alm_model_set_head(alm_model* m, const alm_proj_src* head);
+/* Make the model this rank's tensor-parallel shard (before set_head and
+ * finalize; the context must have joined with alm_ctx_init_tp).  The
+ * model's config then holds the rank's heads, kv heads and FFN width, and
+ * its layers the matching slices: q / k / v and gate / up rows of its heads
+ * and FFN columns, o and down columns (K) of the same, on 64-column blocks.
+ * The head is this rank's vocabulary rows [vocab_offset, vocab_offset +
+ * vocab_local) with vocab_local * world == vocab (alm_model_set_head; the
+ * embedding stays whole).  After the o and down projections the fp32 partial
+ * sums are summed over the ranks (ncclAllReduce), then rounded to fp16 and
+ * added to the residual; the head's per-rank (max, index) pairs are gathered
+ * (ncclAllGather) and the best taken, first index on ties, so every rank
+ * holds the same tokens.  Logits requested by the host (or the sampler) are
+ * gathered whole. */
+ALM_API int alm_model_set_tp(alm_model* m, int vocab_offset, int vocab_local);
 /* *uses_cluster = 1 when the model's single-row forwards run as the cluster
    kernel (alm_ctx_set_cluster_forward enabled and every projection fits it). */
 ALM_API int alm_model_cluster_forward(const alm_model* m, int* uses_cluster);
