@@ -7,7 +7,7 @@
 //     (a contiguous run of qtile records: its output tiles x all k-blocks),
 //     layer after layer and projection after projection, through a ring of
 //     shared-memory slots with bulk copies (TMA engine, mbarrier completion,
-//     no multicast).  Weights do not depend on activations, so the stream
+//     each CTA its own copy).  Weights do not depend on activations, so the stream
 //     runs ahead across phase boundaries and never waits for them;
 //   * eight decoding warps per CTA split the CTA's records into items of
 //     (tile, k-split), the weight's own K split of the standalone GEMV (ksw
