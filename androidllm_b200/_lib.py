@@ -83,6 +83,8 @@ SIGNATURES = {
     "alm_spec_create": [_P, _P, _P, _P, _I, _PP],
     "alm_spec_destroy": [_P],
     "alm_spec_begin": [_P, ctypes.c_int32, _I],
+    "alm_spec_begin_prev": [_P, ctypes.c_int32, ctypes.c_int32, _I],
+    "alm_spec_set_draft_refresh": [_P, _I],
     "alm_spec_run": [_P, _I, _P, _P, _P],
     "alm_spec_state": [_P, _PI32, _PI32],
     "alm_spec_kernel_count": [_P, _PI32],

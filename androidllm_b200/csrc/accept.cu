@@ -236,6 +236,7 @@ __global__ void __launch_bounds__(kAccThreads) accept_kernel(AcceptArgs a) {
     st[2] = base + n + 1;
     if (st[3] < a.cap_steps) a.ring_acc[st[3]] = n;
     st[3] += 1;
+    st[5] = n == 0 ? st[0] : a.cand[n - 1];
     st[0] = tok;
     st[1] += n + 1;
     st[4] += a.cursor_advance;

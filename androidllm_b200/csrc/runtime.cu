@@ -18,9 +18,9 @@
 
 namespace alm {
 cudaError_t launch_spec_prep_draft(const int* state, int* cand, const int* d_argmax, int i, int* tokens,
-                                   int* pos, cudaStream_t st);
+                                   int* pos, int prev_row, int refresh, cudaStream_t st);
 cudaError_t launch_spec_prep_verify(const int* state, int* cand, const int* d_argmax, int k, int* tokens,
-                                    int* pos, cudaStream_t st);
+                                    int* pos, int prev_row, cudaStream_t st);
 cudaError_t launch_spec_accept_greedy(int* state, const int* cand, const int* t_argmax, int k, int* out_tokens,
                                       int* out_accepted, int cap_tokens, int cap_steps, int sampled, cudaStream_t st);
 }  // namespace alm
@@ -294,6 +294,8 @@ struct alm_spec {
   int n_uniforms = 0, cap_uniforms = 0;
   // min(1, p/q) rejection sampling instead of the reference's rule (T > 0)
   bool rejection = false;
+  // the first draft forward re-forwards the token at pos - 1 (state[5])
+  bool refresh = false;
   float* probs = nullptr;      // (k + 1) target rows then k draft rows of vocab fp32
 };
 
@@ -1891,14 +1893,17 @@ static int enqueue_spec_step_rejection(alm_spec* s) {
   const int V = t->cfg.vocab;
   float* p_rows = s->probs;
   float* q_rows = s->probs + static_cast<size_t>(s->k + 1) * V;
+  const int r0 = s->refresh ? 2 : 1;   // rows of draft forward 0; its candidate is the last
   for (int i = 0; i < s->k; ++i) {
+    const int rows = i == 0 ? r0 : 1;
     prof_role(0);
-    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
+    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos,
+                                    i == 1 ? r0 - 1 : 0, s->refresh ? 1 : 0, st));
     prof_mark(ALM_OP_SPEC_PREP, 1);
     prof_role(1);
-    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
+    ALM_TRY(enqueue_forward(d, s->dkv, rows, true, d->ctx->pdl));
     ProbsArgs pa;
-    pa.logits = d->ws.logits;
+    pa.logits = d->ws.logits + static_cast<size_t>(rows - 1) * V;
     pa.ld = V;
     pa.probs = q_rows + static_cast<size_t>(i) * V;
     pa.ldp = V;
@@ -1913,12 +1918,13 @@ static int enqueue_spec_step_rejection(alm_spec* s) {
     da.u = s->uniforms;
     da.cursor = s->state + 4;
     da.u_offset = i;
-    da.out = d->ws.argmax;
+    da.out = d->ws.argmax + (rows - 1);
     ALM_CUDA(launch_draw(da, st));
     prof_mark(ALM_OP_SAMPLE, 1);
   }
   prof_role(0);
-  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
+  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos,
+                                   s->k == 1 ? r0 - 1 : 0, st));
   prof_mark(ALM_OP_SPEC_PREP, s->k + 1);
   prof_role(2);
   ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
@@ -1961,21 +1967,28 @@ static int enqueue_spec_step(alm_spec* s) {
   alm_model* t = s->target;
   cudaStream_t st = t->ctx->stream;
   const bool sampled = s->temperature > 0.f;
+  const int V = d->cfg.vocab;
+  const int r0 = s->refresh ? 2 : 1;   // rows of draft forward 0; its candidate is the last
   for (int i = 0; i < s->k; ++i) {
+    const int rows = i == 0 ? r0 : 1;
     prof_role(0);
-    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos, st));
+    ALM_CUDA(launch_spec_prep_draft(s->state, s->cand, d->ws.argmax, i, d->ws.tokens, d->ws.pos,
+                                    i == 1 ? r0 - 1 : 0, s->refresh ? 1 : 0, st));
     prof_mark(ALM_OP_SPEC_PREP, 1);
     prof_role(1);
-    ALM_TRY(enqueue_forward(d, s->dkv, 1, true, d->ctx->pdl));
-    // draft candidate i: the draft's sample, draw k-step offset i
+    ALM_TRY(enqueue_forward(d, s->dkv, rows, true, d->ctx->pdl));
+    // draft candidate i: the draft's sample of its last row, draw k-step offset i
     if (sampled) {
-      ALM_CUDA(launch_sample(sample_args(d, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, i), 1,
-                             false, st));
+      SampleArgs sa = sample_args(d, s->temperature, s->top_p, s->min_p, s->uniforms, s->state + 4, i);
+      sa.logits += static_cast<size_t>(rows - 1) * V;
+      sa.out += rows - 1;
+      ALM_CUDA(launch_sample(sa, 1, false, st));
       prof_mark(ALM_OP_SAMPLE, 1);
     }
   }
   prof_role(0);
-  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos, st));
+  ALM_CUDA(launch_spec_prep_verify(s->state, s->cand, d->ws.argmax, s->k, t->ws.tokens, t->ws.pos,
+                                   s->k == 1 ? r0 - 1 : 0, st));
   prof_mark(ALM_OP_SPEC_PREP, s->k + 1);
   prof_role(2);
   ALM_TRY(enqueue_forward(t, s->tkv, s->k + 1, true, t->ctx->pdl));
@@ -2086,10 +2099,22 @@ int alm_spec_destroy(alm_spec* s) {
   return ALM_OK;
 }
 
+int alm_spec_begin_prev(alm_spec* s, int32_t prev_token, int32_t token, int pos) {
+  ALM_REQ(s, "null spec");
+  ALM_REQ(prev_token >= 0 && prev_token < s->target->cfg.vocab, "token out of range");
+  ALM_REQ(pos >= 1, "the previous token needs pos >= 1");
+  DeviceGuard g(s->target->ctx->device);
+  s->pinned[4] = prev_token;
+  ALM_CUDA(cudaMemcpyAsync(s->state + 5, s->pinned + 4, sizeof(int), cudaMemcpyHostToDevice,
+                           s->target->ctx->stream));
+  return alm_spec_begin(s, token, pos);
+}
+
 int alm_spec_begin(alm_spec* s, int32_t token, int pos) {
   ALM_REQ(s, "null spec");
   ALM_REQ(token >= 0 && token < s->target->cfg.vocab, "token out of range");
   ALM_REQ(pos >= 0, "negative position");
+  ALM_REQ(pos >= 1 || !s->refresh, "the draft refresh needs pos >= 1");
   DeviceGuard g(s->target->ctx->device);
   s->pinned[0] = token;
   s->pinned[1] = pos;
@@ -2130,6 +2155,14 @@ int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min
   s->temperature = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
   s->top_p = top_p;
   s->min_p = min_p;
+  return capture_spec_graph(s);
+}
+
+int alm_spec_set_draft_refresh(alm_spec* s, int enable) {
+  ALM_REQ(s, "null spec");
+  DeviceGuard g(s->target->ctx->device);
+  ALM_CUDA(cudaStreamSynchronize(s->target->ctx->stream));
+  s->refresh = enable != 0;
   return capture_spec_graph(s);
 }
 

@@ -18,13 +18,17 @@ streaming was a phone's RAM; a B200 holds the model many times over):
   the K draft samples, then one per verified target row up to the first
   rejection; a plain step takes one draw.
 
-``seed`` (not in the reference, whose generator is unseeded) makes the
-stream reproducible.  ``accept_rule="rejection"`` (not in the reference)
-accepts sampled candidates by speculative rejection sampling instead: u <
-min(1, p/q), the residual max(0, p - q) resampled at the first rejection,
-2k + 1 draws per step (``alm_spec_set_rejection``).  Out of the path and not carried over: prompt-prefix KV
-reuse, layer skipping, throttling, grammar masking (grammar disables
-speculation in the reference too) and the tokenizer.
+The target's cache keeps the longest common prefix with the previous prompt
+(``engine.py:245-253``; ``ANDROIDLLM_PREFIX_KV=0`` turns it off, as in the
+reference).  Not in the reference: ``seed`` makes the draw stream
+reproducible (the reference's generator is unseeded); ``draft_refresh=True``
+has the draft forward the token before each step's position again, which
+repairs the draft's stale cache entry after a step that accepted every
+candidate; ``accept_rule="rejection"`` accepts sampled candidates by
+speculative rejection sampling (u < min(1, p/q), the residual max(0, p - q)
+resampled at the first rejection, 2k + 1 draws per step).  Out of the path
+and not carried over: layer skipping, throttling, grammar masking (grammar
+disables speculation in the reference too) and the tokenizer.
 """
 import os
 import time
@@ -41,10 +45,11 @@ PREFILL_ROWS = 16
 
 class LayerStreamingEngine:
     def __init__(self, model_dir, keep_layers=0, draft_dir=None, spec_k=0, device=0, seed=None,
-                 accept_rule="reference", _ctx=None):
+                 accept_rule="reference", draft_refresh=False, _ctx=None):
         if accept_rule not in ("reference", "rejection"):
             raise ValueError("accept_rule must be 'reference' or 'rejection'")
         self.accept_rule = accept_rule
+        self.draft_refresh = bool(draft_refresh)
         self.model_dir = model_dir
         self.manifest = load_manifest(model_dir)
         canon = self.manifest["config"]
@@ -76,6 +81,8 @@ class LayerStreamingEngine:
         self._kv = None
         self._spec = None
         self._kv_len = 0
+        self._kv_prompt_ids = None
+        self._prefix_kv = os.environ.get("ANDROIDLLM_PREFIX_KV", "1") not in ("0", "false", "")
 
     # -- caches --------------------------------------------------------------------
     def _kv_capacity(self):
@@ -96,7 +103,28 @@ class LayerStreamingEngine:
         if self._spec is None:
             self._spec = SpecDecoder(self.dm, self.draft.dm, self._target_kv().cache, self._draft_kv().cache,
                                      self.spec_k)
+        self._spec.set_draft_refresh(self.draft_refresh)
         return self._spec
+
+    def _match_prefix(self, ids):
+        """engine.py:245-253: common prefix length with the previous prompt."""
+        if not self._prefix_kv or self._kv is None or not self._kv_prompt_ids:
+            return 0
+        old = self._kv_prompt_ids
+        n = min(len(old), len(ids), self.ctx_len)
+        p = 0
+        while p < n and old[p] == ids[p]:
+            p += 1
+        return p
+
+    @staticmethod
+    def _begin(dec, prev, token, pos):
+        """Set the decoder's state: token at pos, and the token at pos - 1
+        (which the draft refresh forwards again) when there is one."""
+        if prev is None or pos < 1:
+            dec.begin(token, pos)
+        else:
+            dec.begin(token, pos, prev=int(prev))
 
     # -- reference-compatible pieces --------------------------------------------------
     def load_layer(self, i):
@@ -188,14 +216,26 @@ class LayerStreamingEngine:
         if not prompt_ids:
             raise ValueError("empty prompt")
         kv = self._target_kv()
-        kv.cache.zero()
+        # prompt-prefix reuse across calls (engine.py:245-253, 325-336): the
+        # target's cache keeps the positions of the longest common prefix
+        # with the previous prompt and prefill starts after it
+        pfx = self._match_prefix(prompt_ids)
+        if pfx > 1:
+            start = pfx
+            self.stats["prefix_calls"] += 1
+            self.stats["prefix_tokens"] += pfx
+        else:
+            kv.cache.zero()
+            start = 0
+        self._kv_prompt_ids = prompt_ids
         spec = self.draft is not None and self.spec_k > 0
         if spec:
             for k in ("draft_tokens", "spec_accepted", "spec_bonus", "spec_steps"):
                 self.stats.setdefault(k, 0)
         # prefill: kv[0..n-2] filled, token = id at position n-1 (engine.py:346-354)
         t_pre = time.perf_counter()
-        self._prefill(kv, prompt_ids[:-1], 0)
+        if start < len(prompt_ids) - 1:
+            self._prefill(kv, prompt_ids[start:-1], start)
         token = prompt_ids[-1]
         pos = len(prompt_ids) - 1
         if spec:
@@ -203,7 +243,9 @@ class LayerStreamingEngine:
             dkv.cache.zero()
             self.draft._prefill(dkv, prompt_ids, 0)
             dec = self._spec_decoder()
-            dec.begin(token, pos)
+        prev = prompt_ids[-2] if len(prompt_ids) >= 2 else None
+        if spec:
+            self._begin(dec, prev, token, pos)
         t_pre = time.perf_counter() - t_pre
         generated = []
         steps = 0
@@ -216,13 +258,14 @@ class LayerStreamingEngine:
                 # device, its emitted tokens come back (engine.py:369-387)
                 t0 = time.time()
                 self._feed_spec(dec, temperature, top_p, min_p)
-                dec.begin(token, pos)
+                self._begin(dec, prev, token, pos)
                 emitted, accepted = dec.run(1)
                 if temperature > 0:
                     self._u_used = dec.uniforms_used()
                 self._account(t0, self.spec_k + 1)
                 self.draft._account(t0, self.spec_k)
                 n_draft = accepted[0]
+                prev = emitted[-2] if len(emitted) >= 2 else token
                 token = emitted[-1]
                 pos += len(emitted)
                 steps += 1
@@ -278,7 +321,7 @@ class LayerStreamingEngine:
             "lru_layers": 0,
             "skip_every": 0,
             "ctx_len": self.ctx_len,
-            "prefix_kv": False,
+            "prefix_kv": self._prefix_kv,
             "prefix_calls": self.stats["prefix_calls"],
             "prefix_tokens": self.stats["prefix_tokens"],
             "context_used": self._kv_len,

@@ -490,8 +490,22 @@ class SpecDecoder:
         self._sampling = (0.0, 1.0, 0.0)
         self._uniforms = None
 
-    def begin(self, token, pos):
-        check(lib.alm_spec_begin(self.h, int(token), int(pos)))
+    def begin(self, token, pos, prev=None):
+        """Step state: `token` at position `pos` (and the token at pos - 1,
+        which the draft refresh forwards again)."""
+        if prev is None:
+            check(lib.alm_spec_begin(self.h, int(token), int(pos)))
+        else:
+            check(lib.alm_spec_begin_prev(self.h, int(prev), int(token), int(pos)))
+
+    def set_draft_refresh(self, enable):
+        """Re-forward the token at pos - 1 in every step's first draft
+        forward (fixes the draft's stale cache entry after an all-accept
+        step; off by default, the reference's behaviour)."""
+        enable = bool(enable)
+        if enable != getattr(self, "_refresh", False):
+            check(lib.alm_spec_set_draft_refresh(self.h, 1 if enable else 0))
+            self._refresh = enable
 
     def run(self, n_steps=1):
         """Run n_steps steps; returns (emitted tokens, accepted count per step)."""

@@ -287,6 +287,10 @@ ALM_API int alm_spec_begin(alm_spec* s, int32_t token, int pos);
  * of accepted draft tokens of each step.  The state advances. */
 ALM_API int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emitted_host,
                  int32_t* accepted_host);
+/* alm_spec_begin that also sets the token at pos - 1, which the draft
+ * refresh (alm_spec_set_draft_refresh) forwards again; steps keep it up to
+ * date themselves, and alm_spec_begin leaves the last step's value. */
+ALM_API int alm_spec_begin_prev(alm_spec* s, int32_t prev_token, int32_t token, int pos);
 /* Current (token, pos) state. */
 ALM_API int alm_spec_state(alm_spec* s, int32_t* token, int32_t* pos);
 /* Number of kernel nodes in one speculative step's CUDA graph. */
@@ -296,6 +300,16 @@ ALM_API int alm_spec_kernel_count(alm_spec* s, int32_t* n_kernels);
  * (alm_sample's rule), accepted while they agree.  temperature <= 0 restores
  * the greedy step.  Re-captures the step graph. */
 ALM_API int alm_spec_set_sampling(alm_spec* s, float temperature, float top_p, float min_p);
+/* Draft refresh (no reference counterpart; a fix of the reference's draft
+ * side, androidllm/engine.py:299-303 vs 318-320): after a step that accepts
+ * all k candidates the reference's draft never forwards the last one, so its
+ * cache holds a stale entry at that position.  With enable = 1 the first draft
+ * forward of every step runs two rows, the token at pos - 1 again and the
+ * state token, which rewrites that entry (or recomputes the same values when
+ * it was already right).  Emitted tokens do not change (the target verifies
+ * every candidate); acceptance can only rise.  Off by default (the reference's
+ * behaviour).  Needs pos >= 1.  Re-captures the step graph. */
+ALM_API int alm_spec_set_draft_refresh(alm_spec* s, int enable);
 /* Sampling steps with min(1, p/q) rejection sampling (enable = 1) instead
  * of the reference's rule (engine.py:306-320, the default): each draft
  * candidate is drawn from the draft's softmax(l / T) row (min-p filtered;
