@@ -14,13 +14,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   grid_dep_launch();
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
+// grid (16-dim slice, kv head, row group x span split)
+__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max, int n_split) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
-  attn_pv_pages(a, smem_raw);
+  const int grp = blockIdx.z / n_split, sp = blockIdx.z % n_split;
+  attn_pv_pages(a, smem_raw, sp);
   __syncthreads();
   grid_dep_wait();
-  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh);
+  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, grp, smem_raw, sh, sp, n_split);
 }
 
 }  // namespace
@@ -52,10 +54,11 @@ cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   prof_mark(3 /* ALM_OP_ATTN_SCORES */, a.M);
 
+  const int n_split = a.pv_part ? attn_pv_spans(a.max_ctx) : 1;
   cudaLaunchConfig_t c2 = c1;
-  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a));
+  c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a) * n_split);
   c2.dynamicSmemBytes = attn_pv_smem();
-  return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);
+  return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max, n_split);
 }
 
 }  // namespace alm

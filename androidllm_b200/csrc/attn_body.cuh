@@ -31,7 +31,6 @@ namespace alm {
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / kWarp;
-constexpr int kPvRows = 4;   // query rows per P.V block
 constexpr int kPvVld = 24;   // V slice row stride (halves): conflict-free
 constexpr int kPvPld = kPvSpan + 8;   // P row stride (halves)
 // one load phase per span: V vectors and score float4s within one pass of the block
@@ -261,15 +260,23 @@ ALM_DEV int* attn_pv_pg(unsigned char* smem_raw) {
                                 static_cast<size_t>(kPvRows) * kPvPld * sizeof(half) +
                                 static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float));
 }
-// Page numbers of the first span of positions a P.V block may read (before
-// the block waits for the scores pass; the caller synchronises the block).
-ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw) {
-  stage_pages(a, 0, min(kPvSpan, a.max_ctx), attn_pv_pg(smem_raw));
+// Page numbers of span sp of positions a P.V block may read (before the
+// block waits for the scores pass; the caller synchronises the block).
+ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 0) {
+  const int b = sp * kPvSpan;
+  if (b < a.max_ctx) stage_pages(a, b, min(b + kPvSpan, a.max_ctx), attn_pv_pg(smem_raw));
 }
 
-// Precondition: attn_pv_pages, then a block barrier.
+// Span split of the standalone kernel: block sp of n_split takes span sp
+// when the pass's context needs more than one span; its fp32 partial goes to
+// a.pv_part and the last block of the (slice, kv head, group) to finish adds
+// the partials in span order.  A context of one span takes the unsplit path
+// in block 0 (the other blocks return), so results do not depend on n_split.
+// Rows whose context ends before a span get exact zeros from it, so every
+// row's sum equals the one its own context length gives.
+// Precondition: attn_pv_pages(sp), then a block barrier.
 ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, int grp, unsigned char* smem_raw,
-                          AttnShared& sh) {
+                          AttnShared& sh, int sp = 0, int n_split = 1) {
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
   half* ps = vs + kPvSpan * kPvVld;                  // [kPvRows][kPvPld]
   float* s_acc = reinterpret_cast<float*>(ps + kPvRows * kPvPld);   // [kAttnWarps][kWarp][8]
@@ -284,6 +291,12 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
   const int r0 = grp * kPvRows;                      // first query row of this block
   if (r0 >= n_rows) return;
+  const int needed = (n_ctx + kPvSpan - 1) / kPvSpan;
+  const bool split = a.pv_part != nullptr && n_split > 1 && needed > 1;
+  if (!split && sp > 0) return;
+  if (split && sp >= needed) return;
+  const int span_begin = split ? sp * kPvSpan : 0;
+  const int span_end = split ? min(span_begin + kPvSpan, n_ctx) : n_ctx;
   const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
@@ -331,7 +344,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       lc0[j] = f.y;
     }
   }
-  load_span(0, (min(kPvSpan, n_ctx) + 15) & ~15);
+  load_span(span_begin, (min(kPvSpan, span_end - span_begin) + 15) & ~15);
 
   // row max / sum from the chunk statistics: one warp per row, lane l takes
   // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
@@ -379,10 +392,10 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
 
   const int g = lane >> 2, t = lane & 3;
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for (int base = 0; base < n_ctx; base += kPvSpan) {
-    const int span = min(kPvSpan, n_ctx - base);
+  for (int base = span_begin; base < span_end; base += kPvSpan) {
+    const int span = min(kPvSpan, span_end - base);
     const int span_pad = (span + 15) & ~15;
-    if (base > 0) {   // the first span was loaded with the statistics
+    if (base > span_begin) {   // the first span was loaded with the statistics
       stage_pages(a, base, base + span, s_pg);
       body_sync();
       load_span(base, span_pad);
@@ -434,6 +447,9 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     for (int e = 0; e < 4; ++e) s_acc[(warp * kWarp + lane) * 8 + nt * 4 + e] = acc[nt][e];
   body_sync();
   grid_dep_launch();
+  const int n_pg = attn_pv_groups(a), nds = hd / 16;
+  const size_t key = (static_cast<size_t>(kvh) * nds + ds) * n_pg + grp;   // (kv head, slice, group)
+  float* part = split ? a.pv_part + (key * n_split + sp) * (kPvRows * 16) : nullptr;
   if (warp == 0 && g < kPvRows) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
@@ -441,13 +457,39 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       for (int e = 0; e < 2; ++e) {       // rows g only (d2, d3 belong to zero rows g+8)
         float v = s_acc[lane * 8 + nt * 4 + e];
         for (int w2 = 1; w2 < kAttnWarps; ++w2) v = fadd(v, s_acc[(w2 * kWarp + lane) * 8 + nt * 4 + e]);
+        const int dl = nt * 8 + 2 * t + e;
+        if (split) {
+          part[g * 16 + dl] = v;
+          continue;
+        }
         const int r = r0 + g;
         if (r < n_rows) {
           const int m = r / gq, head = kvh * gq + r % gq;
-          const int d = ds * 16 + nt * 8 + 2 * t + e;
-          a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + d] = __float2half_rn(v);
+          a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + ds * 16 + dl] = __float2half_rn(v);
         }
       }
+  }
+  if (split) {
+    // the last block of this (slice, kv head, group) adds the spans in order
+    __threadfence();
+    body_sync();
+    if (tid == 0) sh.pm[0] = __int_as_float(atomicAdd(&a.pv_ticket[key], 1u) == static_cast<unsigned>(needed - 1));
+    body_sync();
+    if (__float_as_int(sh.pm[0]) != 0) {
+      __threadfence();
+      if (tid < kPvRows * 16) {
+        const int rl = tid / 16, dl = tid % 16;
+        const float* base = a.pv_part + key * n_split * (kPvRows * 16) + tid;
+        float v = __ldcg(base);
+        for (int s2 = 1; s2 < needed; ++s2) v = fadd(v, __ldcg(base + static_cast<size_t>(s2) * (kPvRows * 16)));
+        const int r = r0 + rl;
+        if (r < n_rows) {
+          const int m = r / gq, head = kvh * gq + r % gq;
+          a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + ds * 16 + dl] = __float2half_rn(v);
+        }
+      }
+      if (tid == 0) atomicExch(&a.pv_ticket[key], 0u);
+    }
   }
   body_sync();   // shared memory is reused by the caller's next block
 }

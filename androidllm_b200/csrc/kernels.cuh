@@ -13,6 +13,8 @@ constexpr int kAttnChunk = 64;
 constexpr int kAttnRows = 16;
 // Superchunk of positions the P.V kernel stages in shared memory at once.
 constexpr int kPvSpan = 1024;
+// Query rows per P.V block.
+constexpr int kPvRows = 4;
 
 // ---------------------------------------------------------------------------
 // Tiled quantized weight ("qtile" layout).
@@ -181,7 +183,14 @@ struct AttnArgs {
   float* stats = nullptr;    // (kv_heads, n_rg, n_chunks_max, 16, 2)
   half* ctx = nullptr;       // (M, heads * head_dim)
   int ldc = 0;
+  // P.V split over spans of kPvSpan positions (standalone kernels; null: one
+  // block walks every span): fp32 partials of (slice, kv head, row group)
+  // per span, and a self-resetting ticket per (slice, kv head, row group)
+  float* pv_part = nullptr;
+  unsigned* pv_ticket = nullptr;
 };
+// Spans of kPvSpan positions a context of max_ctx positions holds.
+__host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSpan - 1) / kPvSpan; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
 
 // ---- speculative rejection sampling (accept.cu) ----------------------------

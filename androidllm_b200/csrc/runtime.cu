@@ -198,6 +198,8 @@ struct Work {
   float* sample_scratch = nullptr;   // kMaxRows * vocab fp32 for the sampler
   float* scores = nullptr;
   float* stats = nullptr;
+  float* pv_part = nullptr;      // P.V span partials (contexts of several spans)
+  unsigned* pv_ticket = nullptr;
   // tensor parallelism
   float* o32 = nullptr;        // (kMaxRows, hidden) fp32 partials of the row-split projections
   int* tp_pairs = nullptr;     // (kMaxRows, 2) local argmax, then (world, kMaxRows, 2) gathered
@@ -477,13 +479,23 @@ int ensure_attn(alm_model* m, int max_ctx) {
   const int cap = (max_ctx + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
   dev_free(ws.scores);
   dev_free(ws.stats);
+  dev_free(ws.pv_part);
+  dev_free(ws.pv_ticket);
   ws.scores = nullptr;
   ws.stats = nullptr;
+  ws.pv_part = nullptr;
+  ws.pv_ticket = nullptr;
   ws.attn_ctx = 0;
   // rows padded by one chunk: the P.V kernel reads whole 16-position groups
   const int ld = cap + kAttnChunk;
   ALM_TRY(dev_alloc_t(&ws.scores, static_cast<size_t>(m->cfg.kv_heads) * n_rg * kAttnRows * ld));
   ALM_TRY(dev_alloc_t(&ws.stats, static_cast<size_t>(m->cfg.kv_heads) * n_rg * (cap / kAttnChunk) * kAttnRows * 2));
+  // P.V span split: (kv head, slice, group) keys x spans x kPvRows x 16 partials
+  const size_t keys = static_cast<size_t>(m->cfg.kv_heads) * (m->cfg.head_dim / 16) *
+                      ((kMaxRows * gq + kPvRows - 1) / kPvRows);
+  ALM_TRY(dev_alloc_t(&ws.pv_part, keys * attn_pv_spans(cap) * kPvRows * 16));
+  ALM_TRY(dev_alloc_t(&ws.pv_ticket, keys));
+  ALM_CUDA(cudaMemset(ws.pv_ticket, 0, keys * sizeof(unsigned)));
   ws.attn_ctx = cap;
   ws.score_ld = ld;
   return ALM_OK;
@@ -614,6 +626,8 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.stats = ws.stats;
   a.ctx = ws.ctx;
   a.ldc = qdim;
+  a.pv_part = ws.pv_part;
+  a.pv_ticket = ws.pv_ticket;
   ALM_LAUNCH(launch_attention(a, pdl, st));
   prof_mark(ALM_OP_ATTN_PV, M);
 
@@ -1288,7 +1302,8 @@ int alm_model_destroy(alm_model* m) {
   for (void* p : {(void*)w.tokens, (void*)w.pos, (void*)w.err, (void*)w.x0, (void*)w.s1, (void*)w.s2,
                   (void*)w.ss1, (void*)w.ss2, (void*)w.q, (void*)w.ctx, (void*)w.h, (void*)w.xn, (void*)w.xout,
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
-                  (void*)w.scores, (void*)w.stats, (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
+                  (void*)w.scores, (void*)w.stats, (void*)w.pv_part, (void*)w.pv_ticket,
+                  (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
                   (void*)w.logits_local, (void*)w.logits_gather})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
