@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
   const int grp = blockIdx.z / n_split, sp = blockIdx.z % n_split;
-  attn_pv_pages(a, smem_raw, sp);
+  attn_pv_pages(a, smem_raw, sp, n_split);
   __syncthreads();
   grid_dep_wait();
   attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, grp, smem_raw, sh, sp, n_split);

@@ -260,15 +260,18 @@ ALM_DEV int* attn_pv_pg(unsigned char* smem_raw) {
                                 static_cast<size_t>(kPvRows) * kPvPld * sizeof(half) +
                                 static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float));
 }
-// Page numbers of span sp of positions a P.V block may read (before the
-// block waits for the scores pass; the caller synchronises the block).
-ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 0) {
-  const int b = sp * kPvSpan;
-  if (b < a.max_ctx) stage_pages(a, b, min(b + kPvSpan, a.max_ctx), attn_pv_pg(smem_raw));
+// Page numbers of the first positions a P.V block may read: split span sp
+// (n_split > 1), else the first kPvSpan positions (before the block waits
+// for the scores pass; the caller synchronises the block).
+ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 0, int n_split = 1) {
+  const int b = n_split > 1 ? sp * kPvSplit : 0;
+  const int e = n_split > 1 ? b + kPvSplit : kPvSpan;
+  if (b < a.max_ctx) stage_pages(a, b, min(e, a.max_ctx), attn_pv_pg(smem_raw));
 }
 
-// Span split of the standalone kernel: block sp of n_split takes span sp
-// when the pass's context needs more than one span; its fp32 partial goes to
+// Span split of the standalone kernel: block sp of n_split takes positions
+// [sp * kPvSplit, (sp + 1) * kPvSplit) when the pass's context is longer than
+// one such span (else block 0 walks every position); its fp32 partial goes to
 // a.pv_part and the last block of the (slice, kv head, group) to finish adds
 // the partials in span order.  A context of one span takes the unsplit path
 // in block 0 (the other blocks return), so results do not depend on n_split.
@@ -291,12 +294,12 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
   const int r0 = grp * kPvRows;                      // first query row of this block
   if (r0 >= n_rows) return;
-  const int needed = (n_ctx + kPvSpan - 1) / kPvSpan;
+  const int needed = (n_ctx + kPvSplit - 1) / kPvSplit;
   const bool split = a.pv_part != nullptr && n_split > 1 && needed > 1;
   if (!split && sp > 0) return;
   if (split && sp >= needed) return;
-  const int span_begin = split ? sp * kPvSpan : 0;
-  const int span_end = split ? min(span_begin + kPvSpan, n_ctx) : n_ctx;
+  const int span_begin = split ? sp * kPvSplit : 0;
+  const int span_end = split ? min(span_begin + kPvSplit, n_ctx) : n_ctx;
   const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;

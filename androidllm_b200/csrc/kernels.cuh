@@ -183,14 +183,16 @@ struct AttnArgs {
   float* stats = nullptr;    // (kv_heads, n_rg, n_chunks_max, 16, 2)
   half* ctx = nullptr;       // (M, heads * head_dim)
   int ldc = 0;
-  // P.V split over spans of kPvSpan positions (standalone kernels; null: one
-  // block walks every span): fp32 partials of (slice, kv head, row group)
-  // per span, and a self-resetting ticket per (slice, kv head, row group)
+  // P.V split over spans of kPvSplit positions (standalone kernels; null: one
+  // block walks every position): fp32 partials of (slice, kv head, row
+  // group) per span, and a self-resetting ticket per (slice, kv head, group)
   float* pv_part = nullptr;
   unsigned* pv_ticket = nullptr;
 };
-// Spans of kPvSpan positions a context of max_ctx positions holds.
-__host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSpan - 1) / kPvSpan; }
+// Positions one block of the split P.V pass takes (a context longer than one
+// split span is spread over blocks), and the split spans of max_ctx positions.
+constexpr int kPvSplit = 256;
+__host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSplit - 1) / kPvSplit; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
 
 // ---- speculative rejection sampling (accept.cu) ----------------------------
