@@ -191,7 +191,10 @@ struct AttnArgs {
 };
 // Positions one block of the split P.V pass takes (a context longer than one
 // split span is spread over blocks), and the split spans of max_ctx positions.
-constexpr int kPvSplit = 256;
+// Measured on B200: splitting at 256 positions made 512-768-position
+// contexts slower (more blocks plus the combine), at 1024 it pays from two
+// spans on.
+constexpr int kPvSplit = kPvSpan;
 __host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSplit - 1) / kPvSplit; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
 
