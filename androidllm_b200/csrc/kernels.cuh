@@ -197,6 +197,11 @@ struct AttnArgs {
 constexpr int kPvSplit = kPvSpan;
 __host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSplit - 1) / kPvSplit; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
+// Single-row decode attention in one kernel (attn_decode.cu), bit-identical
+// to launch_attention; attn_decode_ok says whether it takes the shape.
+bool attn_decode_ok(const AttnArgs& a);
+cudaError_t launch_attn_decode(const AttnArgs& a, bool pdl, cudaStream_t st);
+cudaError_t attn_decode_init_attrs();
 
 // ---- speculative rejection sampling (accept.cu) ----------------------------
 constexpr int kAccMaxChunks = 4096;   // rows of up to 4096 * 256 entries

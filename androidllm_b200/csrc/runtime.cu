@@ -149,6 +149,7 @@ struct alm_ctx {
   bool pdl = true;       // programmatic dependent launch between forward kernels
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
   bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
+  bool attn_decode = true;  // single-row attention as one kernel (ALM_ATTN_DECODE=0: two passes)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
   // tensor parallelism: NCCL communicator of this rank (alm_ctx_init_tp)
   void* tp_comm = nullptr;
@@ -628,8 +629,14 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.ldc = qdim;
   a.pv_part = ws.pv_part;
   a.pv_ticket = ws.pv_ticket;
-  ALM_LAUNCH(launch_attention(a, pdl, st));
-  prof_mark(ALM_OP_ATTN_PV, M);
+  if (m->ctx->attn_decode && attn_decode_ok(a)) {
+    // single-row decode: scores, statistics and P.V in one kernel (bit-identical)
+    ALM_LAUNCH(launch_attn_decode(a, pdl, st));
+    prof_mark(ALM_OP_ATTN, M);
+  } else {
+    ALM_LAUNCH(launch_attention(a, pdl, st));
+    prof_mark(ALM_OP_ATTN_PV, M);
+  }
 
   if (m->tp) {
     // row-split O: fp32 partials, sum over ranks, then residual and norm partials
@@ -1012,6 +1019,7 @@ int alm_ctx_create(int device, alm_ctx** out) {
   {
     cudaError_t e = gemv_init_attrs();
     if (e == cudaSuccess) e = attention_init_attrs();
+    if (e == cudaSuccess) e = attn_decode_init_attrs();
     if (e == cudaSuccess) e = rows_init_attrs();
     if (e == cudaSuccess) e = sample_init_attrs();
     if (e != cudaSuccess) return fail(ALM_ERR_CUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
@@ -1024,6 +1032,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
     c->pdl = !(e && e[0] == '1');
     const char* e2 = getenv("ALM_PERSIST");
     c->persist = e2 && e2[0] == '1';
+    const char* e5 = getenv("ALM_ATTN_DECODE");
+    c->attn_decode = !(e5 && e5[0] == '0');
     const char* e4 = getenv("ALM_CLUSTER");
     c->cluster = e4 && e4[0] == '1';
     const char* e3 = getenv("ALM_TC");

@@ -14,7 +14,7 @@ from ._lib import ModelConfig, ProjSrc, check, lib, ptr
 PROJ_BASES = ("q", "k", "v", "o", "gate", "up", "down")   # androidllm/shard.py:111
 # ALM_OP_* codes of include/androidllm_b200.h, in order
 OP_NAMES = ("begin", "embed", "qkv", "attn_scores", "attn_pv", "o", "gate_up", "down", "final_norm", "head",
-            "argmax", "spec_prep", "spec_accept", "sample", "layers")
+            "argmax", "spec_prep", "spec_accept", "sample", "layers", "attn")
 
 # At interpreter exit the order of finalizers is arbitrary (a context could go
 # before the models on it); the process teardown frees device memory anyway.
