@@ -14,11 +14,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   grid_dep_launch();
 }
 
-// grid (16-dim slice, kv head, row group x span split)
+// grid (16-dim slice, kv head, span x row group): the blocks of span 0 come
+// first, so the ones a shorter context leaves idle are scheduled last
 __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max, int n_split) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
-  const int grp = blockIdx.z / n_split, sp = blockIdx.z % n_split;
+  const int n_pg = gridDim.z / n_split;
+  const int grp = blockIdx.z % n_pg, sp = blockIdx.z / n_pg;
   attn_pv_pages(a, smem_raw, sp, n_split);
   __syncthreads();
   grid_dep_wait();

@@ -1,8 +1,11 @@
 // Single-row decode attention in one kernel: one block per kv head computes
 // the scores of its query heads over the whole context, the softmax
-// statistics and P.V, so a decode step (every draft forward, plain decoding)
-// launches one attention kernel instead of two and keeps the statistics in
-// shared memory.
+// statistics and P.V, so a decode step launches one attention kernel instead
+// of two and keeps the statistics in shared memory.  Opt-in
+// (ALM_ATTN_DECODE=1): measured on B200 at the Qwen2.5-0.5B draft shape
+// (2 kv heads, 640 positions) one launch takes 39.7 us against about 20 us
+// for the two passes, because two blocks walk the context tile by tile at L2
+// latency.
 //
 // Every value is computed with the arithmetic of the two-pass kernels
 // (attn_body.cuh), so the results are bit-identical to them and a decode row

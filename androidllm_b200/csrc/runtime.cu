@@ -149,7 +149,7 @@ struct alm_ctx {
   bool pdl = true;       // programmatic dependent launch between forward kernels
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
   bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
-  bool attn_decode = true;  // single-row attention as one kernel (ALM_ATTN_DECODE=0: two passes)
+  bool attn_decode = false;  // single-row attention as one kernel (opt-in: ALM_ATTN_DECODE=1)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
   // tensor parallelism: NCCL communicator of this rank (alm_ctx_init_tp)
   void* tp_comm = nullptr;
@@ -1033,7 +1033,7 @@ int alm_ctx_create(int device, alm_ctx** out) {
     const char* e2 = getenv("ALM_PERSIST");
     c->persist = e2 && e2[0] == '1';
     const char* e5 = getenv("ALM_ATTN_DECODE");
-    c->attn_decode = !(e5 && e5[0] == '0');
+    c->attn_decode = e5 && e5[0] == '1';
     const char* e4 = getenv("ALM_CLUSTER");
     c->cluster = e4 && e4[0] == '1';
     const char* e3 = getenv("ALM_TC");

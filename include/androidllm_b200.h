@@ -342,7 +342,7 @@ enum {
   ALM_OP_O = 5, ALM_OP_GATE_UP = 6, ALM_OP_DOWN = 7, ALM_OP_FINAL_NORM = 8, ALM_OP_HEAD = 9,
   ALM_OP_ARGMAX = 10, ALM_OP_SPEC_PREP = 11, ALM_OP_SPEC_ACCEPT = 12, ALM_OP_SAMPLE = 13,
   ALM_OP_LAYERS = 14,  /* embedding and every layer as one cluster kernel */
-  ALM_OP_ATTN = 15     /* single-row attention as one kernel */
+  ALM_OP_ATTN = 15     /* single-row attention as one kernel (opt-in: ALM_ATTN_DECODE=1) */
 };
 /* Device time of every kernel launch of one speculative step (profiling; no
  * counterpart in the reference).  The step is captured once more with a
