@@ -14,17 +14,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   grid_dep_launch();
 }
 
-// grid (16-dim slice, kv head, span x row group): the blocks of span 0 come
-// first, so the ones a shorter context leaves idle are scheduled last
-__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max, int n_split) {
+// One span: grid (16-dim slice, kv head, row group).
+__global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n_chunks_max) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ AttnShared sh;
+  attn_pv_pages(a, smem_raw);
+  __syncthreads();
+  grid_dep_wait();
+  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh);
+}
+
+// Span split (KV capacity above one span): grid (16-dim slice, kv head,
+// span x row group) with the blocks of span 0 first.  Span 0 stages its
+// page numbers before the wait for the scores pass; a later span's block
+// first learns the context length and returns at once when it is not needed.
+__global__ void __launch_bounds__(kAttnThreads) attn_pv_split_kernel(AttnArgs a, int n_chunks_max, int n_split) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ AttnShared sh;
   const int n_pg = gridDim.z / n_split;
   const int grp = blockIdx.z % n_pg, sp = blockIdx.z / n_pg;
-  attn_pv_pages(a, smem_raw, sp, n_split);
+  if (sp == 0) attn_pv_pages(a, smem_raw, 0, n_split);
   __syncthreads();
   grid_dep_wait();
-  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, grp, smem_raw, sh, sp, n_split);
+  if (sp > 0) {
+    if (sp * kPvSplit >= *a.pos + a.M) return;
+    attn_pv_pages(a, smem_raw, sp, n_split);
+    __syncthreads();
+  }
+  attn_pv_body<false, true>(a, n_chunks_max, blockIdx.x, blockIdx.y, grp, smem_raw, sh, sp, n_split);
 }
 
 }  // namespace
@@ -33,7 +50,10 @@ cudaError_t attention_init_attrs() {
   cudaError_t e = cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(attn_scores_smem(256)));
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attn_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(attn_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(attn_pv_smem()));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attn_pv_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(attn_pv_smem()));
 }
 
@@ -60,7 +80,8 @@ cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
   cudaLaunchConfig_t c2 = c1;
   c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a) * n_split);
   c2.dynamicSmemBytes = attn_pv_smem();
-  return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max, n_split);
+  if (n_split == 1) return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);
+  return cudaLaunchKernelEx(&c2, attn_pv_split_kernel, a, n_chunks_max, n_split);
 }
 
 }  // namespace alm

@@ -101,6 +101,7 @@ ALM_DEV void attn_scores_pages(const AttnArgs& a, int chunk, unsigned char* smem
 
 // Scores of (chunk, kv head, row group); n_chunks_max = the grid's chunk count.
 // Precondition: attn_scores_pages for this chunk, then a block barrier.
+template <bool NAMED = false>
 ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, int kvh, int rg, int n_chunks_max,
                               unsigned char* smem_raw, AttnShared& sh) {
   const int hd = a.head_dim, ld = hd + 8;
@@ -164,7 +165,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
     if (i >= nv) break;
     *reinterpret_cast<uint4*>(ks + (i / vec_per_row) * ld + (i % vec_per_row) * 8) = kv8[j];
   }
-  body_sync();
+  body_sync_t<NAMED>();
 
   // warps 0-3: positions c0 + 16 w .. c0 + 16 w + 15 (two n8 tiles); all
   // warps take part in the staging above and in the block barriers below
@@ -213,13 +214,13 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       if (t == 0) sh.red[warp][g + 8 * h] = rmax[h];
     }
   }
-  body_sync();
+  body_sync_t<NAMED>();
   if (tid < kAttnRows) {
     float mx = kNegInf;
     for (int w2 = 0; w2 < kScoreWarps; ++w2) mx = fmaxf(mx, sh.red[w2][tid]);
     sh.mx[tid] = mx;
   }
-  body_sync();
+  body_sync_t<NAMED>();
   float rsum[2] = {0.f, 0.f};
   if (mw) {
 #pragma unroll
@@ -231,7 +232,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
         rsum[e >> 1] = fadd(rsum[e >> 1], ex);
       }
   }
-  body_sync();
+  body_sync_t<NAMED>();
   if (mw) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -240,7 +241,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       if (t == 0) sh.red[warp][g + 8 * h] = rsum[h];
     }
   }
-  body_sync();
+  body_sync_t<NAMED>();
   if (tid < kAttnRows) {
     float l = 0.f;
     for (int w2 = 0; w2 < kScoreWarps; ++w2) l = fadd(l, sh.red[w2][tid]);
@@ -248,7 +249,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
     st[0] = sh.mx[tid];
     st[1] = l;
   }
-  body_sync();   // shared memory is reused by the caller's next block
+  body_sync_t<NAMED>();   // shared memory is reused by the caller's next block
 }
 
 // P.V for (16-dim slice, kv head, group of kPvRows query rows).  Few rows
@@ -277,7 +278,10 @@ ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 
 // in block 0 (the other blocks return), so results do not depend on n_split.
 // Rows whose context ends before a span get exact zeros from it, so every
 // row's sum equals the one its own context length gives.
+// Without SPLIT the body is compiled for one span (sp = 0, n_split = 1):
+// the split's bookkeeping costs a short context about a microsecond.
 // Precondition: attn_pv_pages(sp), then a block barrier.
+template <bool NAMED = false, bool SPLIT = false>
 ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, int grp, unsigned char* smem_raw,
                           AttnShared& sh, int sp = 0, int n_split = 1) {
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
@@ -295,7 +299,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int r0 = grp * kPvRows;                      // first query row of this block
   if (r0 >= n_rows) return;
   const int needed = (n_ctx + kPvSplit - 1) / kPvSplit;
-  const bool split = a.pv_part != nullptr && n_split > 1 && needed > 1;
+  const bool split = SPLIT && a.pv_part != nullptr && n_split > 1 && needed > 1;
   if (!split && sp > 0) return;
   if (split && sp >= needed) return;
   const int span_begin = split ? sp * kPvSplit : 0;
@@ -391,7 +395,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       sh.pl[warp] = l;
     }
   }
-  body_sync();
+  body_sync_t<NAMED>();
 
   const int g = lane >> 2, t = lane & 3;
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -400,7 +404,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     const int span_pad = (span + 15) & ~15;
     if (base > span_begin) {   // the first span was loaded with the statistics
       stage_pages(a, base, base + span, s_pg);
-      body_sync();
+      body_sync_t<NAMED>();
       load_span(base, span_pad);
     }
     const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
@@ -425,7 +429,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
         ps[i_row * kPvPld + pl + e] = __float2half_rn(pv);
       }
     }
-    body_sync();
+    body_sync_t<NAMED>();
     for (int kk = warp; kk < span_pad / 16; kk += kAttnWarps) {
       // A: rows g < kPvRows hold P, rows g+8 and g >= kPvRows are zero
       uint32_t a0 = 0, a2 = 0;
@@ -441,14 +445,14 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       mma16816(acc[0], a0, 0u, a2, 0u, b0, b1);
       mma16816(acc[1], a0, 0u, a2, 0u, b2, b3);
     }
-    body_sync();
+    body_sync_t<NAMED>();
   }
 
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) s_acc[(warp * kWarp + lane) * 8 + nt * 4 + e] = acc[nt][e];
-  body_sync();
+  body_sync_t<NAMED>();
   grid_dep_launch();
   const int n_pg = attn_pv_groups(a), nds = hd / 16;
   const size_t key = (static_cast<size_t>(kvh) * nds + ds) * n_pg + grp;   // (kv head, slice, group)
@@ -475,9 +479,9 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   if (split) {
     // the last block of this (slice, kv head, group) adds the spans in order
     __threadfence();
-    body_sync();
+    body_sync_t<NAMED>();
     if (tid == 0) sh.pm[0] = __int_as_float(atomicAdd(&a.pv_ticket[key], 1u) == static_cast<unsigned>(needed - 1));
-    body_sync();
+    body_sync_t<NAMED>();
     if (__float_as_int(sh.pm[0]) != 0) {
       __threadfence();
       if (tid < kPvRows * 16) {
@@ -494,7 +498,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       if (tid == 0) atomicExch(&a.pv_ticket[key], 0u);
     }
   }
-  body_sync();   // shared memory is reused by the caller's next block
+  body_sync_t<NAMED>();   // shared memory is reused by the caller's next block
 }
 
 }  // namespace alm

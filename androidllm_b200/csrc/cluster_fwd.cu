@@ -545,8 +545,8 @@ ALM_DEV void cf_layer(const FwdParams& P, int li, uint32_t& cbase, uint32_t& n_s
     for (int vb = cta; vb < nvb1; vb += kCfCtas) {
       attn_scores_pages(a, vb % n_chunks, work);
       cons_sync();
-      attn_scores_body(a, P.sqrt_hd, vb % n_chunks, (vb / n_chunks) % kvh, vb / (n_chunks * kvh), ncm, work,
-                       s_cf.attn);
+      attn_scores_body<kCfThreads != 256>(a, P.sqrt_hd, vb % n_chunks, (vb / n_chunks) % kvh,
+                                          vb / (n_chunks * kvh), ncm, work, s_cf.attn);
     }
     if (threadIdx.x == 0) cf_mark(P, 7);
     cf_sync(n_sync, P);
@@ -555,7 +555,8 @@ ALM_DEV void cf_layer(const FwdParams& P, int li, uint32_t& cbase, uint32_t& n_s
     for (int vb = cta; vb < nvb2; vb += kCfCtas) {
       attn_pv_pages(a, work);
       cons_sync();
-      attn_pv_body(a, ncm, vb % nds, (vb / nds) % kvh, vb / (nds * kvh), work, s_cf.attn);
+      attn_pv_body<kCfThreads != 256>(a, ncm, vb % nds, (vb / nds) % kvh, vb / (nds * kvh), work,
+                                      s_cf.attn);
     }
     if (threadIdx.x == 0) cf_mark(P, 8);
     cf_sync(n_sync, P);

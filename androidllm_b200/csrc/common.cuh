@@ -116,6 +116,17 @@ ALM_DEV void body_sync() {
   }
 }
 
+// body_sync with the barrier chosen at compile time (NAMED: named barrier 1
+// over warps 0-7; else the whole block), for bodies on the hot path.
+template <bool NAMED>
+ALM_DEV void body_sync_t() {
+  if constexpr (NAMED) {
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  } else {
+    __syncthreads();
+  }
+}
+
 // Argmax order: larger value first, then the smaller index.
 ALM_DEV bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 == v2 && i1 < i2); }
 

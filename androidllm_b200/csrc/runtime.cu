@@ -265,6 +265,10 @@ struct alm_model {
   bool tp = false;
   int vocab_offset = 0, vocab_local = 0;
   bool tp_need_logits = false;   // gather the full logits after the head
+  // attention passes enqueued now are known to fit one P.V span: launch the
+  // unsplit P.V kernel even when the KV capacity is longer (speed only: the
+  // unsplit kernel walks any context length)
+  bool pv_one_span = false;
 };
 
 struct alm_kv {
@@ -288,6 +292,9 @@ struct alm_spec {
   int* out_acc = nullptr;
   int cap_steps = 0, cap_tokens = 0;
   cudaGraphExec_t graph = nullptr;
+  // the same step with the unsplit P.V kernel, replayed while every pass
+  // fits one P.V span (null when neither KV cache is longer than a span)
+  cudaGraphExec_t graph_short = nullptr;
   int* pinned = nullptr;     // host: 4 + cap_tokens + cap_steps
   int n_kernels = 0;         // kernel nodes in the step graph
   // sampling at temperature > 0 (engine.py:26-45 per draft and target row)
@@ -382,6 +389,15 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src,
     n_counters = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
   }
   const std::vector<int> dst_map = map_of(t.layout);
+  // every destination row must name an existing source row: the repack
+  // kernels index the sources with these entries unchecked
+  ALM_REQ(dst_map.size() >= static_cast<size_t>(rows ? t.n_rb * kRowBlock : t.n_tiles * 16),
+          "row map shorter than the layout");
+  for (const int d : dst_map) {
+    if (d < 0) continue;
+    const int si = d >> 24, r = d & 0xffffff;
+    ALM_REQ(si < n_src && r < srcs[si].out, "row map names a source row that does not exist");
+  }
   std::vector<void*> tmp;
   auto cleanup = [&]() {
     for (void* p : tmp) cudaFree(p);
@@ -627,7 +643,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.stats = ws.stats;
   a.ctx = ws.ctx;
   a.ldc = qdim;
-  a.pv_part = ws.pv_part;
+  a.pv_part = m->pv_one_span ? nullptr : ws.pv_part;
   a.pv_ticket = ws.pv_ticket;
   if (m->ctx->attn_decode && attn_decode_ok(a)) {
     // single-row decode: scores, statistics and P.V in one kernel (bit-identical)
@@ -1365,10 +1381,21 @@ int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint1
     return mp;
   };
   alm_qweight *qkv = nullptr, *o = nullptr, *gu = nullptr, *dn = nullptr;
+  const char* part = "qkv";
   int rc = build_qweight(m->ctx, &p[0], 3, [&qkv_map](int) { return qkv_map; }, qd + 2 * kd, false, &qkv);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, true, &o);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[4], 2, gu_map, 2 * c.intermediate, true, &gu);
-  if (rc == ALM_OK) rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, true, &dn);
+  if (rc == ALM_OK) {
+    part = "o";
+    rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, true, &o);
+  }
+  if (rc == ALM_OK) {
+    part = "gate/up";
+    rc = build_qweight(m->ctx, &p[4], 2, gu_map, 2 * c.intermediate, true, &gu);
+  }
+  if (rc == ALM_OK) {
+    part = "down";
+    rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, true, &dn);
+  }
+  if (rc != ALM_OK) g_err = "layer " + std::to_string(li) + " " + part + ": " + g_err;
   half *nin = nullptr, *npost = nullptr;
   if (rc == ALM_OK) rc = dev_alloc_t(&nin, c.hidden);
   if (rc == ALM_OK) rc = dev_alloc_t(&npost, c.hidden);
@@ -1899,8 +1926,10 @@ int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, 
   ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host, rows * sizeof(int), cudaMemcpyHostToDevice, st));
   const bool head = logits_host != nullptr || argmax_host != nullptr;
   m->tp_need_logits = logits_host != nullptr;
+  m->pv_one_span = pos0 + rows <= kPvSplit;
   const int rc = enqueue_forward(m, kv, rows, head, m->ctx->pdl);
   m->tp_need_logits = false;
+  m->pv_one_span = false;
   ALM_TRY(rc);
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, rows, logits_host, argmax_host);
@@ -2030,19 +2059,12 @@ static int enqueue_spec_step(alm_spec* s) {
   return ALM_OK;
 }
 
-// (Re)capture the step graph for the decoder's current sampling settings.
-static int capture_spec_graph(alm_spec* s) {
-  if (s->temperature > 0.f) {
-    ALM_TRY(ensure_sample_scratch(s->target));
-    ALM_TRY(ensure_sample_scratch(s->draft));
+// Capture one step graph into *exec (destroyed first if set).
+static int capture_step_graph(alm_spec* s, cudaGraphExec_t* exec, int* n_kernels) {
+  if (*exec) {
+    cudaGraphExecDestroy(*exec);
+    *exec = nullptr;
   }
-  if (s->rejection && !s->probs)
-    ALM_TRY(dev_alloc_t(&s->probs, static_cast<size_t>(2 * s->k + 1) * s->target->cfg.vocab));
-  if (s->graph) {
-    cudaGraphExecDestroy(s->graph);
-    s->graph = nullptr;
-  }
-  s->n_kernels = 0;
   cudaStream_t st = s->target->ctx->stream;
   cudaGraph_t graph = nullptr;
   if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
@@ -2058,15 +2080,49 @@ static int capture_spec_graph(alm_spec* s) {
     cudaGraphGetNodes(graph, nullptr, &n_nodes);
     std::vector<cudaGraphNode_t> nodes(n_nodes);
     if (n_nodes) cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
+    int n = 0;
     for (cudaGraphNode_t nd : nodes) {
       cudaGraphNodeType ty;
-      if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->n_kernels;
+      if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++n;
     }
-    e = cudaGraphInstantiate(&s->graph, graph, 0);
+    if (n_kernels) *n_kernels = n;
+    e = cudaGraphInstantiate(exec, graph, 0);
     if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
   }
   if (graph) cudaGraphDestroy(graph);
   return rc;
+}
+
+// (Re)capture the step graphs for the decoder's current sampling settings:
+// the general one and, when a KV cache is longer than one P.V span, the
+// one-span variant.
+static int capture_spec_graph(alm_spec* s) {
+  if (s->temperature > 0.f) {
+    ALM_TRY(ensure_sample_scratch(s->target));
+    ALM_TRY(ensure_sample_scratch(s->draft));
+  }
+  if (s->rejection && !s->probs)
+    ALM_TRY(dev_alloc_t(&s->probs, static_cast<size_t>(2 * s->k + 1) * s->target->cfg.vocab));
+  s->n_kernels = 0;
+  ALM_TRY(capture_step_graph(s, &s->graph, &s->n_kernels));
+  if (s->graph_short) {
+    cudaGraphExecDestroy(s->graph_short);
+    s->graph_short = nullptr;
+  }
+  if (s->tkv->max_len > kPvSplit || s->dkv->max_len > kPvSplit) {
+    s->target->pv_one_span = s->draft->pv_one_span = true;
+    const int rc = capture_step_graph(s, &s->graph_short, nullptr);
+    s->target->pv_one_span = s->draft->pv_one_span = false;
+    ALM_TRY(rc);
+  }
+  return ALM_OK;
+}
+
+// The step graph for n_steps steps from position pos: the one-span variant
+// when no pass of them reaches past one P.V span.
+static cudaGraphExec_t step_graph(const alm_spec* s, int pos, int n_steps) {
+  const long long last = static_cast<long long>(pos) + static_cast<long long>(n_steps) * (s->k + 1) + s->k + 1;
+  return (s->graph_short && last <= kPvSplit) ? s->graph_short : s->graph;
 }
 
 int alm_spec_create(alm_model* target, alm_model* draft, alm_kv* target_kv, alm_kv* draft_kv, int k,
@@ -2113,6 +2169,7 @@ int alm_spec_destroy(alm_spec* s) {
   DeviceGuard g(s->target->ctx->device);
   cudaStreamSynchronize(s->target->ctx->stream);
   if (s->graph) cudaGraphExecDestroy(s->graph);
+  if (s->graph_short) cudaGraphExecDestroy(s->graph_short);
   dev_free(s->state);
   dev_free(s->cand);
   dev_free(s->out_tokens);
@@ -2243,7 +2300,8 @@ int alm_spec_run(alm_spec* s, int n_steps, int32_t* emitted_host, int32_t* n_emi
   ALM_REQ(last_pos < s->target->cfg.max_len && last_pos < s->draft->cfg.max_len, "position beyond the rope table");
   ALM_TRY(check_uniforms(s, n_steps));
   ALM_CUDA(cudaMemsetAsync(s->state + 2, 0, 2 * sizeof(int), st));
-  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(s->graph, st));
+  cudaGraphExec_t graph = step_graph(s, cur[1], n_steps);
+  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(graph, st));
   int* h = s->pinned;
   ALM_CUDA(cudaMemcpyAsync(h, s->state, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   ALM_CUDA(cudaStreamSynchronize(st));
@@ -2288,8 +2346,9 @@ int alm_spec_bench(alm_spec* s, int n_steps, float* ms, int32_t* n_emitted) {
   ALM_CUDA(cudaEventCreate(&e0));
   ALM_CUDA(cudaEventCreate(&e1));
   ALM_CUDA(cudaMemsetAsync(s->state + 2, 0, 2 * sizeof(int), st));
+  cudaGraphExec_t graph = step_graph(s, cur[1], n_steps);
   ALM_CUDA(cudaEventRecord(e0, st));
-  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(s->graph, st));
+  for (int i = 0; i < n_steps; ++i) ALM_CUDA(cudaGraphLaunch(graph, st));
   ALM_CUDA(cudaEventRecord(e1, st));
   ALM_CUDA(cudaEventSynchronize(e1));
   ALM_CUDA(cudaEventElapsedTime(ms, e0, e1));
@@ -2327,7 +2386,11 @@ int alm_spec_profile(alm_spec* s, int cap, int32_t* ops_host, int32_t* rows_host
   } else {
     g_prof = &prof;
     prof_mark(ALM_OP_BEGIN, 0);
+    // the P.V variant the replayed step graphs would use here
+    const bool one_span = step_graph(s, cur[1], 2) != s->graph;
+    s->target->pv_one_span = s->draft->pv_one_span = one_span;
     rc = enqueue_spec_step(s);
+    s->target->pv_one_span = s->draft->pv_one_span = false;
     g_prof = nullptr;
     const cudaError_t e = cudaStreamEndCapture(st, &graph);
     if (rc == ALM_OK && prof.err != cudaSuccess) rc = fail(ALM_ERR_CUDA, cudaGetErrorString(prof.err));

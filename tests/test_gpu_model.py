@@ -172,3 +172,17 @@ def test_spec_greedy_equals_plain_greedy_on_device(models, name):
         # same tokens and same draft decisions as the reference run
         ref_steps, ref_draft, ref_acc, ref_bonus = g["spec_stats"].tolist()
         assert (steps, acc, bonus) == (ref_steps, ref_acc, ref_bonus)
+
+
+def test_spec_across_the_span_boundary(models):
+    """KV caches longer than one 1024-position P.V span: speculative steps
+    replay the one-span step graph while every pass fits the first span and
+    the span-split graph after it; the stream crossing position 1024 equals
+    plain greedy decoding (single-row forwards on either side of the
+    boundary) token for token."""
+    t, d = models["toyu"], models["toyu_draft"]
+    rng = np.random.default_rng(77)
+    prompt = rng.integers(0, t.canon["vocab"], 990).tolist()
+    plain = greedy_plain(t, _kv(t, 2048), prompt, 96)
+    spec, _, _, _ = greedy_spec(t, d, _kv(t, 2048), _kv(d, 2048), prompt, 96, 4)
+    assert spec == plain
