@@ -79,6 +79,9 @@ SIGNATURES = {
     "alm_layer_forward": [_P, _I, _P, _P, _I, _I, _P],
     "alm_head_logits": [_P, _P, _I, _P, _P],
     "alm_forward": [_P, _P, _P, _I, _I, _P, _P],
+    "alm_prefill": [_P, _P, _P, _I, _I],
+    "alm_ctx_set_dense_prefill": [_P, _I],
+    "alm_model_dense_prefill": [_P, _P],
     "alm_forward_trace": [_P, _P, _P, _I, _I, _P, _I, _P, _P],
     "alm_spec_create": [_P, _P, _P, _P, _I, _PP],
     "alm_spec_destroy": [_P],

@@ -299,6 +299,10 @@ cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_pa
 // 16-column tile sums of squares of out (the RESID epilogue's arithmetic).
 cudaError_t launch_tp_resid(const ActIn& res, const float* o32, int M, int H, half* out, float* ss_out, bool pdl,
                             cudaStream_t st);
+// The same with the fp16 outputs of the dense path (batched prefill).
+cudaError_t launch_resid_rows16(const ActIn& res, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,
+                                cudaStream_t st);
+
 // Local argmax of each row from the head GEMV's per-CTA partials, as
 // (value bits, global index = local index + offset) pairs.
 cudaError_t launch_tp_argmax_local(const float* am_val, const int* am_idx, int n_part, int M, int offset,
@@ -308,5 +312,23 @@ cudaError_t launch_tp_argmax_pick(const int* pairs, int world, int M, int* out, 
 // All-gathered local logits (world, M, v_local) -> rows (M, world * v_local).
 cudaError_t launch_tp_logits_reorder(const half* gathered, int world, int M, int v_local, half* out, bool pdl,
                                      cudaStream_t st);
+
+// ---- batched prefill (prefill.cu) ------------------------------------------
+struct PfRopeArgs {
+  const half* qkv = nullptr;   // (M, ld_qkv): q heads, k heads, v heads
+  int ld_qkv = 0;
+  const half* rope = nullptr;  // (max_len, head_dim) cos | sin
+  int pos0 = 0;
+  int heads = 0, kv_heads = 0, head_dim = 0;
+  float* q = nullptr;          // (M, ldq) fp32 after RoPE
+  int ldq = 0;
+  half* kcache = nullptr;
+  half* vcache = nullptr;
+  const int* page_table = nullptr;
+  int page_size = 16;
+};
+cudaError_t launch_pf_rope_kv(const PfRopeArgs& a, int M, bool pdl, cudaStream_t st);
+cudaError_t launch_pf_swiglu(const half* gu, int ld_gu, int inter, int M, half* h, int ld_h, bool pdl,
+                             cudaStream_t st);
 
 }  // namespace alm

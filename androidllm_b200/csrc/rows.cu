@@ -26,11 +26,17 @@ __global__ void __launch_bounds__(kRowThreads) argmax_final_kernel(const float* 
   argmax_final_body(am_val, am_idx, n_part, out, blockIdx.x, sh);
 }
 
-// One row per block: out = fp16(res + fp16(o32)) and the tile sums of squares
+// One row per block: out = fp16(res + fp16(o)) and the tile sums of squares
 // in the RESID epilogue's order (per 16-column tile, lane g of 8 adds the
-// squares of columns g and g + 8, then a butterfly over g).
-__global__ void __launch_bounds__(kRowThreads) tp_resid_kernel(ActIn res, const float* o32, int H, half* out,
-                                                               float* ss_out) {
+// squares of columns g and g + 8, then a butterfly over g).  o: the fp32
+// sums of a row-split projection (tensor parallelism) or the fp16 outputs of
+// the dense path (batched prefill), row stride H.
+ALM_DEV float resid_operand(float v) { return round_h(v); }
+ALM_DEV float resid_operand(half v) { return __half2float(v); }
+
+template <typename OT>
+__global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, const OT* o32, int H, half* out,
+                                                                 float* ss_out) {
   __shared__ float s_den;
   grid_dep_wait();
   const int m = blockIdx.x;
@@ -51,7 +57,7 @@ __global__ void __launch_bounds__(kRowThreads) tp_resid_kernel(ActIn res, const 
       if (live && col < H) {
         const float rv = __half2float(__ldcg(res.x + static_cast<size_t>(m) * res.ld + col));
         const float rval = res.ss ? norm_value(rv, s_den, __half2float(__ldg(res.w + col))) : rv;
-        const float o = round_h(__ldcg(o32 + static_cast<size_t>(m) * H + col));
+        const float o = resid_operand(__ldcg(o32 + static_cast<size_t>(m) * H + col));
         const half s16 = __float2half_rn(fadd(rval, o));
         out[static_cast<size_t>(m) * H + col] = s16;
         const float sf = __half2float(s16);
@@ -155,7 +161,16 @@ cudaError_t launch_tp_resid(const ActIn& res_, const float* o32, int M, int H, h
   set_vec(res);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
-  return cudaLaunchKernelEx(&c, tp_resid_kernel, res, o32, H, out, ss_out);
+  return cudaLaunchKernelEx(&c, resid_rows_kernel<float>, res, o32, H, out, ss_out);
+}
+
+cudaError_t launch_resid_rows16(const ActIn& res_, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,
+                                cudaStream_t st) {
+  ActIn res = res_;
+  set_vec(res);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  return cudaLaunchKernelEx(&c, resid_rows_kernel<half>, res, o16, H, out, ss_out);
 }
 
 cudaError_t launch_tp_argmax_local(const float* am_val, const int* am_idx, int n_part, int M, int offset,

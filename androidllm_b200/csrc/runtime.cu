@@ -151,6 +151,9 @@ struct alm_ctx {
   bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
   bool attn_decode = false;  // single-row attention as one kernel (opt-in: ALM_ATTN_DECODE=1)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
+  // models loaded from now on keep row-layout copies of their projections for
+  // the batched prefill through the dense tcgen05 path (ALM_DENSE_PREFILL=0: off)
+  bool dense_prefill = true;
   // tensor parallelism: NCCL communicator of this rank (alm_ctx_init_tp)
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
@@ -173,6 +176,37 @@ struct Layer {
   alm_qweight* down = nullptr;
   half* n_in = nullptr;
   half* n_post = nullptr;
+};
+
+// Row-layout copies of a layer's projections for the dense prefill: q | k | v
+// rows in order, gate rows then up rows (plain outputs, no fused epilogue).
+struct DenseLayer {
+  alm_qweight* qkv = nullptr;
+  alm_qweight* o = nullptr;
+  alm_qweight* gu = nullptr;
+  alm_qweight* down = nullptr;
+};
+
+// Buffers of one prefill chunk of up to kMaxDenseRows rows.
+struct PrefillWork {
+  int rows = 0;                 // 0: not allocated
+  int* tokens = nullptr;
+  half* xa = nullptr;           // (rows, H) layer input, normalised
+  half* xb = nullptr;           // (rows, H) attention block output, normalised
+  half* qkv = nullptr;          // (rows, ld_qkv)
+  float* q = nullptr;           // (rows, qd) after RoPE
+  half* ctx = nullptr;          // (rows, qd) attention output
+  half* o = nullptr;            // (rows, H) o / down outputs
+  half* s = nullptr;            // (rows, H) residual sums
+  float* ss = nullptr;          // (rows, H / 16) their sums of squares
+  half* gu = nullptr;           // (rows, ld_gu) gate | up
+  half* h = nullptr;            // (rows, ld_h)
+  int ld_qkv = 0, ld_gu = 0, ld_h = 0;
+  float* part = nullptr;        // split-K partials of the dense path
+  size_t part_floats = 0;
+  float* scores = nullptr;      // attention scratch for rows x max_ctx
+  float* stats = nullptr;
+  int attn_ctx = 0, score_ld = 0;
 };
 
 struct Work {
@@ -265,6 +299,8 @@ struct alm_model {
   bool tp = false;
   int vocab_offset = 0, vocab_local = 0;
   bool tp_need_logits = false;   // gather the full logits after the head
+  std::vector<DenseLayer> dense;   // per layer; qkv null: no dense copies
+  PrefillWork pf;
   // attention passes enqueued now are known to fit one P.V span: launch the
   // unsplit P.V kernel even when the KV capacity is longer (speed only: the
   // unsplit kernel walks any context length)
@@ -346,9 +382,42 @@ int check_format(int bits, int block, int in, int in_real) {
 // Build one weight from up to 3 sources with a destination row map for the
 // chosen layout (dst row -> (src << 24) | src row, or -1).  `allow_rows`:
 // the consumer's epilogue exists in the row layout (every one but QKV).
+void free_dense(DenseLayer& D) {
+  alm_qweight_free(D.qkv);
+  alm_qweight_free(D.o);
+  alm_qweight_free(D.gu);
+  alm_qweight_free(D.down);
+  D = DenseLayer{};
+}
+
+void free_prefill_work(PrefillWork& pf) {
+  for (void* p : {(void*)pf.tokens, (void*)pf.xa, (void*)pf.xb, (void*)pf.qkv, (void*)pf.q, (void*)pf.ctx,
+                  (void*)pf.o, (void*)pf.s, (void*)pf.ss, (void*)pf.gu, (void*)pf.h, (void*)pf.part,
+                  (void*)pf.scores, (void*)pf.stats})
+    dev_free(p);
+  pf = PrefillWork{};
+}
+
+// Whether a layer's projections get row-layout copies for the dense prefill:
+// int4 / int8 with 64-column blocks (the row layout's format), whole models
+// only (a tensor-parallel shard prefills through its row-split forward).
+bool dense_prefill_ok(const alm_model* m, const alm_proj_src* p) {
+  if (!m->ctx->dense_prefill || m->tp) return false;
+  for (int i = 0; i < 7; ++i)
+    if ((p[i].bits != 4 && p[i].bits != 8) || p[i].block % 64 != 0) return false;
+  return true;
+}
+
+// Every layer has its row-layout copies.
+bool dense_ready(const alm_model* m) {
+  for (const DenseLayer& D : m->dense)
+    if (!D.qkv) return false;
+  return !m->dense.empty();
+}
+
 int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src,
                   const std::function<std::vector<int>(int)>& map_of, int n_rows, bool allow_rows,
-                  alm_qweight** out) {
+                  alm_qweight** out, bool force_rows = false) {
   const int bits = srcs[0].bits, block = srcs[0].block, in = srcs[0].in, in_real = srcs[0].in_real;
   for (int i = 0; i < n_src; ++i) {
     ALM_TRY(check_format(srcs[i].bits, srcs[i].block, srcs[i].in, srcs[i].in_real));
@@ -371,7 +440,9 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src,
   t.k_blocks = (in + 63) / 64;
   t.sb = bits == 16 ? 0 : (block == 32 ? 2 : 1);
   t.k_real = in_real;
-  const bool rows = allow_rows && use_rows(ctx, bits, block, n_rows, in);
+  if (force_rows)
+    ALM_REQ((bits == 4 || bits == 8) && block % 64 == 0, "the row layout takes int4 / int8 with 64-column blocks");
+  const bool rows = force_rows || (allow_rows && use_rows(ctx, bits, block, n_rows, in));
   size_t n_rec = 0;
   int n_counters = 0;
   if (rows) {
@@ -933,6 +1004,154 @@ int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
   return enqueue_head(m, M, pdl);
 }
 
+// ---- batched prefill through the dense path ----------------------------------
+// Buffers of a prefill chunk (kMaxDenseRows rows) and the attention scratch for
+// contexts of up to max_ctx positions.
+int ensure_prefill(alm_model* m, int max_ctx) {
+  const alm_model_config& c = m->cfg;
+  PrefillWork& pf = m->pf;
+  const int R = kMaxDenseRows, H = c.hidden, qd = c.heads * c.head_dim, kd = c.kv_heads * c.head_dim;
+  const int I = c.intermediate;
+  auto r8 = [](int v) { return (v + 7) / 8 * 8; };   // 16-byte row strides for the tensor-map loads
+  if (pf.rows == 0) {
+    pf.ld_qkv = r8(qd + 2 * kd);
+    pf.ld_gu = r8(2 * I);
+    pf.ld_h = r8(I);
+    // split-K partials of any chunk size the dense path takes (17..R rows)
+    size_t part = 0;
+    for (const DenseLayer& D : m->dense)
+      for (const alm_qweight* w : {D.qkv, D.o, D.gu, D.down})
+        if (w)
+          for (int rows = kMaxRows + 1; rows <= R; ++rows) part = std::max(part, tc_part_floats(w->t, rows));
+    int rc = dev_alloc_t(&pf.tokens, R);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.xa, static_cast<size_t>(R) * H);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.xb, static_cast<size_t>(R) * H);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.qkv, static_cast<size_t>(R) * pf.ld_qkv);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.q, static_cast<size_t>(R) * qd);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.ctx, static_cast<size_t>(R) * qd);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.o, static_cast<size_t>(R) * H);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.s, static_cast<size_t>(R) * H);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.ss, static_cast<size_t>(R) * n_h_tiles(m));
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.gu, static_cast<size_t>(R) * pf.ld_gu);
+    if (rc == ALM_OK) rc = dev_alloc_t(&pf.h, static_cast<size_t>(R) * pf.ld_h);
+    if (rc == ALM_OK && part) rc = dev_alloc_t(&pf.part, part);
+    if (rc != ALM_OK) {
+      free_prefill_work(pf);
+      return rc;
+    }
+    pf.part_floats = part;
+    pf.rows = R;
+  }
+  if (max_ctx > pf.attn_ctx) {
+    dev_free(pf.scores);
+    dev_free(pf.stats);
+    pf.scores = nullptr;
+    pf.stats = nullptr;
+    pf.attn_ctx = 0;
+    const int gq = c.heads / c.kv_heads;
+    const int n_rg = (R * gq + kAttnRows - 1) / kAttnRows;
+    const int cap = (max_ctx + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+    const int ld = cap + kAttnChunk;   // the P.V pass reads whole 16-position groups
+    ALM_TRY(dev_alloc_t(&pf.scores, static_cast<size_t>(c.kv_heads) * n_rg * kAttnRows * ld));
+    ALM_TRY(dev_alloc_t(&pf.stats, static_cast<size_t>(c.kv_heads) * n_rg * (cap / kAttnChunk) * kAttnRows * 2));
+    pf.attn_ctx = cap;
+    pf.score_ld = ld;
+  }
+  return ALM_OK;
+}
+
+// One prefill chunk of M (17..256) rows at positions pos0.. (tokens already
+// in pf.tokens, ws.pos = pos0): every projection through the dense tcgen05
+// path, the fused epilogues' operations in row kernels, the attention passes
+// over the chunk's rows.  Only the KV cache is kept; the last layer stops
+// after its KV write.  The arithmetic is the M <= 16 path's, so the cache
+// equals a 16-row-chunk prefill up to the matmuls' fp32 summation order.
+int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0) {
+  const alm_model_config& c = m->cfg;
+  PrefillWork& pf = m->pf;
+  Work& ws = m->ws;
+  cudaStream_t st = m->ctx->stream;
+  const bool pdl = m->ctx->pdl;
+  const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd, I = c.intermediate;
+  const StepIO io{ws.pos, ws.err};
+  const SplitScratch scr{pf.part, pf.part_floats};
+  auto dense = [&](const alm_qweight* w, const half* x, int ldx, half* y, int ldy) -> int {
+    Epi e;
+    e.out = y;
+    e.ldo = ldy;
+    e.n_out = w->out;
+    ALM_LAUNCH(launch_gemv(w->t, raw_in(x, ldx, w->in_real), M, EPI_STORE, e, io, scr, pdl, st));
+    return ALM_OK;
+  };
+  EmbedArgs ea;
+  ea.table = m->embed_table;
+  ea.scale = m->embed_scale;
+  ea.bits = m->embed_bits;
+  ea.block = m->embed_block;
+  ea.nsb = m->embed_nsb;
+  ea.hidden = H;
+  ea.row_bytes = m->embed_row_bytes;
+  ea.vocab = c.vocab;
+  ea.tokens = pf.tokens;
+  ea.out = pf.xa;
+  ea.M = M;
+  ea.err = ws.err;
+  ALM_LAUNCH(launch_embed(ea, pdl, st));
+  for (int li = 0; li < c.layers; ++li) {
+    const Layer& L = m->layers[li];
+    const DenseLayer& D = m->dense[li];
+    if (li > 0) {
+      // the layer's input: the previous layer's output under its n_post norm
+      const ActIn prev = deferred_in(m, pf.s, pf.ss, m->layers[li - 1].n_post);
+      ALM_LAUNCH(launch_rownorm(prev, M, nullptr, 0.f, pf.xa, H, pdl, st));
+    }
+    ALM_TRY(dense(D.qkv, pf.xa, H, pf.qkv, pf.ld_qkv));
+    PfRopeArgs ra;
+    ra.qkv = pf.qkv;
+    ra.ld_qkv = pf.ld_qkv;
+    ra.rope = m->rope;
+    ra.pos0 = pos0;
+    ra.heads = c.heads;
+    ra.kv_heads = c.kv_heads;
+    ra.head_dim = hd;
+    ra.q = pf.q;
+    ra.ldq = qd;
+    ra.kcache = kv->k + static_cast<size_t>(li) * kv->layer_elems;
+    ra.vcache = kv->v + static_cast<size_t>(li) * kv->layer_elems;
+    ra.page_table = kv->page_table;
+    ra.page_size = kv->page_size;
+    ALM_LAUNCH(launch_pf_rope_kv(ra, M, pdl, st));
+    AttnArgs a;
+    a.q = pf.q;
+    a.ldq = qd;
+    a.kcache = ra.kcache;
+    a.vcache = ra.vcache;
+    a.page_table = kv->page_table;
+    a.page_size = kv->page_size;
+    a.heads = c.heads;
+    a.kv_heads = c.kv_heads;
+    a.head_dim = hd;
+    a.M = M;
+    a.pos = ws.pos;
+    a.max_ctx = pos0 + M;   // exact: the host knows this chunk's context
+    a.scores = pf.scores;
+    a.score_ld = pf.score_ld;
+    a.stats = pf.stats;
+    a.ctx = pf.ctx;
+    a.ldc = qd;
+    ALM_LAUNCH(launch_attention(a, pdl, st));
+    if (li == c.layers - 1) break;
+    ALM_TRY(dense(D.o, pf.ctx, qd, pf.o, H));
+    ALM_LAUNCH(launch_resid_rows16(raw_in(pf.xa, H, H), pf.o, M, H, pf.s, pf.ss, pdl, st));
+    ALM_LAUNCH(launch_rownorm(deferred_in(m, pf.s, pf.ss, L.n_in), M, nullptr, 0.f, pf.xb, H, pdl, st));
+    ALM_TRY(dense(D.gu, pf.xb, H, pf.gu, pf.ld_gu));
+    ALM_LAUNCH(launch_pf_swiglu(pf.gu, pf.ld_gu, I, M, pf.h, pf.ld_h, pdl, st));
+    ALM_TRY(dense(D.down, pf.h, pf.ld_h, pf.o, H));
+    ALM_LAUNCH(launch_resid_rows16(raw_in(pf.xb, H, H), pf.o, M, H, pf.s, pf.ss, pdl, st));
+  }
+  return ALM_OK;
+}
+
 // Sampler arguments for rows of a model's last logits, writing the picks
 // into its argmax buffer.
 SampleArgs sample_args(alm_model* m, float temperature, float top_p, float min_p, const double* uniforms,
@@ -1054,6 +1273,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
     c->cluster = e4 && e4[0] == '1';
     const char* e3 = getenv("ALM_TC");
     if (e3 && (e3[0] == '0' || e3[0] == '1' || e3[0] == '2')) c->tc = e3[0] - '0';
+    const char* e6 = getenv("ALM_DENSE_PREFILL");
+    c->dense_prefill = !(e6 && e6[0] == '0');
   }
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
@@ -1295,6 +1516,7 @@ int alm_model_create(alm_ctx* ctx, const alm_model_config* cfg, const uint16_t* 
   m->ctx = ctx;
   m->cfg = c;
   m->layers.resize(c.layers);
+  m->dense.resize(c.layers);
   const size_t n = static_cast<size_t>(c.max_len) * c.head_dim;
   int rc = dev_alloc_t(&m->rope, n);
   if (rc == ALM_OK && cudaMemcpy(m->rope, rope_host, n * sizeof(half), cudaMemcpyHostToDevice) != cudaSuccess)
@@ -1319,6 +1541,8 @@ int alm_model_destroy(alm_model* m) {
     dev_free(L.n_in);
     dev_free(L.n_post);
   }
+  for (DenseLayer& D : m->dense) free_dense(D);
+  free_prefill_work(m->pf);
   alm_qweight_free(m->head);
   dev_free(m->rope);
   dev_free(m->embed_table);
@@ -1395,6 +1619,40 @@ int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint1
     part = "down";
     rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, true, &dn);
   }
+  // row-layout copies for the batched prefill (dense tcgen05 path)
+  DenseLayer D;
+  if (rc == ALM_OK && dense_prefill_ok(m, p)) {
+    const int I = c.intermediate;
+    auto qkv_rows = [qd, kd](int layout) {
+      std::vector<int> mp(padded_rows(qd + 2 * kd, layout), -1);
+      for (int r = 0; r < qd; ++r) mp[r] = r;
+      for (int r = 0; r < kd; ++r) mp[qd + r] = (1 << 24) | r;
+      for (int r = 0; r < kd; ++r) mp[qd + kd + r] = (2 << 24) | r;
+      return mp;
+    };
+    auto gu_rows = [I](int layout) {
+      std::vector<int> mp(padded_rows(2 * I, layout), -1);
+      for (int j = 0; j < I; ++j) {
+        mp[j] = j;
+        mp[I + j] = (1 << 24) | j;
+      }
+      return mp;
+    };
+    part = "qkv (row layout)";
+    rc = build_qweight(m->ctx, &p[0], 3, qkv_rows, qd + 2 * kd, true, &D.qkv, true);
+    if (rc == ALM_OK) {
+      part = "o (row layout)";
+      rc = build_qweight(m->ctx, &p[3], 1, identity_map(c.hidden), c.hidden, true, &D.o, true);
+    }
+    if (rc == ALM_OK) {
+      part = "gate/up (row layout)";
+      rc = build_qweight(m->ctx, &p[4], 2, gu_rows, 2 * I, true, &D.gu, true);
+    }
+    if (rc == ALM_OK) {
+      part = "down (row layout)";
+      rc = build_qweight(m->ctx, &p[6], 1, identity_map(c.hidden), c.hidden, true, &D.down, true);
+    }
+  }
   if (rc != ALM_OK) g_err = "layer " + std::to_string(li) + " " + part + ": " + g_err;
   half *nin = nullptr, *npost = nullptr;
   if (rc == ALM_OK) rc = dev_alloc_t(&nin, c.hidden);
@@ -1407,10 +1665,13 @@ int alm_model_set_layer(alm_model* m, int li, const alm_proj_src* p, const uint1
     alm_qweight_free(o);
     alm_qweight_free(gu);
     alm_qweight_free(dn);
+    free_dense(D);
     dev_free(nin);
     dev_free(npost);
     return rc;
   }
+  free_dense(m->dense[li]);
+  m->dense[li] = D;
   alm_qweight_free(L.qkv);
   alm_qweight_free(L.o);
   alm_qweight_free(L.gu);
@@ -1912,6 +2173,57 @@ int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, flo
     rc = fail(ALM_ERR_CUDA, "sample failed");
   dev_free(du);
   return rc;
+}
+
+// Fill the KV cache for positions pos0 .. pos0 + n - 1 from the tokens
+// (androidllm/engine.py:345-361 runs them as n single-token forwards):
+// chunks of up to 256 rows through the dense path when the model has its
+// row-layout copies (a tail of at most 16 rows, or any chunk without them,
+// through the M <= 16 forward).  No logits.
+int alm_prefill(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int n, int pos0) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(tokens_host && kv, "null argument");
+  ALM_TRY(check_layers(m));
+  ALM_REQ(n >= 1, "n must be positive");
+  ALM_REQ(kv->n_layers == m->cfg.layers && kv->kv_heads == m->cfg.kv_heads && kv->head_dim == m->cfg.head_dim,
+          "kv cache shape mismatch");
+  ALM_REQ(pos0 >= 0 && static_cast<long long>(pos0) + n <= kv->max_len, "pos out of kv cache range");
+  ALM_REQ(static_cast<long long>(pos0) + n <= m->cfg.max_len, "pos out of rope table range");
+  DeviceGuard g(m->ctx->device);
+  ALM_TRY(ensure_attn(m, kv->max_len));
+  const bool dense = dense_ready(m);
+  if (dense) ALM_TRY(ensure_prefill(m, kv->max_len));
+  cudaStream_t st = m->ctx->stream;
+  for (int done = 0; done < n;) {
+    const int rows = std::min(n - done, dense ? kMaxDenseRows : kMaxRows);
+    const int p = pos0 + done;
+    ALM_TRY(set_pos(m, p));
+    if (rows > kMaxRows) {
+      ALM_CUDA(cudaMemcpyAsync(m->pf.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice, st));
+      ALM_TRY(enqueue_prefill_dense(m, kv, rows, p));
+    } else {
+      ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice, st));
+      m->pv_one_span = p + rows <= kPvSplit;
+      const int rc = enqueue_forward(m, kv, rows, false, m->ctx->pdl);
+      m->pv_one_span = false;
+      ALM_TRY(rc);
+    }
+    ALM_TRY(sync_and_check(m));
+    done += rows;
+  }
+  return ALM_OK;
+}
+
+int alm_ctx_set_dense_prefill(alm_ctx* ctx, int enable) {
+  ALM_REQ(ctx, "null context");
+  ctx->dense_prefill = enable != 0;
+  return ALM_OK;
+}
+
+int alm_model_dense_prefill(const alm_model* m, int* dense) {
+  ALM_REQ(m && dense, "null argument");
+  *dense = dense_ready(m) ? 1 : 0;
+  return ALM_OK;
 }
 
 int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0, float* logits_host,

@@ -40,7 +40,6 @@ from .models.llama import KVList, LlamaModel
 from .ops import DeviceKV, DeviceModel, SpecDecoder, default_context, load_manifest
 from . import safetensors
 
-PREFILL_ROWS = 16
 
 
 class LayerStreamingEngine:
@@ -148,10 +147,10 @@ class LayerStreamingEngine:
         self.stats["compute_tokens"] += self.n_layers * rows
 
     def _prefill(self, kv, ids, pos0):
+        """The prompt's KV entries (androidllm/engine.py:345-361), in chunks of
+        up to 256 rows through the dense path (DeviceModel.prefill)."""
         t0 = time.time()
-        for i in range(0, len(ids), PREFILL_ROWS):
-            chunk = ids[i:i + PREFILL_ROWS]
-            self.dm.forward(kv.cache, chunk, pos0 + i, logits=False, argmax=False)
+        self.dm.prefill(kv.cache, ids, pos0)
         self._account(t0, len(ids))
 
     # -- uniform draws (one stream, consumed in the reference's order) ---------------

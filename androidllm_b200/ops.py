@@ -49,6 +49,12 @@ class Context:
         launch per layer operation (the default)."""
         check(lib.alm_ctx_set_cluster_forward(self.h, 1 if enable else 0))
 
+    def set_dense_prefill(self, enable):
+        """Whether models loaded on this context from now on keep row-layout
+        copies of their projections so that prefill runs through the dense
+        tcgen05 path (default on)."""
+        check(lib.alm_ctx_set_dense_prefill(self.h, 1 if enable else 0))
+
     def set_gemv_layout(self, mode):
         """Layout of weights uploaded from now on: 0 = 16-row tiles (mma.sync
         GEMV, the default), 1 = 128-row records (tcgen05 kernel) for weights of
@@ -305,6 +311,19 @@ class DeviceModel:
 
     def finalize(self):
         check(lib.alm_model_finalize(self.h))
+
+    def uses_dense_prefill(self):
+        """Whether prefill runs its chunks through the dense tcgen05 path."""
+        v = ctypes.c_int32()
+        check(lib.alm_model_dense_prefill(self.h, ctypes.byref(v)))
+        return bool(v.value)
+
+    def prefill(self, kv, tokens, pos0=0):
+        """Fill kv for positions pos0 .. pos0 + len(tokens) - 1 (alm_prefill):
+        the prompt's forwards without logits, in chunks of up to 256 rows."""
+        tok = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        if tok.size:
+            check(lib.alm_prefill(self.h, kv.h, ptr(tok), int(tok.size), int(pos0)))
 
     def uses_cluster_forward(self):
         """Whether single-row forwards run as the 16-CTA cluster kernel."""

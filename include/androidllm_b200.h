@@ -254,6 +254,19 @@ ALM_API int alm_model_sample(alm_model* m, int rows, float temperature, float to
  * pos0..pos0+rows-1 (androidllm/engine.py:255-286 without sampling). */
 ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
                 float* logits_host, int32_t* argmax_host);
+/* Prompt prefill: fills the KV cache for positions pos0..pos0+n-1 from the
+ * tokens, no logits.  Replaces the per-token forwards of the prompt in
+ * androidllm/engine.py:345-361.  Chunks of up to 256 rows run every
+ * projection through the dense tcgen05 path when the model keeps row-layout
+ * copies (alm_model_dense_prefill), the rest in forwards of up to 16 rows. */
+ALM_API int alm_prefill(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int n, int pos0);
+/* Whether models created on this context from now on keep row-layout copies
+ * of their int4 / int8 (64-column block) projections for alm_prefill
+ * (default on; ALM_DENSE_PREFILL=0 turns the default off).  The copies take
+ * as much device memory as the layers' weights. */
+ALM_API int alm_ctx_set_dense_prefill(alm_ctx* ctx, int enable);
+/* *dense = 1 when every layer of the model has its row-layout copies. */
+ALM_API int alm_model_dense_prefill(const alm_model* m, int* dense);
 /* Profiling (no counterpart in the reference): alm_forward with the head,
  * run as the persistent forward kernel (rows <= 8), recording global-timer
  * nanoseconds; for rows = 1 of a model on the cluster forward, the cluster

@@ -64,14 +64,14 @@ def _emulate(t, d, prompt, n, k, seed, temperature, top_p, min_p):
     sampler: the reference's rule and draw order, independent of the
     engine's graph, uniform stream and acceptance kernel."""
     from androidllm_b200.ops import DeviceKV
-    from gpu_helpers import prefill
     rng = np.random.default_rng(seed)
     draw = lambda lg: osamp.sample_fixed(lg, temperature, top_p, min_p, rng.random())
+    # the prompt prefilled the way the engine does it (DeviceModel.prefill)
     tkv = DeviceKV(t, 256, 16)
-    prefill(t, tkv, prompt[:-1])
+    t.prefill(tkv, prompt[:-1])
     if d is not None:
         dkv = DeviceKV(d, 256, 16)
-        prefill(d, dkv, prompt)
+        d.prefill(dkv, prompt)
     token, pos, out = prompt[-1], len(prompt) - 1, []
     while len(out) < n:
         if d is None:
