@@ -52,10 +52,10 @@ __host__ __device__ inline size_t attn_pv_smem() {
          static_cast<size_t>(kAttnWarps) * kWarp * 8 * sizeof(float) + (kPvSpan + 1) * sizeof(int);
 }
 __host__ __device__ inline int attn_row_groups(const AttnArgs& a) {
-  return (a.M * (a.heads / a.kv_heads) + kAttnRows - 1) / kAttnRows;
+  return a.seqs ? a.n_rg : (a.M * (a.heads / a.kv_heads) + kAttnRows - 1) / kAttnRows;
 }
 __host__ __device__ inline int attn_pv_groups(const AttnArgs& a) {
-  return (a.M * (a.heads / a.kv_heads) + kPvRows - 1) / kPvRows;
+  return a.seqs ? a.n_pg : (a.M * (a.heads / a.kv_heads) + kPvRows - 1) / kPvRows;
 }
 __host__ __device__ inline int attn_chunks_max(const AttnArgs& a) { return (a.max_ctx + kAttnChunk - 1) / kAttnChunk; }
 
@@ -72,11 +72,40 @@ ALM_DEV void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_
 }
 
 // Page numbers of the positions [p_begin, p_end) -> s_pg (read from global
-// memory once, so every K / V load needs one round trip, not two).
-ALM_DEV void stage_pages(const AttnArgs& a, int p_begin, int p_end, int* s_pg) {
+// memory once, so every K / V load needs one round trip, not two); ptab: the
+// sequence's page table (null: the pass's).
+ALM_DEV void stage_pages(const AttnArgs& a, int p_begin, int p_end, int* s_pg, const int* ptab = nullptr) {
+  const int* pt = ptab ? ptab : a.page_table;
   const int pg0 = p_begin / a.page_size;
   const int n_pg = (p_end - 1) / a.page_size - pg0 + 1;
-  for (int i = threadIdx.x; i < n_pg; i += kAttnThreads) s_pg[i] = __ldcg(a.page_table + pg0 + i);
+  for (int i = threadIdx.x; i < n_pg; i += kAttnThreads) s_pg[i] = __ldcg(pt + pg0 + i);
+}
+
+// The sequence a scores row group (pv = false) or P.V group (pv = true)
+// belongs to: its first activation row, rows, first position, page table,
+// the group's index within the sequence and the sequence's first scores row
+// group.  One sequence of M rows at *a.pos when the pass has no sequences.
+struct AttnSeqView {
+  int m0, n_tok, pos0, local, g0;
+  const int* ptab;
+};
+ALM_DEV AttnSeqView attn_seq_view(const AttnArgs& a, int group, bool pv) {
+  AttnSeqView v{0, a.M, 0, group, 0, a.page_table};
+  if (!a.seqs) {
+    v.pos0 = *a.pos;
+    return v;
+  }
+  int s = 0;
+  for (int i = 1; i < a.n_seq; ++i)
+    if ((pv ? a.seqs[i].p0 : a.seqs[i].g0) <= group) s = i;
+  const AttnSeq q = a.seqs[s];
+  v.m0 = q.m0;
+  v.n_tok = q.n_tok;
+  v.pos0 = q.pos0;
+  v.local = group - (pv ? q.p0 : q.g0);
+  v.g0 = q.g0;
+  v.ptab = a.page_table + q.pt_off;
+  return v;
 }
 
 // Row of position pos (pages of the staged range start at page pg0).
@@ -95,6 +124,7 @@ ALM_DEV int* attn_scores_pg(const AttnArgs& a, unsigned char* smem_raw) {
                                                sizeof(half));
 }
 ALM_DEV void attn_scores_pages(const AttnArgs& a, int chunk, unsigned char* smem_raw) {
+  if (a.seqs) return;   // a multi-sequence pass stages its sequence's pages after the wait
   const int c0 = chunk * kAttnChunk;
   if (c0 < a.max_ctx) stage_pages(a, c0, min(c0 + kAttnChunk, a.max_ctx), attn_scores_pg(a, smem_raw));
 }
@@ -110,15 +140,22 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   half* ks = qlo + kAttnRows * ld;   // [64][ld]
   const int* s_pg = attn_scores_pg(a, smem_raw);
 
-  const int pos0 = *a.pos;
-  const int n_ctx = pos0 + a.M;
+  // rg: the pass's row group (the scratch layout); lg: within its sequence
+  const AttnSeqView sv = attn_seq_view(a, rg, false);
+  const int pos0 = sv.pos0;
+  const int n_ctx = pos0 + sv.n_tok;
   const int c0 = chunk * kAttnChunk;
   if (c0 >= n_ctx) return;
   const int gq = a.heads / a.kv_heads;
-  const int n_rows = a.M * gq;
-  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
+  const int n_rows = sv.n_tok * gq;
+  const int n_rg = attn_row_groups(a);
+  const int lg = sv.local;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const int pg0 = c0 / a.page_size;
+  if (a.seqs) {
+    stage_pages(a, c0, min(c0 + kAttnChunk, n_ctx), attn_scores_pg(a, smem_raw), sv.ptab);
+    body_sync_t<NAMED>();
+  }
 
   // Q rows (-> fp16 hi/lo) and the K chunk: every load issued before any is
   // used (one round trip); hd <= 256 keeps each within one pass of the block
@@ -130,10 +167,10 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   for (int j = 0; j < 4; ++j) {
     const int i = j * kAttnThreads + tid;
     const int rl = i / per_row, d4 = i % per_row;
-    const int r = rg * kAttnRows + rl;
+    const int r = lg * kAttnRows + rl;
     qv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (i < n4 && r < n_rows) {
-      const int m = r / gq, head = kvh * gq + r % gq;
+      const int m = sv.m0 + r / gq, head = kvh * gq + r % gq;
       qv[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
     }
   }
@@ -198,7 +235,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int rl = g + 8 * (e >> 1);
-        const int r = rg * kAttnRows + rl;
+        const int r = lg * kAttnRows + rl;
         const int p = c0 + warp * 16 + nt * 8 + 2 * t + (e & 1);
         float s = kNegInf;
         if (r < n_rows && p < n_ctx && p <= pos0 + r / gq) s = fdiv(acc[nt][e], inv_sqrt_den);
@@ -265,6 +302,7 @@ ALM_DEV int* attn_pv_pg(unsigned char* smem_raw) {
 // (n_split > 1), else the first kPvSpan positions (before the block waits
 // for the scores pass; the caller synchronises the block).
 ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 0, int n_split = 1) {
+  if (a.seqs) return;   // a multi-sequence pass stages its sequence's pages after the wait
   const int b = n_split > 1 ? sp * kPvSplit : 0;
   const int e = n_split > 1 ? b + kPvSplit : kPvSpan;
   if (b < a.max_ctx) stage_pages(a, b, min(e, a.max_ctx), attn_pv_pg(smem_raw));
@@ -290,13 +328,15 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   int* s_pg = attn_pv_pg(smem_raw);                  // pages of the current span
 
   const int hd = a.head_dim;
-  const int pos0 = *a.pos;
-  const int n_ctx = pos0 + a.M;
+  // grp: the pass's P.V group; r0: this block's first row within its sequence
+  const AttnSeqView seq = attn_seq_view(a, grp, true);
+  const int pos0 = seq.pos0;
+  const int n_ctx = pos0 + seq.n_tok;
   const int n_chunks = (n_ctx + kAttnChunk - 1) / kAttnChunk;
   const int gq = a.heads / a.kv_heads;
-  const int n_rows = a.M * gq;
-  const int n_rg = (n_rows + kAttnRows - 1) / kAttnRows;
-  const int r0 = grp * kPvRows;                      // first query row of this block
+  const int n_rows = seq.n_tok * gq;
+  const int n_rg = attn_row_groups(a);
+  const int r0 = seq.local * kPvRows;
   if (r0 >= n_rows) return;
   const int needed = (n_ctx + kPvSplit - 1) / kPvSplit;
   const bool split = SPLIT && a.pv_part != nullptr && n_split > 1 && needed > 1;
@@ -304,10 +344,14 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   if (split && sp >= needed) return;
   const int span_begin = split ? sp * kPvSplit : 0;
   const int span_end = split ? min(span_begin + kPvSplit, n_ctx) : n_ctx;
-  const int rg = r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group
+  const int rg = seq.g0 + r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group of the pass
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const size_t srow0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows + rl0;
   const float* st = a.stats + ((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max) * kAttnRows * 2;
+  if (a.seqs) {   // the sequence's pages of the first span (attn_pv_pages staged nothing)
+    stage_pages(a, span_begin, min(span_begin + kPvSpan, span_end), s_pg, seq.ptab);
+    body_sync_t<NAMED>();
+  }
 
   // One load phase for a span: the V slice (16 dims = two 16 B vectors per
   // position: span_pad * 2 <= kAttnThreads * 8 vectors) and this block's
@@ -403,7 +447,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     const int span = min(kPvSpan, span_end - base);
     const int span_pad = (span + 15) & ~15;
     if (base > span_begin) {   // the first span was loaded with the statistics
-      stage_pages(a, base, base + span, s_pg);
+      stage_pages(a, base, base + span, s_pg, seq.ptab);
       body_sync_t<NAMED>();
       load_span(base, span_pad);
     }
@@ -471,7 +515,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
         }
         const int r = r0 + g;
         if (r < n_rows) {
-          const int m = r / gq, head = kvh * gq + r % gq;
+          const int m = seq.m0 + r / gq, head = kvh * gq + r % gq;
           a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + ds * 16 + dl] = __float2half_rn(v);
         }
       }
@@ -491,7 +535,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
         for (int s2 = 1; s2 < needed; ++s2) v = fadd(v, __ldcg(base + static_cast<size_t>(s2) * (kPvRows * 16)));
         const int r = r0 + rl;
         if (r < n_rows) {
-          const int m = r / gq, head = kvh * gq + r % gq;
+          const int m = seq.m0 + r / gq, head = kvh * gq + r % gq;
           a.ctx[static_cast<size_t>(m) * a.ldc + head * hd + ds * 16 + dl] = __float2half_rn(v);
         }
       }

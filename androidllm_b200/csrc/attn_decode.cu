@@ -342,7 +342,7 @@ cudaError_t attn_decode_init_attrs() {
 
 bool attn_decode_ok(const AttnArgs& a) {
   const int nsl = a.head_dim / 16;
-  return a.M == 1 && a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= kAttnRows && a.head_dim % 16 == 0 &&
+  return a.seqs == nullptr && a.M == 1 && a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= kAttnRows && a.head_dim % 16 == 0 &&
          (nsl == 1 || nsl == 2 || nsl == 4 || nsl == 8) &&
          attn_decode_smem(a.head_dim, a.max_ctx, a.page_size) <= 200 * 1024;
 }

@@ -439,7 +439,10 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
     if (owner) {
       const int hd = epi.head_dim, half_d = hd / 2, tph = hd / 16;
       const int tq = epi.heads * tph, tk = epi.kv_heads * tph;
-      const int pos0 = *io.pos;
+      // row m's position and page table: pos0 + m, or its sequence's (epi.rows)
+      const int pos0 = epi.rows ? 0 : *io.pos;
+      auto row_pos = [&](int m) { return epi.rows ? epi.rows[m].x : pos0 + m; };
+      auto row_pages = [&](int m) { return epi.rows ? epi.page_table + epi.rows[m].y : epi.page_table; };
       if (tile < tq + tk) {
         const bool is_q = tile < tq;
         const int head = is_q ? tile / tph : (tile - tq) / tph;
@@ -450,7 +453,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int m = nt * 8 + 2 * t + j;
-            const size_t rb = static_cast<size_t>(m < M ? pos0 + m : pos0) * hd;
+            const size_t rb = static_cast<size_t>(row_pos(m < M ? m : 0)) * hd;
             cs[nt][j] = __half2float(__ldg(epi.rope + rb + dlo));
             sn[nt][j] = __half2float(__ldg(epi.rope + rb + half_d + dlo));
           }
@@ -460,7 +463,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
           for (int j = 0; j < 2; ++j) {
             const int m = nt * 8 + 2 * t + j;
             if (m >= M) continue;
-            const int pos = pos0 + m;
+            const int pos = row_pos(m);
             const float a = round_h(acc[nt][j]), b = round_h(acc[nt][2 + j]);
             const float c = cs[nt][j];
             const float sv = sn[nt][j];
@@ -471,7 +474,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
               q[dlo] = rlo;
               q[dhi] = rhi;
             } else {
-              const int page = epi.page_table[pos / epi.page_size];
+              const int page = row_pages(m)[pos / epi.page_size];
               half* kp = epi.kcache +
                          ((static_cast<size_t>(page) * epi.kv_heads + head) * epi.page_size + pos % epi.page_size) * hd;
               kp[dlo] = __float2half_rn(rlo);
@@ -487,8 +490,8 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
           for (int j = 0; j < 2; ++j) {
             const int m = nt * 8 + 2 * t + j;
             if (m >= M) continue;
-            const int pos = pos0 + m;
-            const int page = epi.page_table[pos / epi.page_size];
+            const int pos = row_pos(m);
+            const int page = row_pages(m)[pos / epi.page_size];
             half* vp = epi.vcache +
                        ((static_cast<size_t>(page) * epi.kv_heads + head) * epi.page_size + pos % epi.page_size) * hd;
             vp[d0] = __float2half_rn(acc[nt][j]);

@@ -119,6 +119,9 @@ struct Epi {
   int page_size = 16;
   int heads = 0, kv_heads = 0, head_dim = 0;
   const half* rope = nullptr;   // (max_len, head_dim) fp16 [cos | sin]
+  // QKV of a multi-sequence pass: per activation row {position, offset of
+  // its sequence's row of the page table} (null: pos0 + m, offset 0)
+  const int2* rows = nullptr;
   // RESID
   ActIn res;
   float* ss_out = nullptr;      // (M, n_tiles) partial sums of squares
@@ -168,6 +171,14 @@ constexpr int kMaxDenseRows = 256;
 // CTAs along the output rows (argmax partials of a LOGITS launch).
 int gemv_out_blocks(const QTile& w);
 
+// One sequence of a multi-sequence attention pass: activation rows m0 ..
+// m0 + n_tok - 1 at positions pos0 .., its pages at page_table + pt_off; its
+// scores row groups start at g0 and its P.V groups at p0 (no group holds
+// rows of two sequences, so a block reads one sequence's K / V).
+struct AttnSeq {
+  int m0, n_tok, pos0, pt_off, g0, p0;
+};
+
 struct AttnArgs {
   const float* q = nullptr;  int ldq = 0;
   const half* kcache = nullptr;
@@ -188,6 +199,11 @@ struct AttnArgs {
   // group) per span, and a self-resetting ticket per (slice, kv head, group)
   float* pv_part = nullptr;
   unsigned* pv_ticket = nullptr;
+  // multi-sequence pass (null: one sequence of M rows at *pos): the
+  // sequences (device, written before the launch) and the pass's total
+  // scores row groups and P.V groups
+  const AttnSeq* seqs = nullptr;
+  int n_seq = 0, n_rg = 0, n_pg = 0;
 };
 // Positions one block of the split P.V pass takes (a context longer than one
 // split span is spread over blocks), and the split spans of max_ctx positions.

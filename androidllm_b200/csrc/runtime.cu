@@ -243,6 +243,9 @@ struct Work {
   int attn_ctx = 0;       // capacity of the attention scratch (positions)
   int score_ld = 0;       // row stride of the score scratch
   int* pinned = nullptr;  // host staging for small copies
+  // multi-sequence passes: per row {position, page-table offset}, per sequence AttnSeq
+  int2* rows = nullptr;
+  AttnSeq* seqs = nullptr;
 };
 
 int dev_alloc(void** p, size_t bytes) {
@@ -300,6 +303,8 @@ struct alm_model {
   int vocab_offset = 0, vocab_local = 0;
   bool tp_need_logits = false;   // gather the full logits after the head
   std::vector<DenseLayer> dense;   // per layer; qkv null: no dense copies
+  // the forward being enqueued is a multi-sequence pass (ws.rows / ws.seqs)
+  int ms_n_seq = 0, ms_n_rg = 0, ms_n_pg = 0;
   PrefillWork pf;
   // attention passes enqueued now are known to fit one P.V span: launch the
   // unsplit P.V kernel even when the KV capacity is longer (speed only: the
@@ -309,7 +314,10 @@ struct alm_model {
 
 struct alm_kv {
   alm_ctx* ctx = nullptr;
+  // n_slots sequences of max_len positions each; slot s's page numbers are
+  // row s of the page table (pages_per_slot entries)
   int n_layers = 0, kv_heads = 0, head_dim = 0, page_size = 16, n_pages = 0, max_len = 0;
+  int n_slots = 1, pages_per_slot = 0;
   size_t layer_elems = 0;
   half* k = nullptr;
   half* v = nullptr;
@@ -563,7 +571,9 @@ int ensure_attn(alm_model* m, int max_ctx) {
   Work& ws = m->ws;
   if (max_ctx <= ws.attn_ctx) return ALM_OK;
   const int gq = m->cfg.heads / m->cfg.kv_heads;
-  const int n_rg = (kMaxRows * gq + kAttnRows - 1) / kAttnRows;
+  // row groups of the largest pass; a multi-sequence pass starts a group per
+  // sequence, which adds at most one per sequence
+  const int n_rg = (kMaxRows * gq + kAttnRows - 1) / kAttnRows + kMaxRows;
   const int cap = (max_ctx + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
   dev_free(ws.scores);
   dev_free(ws.stats);
@@ -693,6 +703,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   e.kv_heads = c.kv_heads;
   e.head_dim = c.head_dim;
   e.rope = m->rope;
+  if (m->ms_n_seq) e.rows = ws.rows;
   ALM_LAUNCH(launch_gemv(L.qkv->t, in, M, EPI_QKV, e, io, scr, pdl, st));
   prof_mark(ALM_OP_QKV, M);
 
@@ -716,6 +727,13 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
   a.ldc = qdim;
   a.pv_part = m->pv_one_span ? nullptr : ws.pv_part;
   a.pv_ticket = ws.pv_ticket;
+  if (m->ms_n_seq) {
+    a.seqs = ws.seqs;
+    a.n_seq = m->ms_n_seq;
+    a.n_rg = m->ms_n_rg;
+    a.n_pg = m->ms_n_pg;
+    a.pv_part = nullptr;
+  }
   if (m->ctx->attn_decode && attn_decode_ok(a)) {
     // single-row decode: scores, statistics and P.V in one kernel (bit-identical)
     ALM_LAUNCH(launch_attn_decode(a, pdl, st));
@@ -965,9 +983,10 @@ int build_cluster_fwd(alm_model* m) {
 // Embedding (tokens already in ws.tokens, position in ws.pos) -> all layers ->
 // final norms -> head.
 int enqueue_forward(alm_model* m, alm_kv* kv, int M, bool head, bool pdl) {
-  if (m->ctx->persist && m->fwd_grid > 0 && M <= kPersistRows) return enqueue_forward_persistent(m, kv, M, head);
+  if (m->ctx->persist && m->fwd_grid > 0 && M <= kPersistRows && m->ms_n_seq == 0)
+    return enqueue_forward_persistent(m, kv, M, head);
   Work& ws = m->ws;
-  if (M == 1 && m->ctx->cluster && m->cf_ok) {
+  if (M == 1 && m->ctx->cluster && m->cf_ok && m->ms_n_seq == 0) {
     // embedding and every layer in one cluster launch, then the final norm
     // and the head over the whole GPU
     ALM_LAUNCH(launch_cluster_fwd(forward_params(m, kv, 1, false), m->cf_smem, pdl, m->ctx->stream));
@@ -1066,7 +1085,7 @@ int ensure_prefill(alm_model* m, int max_ctx) {
 // over the chunk's rows.  Only the KV cache is kept; the last layer stops
 // after its KV write.  The arithmetic is the M <= 16 path's, so the cache
 // equals a 16-row-chunk prefill up to the matmuls' fp32 summation order.
-int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0) {
+int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0, int slot) {
   const alm_model_config& c = m->cfg;
   PrefillWork& pf = m->pf;
   Work& ws = m->ws;
@@ -1118,7 +1137,7 @@ int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0) {
     ra.ldq = qd;
     ra.kcache = kv->k + static_cast<size_t>(li) * kv->layer_elems;
     ra.vcache = kv->v + static_cast<size_t>(li) * kv->layer_elems;
-    ra.page_table = kv->page_table;
+    ra.page_table = kv->page_table + static_cast<size_t>(slot) * kv->pages_per_slot;
     ra.page_size = kv->page_size;
     ALM_LAUNCH(launch_pf_rope_kv(ra, M, pdl, st));
     AttnArgs a;
@@ -1126,7 +1145,7 @@ int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0) {
     a.ldq = qd;
     a.kcache = ra.kcache;
     a.vcache = ra.vcache;
-    a.page_table = kv->page_table;
+    a.page_table = ra.page_table;
     a.page_size = kv->page_size;
     a.heads = c.heads;
     a.kv_heads = c.kv_heads;
@@ -1554,7 +1573,7 @@ int alm_model_destroy(alm_model* m) {
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
                   (void*)w.scores, (void*)w.stats, (void*)w.pv_part, (void*)w.pv_ticket,
                   (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
-                  (void*)w.logits_local, (void*)w.logits_gather})
+                  (void*)w.logits_local, (void*)w.logits_gather, (void*)w.rows, (void*)w.seqs})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
   dev_free(m->fwd_layers);
@@ -1778,6 +1797,8 @@ int alm_model_finalize(alm_model* m) {
   if (!ws.x0) {
     const int H = c.hidden, ht = n_h_tiles(m), qd = c.heads * c.head_dim;
     ALM_TRY(dev_alloc_t(&ws.tokens, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.rows, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.seqs, kMaxRows));
     ALM_TRY(dev_alloc_t(&ws.pos, 1));
     ALM_TRY(dev_alloc_t(&ws.err, 1));
     ALM_CUDA(cudaMemset(ws.err, 0, sizeof(int)));
@@ -1829,8 +1850,13 @@ int alm_model_finalize(alm_model* m) {
 
 // ---- KV ------------------------------------------------------------------------
 int alm_kv_create(alm_ctx* ctx, const alm_model* m, int max_len, int page_size, alm_kv** out) {
+  return alm_kv_create_slots(ctx, m, 1, max_len, page_size, out);
+}
+
+int alm_kv_create_slots(alm_ctx* ctx, const alm_model* m, int n_slots, int max_len, int page_size, alm_kv** out) {
   ALM_REQ(ctx && m && out, "null argument");
   ALM_REQ(max_len > 0 && page_size > 0 && page_size <= 256, "invalid kv geometry");
+  ALM_REQ(n_slots >= 1 && n_slots <= 4096, "n_slots must be in 1..4096");
   DeviceGuard g(ctx->device);
   auto* kv = new alm_kv();
   kv->ctx = ctx;
@@ -1838,7 +1864,9 @@ int alm_kv_create(alm_ctx* ctx, const alm_model* m, int max_len, int page_size, 
   kv->kv_heads = m->cfg.kv_heads;
   kv->head_dim = m->cfg.head_dim;
   kv->page_size = page_size;
-  kv->n_pages = (max_len + page_size - 1) / page_size;
+  kv->n_slots = n_slots;
+  kv->pages_per_slot = (max_len + page_size - 1) / page_size;
+  kv->n_pages = n_slots * kv->pages_per_slot;
   kv->max_len = max_len;
   kv->layer_elems = static_cast<size_t>(kv->n_pages) * page_size * kv->kv_heads * kv->head_dim;
   int rc = dev_alloc_t(&kv->k, kv->layer_elems * kv->n_layers);
@@ -1879,9 +1907,10 @@ int alm_kv_zero(alm_kv* kv) {
   return ALM_OK;
 }
 
-static int kv_copy(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host,
+static int kv_copy(alm_kv* kv, int slot, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host,
                    const uint16_t* k_in, const uint16_t* v_in) {
   ALM_REQ(kv, "null kv");
+  ALM_REQ(slot >= 0 && slot < kv->n_slots, "slot out of range");
   ALM_REQ(layer >= 0 && layer < kv->n_layers && pos0 >= 0 && n >= 0 && pos0 + n <= kv->max_len,
           "kv range out of bounds");
   DeviceGuard g(kv->ctx->device);
@@ -1896,7 +1925,8 @@ static int kv_copy(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uin
     for (int i = 0; i < n; ++i) {
       const int p = pos0 + i;
       for (int h = 0; h < kv->kv_heads; ++h) {
-        half* src = base + ((static_cast<size_t>(pt[p / kv->page_size]) * kv->kv_heads + h) * kv->page_size +
+        const int page = pt[static_cast<size_t>(slot) * kv->pages_per_slot + p / kv->page_size];
+        half* src = base + ((static_cast<size_t>(page) * kv->kv_heads + h) * kv->page_size +
                             p % kv->page_size) * kv->head_dim;
         const size_t off = (static_cast<size_t>(i) * kv->kv_heads + h) * kv->head_dim;
         if (out) ALM_CUDA(cudaMemcpy(out + off, src, row, cudaMemcpyDeviceToHost));
@@ -1908,10 +1938,26 @@ static int kv_copy(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uin
 }
 
 int alm_kv_read(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host) {
-  return kv_copy(kv, layer, pos0, n, k_host, v_host, nullptr, nullptr);
+  return kv_copy(kv, 0, layer, pos0, n, k_host, v_host, nullptr, nullptr);
 }
 int alm_kv_write(alm_kv* kv, int layer, int pos0, int n, const uint16_t* k_host, const uint16_t* v_host) {
-  return kv_copy(kv, layer, pos0, n, nullptr, nullptr, k_host, v_host);
+  return kv_copy(kv, 0, layer, pos0, n, nullptr, nullptr, k_host, v_host);
+}
+int alm_kv_read_slot(alm_kv* kv, int slot, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host) {
+  return kv_copy(kv, slot, layer, pos0, n, k_host, v_host, nullptr, nullptr);
+}
+
+int alm_kv_set_pages(alm_kv* kv, int slot, const int32_t* pages_host, int n) {
+  ALM_REQ(kv && pages_host, "null argument");
+  ALM_REQ(slot >= 0 && slot < kv->n_slots, "slot out of range");
+  ALM_REQ(n >= 1 && n <= kv->pages_per_slot, "page count out of range");
+  for (int i = 0; i < n; ++i)
+    ALM_REQ(pages_host[i] >= 0 && pages_host[i] < kv->n_pages, "page number out of range");
+  DeviceGuard g(kv->ctx->device);
+  ALM_CUDA(cudaStreamSynchronize(kv->ctx->stream));
+  ALM_CUDA(cudaMemcpy(kv->page_table + static_cast<size_t>(slot) * kv->pages_per_slot, pages_host, n * sizeof(int),
+                      cudaMemcpyHostToDevice));
+  return ALM_OK;
 }
 
 // ---- forward --------------------------------------------------------------------
@@ -2148,9 +2194,14 @@ int alm_accept(alm_ctx* ctx, const uint16_t* target_logits_host, const float* dr
 
 int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
                      const double* uniforms_host, int32_t* out_host) {
+  return alm_model_sample_rows(m, 0, rows, temperature, top_p, min_p, uniforms_host, out_host);
+}
+
+int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, float top_p, float min_p,
+                          const double* uniforms_host, int32_t* out_host) {
   ALM_TRY(check_ready(m));
   ALM_REQ(out_host && (uniforms_host || !(temperature > 0.f)), "null argument");
-  ALM_REQ(rows >= 1 && rows <= kMaxRows, "rows must be in 1..16");
+  ALM_REQ(row0 >= 0 && rows >= 1 && row0 + rows <= kMaxRows, "rows must lie in 0..15");
   ALM_REQ(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
   ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
   DeviceGuard g(m->ctx->device);
@@ -2164,15 +2215,84 @@ int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, flo
     rc = fail(ALM_ERR_CUDA, "upload failed");
   if (rc == ALM_OK) {
     const float t = temperature > 0.f ? std::max(temperature, 1e-9f) : 0.f;
-    const cudaError_t e = launch_sample(sample_args(m, t, top_p, min_p, du, nullptr, 0), rows, false, st);
+    SampleArgs sa = sample_args(m, t, top_p, min_p, du, nullptr, 0);
+    sa.logits += static_cast<size_t>(row0) * sa.ld;
+    sa.out += row0;
+    const cudaError_t e = launch_sample(sa, rows, false, st);
     if (e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("sample: ") + cudaGetErrorString(e));
   }
-  if (rc == ALM_OK && (cudaMemcpyAsync(out_host, m->ws.argmax, rows * sizeof(int), cudaMemcpyDeviceToHost, st) !=
+  if (rc == ALM_OK && (cudaMemcpyAsync(out_host, m->ws.argmax + row0, rows * sizeof(int), cudaMemcpyDeviceToHost,
+                                       st) !=
                            cudaSuccess ||
                        cudaStreamSynchronize(st) != cudaSuccess))
     rc = fail(ALM_ERR_CUDA, "sample failed");
   dev_free(du);
   return rc;
+}
+
+// Check and upload a multi-sequence pass's rows and sequences (ws.rows,
+// ws.seqs) and mark the model's next enqueue as that pass; *M_out = rows.
+static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
+                      const int32_t* pos0, int* M_out) {
+  ALM_REQ(!m->tp, "multi-sequence passes run on whole models");
+  ALM_REQ(n_seq >= 1 && n_seq <= kMaxRows, "n_seq must be in 1..16");
+  ALM_REQ(kv->n_layers == m->cfg.layers && kv->kv_heads == m->cfg.kv_heads && kv->head_dim == m->cfg.head_dim,
+          "kv cache shape mismatch");
+  const int gq = m->cfg.heads / m->cfg.kv_heads;
+  std::vector<int2> rows;
+  std::vector<AttnSeq> seqs(n_seq);
+  int g = 0, pg = 0;
+  for (int s = 0; s < n_seq; ++s) {
+    ALM_REQ(slots[s] >= 0 && slots[s] < kv->n_slots, "slot out of range");
+    for (int t = 0; t < s; ++t) ALM_REQ(slots[t] != slots[s], "two sequences of one pass share a slot");
+    ALM_REQ(n_tok[s] >= 1 && pos0[s] >= 0, "every sequence needs rows at non-negative positions");
+    ALM_REQ(static_cast<long long>(pos0[s]) + n_tok[s] <= kv->max_len &&
+                static_cast<long long>(pos0[s]) + n_tok[s] <= m->cfg.max_len,
+            "pos out of kv cache or rope table range");
+    ALM_REQ(static_cast<int>(rows.size()) + n_tok[s] <= kMaxRows, "at most 16 rows per pass");
+    const int off = slots[s] * kv->pages_per_slot;
+    seqs[s] = AttnSeq{static_cast<int>(rows.size()), n_tok[s], pos0[s], off, g, pg};
+    for (int t = 0; t < n_tok[s]; ++t) rows.push_back(make_int2(pos0[s] + t, off));
+    g += (n_tok[s] * gq + kAttnRows - 1) / kAttnRows;
+    pg += (n_tok[s] * gq + kPvRows - 1) / kPvRows;
+  }
+  ALM_TRY(ensure_attn(m, kv->max_len));
+  ALM_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  ALM_CUDA(cudaMemcpy(m->ws.rows, rows.data(), rows.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  ALM_CUDA(cudaMemcpy(m->ws.seqs, seqs.data(), seqs.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice));
+  ALM_TRY(set_pos(m, 0));
+  m->ms_n_seq = n_seq;
+  m->ms_n_rg = g;
+  m->ms_n_pg = pg;
+  *M_out = static_cast<int>(rows.size());
+  return ALM_OK;
+}
+
+static void clear_seqs(alm_model* m) { m->ms_n_seq = m->ms_n_rg = m->ms_n_pg = 0; }
+
+// Several sequences in one pass: sequence s has n_tok[s] rows (its tokens
+// in order in tokens_host) at positions pos0[s] .. of KV slot slots[s].  The
+// weights stream once for all rows; every row's result equals its
+// sequence's own forward (rows never mix in a reduction).
+int alm_forward_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
+                     const int32_t* pos0, const int32_t* tokens_host, float* logits_host, int32_t* argmax_host) {
+  ALM_TRY(check_ready(m));
+  ALM_REQ(kv && slots && n_tok && pos0 && tokens_host, "null argument");
+  ALM_TRY(check_layers(m));
+  DeviceGuard gd(m->ctx->device);
+  int M = 0;
+  ALM_TRY(stage_seqs(m, kv, n_seq, slots, n_tok, pos0, &M));
+  int rc = ALM_OK;
+  if (cudaMemcpy(m->ws.tokens, tokens_host, M * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    rc = fail(ALM_ERR_CUDA, "token upload failed");
+  const bool head = logits_host != nullptr || argmax_host != nullptr;
+  m->tp_need_logits = logits_host != nullptr;
+  if (rc == ALM_OK) rc = enqueue_forward(m, kv, M, head, m->ctx->pdl);
+  clear_seqs(m);
+  m->tp_need_logits = false;
+  ALM_TRY(rc);
+  ALM_TRY(sync_and_check(m));
+  return copy_logits_out(m, M, logits_host, argmax_host);
 }
 
 // Fill the KV cache for positions pos0 .. pos0 + n - 1 from the tokens
@@ -2181,7 +2301,12 @@ int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, flo
 // row-layout copies (a tail of at most 16 rows, or any chunk without them,
 // through the M <= 16 forward).  No logits.
 int alm_prefill(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int n, int pos0) {
+  return alm_prefill_slot(m, kv, 0, tokens_host, n, pos0);
+}
+
+int alm_prefill_slot(alm_model* m, alm_kv* kv, int slot, const int32_t* tokens_host, int n, int pos0) {
   ALM_TRY(check_ready(m));
+  ALM_REQ(kv && slot >= 0 && slot < kv->n_slots, "slot out of range");
   ALM_REQ(tokens_host && kv, "null argument");
   ALM_TRY(check_layers(m));
   ALM_REQ(n >= 1, "n must be positive");
@@ -2200,7 +2325,17 @@ int alm_prefill(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int n, int
     ALM_TRY(set_pos(m, p));
     if (rows > kMaxRows) {
       ALM_CUDA(cudaMemcpyAsync(m->pf.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice, st));
-      ALM_TRY(enqueue_prefill_dense(m, kv, rows, p));
+      ALM_TRY(enqueue_prefill_dense(m, kv, rows, p, slot));
+    } else if (slot != 0) {
+      // a short chunk of another slot: a one-sequence multi-sequence pass
+      int M = 0;
+      ALM_TRY(stage_seqs(m, kv, 1, &slot, &rows, &p, &M));
+      int rc = ALM_OK;
+      if (cudaMemcpy(m->ws.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(ALM_ERR_CUDA, "token upload failed");
+      if (rc == ALM_OK) rc = enqueue_forward(m, kv, rows, false, m->ctx->pdl);
+      clear_seqs(m);
+      ALM_TRY(rc);
     } else {
       ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice, st));
       m->pv_one_span = p + rows <= kPvSplit;

@@ -84,6 +84,25 @@ class LayerStreamingEngine:
         self._prefix_kv = os.environ.get("ANDROIDLLM_PREFIX_KV", "1") not in ("0", "false", "")
 
     # -- caches --------------------------------------------------------------------
+    def batch_runner(self, slots=None):
+        """The device side of batched sessions (androidllm_b200.batching):
+        slot KV caches for ``slots`` concurrent sessions (default
+        ANDROIDLLM_BATCH_MAX, else 8), created on first use."""
+        if getattr(self, "_batch", None) is None:
+            from .batching import BatchRunner
+            n = int(slots or os.environ.get("ANDROIDLLM_BATCH_MAX", "8"))
+            self._batch = BatchRunner(self, slots=n)
+        return self._batch
+
+    def generate_batch(self, prompts, max_new_tokens=64, temperature=0.8, top_p=0.9, min_p=0.0, seeds=None,
+                       stop_ids=()):
+        """Generate for several prompts at once (every session advances in
+        each step, the weights stream once per pass for all of them); each
+        result equals generate() for that prompt alone (with seeds[i] as the
+        engine's seed when sampling)."""
+        from .batching import run_batch
+        return run_batch(self, prompts, max_new_tokens, temperature, top_p, min_p, seeds, stop_ids)
+
     def _kv_capacity(self):
         return self.ctx_len + self.spec_k + 1
 
@@ -299,6 +318,9 @@ class LayerStreamingEngine:
         return generated
 
     def close(self):
+        if getattr(self, "_batch", None) is not None:
+            self._batch.close()
+            self._batch = None
         if self._spec is not None:
             self._spec.close()
             self._spec = None

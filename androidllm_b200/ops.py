@@ -318,12 +318,13 @@ class DeviceModel:
         check(lib.alm_model_dense_prefill(self.h, ctypes.byref(v)))
         return bool(v.value)
 
-    def prefill(self, kv, tokens, pos0=0):
-        """Fill kv for positions pos0 .. pos0 + len(tokens) - 1 (alm_prefill):
-        the prompt's forwards without logits, in chunks of up to 256 rows."""
+    def prefill(self, kv, tokens, pos0=0, slot=0):
+        """Fill kv (slot ``slot``) for positions pos0 .. pos0 + len(tokens) - 1
+        (alm_prefill_slot): the prompt's forwards without logits, in chunks of
+        up to 256 rows."""
         tok = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
         if tok.size:
-            check(lib.alm_prefill(self.h, kv.h, ptr(tok), int(tok.size), int(pos0)))
+            check(lib.alm_prefill_slot(self.h, kv.h, int(slot), ptr(tok), int(tok.size), int(pos0)))
 
     def uses_cluster_forward(self):
         """Whether single-row forwards run as the 16-CTA cluster kernel."""
@@ -385,6 +386,31 @@ class DeviceModel:
         am = np.empty(rows, np.int32) if argmax else None
         check(lib.alm_forward(self.h, kv.h, ptr(tok), rows, int(pos0), ptr(lg), ptr(am)))
         return lg, am
+
+    def sample_rows(self, row0, rows, temperature, top_p=1.0, min_p=0.0, uniforms=None):
+        """alm_model_sample_rows: sample rows row0 .. row0 + rows - 1 of the last
+        forward's logits (one sequence of a multi-sequence pass)."""
+        u = np.ascontiguousarray(np.zeros(rows) if uniforms is None else uniforms, dtype=np.float64).reshape(-1)
+        out = np.empty(rows, np.int32)
+        check(lib.alm_model_sample_rows(self.h, int(row0), int(rows), float(temperature), float(top_p),
+                                        float(min_p), ptr(u), ptr(out)))
+        return out
+
+    def forward_seqs(self, kv, seqs, logits=False, argmax=True):
+        """One pass over several sequences (alm_forward_seqs): ``seqs`` is a
+        list of (slot, tokens, pos0); returns per-sequence lists of logits rows
+        (or None) and argmax rows (or None)."""
+        slots = np.array([int(s) for s, _, _ in seqs], np.int32)
+        n_tok = np.array([len(t) for _, t, _ in seqs], np.int32)
+        pos = np.array([int(p) for _, _, p in seqs], np.int32)
+        tok = np.ascontiguousarray(np.concatenate([np.asarray(t, np.int32).reshape(-1) for _, t, _ in seqs]))
+        rows = tok.size
+        lg = np.empty((rows, self.canon["vocab"]), np.float32) if logits else None
+        am = np.empty(rows, np.int32) if argmax else None
+        check(lib.alm_forward_seqs(self.h, kv.h, len(seqs), ptr(slots), ptr(n_tok), ptr(pos), ptr(tok), ptr(lg),
+                                   ptr(am)))
+        cuts = np.cumsum(n_tok)[:-1]
+        return (np.split(lg, cuts) if logits else None), (np.split(am, cuts) if argmax else None)
 
     def sample(self, rows, temperature, top_p=1.0, min_p=0.0, uniforms=None):
         """alm_model_sample: sample the first rows of the last forward's logits."""
@@ -459,25 +485,36 @@ def read_layer(model_dir, man, i):
 
 
 class DeviceKV:
-    """Paged fp16 KV cache of every layer of one model (alm_kv)."""
+    """Paged fp16 KV cache of every layer of one model (alm_kv): ``slots``
+    sequences of ``max_len`` positions each (single-sequence calls use slot 0)."""
 
-    def __init__(self, model, max_len, page_size=16):
+    def __init__(self, model, max_len, page_size=16, slots=1):
         h = ctypes.c_void_p()
-        check(lib.alm_kv_create(model.ctx.h, model.h, int(max_len), int(page_size), ctypes.byref(h)))
+        if slots == 1:
+            check(lib.alm_kv_create(model.ctx.h, model.h, int(max_len), int(page_size), ctypes.byref(h)))
+        else:
+            check(lib.alm_kv_create_slots(model.ctx.h, model.h, int(slots), int(max_len), int(page_size),
+                                          ctypes.byref(h)))
         self.h = h
         self.model = model
         self.max_len = int(max_len)
         self.page_size = int(page_size)
+        self.slots = int(slots)
 
     def zero(self):
         check(lib.alm_kv_zero(self.h))
 
-    def read(self, layer, pos0, n):
+    def read(self, layer, pos0, n, slot=0):
         c = self.model.canon
         shape = (n, c["kv_heads"], c["head_dim"])
         k, v = np.empty(shape, np.float16), np.empty(shape, np.float16)
-        check(lib.alm_kv_read(self.h, int(layer), int(pos0), int(n), ptr(k), ptr(v)))
+        check(lib.alm_kv_read_slot(self.h, int(slot), int(layer), int(pos0), int(n), ptr(k), ptr(v)))
         return k, v
+
+    def set_pages(self, slot, pages):
+        """Map slot's first len(pages) pages to the given physical pages."""
+        pg = np.ascontiguousarray(pages, dtype=np.int32).reshape(-1)
+        check(lib.alm_kv_set_pages(self.h, int(slot), ptr(pg), int(pg.size)))
 
     def write(self, layer, pos0, k, v):
         k, v = _f16(k), _f16(v)

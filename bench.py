@@ -49,6 +49,13 @@ WORKLOADS = {
     "toy": ("toy", dict(attn_bits=4, mlp_bits=4, block=64, embed_bits=0), None, None),
 }
 TP_WORKLOAD = "qwen2.5-7b"
+# continuous batching: sessions per GPU, prompt and output length ranges,
+# temperature (the 64-sequence / 8-GPU configuration, 8 per GPU)
+BATCH_WORKLOAD = "qwen2.5-1.5b-batch"
+BATCH_SESSIONS = 8
+BATCH_PROMPT = (128, 1024)
+BATCH_OUTPUT = (64, 512)
+BATCH_TEMPERATURE = 0.8
 TP_SPEC_K = 6
 TP_PROMPT_LEN = 2048
 
@@ -552,6 +559,93 @@ def run_ours(args):
 # --------------------------------------------------------------------------
 # tensor-parallel arm: the Qwen2.5-7B-shaped target split over the ranks
 # --------------------------------------------------------------------------
+def run_batch(args):
+    """Continuous batching of speculative sessions (one process per GPU, data
+    parallel): BATCH_SESSIONS sessions per GPU with seeded prompt lengths in
+    BATCH_PROMPT and output lengths in BATCH_OUTPUT, k = 4, T = 0.8 with
+    seeded per-session uniforms, paged KV of 16-position pages, all sessions
+    advanced together (LayerStreamingEngine.generate_batch).  value =
+    generated tokens of all ranks / the slowest rank's time; the same
+    sessions one after the other through generate() give the sequential
+    figure it is compared with."""
+    rank, world, local = dist_env()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    if rank == 0:
+        tdir, ddir = prepare_models("qwen2.5-1.5b")
+    if dist is not None:
+        dist.barrier()
+        tdir, ddir = prepare_models("qwen2.5-1.5b")
+    os.environ["ANDROIDLLM_MAX_CTX"] = str(BATCH_PROMPT[1] + BATCH_OUTPUT[1] + 2 * (SPEC_K + 1))
+    from androidllm_b200.engine import LayerStreamingEngine
+    eng = LayerStreamingEngine(tdir, draft_dir=ddir, spec_k=SPEC_K, device=local)
+    eng.batch_runner(slots=BATCH_SESSIONS)
+    rng = np.random.default_rng(1000 + rank)
+    V = eng.canon["vocab"]
+    prompts = [rng.integers(0, V, int(rng.integers(BATCH_PROMPT[0], BATCH_PROMPT[1] + 1))).tolist()
+               for _ in range(BATCH_SESSIONS)]
+    outs = [int(rng.integers(BATCH_OUTPUT[0], BATCH_OUTPUT[1] + 1)) for _ in range(BATCH_SESSIONS)]
+    seeds = [10_000 * rank + i for i in range(BATCH_SESSIONS)]
+    # warm-up: a short batch (kernels, caches)
+    eng.generate_batch([p[:64] for p in prompts[:2]], max_new_tokens=8, temperature=BATCH_TEMPERATURE,
+                       seeds=seeds[:2])
+    clk = ClockSampler(local).__enter__()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    got = eng.generate_batch(prompts, max_new_tokens=outs, temperature=BATCH_TEMPERATURE, top_p=0.9,
+                             seeds=seeds)
+    secs = time.perf_counter() - t0
+    clk.__exit__(None, None, None)
+    tokens = sum(len(g) for g in got)
+    # the same sessions one at a time through generate() (the reference's
+    # scheduler visits one session per work unit): rank 0, first sessions
+    seq = None
+    if rank == 0 and not args.no_cpu_baseline:
+        n_seq = 2
+        t1 = time.perf_counter()
+        n_tok = 0
+        for i in range(n_seq):
+            n_tok += len(eng.generate(prompts[i], max_new_tokens=outs[i], temperature=BATCH_TEMPERATURE,
+                                      top_p=0.9))
+        seq = n_tok / (time.perf_counter() - t1)
+    if dist is not None:
+        import torch
+        t = torch.tensor([secs, float(tokens)], dtype=torch.float64, device=torch.device("cuda", local))
+        mx, sm = t.clone(), t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        secs, tokens = float(mx[0]), int(sm[1])
+    if rank == 0:
+        line = {
+            "metric": "continuous-batching spec-decode tokens/sec (k=4, T=0.8) at Qwen2.5-1.5B int4, "
+                      f"{BATCH_SESSIONS} sessions per GPU",
+            "value": round(tokens / secs, 2), "unit": "tokens/s", "n_gpus": world, "steps": 1, "warmup": 1,
+            "ms_per_step": round(secs * 1000.0, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": BATCH_WORKLOAD, "sessions_per_gpu": BATCH_SESSIONS,
+                       "prompt_len": list(BATCH_PROMPT), "output_len": list(BATCH_OUTPUT), "k": SPEC_K,
+                       "temperature": BATCH_TEMPERATURE, "top_p": 0.9, "kv_page": 16,
+                       "parallelism": f"dp{world}", "timed": "prefill + decode of every session, host-timed"},
+            "tokens": tokens, "seconds": round(secs, 3),
+            "sequential_tokens_per_s": None if seq is None else round(seq, 2),
+            "gpu_launches": None,
+            "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_tp(args):
     """Speculative decoding (k = 6, greedy) of the Qwen2.5-7B-shaped target
     (int4 attention / int8 MLP / int8 head, block 64) split over the ranks
@@ -951,7 +1045,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1024)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen2.5-1.5b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [BATCH_WORKLOAD], default="qwen2.5-1.5b")
     ap.add_argument("--cpu-samples", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", type=int, default=0,
@@ -990,6 +1084,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == BATCH_WORKLOAD:
+        return run_batch(args)
     if args.workload == TP_WORKLOAD or dist_env()[1] > 1:
         return run_tp(args)
     return run_ours(args)

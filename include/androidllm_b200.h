@@ -200,6 +200,17 @@ ALM_API int alm_kv_zero(alm_kv* kv);
 ALM_API int alm_kv_read(alm_kv* kv, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host);
 /* Copy (n, kv_heads, head_dim) fp16 rows into the cache at [pos0, pos0+n). */
 ALM_API int alm_kv_write(alm_kv* kv, int layer, int pos0, int n, const uint16_t* k_host, const uint16_t* v_host);
+/* A cache of n_slots sequences (one per concurrent session of
+ * androidllm/batching.py:32-149) of max_len positions each, in pages of
+ * page_size positions; slot s starts on pages s * ceil(max_len / page_size)..
+ * Single-sequence calls use slot 0. */
+ALM_API int alm_kv_create_slots(alm_ctx* ctx, const alm_model* m, int n_slots, int max_len, int page_size,
+                                alm_kv** out);
+/* alm_kv_read of slot `slot`. */
+ALM_API int alm_kv_read_slot(alm_kv* kv, int slot, int layer, int pos0, int n, uint16_t* k_host, uint16_t* v_host);
+/* Map the first n pages of slot `slot` to physical pages pages_host[0..n) of
+ * the cache (any of its n_slots * pages-per-slot pages). */
+ALM_API int alm_kv_set_pages(alm_kv* kv, int slot, const int32_t* pages_host, int n);
 
 /* ---- forward ------------------------------------------------------------------ */
 /* Replaces androidllm_rs/src/lib.rs:226 layer_forward (and llama.py:96-128):
@@ -250,16 +261,30 @@ ALM_API int alm_accept(alm_ctx* ctx, const uint16_t* target_logits_host, const f
  * (alm_forward with a head) without copying them to the host. */
 ALM_API int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
                        const double* uniforms_host, int32_t* out_host);
+/* alm_model_sample on rows row0 .. row0 + rows - 1 of the last logits (one
+ * sequence of a multi-sequence pass). */
+ALM_API int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, float top_p, float min_p,
+                                  const double* uniforms_host, int32_t* out_host);
 /* Embedding + every layer + final norm + head for tokens at positions
  * pos0..pos0+rows-1 (androidllm/engine.py:255-286 without sampling). */
 ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int rows, int pos0,
                 float* logits_host, int32_t* argmax_host);
+/* Several sequences in one forward (batched sessions; the reference steps
+ * them one at a time, androidllm/batching.py:200-272): sequence s has
+ * n_tok[s] consecutive rows of tokens_host at positions pos0[s].. of KV slot
+ * slots[s] (distinct slots, at most 16 rows in all).  Logits / argmax rows
+ * follow tokens_host; each equals its sequence's own alm_forward. */
+ALM_API int alm_forward_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
+                             const int32_t* pos0, const int32_t* tokens_host, float* logits_host,
+                             int32_t* argmax_host);
 /* Prompt prefill: fills the KV cache for positions pos0..pos0+n-1 from the
  * tokens, no logits.  Replaces the per-token forwards of the prompt in
  * androidllm/engine.py:345-361.  Chunks of up to 256 rows run every
  * projection through the dense tcgen05 path when the model keeps row-layout
  * copies (alm_model_dense_prefill), the rest in forwards of up to 16 rows. */
 ALM_API int alm_prefill(alm_model* m, alm_kv* kv, const int32_t* tokens_host, int n, int pos0);
+/* alm_prefill into KV slot `slot` (alm_kv_create_slots). */
+ALM_API int alm_prefill_slot(alm_model* m, alm_kv* kv, int slot, const int32_t* tokens_host, int n, int pos0);
 /* Whether models created on this context from now on keep row-layout copies
  * of their int4 / int8 (64-column block) projections for alm_prefill
  * (default on; ALM_DENSE_PREFILL=0 turns the default off).  The copies take
