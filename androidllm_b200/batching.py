@@ -96,10 +96,35 @@ class BatchRunner:
         if plain:
             self._plain_steps(plain)
 
-    def _pick(self, model, am, row0, rows, sess, draws):
-        if sess.temperature > 0:
-            return [int(t) for t in model.sample_rows(row0, rows, sess.temperature, sess.top_p, sess.min_p, draws)]
-        return [int(t) for t in am]
+    @staticmethod
+    def _picks(model, am, parts):
+        """The tokens of a pass's sequences: parts = [(session, rows, draws)]
+        in row order; greedy sessions take the pass's argmax rows, sampling
+        sessions the device sampler, one call per run of consecutive sessions
+        with the same settings."""
+        out, row0, i = [], 0, 0
+        while i < len(parts):
+            s, n, u = parts[i]
+            if not s.temperature > 0:
+                out.append([int(t) for t in am[i]])
+                row0 += n
+                i += 1
+                continue
+            j, rows, us = i, 0, []
+            key = (s.temperature, s.top_p, s.min_p)
+            while j < len(parts) and parts[j][0].temperature > 0 and \
+                    (parts[j][0].temperature, parts[j][0].top_p, parts[j][0].min_p) == key:
+                rows += parts[j][1]
+                us.append(parts[j][2])
+                j += 1
+            picks = model.sample_rows(row0, rows, s.temperature, s.top_p, s.min_p, np.concatenate(us))
+            k = 0
+            for p in parts[i:j]:
+                out.append([int(t) for t in picks[k:k + p[1]]])
+                k += p[1]
+            row0 += rows
+            i = j
+        return out
 
     def _plain_steps(self, sessions):
         dm = self.engine.dm
@@ -108,10 +133,10 @@ class BatchRunner:
             for s in group:
                 s._ensure_draws(1)
             _, am = dm.forward_seqs(self.tkv, [(s.slot, [s.token], s.pos) for s in group])
-            for r, s in enumerate(group):
-                tok = self._pick(dm, am[r], r, 1, s, s._draws(1))[0]
+            picks = self._picks(dm, am, [(s, 1, s._draws(1)) for s in group])
+            for s, p in zip(group, picks):
                 s._consume(1)
-                s._advance([tok], 0)
+                s._advance([p[0]], 0)
 
     def _spec_steps(self, sessions):
         e, d = self.engine, self.draft.dm
@@ -125,11 +150,13 @@ class BatchRunner:
             for i in range(0, len(sessions), MAX_PASS_ROWS):
                 group = sessions[i:i + MAX_PASS_ROWS]
                 _, am = d.forward_seqs(self.dkv, [(s.slot, [dtok[id(s)]], s.pos + j) for s in group])
-                for r, s in enumerate(group):
+                parts = []
+                for s in group:
                     u = s._draws(K)
-                    c = self._pick(d, am[r], r, 1, s, None if u is None else u[j:j + 1])[0]
-                    cands[id(s)].append(c)
-                    dtok[id(s)] = c
+                    parts.append((s, 1, None if u is None else u[j:j + 1]))
+                for s, p in zip(group, self._picks(d, am, parts)):
+                    cands[id(s)].append(p[0])
+                    dtok[id(s)] = p[0]
         e.stats["draft_tokens"] = e.stats.get("draft_tokens", 0) + K * len(sessions)
         # verify: k + 1 rows per session, as many sessions per pass as fit
         per = max(1, MAX_PASS_ROWS // (K + 1))
@@ -137,9 +164,11 @@ class BatchRunner:
         for i in range(0, len(sessions), per):
             group = sessions[i:i + per]
             _, am = dm.forward_seqs(self.tkv, [(s.slot, [s.token] + cands[id(s)], s.pos) for s in group])
-            for r, s in enumerate(group):
+            parts = []
+            for s in group:
                 u = s._draws(2 * K + 1)
-                picks = self._pick(dm, am[r], r * (K + 1), K + 1, s, None if u is None else u[K:])
+                parts.append((s, K + 1, None if u is None else u[K:]))
+            for s, picks in zip(group, self._picks(dm, am, parts)):
                 c = cands[id(s)]
                 emitted = []
                 for k in range(K):
@@ -441,19 +470,32 @@ class BatchScheduler:
 
 
 def run_batch(engine, prompts, max_new_tokens=64, temperature=0.0, top_p=0.9, min_p=0.0, seeds=None,
-              stop_ids=()):
-    """Generate for every prompt concurrently (no thread): all sessions
-    advance together until each is done.  Returns the token lists and frees
-    the slots."""
+              stop_ids=(), max_active=None):
+    """Generate for every prompt (no thread): at most ``max_active``
+    sessions (default: all) advance together; a finished session frees its
+    slot for the next prompt in line (continuous batching).  Returns the
+    token lists in prompt order and frees the slots."""
+    outs = _broadcast(max_new_tokens, len(prompts))
     sessions = [Session(engine, p, max_new_tokens=m, temperature=temperature, top_p=top_p, min_p=min_p,
                         stop_ids=stop_ids, seed=None if seeds is None else seeds[i])
-                for i, (p, m) in enumerate(zip(prompts, _broadcast(max_new_tokens, len(prompts))))]
+                for i, (p, m) in enumerate(zip(prompts, outs))]
     runner = engine.batch_runner()
+    cap = min(len(sessions), int(max_active or len(sessions)), runner.slots)
+    queue = deque(sessions)
+    active = []
     try:
-        active = list(sessions)
-        while active:
+        while queue or active:
+            while queue and len(active) < cap:
+                active.append(queue.popleft())
             res = advance(active)
-            active = [s for s, (fin, _) in zip(active, res) if not fin]
+            still = []
+            for s, (fin, _) in zip(active, res):
+                if fin:
+                    runner.release_slot(s.slot)
+                    s.slot = None
+                else:
+                    still.append(s)
+            active = still
     finally:
         for s in sessions:
             runner.release_slot(s.slot)

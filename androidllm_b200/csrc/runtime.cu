@@ -4,6 +4,8 @@
 
 #include <algorithm>
 #include <functional>
+#include <map>
+#include <tuple>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -246,6 +248,8 @@ struct Work {
   // multi-sequence passes: per row {position, page-table offset}, per sequence AttnSeq
   int2* rows = nullptr;
   AttnSeq* seqs = nullptr;
+  double* u_rows = nullptr;      // (kMaxRows) uniforms of alm_model_sample_rows
+  unsigned char* seq_host = nullptr;   // pinned staging of rows, sequences and tokens
 };
 
 int dev_alloc(void** p, size_t bytes) {
@@ -305,6 +309,10 @@ struct alm_model {
   std::vector<DenseLayer> dense;   // per layer; qkv null: no dense copies
   // the forward being enqueued is a multi-sequence pass (ws.rows / ws.seqs)
   int ms_n_seq = 0, ms_n_rg = 0, ms_n_pg = 0;
+  // captured multi-sequence passes: (kv, rows, sequences, row groups, P.V
+  // groups, head) -> graph; their inputs are device arrays, so a pass of the
+  // same shape replays the graph (cleared when the scratch is reallocated)
+  std::map<std::tuple<const alm_kv*, int, int, int, int, int>, cudaGraphExec_t> ms_graphs;
   PrefillWork pf;
   // attention passes enqueued now are known to fit one P.V span: launch the
   // unsplit P.V kernel even when the KV capacity is longer (speed only: the
@@ -370,6 +378,8 @@ size_t src_bytes(int bits, int rows, int k_pad) {
 // With mode 1, weights at least this large take the row layout (tcgen05
 // kernel); smaller ones keep the mma.sync tile layout.
 constexpr size_t kRowMinBytes = 4u << 20;
+// pinned staging of a multi-sequence pass: rows, sequences, tokens
+constexpr size_t kSeqStaging = kMaxRows * (sizeof(int2) + sizeof(AttnSeq) + sizeof(int));
 
 bool use_rows(const alm_ctx* ctx, int bits, int block, int n_rows, int in) {
   if ((bits != 4 && bits != 8) || block % 64 != 0 || ctx->tc == 0) return false;
@@ -570,6 +580,8 @@ int ensure_part(Work& ws, size_t need) {
 int ensure_attn(alm_model* m, int max_ctx) {
   Work& ws = m->ws;
   if (max_ctx <= ws.attn_ctx) return ALM_OK;
+  for (auto& kvg : m->ms_graphs) cudaGraphExecDestroy(kvg.second);   // they hold the old scratch
+  m->ms_graphs.clear();
   const int gq = m->cfg.heads / m->cfg.kv_heads;
   // row groups of the largest pass; a multi-sequence pass starts a group per
   // sequence, which adds at most one per sequence
@@ -1562,6 +1574,8 @@ int alm_model_destroy(alm_model* m) {
   }
   for (DenseLayer& D : m->dense) free_dense(D);
   free_prefill_work(m->pf);
+  for (auto& kvg : m->ms_graphs) cudaGraphExecDestroy(kvg.second);
+  m->ms_graphs.clear();
   alm_qweight_free(m->head);
   dev_free(m->rope);
   dev_free(m->embed_table);
@@ -1573,9 +1587,11 @@ int alm_model_destroy(alm_model* m) {
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
                   (void*)w.scores, (void*)w.stats, (void*)w.pv_part, (void*)w.pv_ticket,
                   (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
-                  (void*)w.logits_local, (void*)w.logits_gather, (void*)w.rows, (void*)w.seqs})
+                  (void*)w.logits_local, (void*)w.logits_gather, (void*)w.rows, (void*)w.seqs,
+                  (void*)w.u_rows})
     dev_free(p);
   if (w.pinned) cudaFreeHost(w.pinned);
+  if (w.seq_host) cudaFreeHost(w.seq_host);
   dev_free(m->fwd_layers);
   dev_free(m->fwd_bar);
   delete m;
@@ -1799,6 +1815,8 @@ int alm_model_finalize(alm_model* m) {
     ALM_TRY(dev_alloc_t(&ws.tokens, kMaxRows));
     ALM_TRY(dev_alloc_t(&ws.rows, kMaxRows));
     ALM_TRY(dev_alloc_t(&ws.seqs, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.u_rows, kMaxRows));
+    ALM_CUDA(cudaMallocHost(&ws.seq_host, kSeqStaging));
     ALM_TRY(dev_alloc_t(&ws.pos, 1));
     ALM_TRY(dev_alloc_t(&ws.err, 1));
     ALM_CUDA(cudaMemset(ws.err, 0, sizeof(int)));
@@ -2207,8 +2225,7 @@ int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, f
   DeviceGuard g(m->ctx->device);
   ALM_TRY(ensure_sample_scratch(m));
   cudaStream_t st = m->ctx->stream;
-  double* du = nullptr;
-  ALM_TRY(dev_alloc_t(&du, static_cast<size_t>(rows)));
+  double* du = m->ws.u_rows;
   int rc = ALM_OK;
   if (uniforms_host &&
       cudaMemcpyAsync(du, uniforms_host, rows * sizeof(double), cudaMemcpyHostToDevice, st) != cudaSuccess)
@@ -2226,14 +2243,13 @@ int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, f
                            cudaSuccess ||
                        cudaStreamSynchronize(st) != cudaSuccess))
     rc = fail(ALM_ERR_CUDA, "sample failed");
-  dev_free(du);
   return rc;
 }
 
 // Check and upload a multi-sequence pass's rows and sequences (ws.rows,
 // ws.seqs) and mark the model's next enqueue as that pass; *M_out = rows.
 static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
-                      const int32_t* pos0, int* M_out) {
+                      const int32_t* pos0, const int32_t* tokens_host, int* M_out) {
   ALM_REQ(!m->tp, "multi-sequence passes run on whole models");
   ALM_REQ(n_seq >= 1 && n_seq <= kMaxRows, "n_seq must be in 1..16");
   ALM_REQ(kv->n_layers == m->cfg.layers && kv->kv_heads == m->cfg.kv_heads && kv->head_dim == m->cfg.head_dim,
@@ -2257,10 +2273,19 @@ static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots,
     pg += (n_tok[s] * gq + kPvRows - 1) / kPvRows;
   }
   ALM_TRY(ensure_attn(m, kv->max_len));
-  ALM_CUDA(cudaStreamSynchronize(m->ctx->stream));
-  ALM_CUDA(cudaMemcpy(m->ws.rows, rows.data(), rows.size() * sizeof(int2), cudaMemcpyHostToDevice));
-  ALM_CUDA(cudaMemcpy(m->ws.seqs, seqs.data(), seqs.size() * sizeof(AttnSeq), cudaMemcpyHostToDevice));
-  ALM_TRY(set_pos(m, 0));
+  // one pinned staging area, three async copies on the model's stream (the
+  // previous call on this stream has finished: every call ends synchronised)
+  const int M = static_cast<int>(rows.size());
+  unsigned char* h = m->ws.seq_host;
+  std::memcpy(h, rows.data(), M * sizeof(int2));
+  std::memcpy(h + kMaxRows * sizeof(int2), seqs.data(), n_seq * sizeof(AttnSeq));
+  std::memcpy(h + kMaxRows * (sizeof(int2) + sizeof(AttnSeq)), tokens_host, M * sizeof(int));
+  cudaStream_t st = m->ctx->stream;
+  ALM_CUDA(cudaMemcpyAsync(m->ws.rows, h, M * sizeof(int2), cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaMemcpyAsync(m->ws.seqs, h + kMaxRows * sizeof(int2), n_seq * sizeof(AttnSeq),
+                           cudaMemcpyHostToDevice, st));
+  ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, h + kMaxRows * (sizeof(int2) + sizeof(AttnSeq)), M * sizeof(int),
+                           cudaMemcpyHostToDevice, st));
   m->ms_n_seq = n_seq;
   m->ms_n_rg = g;
   m->ms_n_pg = pg;
@@ -2281,15 +2306,30 @@ int alm_forward_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, 
   ALM_TRY(check_layers(m));
   DeviceGuard gd(m->ctx->device);
   int M = 0;
-  ALM_TRY(stage_seqs(m, kv, n_seq, slots, n_tok, pos0, &M));
-  int rc = ALM_OK;
-  if (cudaMemcpy(m->ws.tokens, tokens_host, M * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
-    rc = fail(ALM_ERR_CUDA, "token upload failed");
+  ALM_TRY(stage_seqs(m, kv, n_seq, slots, n_tok, pos0, tokens_host, &M));
   const bool head = logits_host != nullptr || argmax_host != nullptr;
-  m->tp_need_logits = logits_host != nullptr;
-  if (rc == ALM_OK) rc = enqueue_forward(m, kv, M, head, m->ctx->pdl);
+  const auto key = std::make_tuple(static_cast<const alm_kv*>(kv), M, n_seq, m->ms_n_rg, m->ms_n_pg, head ? 1 : 0);
+  cudaStream_t st = m->ctx->stream;
+  int rc = ALM_OK;
+  auto it = m->ms_graphs.find(key);
+  if (it == m->ms_graphs.end()) {
+    // first pass of this shape: capture it (the staging copies are already queued)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      rc = fail(ALM_ERR_CUDA, "graph capture failed to start");
+    } else {
+      rc = enqueue_forward(m, kv, M, head, m->ctx->pdl);
+      const cudaError_t e = cudaStreamEndCapture(st, &graph);
+      if (rc == ALM_OK && e != cudaSuccess) rc = fail(ALM_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+      if (rc == ALM_OK && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+        rc = fail(ALM_ERR_CUDA, "instantiate of a multi-sequence pass failed");
+      if (graph) cudaGraphDestroy(graph);
+    }
+    if (rc == ALM_OK) it = m->ms_graphs.emplace(key, exec).first;
+  }
+  if (rc == ALM_OK && cudaGraphLaunch(it->second, st) != cudaSuccess) rc = fail(ALM_ERR_CUDA, "pass launch failed");
   clear_seqs(m);
-  m->tp_need_logits = false;
   ALM_TRY(rc);
   ALM_TRY(sync_and_check(m));
   return copy_logits_out(m, M, logits_host, argmax_host);
@@ -2329,11 +2369,8 @@ int alm_prefill_slot(alm_model* m, alm_kv* kv, int slot, const int32_t* tokens_h
     } else if (slot != 0) {
       // a short chunk of another slot: a one-sequence multi-sequence pass
       int M = 0;
-      ALM_TRY(stage_seqs(m, kv, 1, &slot, &rows, &p, &M));
-      int rc = ALM_OK;
-      if (cudaMemcpy(m->ws.tokens, tokens_host + done, rows * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
-        rc = fail(ALM_ERR_CUDA, "token upload failed");
-      if (rc == ALM_OK) rc = enqueue_forward(m, kv, rows, false, m->ctx->pdl);
+      ALM_TRY(stage_seqs(m, kv, 1, &slot, &rows, &p, tokens_host + done, &M));
+      const int rc = enqueue_forward(m, kv, rows, false, m->ctx->pdl);
       clear_seqs(m);
       ALM_TRY(rc);
     } else {

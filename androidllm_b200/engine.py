@@ -95,13 +95,14 @@ class LayerStreamingEngine:
         return self._batch
 
     def generate_batch(self, prompts, max_new_tokens=64, temperature=0.8, top_p=0.9, min_p=0.0, seeds=None,
-                       stop_ids=()):
-        """Generate for several prompts at once (every session advances in
-        each step, the weights stream once per pass for all of them); each
-        result equals generate() for that prompt alone (with seeds[i] as the
-        engine's seed when sampling)."""
+                       stop_ids=(), max_active=None):
+        """Generate for several prompts at once (every active session advances
+        in each step, the weights stream once per pass for all of them; at
+        most max_active at a time, the rest queued); each result equals
+        generate() for that prompt alone (with seeds[i] as the engine's seed
+        when sampling)."""
         from .batching import run_batch
-        return run_batch(self, prompts, max_new_tokens, temperature, top_p, min_p, seeds, stop_ids)
+        return run_batch(self, prompts, max_new_tokens, temperature, top_p, min_p, seeds, stop_ids, max_active)
 
     def _kv_capacity(self):
         return self.ctx_len + self.spec_k + 1

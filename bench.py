@@ -52,7 +52,8 @@ TP_WORKLOAD = "qwen2.5-7b"
 # continuous batching: sessions per GPU, prompt and output length ranges,
 # temperature (the 64-sequence / 8-GPU configuration, 8 per GPU)
 BATCH_WORKLOAD = "qwen2.5-1.5b-batch"
-BATCH_SESSIONS = 8
+BATCH_SESSIONS = 8          # active at a time per GPU
+BATCH_QUEUE = 24            # sessions per GPU in all (continuous batching: a finished one's slot takes the next)
 BATCH_PROMPT = (128, 1024)
 BATCH_OUTPUT = (64, 512)
 BATCH_TEMPERATURE = 0.8
@@ -561,13 +562,14 @@ def run_ours(args):
 # --------------------------------------------------------------------------
 def run_batch(args):
     """Continuous batching of speculative sessions (one process per GPU, data
-    parallel): BATCH_SESSIONS sessions per GPU with seeded prompt lengths in
+    parallel): BATCH_QUEUE sessions per GPU with seeded prompt lengths in
     BATCH_PROMPT and output lengths in BATCH_OUTPUT, k = 4, T = 0.8 with
-    seeded per-session uniforms, paged KV of 16-position pages, all sessions
-    advanced together (LayerStreamingEngine.generate_batch).  value =
-    generated tokens of all ranks / the slowest rank's time; the same
-    sessions one after the other through generate() give the sequential
-    figure it is compared with."""
+    seeded per-session uniforms, paged KV of 16-position pages, at most
+    BATCH_SESSIONS active and advanced together, a finished session's slot
+    taken by the next (LayerStreamingEngine.generate_batch).  value =
+    generated tokens of all ranks / the slowest rank's time; sessions one
+    after the other through generate() give the sequential figure it is
+    compared with."""
     rank, world, local = dist_env()
     dist = None
     if world > 1:
@@ -590,9 +592,9 @@ def run_batch(args):
     rng = np.random.default_rng(1000 + rank)
     V = eng.canon["vocab"]
     prompts = [rng.integers(0, V, int(rng.integers(BATCH_PROMPT[0], BATCH_PROMPT[1] + 1))).tolist()
-               for _ in range(BATCH_SESSIONS)]
-    outs = [int(rng.integers(BATCH_OUTPUT[0], BATCH_OUTPUT[1] + 1)) for _ in range(BATCH_SESSIONS)]
-    seeds = [10_000 * rank + i for i in range(BATCH_SESSIONS)]
+               for _ in range(BATCH_QUEUE)]
+    outs = [int(rng.integers(BATCH_OUTPUT[0], BATCH_OUTPUT[1] + 1)) for _ in range(BATCH_QUEUE)]
+    seeds = [10_000 * rank + i for i in range(BATCH_QUEUE)]
     # warm-up: a short batch (kernels, caches)
     eng.generate_batch([p[:64] for p in prompts[:2]], max_new_tokens=8, temperature=BATCH_TEMPERATURE,
                        seeds=seeds[:2])
@@ -601,7 +603,7 @@ def run_batch(args):
         dist.barrier()
     t0 = time.perf_counter()
     got = eng.generate_batch(prompts, max_new_tokens=outs, temperature=BATCH_TEMPERATURE, top_p=0.9,
-                             seeds=seeds)
+                             seeds=seeds, max_active=BATCH_SESSIONS)
     secs = time.perf_counter() - t0
     clk.__exit__(None, None, None)
     tokens = sum(len(g) for g in got)
@@ -631,6 +633,7 @@ def run_batch(args):
             "ms_per_step": round(secs * 1000.0, 2), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": BATCH_WORKLOAD, "sessions_per_gpu": BATCH_SESSIONS,
+                       "queued_sessions_per_gpu": BATCH_QUEUE,
                        "prompt_len": list(BATCH_PROMPT), "output_len": list(BATCH_OUTPUT), "k": SPEC_K,
                        "temperature": BATCH_TEMPERATURE, "top_p": 0.9, "kv_page": 16,
                        "parallelism": f"dp{world}", "timed": "prefill + decode of every session, host-timed"},

@@ -91,6 +91,20 @@ def test_generate_batch_equals_generate(model_dirs, temperature):
     eng.close()
 
 
+def test_continuous_batching_queue(model_dirs):
+    """Five prompts with at most two sessions active (a finished session's
+    slot takes the next prompt): the tokens of each prompt are unchanged."""
+    from androidllm_b200.engine import LayerStreamingEngine
+    eng = LayerStreamingEngine(model_dirs["toyu"], draft_dir=model_dirs["toyu_draft"], spec_k=4)
+    prompts = _prompts(5, 32000, seed=21)
+    outs = [8, 30, 12, 25, 5]
+    all_at_once = eng.generate_batch(prompts, max_new_tokens=outs, temperature=0.0)
+    two = eng.generate_batch(prompts, max_new_tokens=outs, temperature=0.0, max_active=2)
+    assert two == all_at_once
+    assert [len(g) for g in two] == outs
+    eng.close()
+
+
 def test_generate_batch_without_draft(model_dirs):
     """Sessions of an engine without a draft take plain batched steps (one
     row per session per pass): equal to generate() per prompt."""
