@@ -204,6 +204,14 @@ struct AttnArgs {
   // scores row groups and P.V groups
   const AttnSeq* seqs = nullptr;
   int n_seq = 0, n_rg = 0, n_pg = 0;
+  // one-launch attention (attn_fused.cu): per (kv head, row group) a count
+  // of published chunk statistics and a ticket of finished chunk partials
+  // (both self-resetting), the fp32 P.V partials of every chunk, and the
+  // word a wait that gives up sets (2)
+  unsigned* fz_count = nullptr;
+  unsigned* fz_ticket = nullptr;
+  float* fz_part = nullptr;
+  int* err = nullptr;
 };
 // Positions one block of the split P.V pass takes (a context longer than one
 // split span is spread over blocks), and the split spans of max_ctx positions.
@@ -213,6 +221,11 @@ struct AttnArgs {
 constexpr int kPvSplit = kPvSpan;
 __host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSplit - 1) / kPvSplit; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
+// Scores, statistics and P.V in one launch when the pass's blocks fit on
+// the GPU at once (fz_* set); false: the caller runs launch_attention.
+bool attn_fused_ok(const AttnArgs& a);
+cudaError_t launch_attn_fused(const AttnArgs& a, bool pdl, cudaStream_t st);
+cudaError_t attn_fused_init_attrs(int n_sms);
 // Single-row decode attention in one kernel (attn_decode.cu), bit-identical
 // to launch_attention; attn_decode_ok says whether it takes the shape.
 bool attn_decode_ok(const AttnArgs& a);

@@ -152,6 +152,7 @@ struct alm_ctx {
   bool persist = false;  // forwards of <= 8 rows as one persistent kernel
   bool cluster = false;  // single-row forwards of small models as one cluster kernel (opt-in)
   bool attn_decode = false;  // single-row attention as one kernel (opt-in: ALM_ATTN_DECODE=1)
+  bool attn_fused = false;   // scores + P.V in one launch when the grid fits (opt-in: ALM_ATTN_FUSED=1)
   int tc = 0;            // row layout (tcgen05 GEMV): 0 never, 1 large weights, 2 always
   // models loaded from now on keep row-layout copies of their projections for
   // the batched prefill through the dense tcgen05 path (ALM_DENSE_PREFILL=0: off)
@@ -237,6 +238,9 @@ struct Work {
   float* stats = nullptr;
   float* pv_part = nullptr;      // P.V span partials (contexts of several spans)
   unsigned* pv_ticket = nullptr;
+  unsigned* fz_count = nullptr;  // one-launch attention: counts, tickets, chunk partials
+  unsigned* fz_ticket = nullptr;
+  float* fz_part = nullptr;
   // tensor parallelism
   float* o32 = nullptr;        // (kMaxRows, hidden) fp32 partials of the row-split projections
   int* tp_pairs = nullptr;     // (kMaxRows, 2) local argmax, then (world, kMaxRows, 2) gathered
@@ -591,10 +595,16 @@ int ensure_attn(alm_model* m, int max_ctx) {
   dev_free(ws.stats);
   dev_free(ws.pv_part);
   dev_free(ws.pv_ticket);
+  dev_free(ws.fz_count);
+  dev_free(ws.fz_ticket);
+  dev_free(ws.fz_part);
   ws.scores = nullptr;
   ws.stats = nullptr;
   ws.pv_part = nullptr;
   ws.pv_ticket = nullptr;
+  ws.fz_count = nullptr;
+  ws.fz_ticket = nullptr;
+  ws.fz_part = nullptr;
   ws.attn_ctx = 0;
   // rows padded by one chunk: the P.V kernel reads whole 16-position groups
   const int ld = cap + kAttnChunk;
@@ -606,6 +616,14 @@ int ensure_attn(alm_model* m, int max_ctx) {
   ALM_TRY(dev_alloc_t(&ws.pv_part, keys * attn_pv_spans(cap) * kPvRows * 16));
   ALM_TRY(dev_alloc_t(&ws.pv_ticket, keys));
   ALM_CUDA(cudaMemset(ws.pv_ticket, 0, keys * sizeof(unsigned)));
+  // one-launch attention: (kv head, row group) counters and tickets, and a
+  // (kv head, row group, chunk) partial of 16 rows x head_dim
+  const size_t fz_keys = static_cast<size_t>(m->cfg.kv_heads) * n_rg;
+  ALM_TRY(dev_alloc_t(&ws.fz_count, fz_keys));
+  ALM_TRY(dev_alloc_t(&ws.fz_ticket, fz_keys));
+  ALM_CUDA(cudaMemset(ws.fz_count, 0, fz_keys * sizeof(unsigned)));
+  ALM_CUDA(cudaMemset(ws.fz_ticket, 0, fz_keys * sizeof(unsigned)));
+  ALM_TRY(dev_alloc_t(&ws.fz_part, fz_keys * (cap / kAttnChunk) * kAttnRows * m->cfg.head_dim));
   ws.attn_ctx = cap;
   ws.score_ld = ld;
   return ALM_OK;
@@ -746,9 +764,18 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
     a.n_pg = m->ms_n_pg;
     a.pv_part = nullptr;
   }
+  if (m->ctx->attn_fused) {
+    a.fz_count = ws.fz_count;
+    a.fz_ticket = ws.fz_ticket;
+    a.fz_part = ws.fz_part;
+    a.err = ws.err;
+  }
   if (m->ctx->attn_decode && attn_decode_ok(a)) {
     // single-row decode: scores, statistics and P.V in one kernel (bit-identical)
     ALM_LAUNCH(launch_attn_decode(a, pdl, st));
+    prof_mark(ALM_OP_ATTN, M);
+  } else if (attn_fused_ok(a)) {
+    ALM_LAUNCH(launch_attn_fused(a, pdl, st));
     prof_mark(ALM_OP_ATTN, M);
   } else {
     ALM_LAUNCH(launch_attention(a, pdl, st));
@@ -1294,6 +1321,13 @@ int alm_ctx_create(int device, alm_ctx** out) {
   c->device = device;
   c->n_sms = n_sms_of(device);
   {
+    const cudaError_t e = attn_fused_init_attrs(c->n_sms);
+    if (e != cudaSuccess) {
+      delete c;
+      return fail(ALM_ERR_CUDA, std::string("kernel attributes: ") + cudaGetErrorString(e));
+    }
+  }
+  {
     const char* e = getenv("ALM_NO_PDL");
     c->pdl = !(e && e[0] == '1');
     const char* e2 = getenv("ALM_PERSIST");
@@ -1306,6 +1340,8 @@ int alm_ctx_create(int device, alm_ctx** out) {
     if (e3 && (e3[0] == '0' || e3[0] == '1' || e3[0] == '2')) c->tc = e3[0] - '0';
     const char* e6 = getenv("ALM_DENSE_PREFILL");
     c->dense_prefill = !(e6 && e6[0] == '0');
+    const char* e7 = getenv("ALM_ATTN_FUSED");
+    c->attn_fused = e7 && e7[0] == '1';
   }
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete c;
@@ -1349,6 +1385,12 @@ int alm_ctx_init_tp(alm_ctx* ctx, int rank, int world, const uint8_t* id) {
 int alm_ctx_set_persistent(alm_ctx* ctx, int enable) {
   ALM_REQ(ctx, "null context");
   ctx->persist = enable != 0;
+  return ALM_OK;
+}
+
+int alm_ctx_set_attn_fused(alm_ctx* ctx, int enable) {
+  ALM_REQ(ctx, "null context");
+  ctx->attn_fused = enable != 0;
   return ALM_OK;
 }
 
@@ -1586,6 +1628,7 @@ int alm_model_destroy(alm_model* m) {
                   (void*)w.ss1, (void*)w.ss2, (void*)w.q, (void*)w.ctx, (void*)w.h, (void*)w.xn, (void*)w.xout,
                   (void*)w.logits, (void*)w.am_val, (void*)w.am_idx, (void*)w.argmax, (void*)w.part,
                   (void*)w.scores, (void*)w.stats, (void*)w.pv_part, (void*)w.pv_ticket,
+                  (void*)w.fz_count, (void*)w.fz_ticket, (void*)w.fz_part,
                   (void*)w.sample_scratch, (void*)w.o32, (void*)w.tp_pairs,
                   (void*)w.logits_local, (void*)w.logits_gather, (void*)w.rows, (void*)w.seqs,
                   (void*)w.u_rows})

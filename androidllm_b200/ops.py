@@ -49,6 +49,13 @@ class Context:
         launch per layer operation (the default)."""
         check(lib.alm_ctx_set_cluster_forward(self.h, 1 if enable else 0))
 
+    def set_attn_fused(self, enable):
+        """Attention of decode / verify passes in one launch (opt-in, slower on
+        B200 at the benchmark's shapes) or as the two passes (scores, then
+        P.V; the default, which the persistent and cluster forwards
+        reproduce bit for bit)."""
+        check(lib.alm_ctx_set_attn_fused(self.h, 1 if enable else 0))
+
     def set_dense_prefill(self, enable):
         """Whether models loaded on this context from now on keep row-layout
         copies of their projections so that prefill runs through the dense

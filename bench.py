@@ -169,7 +169,7 @@ def step_profile_groups(prof, tman, dman, pos, k):
             c = man["config"]
             ctx = pos + (fwd + 1 if role == "draft" else k + 1)
             nbytes = c["kv_heads"] * ctx * c["head_dim"] * 2 * (2 if op == "attn" else 1)
-            name = "attn_decode_kernel (scores + P.V)" if op == "attn" else f"{op}_kernel"
+            name = "attn_fused_kernel (scores + P.V)" if op == "attn" else f"{op}_kernel"
             desc = f"{name} hd={c['head_dim']} group={c['heads'] // c['kv_heads']} ctx~{ctx}, M={rows}"
         key = f"{role}.{op}"
         g = groups.setdefault(key, {"key": key, "kernel": f"{role} {desc}", "launches": 0, "us": 0.0, "bytes": 0})

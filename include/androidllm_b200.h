@@ -72,6 +72,15 @@ ALM_API int alm_ctx_set_persistent(alm_ctx* ctx, int enable);
    Qwen2.5-0.5B draft shape it is slower (2.8 ms against 0.87 ms per
    forward): 16 SMs cannot decode int4 weights as fast as the whole GPU.
    Graphs captured earlier keep their kernels. */
+/* Attention of decode / verify passes as one launch (scores, statistics and
+ * P.V; the probabilities are the two passes' bit for bit, the P.V sums are
+ * added per 64-position chunk and then across chunks) when the pass's blocks
+ * fit on the GPU at once, else the two passes (opt-in, default off;
+ * ALM_ATTN_FUSED=1 turns the default on).  Measured slower on B200 than the
+ * two passes at the benchmark's shapes; passes of different grid sizes may
+ * take different paths, so results are bit-equal across passes only at
+ * settings where both take the same one. */
+ALM_API int alm_ctx_set_attn_fused(alm_ctx* ctx, int enable);
 ALM_API int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable);
 /* Weight layout chosen by later uploads: 0 (the default) = 16-row tiles for
    the mma.sync GEMV; 1 = 128-row records for the tcgen05 kernel for weights of
@@ -380,7 +389,7 @@ enum {
   ALM_OP_O = 5, ALM_OP_GATE_UP = 6, ALM_OP_DOWN = 7, ALM_OP_FINAL_NORM = 8, ALM_OP_HEAD = 9,
   ALM_OP_ARGMAX = 10, ALM_OP_SPEC_PREP = 11, ALM_OP_SPEC_ACCEPT = 12, ALM_OP_SAMPLE = 13,
   ALM_OP_LAYERS = 14,  /* embedding and every layer as one cluster kernel */
-  ALM_OP_ATTN = 15     /* single-row attention as one kernel (opt-in: ALM_ATTN_DECODE=1) */
+  ALM_OP_ATTN = 15     /* attention as one launch (alm_ctx_set_attn_fused, or the opt-in single-row kernel) */
 };
 /* Device time of every kernel launch of one speculative step (profiling; no
  * counterpart in the reference).  The step is captured once more with a

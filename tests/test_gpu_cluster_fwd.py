@@ -1,5 +1,6 @@
 """The single-row cluster forward (one 16-CTA thread-block cluster runs every
-layer) against the per-operation launches it replaces: bit-identical logits,
+layer) against the per-operation launches it replaces (two-pass attention):
+bit-identical logits,
 argmax and KV entries, on the golden models and at the benchmark's draft
 shape (Qwen2.5-0.5B layers over a 776-position seeded cache), so the
 reference parity of the per-operation path carries over; and the draft shape's
@@ -21,6 +22,7 @@ pytestmark = pytest.mark.gpu
 def ctx():
     from androidllm_b200.ops import Context
     c = Context(0)
+    c.set_attn_fused(False)   # the cluster kernel reproduces the two attention passes
     c.set_cluster_forward(True)
     yield c
     c.set_cluster_forward(False)

@@ -1,6 +1,7 @@
 """The persistent forward kernel (one launch per forward of <= 8 rows) against
-the per-operation launches: same device bodies, so logits, argmax and the
-paged KV cache must be bit-identical, for decode rows and verify rows."""
+the per-operation launches with two-pass attention: same device bodies, so
+logits, argmax and the paged KV cache must be bit-identical, for decode rows
+and verify rows."""
 import numpy as np
 import pytest
 from gpu_helpers import prefill
@@ -11,7 +12,9 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture(scope="module")
 def ctx():
     from androidllm_b200.ops import Context
-    return Context(0)
+    c = Context(0)
+    c.set_attn_fused(False)   # the persistent kernel reproduces the two attention passes
+    return c
 
 
 @pytest.fixture(scope="module")
