@@ -82,6 +82,9 @@ SIGNATURES = {
     "alm_prefill": [_P, _P, _P, _I, _I],
     "alm_prefill_slot": [_P, _P, _I, _P, _I, _I],
     "alm_ctx_set_attn_fused": [_P, _I],
+    "alm_tp_p2p_open": [_P, _I, _P],
+    "alm_tp_p2p_connect": [_P, _P],
+    "alm_ctx_set_tp_p2p": [_P, _I],
     "alm_model_sample_rows": [_P, _I, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P],
     "alm_forward_seqs": [_P, _P, _I, _P, _P, _P, _P, _P, _P],
     "alm_kv_create_slots": [_P, _P, _I, _I, _I, _P],

@@ -328,6 +328,35 @@ cudaError_t launch_argmax_final(const float* am_val, const int* am_idx, int n_pa
 // 16-column tile sums of squares of out (the RESID epilogue's arithmetic).
 cudaError_t launch_tp_resid(const ActIn& res, const float* o32, int M, int H, half* out, float* ss_out, bool pdl,
                             cudaStream_t st);
+// Peer-memory all-reduce of a row-split projection (the ranks of one node):
+// every rank owns an area of two parity slots x world ranks x rows rows of
+// row_floats fp32, then two x world x rows flags; areas[r] is rank r's area
+// in this process's address space (its own, or a peer's mapping).
+struct TpP2p {
+  float* areas[8] = {};
+  int world = 0, rank = 0, rows = 0, row_floats = 0;
+  unsigned* counters = nullptr;   // this rank's per-row call counts (rows)
+  int* err = nullptr;             // set to 2 if a wait gave up
+};
+constexpr int kTpP2pMaxWorld = 8;
+constexpr int kTpP2pHandleBytes = 64;   // a CUDA IPC memory handle
+constexpr long long kTpP2pSpinLimit = 1ll << 20;   // polls per peer flag (well under a second)
+__host__ __device__ inline size_t tp_p2p_data_floats(int world, int rows, int row_floats) {
+  return static_cast<size_t>(2) * world * rows * row_floats;
+}
+__host__ __device__ inline size_t tp_p2p_area_bytes(int world, int rows, int row_floats) {
+  return tp_p2p_data_floats(world, rows, row_floats) * sizeof(float) +
+         static_cast<size_t>(2) * world * rows * sizeof(unsigned);
+}
+__host__ __device__ inline float* tp_p2p_data(const TpP2p& p, float* area, int parity, int src, int m) {
+  return area + ((static_cast<size_t>(parity) * p.world + src) * p.rows + m) * p.row_floats;
+}
+__host__ __device__ inline unsigned* tp_p2p_flag(const TpP2p& p, float* area, int parity, int src, int m) {
+  unsigned* flags = reinterpret_cast<unsigned*>(area + tp_p2p_data_floats(p.world, p.rows, p.row_floats));
+  return flags + (static_cast<size_t>(parity) * p.world + src) * p.rows + m;
+}
+cudaError_t launch_tp_p2p_resid(const ActIn& res, const float* o32, int M, int H, half* out, float* ss_out,
+                                const TpP2p& p, bool pdl, cudaStream_t st);
 // The same with the fp16 outputs of the dense path (batched prefill).
 cudaError_t launch_resid_rows16(const ActIn& res, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,
                                 cudaStream_t st);

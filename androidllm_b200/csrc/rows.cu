@@ -34,12 +34,12 @@ __global__ void __launch_bounds__(kRowThreads) argmax_final_kernel(const float* 
 ALM_DEV float resid_operand(float v) { return round_h(v); }
 ALM_DEV float resid_operand(half v) { return __half2float(v); }
 
-template <typename OT>
-__global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, const OT* o32, int H, half* out,
-                                                                 float* ss_out) {
+// Row m: out = fp16(res + operand(col)) and the tile sums of squares in the
+// RESID epilogue's order; operand(col) is the projection's value (fp32,
+// rounded to fp16 like the epilogue's accumulator).
+template <typename Operand>
+ALM_DEV void resid_row(const ActIn& res, int m, int H, half* out, float* ss_out, Operand operand) {
   __shared__ float s_den;
-  grid_dep_wait();
-  const int m = blockIdx.x;
   if (res.ss && threadIdx.x < kWarp) {
     const float d = row_denominator(res, m);
     if (threadIdx.x == 0) s_den = d;
@@ -57,8 +57,7 @@ __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, cons
       if (live && col < H) {
         const float rv = __half2float(__ldcg(res.x + static_cast<size_t>(m) * res.ld + col));
         const float rval = res.ss ? norm_value(rv, s_den, __half2float(__ldg(res.w + col))) : rv;
-        const float o = resid_operand(__ldcg(o32 + static_cast<size_t>(m) * H + col));
-        const half s16 = __float2half_rn(fadd(rval, o));
+        const half s16 = __float2half_rn(fadd(rval, operand(col)));
         out[static_cast<size_t>(m) * H + col] = s16;
         const float sf = __half2float(s16);
         sq = r == 0 ? fmul(sf, sf) : fadd(sq, fmul(sf, sf));
@@ -69,6 +68,79 @@ __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, cons
     sq = fadd(sq, __shfl_xor_sync(0xffffffffu, sq, 4));
     if (live && g == 0) ss_out[static_cast<size_t>(m) * n_tiles + tile] = sq;
   }
+}
+
+template <typename OT>
+__global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, const OT* o32, int H, half* out,
+                                                                 float* ss_out) {
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  const OT* row = o32 + static_cast<size_t>(m) * H;
+  resid_row(res, m, H, out, ss_out, [&](int col) { return resid_operand(__ldcg(row + col)); });
+  grid_dep_launch();
+}
+
+// Tensor parallelism over peer memory: block m sends row m of this rank's
+// fp32 partial to every peer's receive slot (parity = the row's call count
+// & 1, so a peer one call ahead writes the other slot), raises the peer's
+// flag for (this rank, row m) to count + 1 with a system-scope release,
+// waits (bounded) for every peer's flag, and adds the ranks' rows in rank
+// order — the same sum on every rank — before the residual.
+ALM_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+ALM_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kRowThreads) tp_p2p_resid_kernel(ActIn res, const float* o32, int H, half* out,
+                                                                   float* ss_out, TpP2p p) {
+  __shared__ unsigned s_epoch;
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  if (threadIdx.x == 0) s_epoch = p.counters[m];
+  __syncthreads();
+  const unsigned epoch = s_epoch, val = epoch + 1;
+  const int parity = static_cast<int>(epoch & 1u);
+  const float* mine = o32 + static_cast<size_t>(m) * H;
+  // send row m to every peer: slot (parity, this rank, m) of its area
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    float* dst = tp_p2p_data(p, p.areas[r], parity, p.rank, m);
+    for (int c = threadIdx.x; c < H; c += kRowThreads) dst[c] = __ldcg(mine + c);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < p.world; ++r)
+      if (r != p.rank) st_release_sys(tp_p2p_flag(p, p.areas[r], parity, p.rank, m), val);
+    // wait for every peer's row m in this rank's own area
+    for (int r = 0; r < p.world; ++r) {
+      if (r == p.rank) continue;
+      const unsigned* f = tp_p2p_flag(p, p.areas[p.rank], parity, r, m);
+      long long spins = 0;
+      while (ld_acquire_sys(f) < val) {
+        if (++spins > kTpP2pSpinLimit) {
+          if (p.err) atomicExch(p.err, 2);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+  }
+  __syncthreads();
+  resid_row(res, m, H, out, ss_out, [&](int col) {
+    float v = 0.f;
+    for (int r = 0; r < p.world; ++r) {
+      const float x = r == p.rank ? __ldcg(mine + col) : __ldcg(tp_p2p_data(p, p.areas[p.rank], parity, r, m) + col);
+      v = r == 0 ? x : fadd(v, x);
+    }
+    return round_h(v);
+  });
+  __syncthreads();
+  if (threadIdx.x == 0) p.counters[m] = val;
   grid_dep_launch();
 }
 
@@ -162,6 +234,16 @@ cudaError_t launch_tp_resid(const ActIn& res_, const float* o32, int M, int H, h
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
   return cudaLaunchKernelEx(&c, resid_rows_kernel<float>, res, o32, H, out, ss_out);
+}
+
+cudaError_t launch_tp_p2p_resid(const ActIn& res_, const float* o32, int M, int H, half* out, float* ss_out,
+                                const TpP2p& p, bool pdl, cudaStream_t st) {
+  if (M < 1 || M > p.rows || H > p.row_floats || p.world < 2) return cudaErrorInvalidValue;
+  ActIn res = res_;
+  set_vec(res);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  return cudaLaunchKernelEx(&c, tp_p2p_resid_kernel, res, o32, H, out, ss_out, p);
 }
 
 cudaError_t launch_resid_rows16(const ActIn& res_, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,

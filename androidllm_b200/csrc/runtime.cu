@@ -160,6 +160,11 @@ struct alm_ctx {
   // tensor parallelism: NCCL communicator of this rank (alm_ctx_init_tp)
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
+  // peer-memory all-reduce of the row-split projections (alm_tp_p2p_*):
+  // this rank's area, the peers' mapped areas, and whether it is in use
+  TpP2p p2p;
+  float* p2p_own = nullptr;
+  bool p2p_ready = false, tp_p2p = false;
 };
 
 struct alm_qweight {
@@ -706,6 +711,13 @@ int enqueue_tp_rowsplit(alm_model* m, const alm_qweight* w, const ActIn& in, int
   e.ldo = H;
   e.n_out = H;
   ALM_LAUNCH(launch_gemv(w->t, in, M, EPI_STORE32, e, StepIO{ws.pos, ws.err}, scratch_of(m), pdl, st));
+  if (m->ctx->tp_p2p) {
+    // one kernel: exchange over peer memory, rank-order sum, residual
+    TpP2p p = m->ctx->p2p;
+    p.err = ws.err;
+    ALM_LAUNCH(launch_tp_p2p_resid(res, ws.o32, M, H, out, ss_out, p, pdl, st));
+    return ALM_OK;
+  }
   std::string err;
   if (tp_allreduce_sum_f32(m->ctx->tp_comm, ws.o32, static_cast<size_t>(M) * H, st, &err))
     return fail(ALM_ERR_CUDA, err);
@@ -1355,6 +1367,11 @@ int alm_ctx_destroy(alm_ctx* ctx) {
   if (!ctx) return ALM_OK;
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  if (ctx->p2p_ready)
+    for (int r = 0; r < ctx->p2p.world; ++r)
+      if (r != ctx->p2p.rank && ctx->p2p.areas[r]) cudaIpcCloseMemHandle(ctx->p2p.areas[r]);
+  dev_free(ctx->p2p_own);
+  dev_free(ctx->p2p.counters);
   tp_comm_destroy(ctx->tp_comm);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1379,6 +1396,64 @@ int alm_ctx_init_tp(alm_ctx* ctx, int rank, int world, const uint8_t* id) {
   ctx->tp_comm = comm;
   ctx->tp_rank = rank;
   ctx->tp_world = world;
+  return ALM_OK;
+}
+
+int alm_tp_p2p_open(alm_ctx* ctx, int row_floats, uint8_t* handle_out) {
+  ALM_REQ(ctx && handle_out, "null argument");
+  ALM_REQ(ctx->tp_comm && ctx->tp_world >= 2 && ctx->tp_world <= kTpP2pMaxWorld,
+          "peer all-reduce needs a tensor-parallel context of 2..8 ranks");
+  ALM_REQ(row_floats > 0 && row_floats % 4 == 0, "row_floats must be a positive multiple of 4");
+  ALM_REQ(!ctx->p2p_own, "peer all-reduce already opened");
+  DeviceGuard g(ctx->device);
+  TpP2p& p = ctx->p2p;
+  p.world = ctx->tp_world;
+  p.rank = ctx->tp_rank;
+  p.rows = kMaxRows;
+  p.row_floats = row_floats;
+  const size_t bytes = tp_p2p_area_bytes(p.world, p.rows, p.row_floats);
+  ALM_TRY(dev_alloc(reinterpret_cast<void**>(&ctx->p2p_own), bytes));
+  ALM_CUDA(cudaMemset(ctx->p2p_own, 0, bytes));
+  ALM_TRY(dev_alloc_t(&p.counters, kMaxRows));
+  ALM_CUDA(cudaMemset(p.counters, 0, kMaxRows * sizeof(unsigned)));
+  static_assert(sizeof(cudaIpcMemHandle_t) == kTpP2pHandleBytes, "IPC handle size");
+  ALM_CUDA(cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), ctx->p2p_own));
+  return ALM_OK;
+}
+
+int alm_tp_p2p_connect(alm_ctx* ctx, const uint8_t* handles) {
+  ALM_REQ(ctx && handles, "null argument");
+  ALM_REQ(ctx->p2p_own && !ctx->p2p_ready, "open the peer all-reduce first (once)");
+  DeviceGuard g(ctx->device);
+  TpP2p& p = ctx->p2p;
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) {
+      p.areas[r] = ctx->p2p_own;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + static_cast<size_t>(r) * kTpP2pHandleBytes, sizeof(h));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != p.rank && p.areas[q]) cudaIpcCloseMemHandle(p.areas[q]);
+      for (float*& a : p.areas) a = nullptr;
+      return fail(ALM_ERR_CUDA, std::string("peer area of rank ") + std::to_string(r) + ": " + cudaGetErrorString(e));
+    }
+    p.areas[r] = static_cast<float*>(ptr);
+  }
+  // every rank's area is zeroed before any rank sends: the caller connects
+  // all ranks before the first forward
+  ctx->p2p_ready = true;
+  ctx->tp_p2p = true;
+  return ALM_OK;
+}
+
+int alm_ctx_set_tp_p2p(alm_ctx* ctx, int enable) {
+  ALM_REQ(ctx, "null context");
+  ALM_REQ(!enable || ctx->p2p_ready, "the peer all-reduce is not connected");
+  ctx->tp_p2p = enable != 0;
   return ALM_OK;
 }
 

@@ -49,6 +49,10 @@ class Context:
         launch per layer operation (the default)."""
         check(lib.alm_ctx_set_cluster_forward(self.h, 1 if enable else 0))
 
+    def set_tp_p2p(self, enable):
+        """Row-split all-reduce over peer memory (after tp.enable_p2p) or NCCL."""
+        check(lib.alm_ctx_set_tp_p2p(self.h, 1 if enable else 0))
+
     def set_attn_fused(self, enable):
         """Attention of decode / verify passes in one launch (opt-in, slower on
         B200 at the benchmark's shapes) or as the two passes (scores, then

@@ -47,6 +47,21 @@ def init_context_tp(ctx, rank, world, uid):
     check(lib.alm_ctx_init_tp(ctx.h, int(rank), int(world), ptr(buf)))
 
 
+def enable_p2p(ctx, row_floats):
+    """Switch the row-split projections' all-reduce from NCCL to the peer-memory
+    kernel (alm_tp_p2p_*): every rank opens its receive area, the CUDA IPC
+    handles are exchanged over torch.distributed, every rank maps the others'.
+    Collective: every rank calls it after init_context_tp, before a forward."""
+    import torch.distributed as dist
+    h = np.zeros(64, np.uint8)
+    check(lib.alm_tp_p2p_open(ctx.h, int(row_floats), ptr(h)))
+    handles = [None] * dist.get_world_size()
+    dist.all_gather_object(handles, bytes(h))
+    buf = np.frombuffer(b"".join(handles), dtype=np.uint8).copy()
+    check(lib.alm_tp_p2p_connect(ctx.h, ptr(buf)))
+    dist.barrier()
+
+
 def tp_plan(canon, world, block=64, down_in=None):
     """Per-rank ranges: q heads, kv heads, FFN columns, vocabulary rows.
 
@@ -183,5 +198,5 @@ def device_model_tp(ctx, model_dir, rank, world):
     return m
 
 
-__all__ = ["nccl_unique_id", "init_context_tp", "tp_plan", "slice_rows", "slice_cols", "local_canon",
+__all__ = ["nccl_unique_id", "init_context_tp", "enable_p2p", "tp_plan", "slice_rows", "slice_cols", "local_canon",
            "shard_layer", "head_rows", "device_model_tp"]

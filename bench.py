@@ -652,8 +652,9 @@ def run_batch(args):
 def run_tp(args):
     """Speculative decoding (k = 6, greedy) of the Qwen2.5-7B-shaped target
     (int4 attention / int8 MLP / int8 head, block 64) split over the ranks
-    by tensor parallelism (heads, FFN and vocabulary; NCCL all-reduce after o
-    and down, all-gathered head argmax), with the 0.5B-shaped int4 draft
+    by tensor parallelism (heads, FFN and vocabulary; an all-reduce after o
+    and down through NCCL — over peer memory with ALM_TP_P2P=1 — and an
+    all-gathered head argmax), with the 0.5B-shaped int4 draft
     replicated on every rank.  2048-token prompt, 256-token episodes; exactly
     --steps steps timed, their start positions spread over the episode."""
     import datetime
@@ -677,6 +678,8 @@ def run_tp(args):
         uid = [tp.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         tp.init_context_tp(ctx, rank, world, uid[0])
+        if os.environ.get("ALM_TP_P2P", "0") == "1":
+            tp.enable_p2p(ctx, canon_of(WORKLOADS[TP_WORKLOAD][0])["hidden"])
         t = tp.device_model_tp(ctx, tdir, rank, world)
     else:
         t = DeviceModel.from_dir(ctx, tdir)
@@ -741,6 +744,8 @@ def run_tp(args):
                    "draft": "qwen2.5-0.5b: int4, vocabulary 152064", "k": TP_SPEC_K, "batch": 1,
                    "prompt_len": TP_PROMPT_LEN, "episode_tokens": EPISODE_TOKENS, "temperature": 0,
                    "parallelism": f"tp{world}", "positions_timed": [starts[0], starts[-1]],
+                   "allreduce": ("peer memory" if world > 1 and os.environ.get("ALM_TP_P2P", "0") == "1"
+                                 else "nccl" if world > 1 else None),
                    "l2": "weights (>= 1 GB streamed per step per rank) exceed the 126 MB L2; no flush needed"},
         "e2e": {"value": round((len(stream) - 1) / t_e2e, 3), "unit": "tokens/s",
                 "scope": "SpecDecoder.run(1) per step from the host (state in, emitted tokens out)",

@@ -192,6 +192,19 @@ ALM_API int alm_model_set_head(alm_model* m, const alm_proj_src* head);
  * holds the same tokens.  Logits requested by the host (or the sampler) are
  * gathered whole. */
 ALM_API int alm_model_set_tp(alm_model* m, int vocab_offset, int vocab_local);
+/* Peer-memory all-reduce for the row-split projections (o, down) in place of
+ * NCCL: each rank opens a receive area sized for rows of row_floats fp32 (the
+ * model's hidden size) and gets its CUDA IPC handle (64 bytes) in
+ * handle_out; once every rank has every handle (world x 64 bytes in rank
+ * order), alm_tp_p2p_connect maps the peers' areas.  A row-split projection
+ * then runs its GEMV and one kernel that writes each row to every peer,
+ * waits for theirs (bounded) and adds the ranks in rank order — the same sum
+ * on every rank — before the residual.  Every rank must connect before any
+ * forward; no multicast is used. */
+ALM_API int alm_tp_p2p_open(alm_ctx* ctx, int row_floats, uint8_t* handle_out);
+ALM_API int alm_tp_p2p_connect(alm_ctx* ctx, const uint8_t* handles);
+/* Use the peer all-reduce (1, after connecting) or NCCL (0). */
+ALM_API int alm_ctx_set_tp_p2p(alm_ctx* ctx, int enable);
 /* *uses_cluster = 1 when the model's single-row forwards run as the cluster
    kernel (alm_ctx_set_cluster_forward enabled and every projection fits it). */
 ALM_API int alm_model_cluster_forward(const alm_model* m, int* uses_cluster);

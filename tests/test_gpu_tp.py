@@ -1,7 +1,8 @@
 """Tensor parallelism on two GPUs (skipped with fewer): two processes, one
 per GPU, each load their shard of the model (alm_model_set_tp: heads, FFN
-and vocabulary split, NCCL all-reduce after o and down, all-gathered head
-argmax) and must reproduce the single-GPU model: logits within 1e-2 with the
+and vocabulary split, an all-reduce after o and down — NCCL, or the
+peer-memory kernel — and an all-gathered head argmax) and must reproduce
+the single-GPU model: logits within 1e-2 with the
 same argmax, the same greedy tokens wherever the single-GPU top-1/top-2
 margin exceeds an fp16 ulp, identical results on both ranks, and greedy
 speculative decoding (the draft replicated on each rank) equal to the
@@ -42,7 +43,7 @@ def _greedy(m, kv, prompt, n_new):
     return out, np.stack(lgs)
 
 
-def _worker(rank, world, port, tdir, ddir, prompt, n_new, out_dir):
+def _worker(rank, world, port, tdir, ddir, prompt, n_new, out_dir, p2p):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -59,6 +60,9 @@ def _worker(rank, world, port, tdir, ddir, prompt, n_new, out_dir):
     uid = [tp.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     tp.init_context_tp(ctx, rank, world, uid[0])
+    if p2p:
+        from androidllm_b200.ops import load_manifest
+        tp.enable_p2p(ctx, load_manifest(tdir)["config"]["hidden"])
     t = tp.device_model_tp(ctx, tdir, rank, world)
     kv = DeviceKV(t, len(prompt) + n_new + 16)
     toks, lgs = _greedy(t, kv, prompt, n_new)
@@ -84,8 +88,9 @@ def _worker(rank, world, port, tdir, ddir, prompt, n_new, out_dir):
 
 
 @pytest.mark.skipif(_n_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "p2p"])
 @pytest.mark.parametrize("name", ["toy", "minq"])
-def test_tp2_matches_single_gpu(model_dirs, tmp_path, name):
+def test_tp2_matches_single_gpu(model_dirs, tmp_path, name, p2p):
     import torch.multiprocessing as mp
     from conftest import golden
     from androidllm_b200 import shard
@@ -98,7 +103,7 @@ def test_tp2_matches_single_gpu(model_dirs, tmp_path, name):
     g = golden(f"{name}.npz")
     prompt = [int(x) for x in g["prompt"]][:24]
     n_new = 24
-    mp.spawn(_worker, args=(2, _free_port(), tdir, ddir, prompt, n_new, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), tdir, ddir, prompt, n_new, str(tmp_path), p2p), nprocs=2, join=True)
     r0, r1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / "rank1.npz")
     full = np.load(tmp_path / "full.npz")
     # both ranks hold the same tokens and logits
