@@ -87,10 +87,21 @@ def _worker(rank, world, port, tdir, ddir, prompt, n_new, out_dir, p2p):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(_n_gpus() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "p2p"])
 @pytest.mark.parametrize("name", ["toy", "minq"])
-def test_tp2_matches_single_gpu(model_dirs, tmp_path, name, p2p):
+def test_tp_matches_single_gpu(model_dirs, tmp_path, name, p2p, world):
+    """world ranks (skipped with fewer GPUs, or when the model's heads do not
+    split over them): at 4 and 8 ranks the toy's 2 kv heads are shared and
+    their query heads split."""
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from androidllm_b200 import tp
+    from androidllm_b200.ops import load_manifest
+    try:
+        tp.tp_plan(load_manifest(model_dirs[name])["config"], world)
+    except ValueError as exc:   # e.g. one 32-dim head is not a 64-column block of o
+        pytest.skip(f"{name} does not split over {world} ranks: {exc}")
     import torch.multiprocessing as mp
     from conftest import golden
     from androidllm_b200 import shard
@@ -103,10 +114,11 @@ def test_tp2_matches_single_gpu(model_dirs, tmp_path, name, p2p):
     g = golden(f"{name}.npz")
     prompt = [int(x) for x in g["prompt"]][:24]
     n_new = 24
-    mp.spawn(_worker, args=(2, _free_port(), tdir, ddir, prompt, n_new, str(tmp_path), p2p), nprocs=2, join=True)
-    r0, r1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / "rank1.npz")
+    mp.spawn(_worker, args=(world, _free_port(), tdir, ddir, prompt, n_new, str(tmp_path), p2p), nprocs=world,
+             join=True)
+    r0, r1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / f"rank{world - 1}.npz")
     full = np.load(tmp_path / "full.npz")
-    # both ranks hold the same tokens and logits
+    # the first and last ranks hold the same tokens and logits
     assert np.array_equal(r0["toks"], r1["toks"])
     assert np.array_equal(r0["logits"].view(np.uint32), r1["logits"].view(np.uint32))
     # the first step's logits against the single GPU, then teacher-free greedy
