@@ -930,6 +930,28 @@ def run_profile(args):
     return 0
 
 
+def run_profile_prefill(args):
+    """Load the workload's target and prefill --profile-prefill N prompt tokens
+    inside a CUDA profiler capture range (start ncu with --profile-from-start
+    off): 256-row chunks through the dense tcgen05 path."""
+    from androidllm_b200._lib import lib
+    from androidllm_b200.ops import Context, DeviceKV, DeviceModel
+    tdir, _ = prepare_models(args.workload)
+    ctx = Context(0)
+    t = DeviceModel.from_dir(ctx, tdir)
+    n = int(args.profile_prefill)
+    kv = DeviceKV(t, n + 16)
+    toks = np.random.default_rng(5).integers(0, t.canon["vocab"], n).tolist()
+    t.prefill(kv, toks, 0)                       # warm-up (scratch, caches)
+    lib.alm_profiler_range(1)
+    t0 = time.perf_counter()
+    t.prefill(kv, toks, 0)
+    secs = time.perf_counter() - t0
+    lib.alm_profiler_range(0)
+    print(json.dumps({"profile_prefill_tokens": n, "ms": secs * 1e3, "dense": t.uses_dense_prefill()}))
+    return 0
+
+
 _PHASES = ("qkv", "scores", "pv", "o", "gu", "down")
 
 
@@ -1059,6 +1081,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="run N steps inside a profiler capture range and exit")
     ap.add_argument("--summarize-ncu", metavar="CSV", help="aggregate an ncu launch list and exit")
+    ap.add_argument("--profile-prefill", type=int, default=0, metavar="N",
+                    help="prefill N tokens of the target inside a profiler capture range and exit")
     ap.add_argument("--temperature", type=float, default=0.0,
                     help="--profile: sampling steps at this temperature (0: greedy)")
     ap.add_argument("--top-p", type=float, default=0.9, help="--profile: nucleus of the sampling steps")
@@ -1084,6 +1108,8 @@ def main():
         return summarize_ncu(args.summarize_ncu)
     if args.profile:
         return run_profile(args)
+    if args.profile_prefill:
+        return run_profile_prefill(args)
     if args.trace_forward:
         return run_trace_forward(args)
     if args.trace_cluster:
