@@ -318,10 +318,12 @@ struct alm_model {
   std::vector<DenseLayer> dense;   // per layer; qkv null: no dense copies
   // the forward being enqueued is a multi-sequence pass (ws.rows / ws.seqs)
   int ms_n_seq = 0, ms_n_rg = 0, ms_n_pg = 0;
-  // captured multi-sequence passes: (kv, rows, sequences, row groups, P.V
-  // groups, head) -> graph; their inputs are device arrays, so a pass of the
-  // same shape replays the graph (cleared when the scratch is reallocated)
-  std::map<std::tuple<const alm_kv*, int, int, int, int, int>, cudaGraphExec_t> ms_graphs;
+  // captured multi-sequence passes: (the KV cache's buffers and geometry,
+  // rows, sequences, row groups, P.V groups, head) -> graph.  Their inputs
+  // are device arrays, so a pass of the same shape on the same buffers
+  // replays the graph (cleared when the model's scratch is reallocated).
+  using MsKey = std::tuple<const void*, const void*, const void*, int, int, int, int, int, int, int>;
+  std::map<MsKey, cudaGraphExec_t> ms_graphs;
   PrefillWork pf;
   // attention passes enqueued now are known to fit one P.V span: launch the
   // unsplit P.V kernel even when the KV capacity is longer (speed only: the
@@ -2426,7 +2428,8 @@ int alm_forward_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, 
   int M = 0;
   ALM_TRY(stage_seqs(m, kv, n_seq, slots, n_tok, pos0, tokens_host, &M));
   const bool head = logits_host != nullptr || argmax_host != nullptr;
-  const auto key = std::make_tuple(static_cast<const alm_kv*>(kv), M, n_seq, m->ms_n_rg, m->ms_n_pg, head ? 1 : 0);
+  const alm_model::MsKey key{kv->k, kv->v, kv->page_table, kv->max_len, kv->pages_per_slot, M, n_seq, m->ms_n_rg,
+                             m->ms_n_pg, head ? 1 : 0};
   cudaStream_t st = m->ctx->stream;
   int rc = ALM_OK;
   auto it = m->ms_graphs.find(key);
