@@ -57,27 +57,37 @@ cudaError_t attention_init_attrs() {
                               static_cast<int>(attn_pv_smem()));
 }
 
-cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
+cudaError_t launch_attention_scores(const AttnArgs& a, bool pdl, cudaStream_t st) {
   if (a.head_dim % 16 || a.head_dim > 256 || a.heads % a.kv_heads) return cudaErrorInvalidValue;
-  const int n_chunks_max = attn_chunks_max(a);
   const float den = static_cast<float>(sqrt(static_cast<double>(a.head_dim)));
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-
   cudaLaunchConfig_t c1 = {};
-  c1.gridDim = dim3(n_chunks_max, a.kv_heads, attn_row_groups(a));
+  c1.gridDim = dim3(attn_chunks_max(a), a.kv_heads, attn_row_groups(a));
   c1.blockDim = dim3(kAttnThreads);
   c1.dynamicSmemBytes = attn_scores_smem(a.head_dim);
   c1.stream = st;
   c1.attrs = attr;
   c1.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&c1, attn_scores_kernel, a, den);
-  if (e != cudaSuccess) return e;
-  prof_mark(3 /* ALM_OP_ATTN_SCORES */, a.M);
+  if (e == cudaSuccess) prof_mark(3 /* ALM_OP_ATTN_SCORES */, a.M);
+  return e;
+}
 
+cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st) {
+  const cudaError_t e = launch_attention_scores(a, pdl, st);
+  if (e != cudaSuccess) return e;
+  const int n_chunks_max = attn_chunks_max(a);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   const int n_split = a.pv_part ? attn_pv_spans(a.max_ctx) : 1;
-  cudaLaunchConfig_t c2 = c1;
+  cudaLaunchConfig_t c2 = {};
+  c2.blockDim = dim3(kAttnThreads);
+  c2.stream = st;
+  c2.attrs = attr;
+  c2.numAttrs = pdl ? 1 : 0;
   c2.gridDim = dim3(a.head_dim / 16, a.kv_heads, attn_pv_groups(a) * n_split);
   c2.dynamicSmemBytes = attn_pv_smem();
   if (n_split == 1) return cudaLaunchKernelEx(&c2, attn_pv_kernel, a, n_chunks_max);

@@ -151,6 +151,23 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   const int n_rg = attn_row_groups(a);
   const int lg = sv.local;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  // A chunk past the position of the group's last row is masked for every
+  // row of the group (the first chunks of a long prefill's early groups):
+  // its scores are -inf and its statistics (-inf, 0), the values the
+  // products would give, written without loading K or multiplying.
+  if (lg * kAttnRows >= n_rows || c0 > pos0 + min(n_rows - 1, lg * kAttnRows + kAttnRows - 1) / gq) {
+    const size_t row0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
+    for (int i = tid; i < kAttnRows * kAttnChunk; i += kAttnThreads) {
+      const int p = c0 + i % kAttnChunk;
+      if (p < n_ctx) a.scores[(row0 + i / kAttnChunk) * a.score_ld + p] = kNegInf;
+    }
+    if (tid < kAttnRows) {
+      float* st = a.stats + (((static_cast<size_t>(kvh) * n_rg + rg) * n_chunks_max + chunk) * kAttnRows + tid) * 2;
+      st[0] = kNegInf;
+      st[1] = 0.f;
+    }
+    return;
+  }
   const int pg0 = c0 / a.page_size;
   if (a.seqs) {
     stage_pages(a, c0, min(c0 + kAttnChunk, n_ctx), attn_scores_pg(a, smem_raw), sv.ptab);

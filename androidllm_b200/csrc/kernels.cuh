@@ -221,6 +221,15 @@ struct AttnArgs {
 constexpr int kPvSplit = kPvSpan;
 __host__ __device__ inline int attn_pv_spans(int max_ctx) { return (max_ctx + kPvSplit - 1) / kPvSplit; }
 cudaError_t launch_attention(const AttnArgs& a, bool pdl, cudaStream_t st);
+// The scores pass alone (scores and chunk statistics).
+cudaError_t launch_attention_scores(const AttnArgs& a, bool pdl, cudaStream_t st);
+// Scores, then a P.V pass with 16 query rows per block (attn_prefill.cu):
+// for passes of many rows (the batched prefill), where V is then read once
+// per 16 rows.  Equal to launch_attention up to the fp32 order of the P.V
+// sums; page_size >= 16, no split partials.
+bool attn_rows16_ok(const AttnArgs& a);
+cudaError_t launch_attention_rows16(const AttnArgs& a, bool pdl, cudaStream_t st);
+cudaError_t attn_prefill_init_attrs();
 // Scores, statistics and P.V in one launch when the pass's blocks fit on
 // the GPU at once (fz_* set); false: the caller runs launch_attention.
 bool attn_fused_ok(const AttnArgs& a);
