@@ -92,6 +92,7 @@ SIGNATURES = {
     "alm_kv_set_pages": [_P, _I, _P, _I],
     "alm_ctx_set_dense_prefill": [_P, _I],
     "alm_model_dense_prefill": [_P, _P],
+    "alm_model_max_pass_rows": [_P, _P],
     "alm_forward_trace": [_P, _P, _P, _I, _I, _P, _I, _P, _P],
     "alm_spec_create": [_P, _P, _P, _P, _I, _PP],
     "alm_spec_destroy": [_P],

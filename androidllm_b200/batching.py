@@ -11,8 +11,8 @@ same visit:
   pages, one page-table row per slot) for the target and one for the draft;
 * a speculative step of B sessions runs the k draft forwards as k
   multi-sequence passes of B rows (one per session) and the verification as
-  passes of up to 16 rows (k + 1 per session): the weights stream once per
-  pass for all its sessions (alm_forward_seqs);
+  passes of up to 64 rows (k + 1 per session; alm_model_max_pass_rows): the
+  weights stream once per pass for all its sessions (alm_forward_seqs);
 * prompts are prefilled into their slots in chunks of up to 256 rows
   through the dense path (alm_prefill_slot).
 
@@ -39,7 +39,7 @@ import numpy as np
 
 from .ops import DeviceKV
 
-MAX_PASS_ROWS = 16   # rows of one multi-sequence pass
+MAX_PASS_SEQS = 16   # sequences of one multi-sequence pass
 
 
 def kv_bytes_per_session(engine, ctx_len=None):
@@ -63,6 +63,7 @@ class BatchRunner:
         self.tkv = DeviceKV(engine.dm, self.cap, 16, slots=self.slots)
         self.draft = engine.draft
         self.dkv = DeviceKV(self.draft.dm, self.cap, 16, slots=self.slots) if self.draft is not None else None
+        self.pass_rows = engine.dm.max_pass_rows()
         self._free = list(range(self.slots))
         self._lock = threading.Lock()
 
@@ -128,8 +129,8 @@ class BatchRunner:
 
     def _plain_steps(self, sessions):
         dm = self.engine.dm
-        for i in range(0, len(sessions), MAX_PASS_ROWS):
-            group = sessions[i:i + MAX_PASS_ROWS]
+        for i in range(0, len(sessions), MAX_PASS_SEQS):
+            group = sessions[i:i + MAX_PASS_SEQS]
             for s in group:
                 s._ensure_draws(1)
             _, am = dm.forward_seqs(self.tkv, [(s.slot, [s.token], s.pos) for s in group])
@@ -147,8 +148,8 @@ class BatchRunner:
         cands = {id(s): [] for s in sessions}
         dtok = {id(s): s.token for s in sessions}
         for j in range(K):
-            for i in range(0, len(sessions), MAX_PASS_ROWS):
-                group = sessions[i:i + MAX_PASS_ROWS]
+            for i in range(0, len(sessions), MAX_PASS_SEQS):
+                group = sessions[i:i + MAX_PASS_SEQS]
                 _, am = d.forward_seqs(self.dkv, [(s.slot, [dtok[id(s)]], s.pos + j) for s in group])
                 parts = []
                 for s in group:
@@ -159,8 +160,8 @@ class BatchRunner:
                     dtok[id(s)] = p[0]
         e.stats["draft_tokens"] = e.stats.get("draft_tokens", 0) + K * len(sessions)
         # verify: k + 1 rows per session, as many sessions per pass as fit
-        per = max(1, MAX_PASS_ROWS // (K + 1))
         dm = e.dm
+        per = max(1, min(MAX_PASS_SEQS, self.pass_rows // (K + 1)))
         for i in range(0, len(sessions), per):
             group = sessions[i:i + per]
             _, am = dm.forward_seqs(self.tkv, [(s.slot, [s.token] + cands[id(s)], s.pos) for s in group])
@@ -508,4 +509,4 @@ def _broadcast(v, n):
 
 
 __all__ = ["BatchRunner", "BatchScheduler", "Session", "SessionPool", "advance", "kv_bytes_per_session",
-           "run_batch", "MAX_PASS_ROWS"]
+           "run_batch", "MAX_PASS_SEQS"]

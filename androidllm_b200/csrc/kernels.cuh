@@ -8,6 +8,11 @@ namespace alm {
 
 // Largest number of activation rows (tokens) one forward processes.
 constexpr int kMaxRows = 16;
+// Rows of one multi-sequence pass: the GEMV runs more than kMaxRows rows as
+// row groups of kMaxRows (one set of CTAs per group, each computing exactly
+// what a pass of its rows alone computes).
+constexpr int kMaxPassRows = 64;
+constexpr int kMaxRowGroups = kMaxPassRows / kMaxRows;
 // Attention position chunk and row group.
 constexpr int kAttnChunk = 64;
 constexpr int kAttnRows = 16;

@@ -390,7 +390,7 @@ size_t src_bytes(int bits, int rows, int k_pad) {
 // kernel); smaller ones keep the mma.sync tile layout.
 constexpr size_t kRowMinBytes = 4u << 20;
 // pinned staging of a multi-sequence pass: rows, sequences, tokens
-constexpr size_t kSeqStaging = kMaxRows * (sizeof(int2) + sizeof(AttnSeq) + sizeof(int));
+constexpr size_t kSeqStaging = kMaxPassRows * (sizeof(int2) + sizeof(AttnSeq) + sizeof(int));
 
 bool use_rows(const alm_ctx* ctx, int bits, int block, int n_rows, int in) {
   if ((bits != 4 && bits != 8) || block % 64 != 0 || ctx->tc == 0) return false;
@@ -486,7 +486,7 @@ int build_qweight(alm_ctx* ctx, const alm_proj_src* srcs, int n_src,
     const int vec = bits == 4 ? 1 : bits == 8 ? 2 : 4;
     t.rec_u4 = vec * kWarp + t.sb * 2;   // codes + 8 half2 scales (32 B) per set
     n_rec = static_cast<size_t>(t.n_tiles) * t.k_blocks;
-    n_counters = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+    n_counters = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw) * kMaxRowGroups;   // per row group
   }
   const std::vector<int> dst_map = map_of(t.layout);
   // every destination row must name an existing source row: the repack
@@ -576,7 +576,7 @@ std::function<std::vector<int>(int)> identity_map(int rows) {
 }
 
 // Split-K scratch large enough for weight w (floats).
-size_t split_need(const alm_qweight* w) { return w ? gemv_part_floats(w->t) : 0; }
+size_t split_need(const alm_qweight* w) { return w ? gemv_part_floats(w->t, kMaxPassRows) : 0; }
 
 int ensure_part(Work& ws, size_t need) {
   if (need <= ws.part_floats) return ALM_OK;
@@ -590,13 +590,15 @@ int ensure_part(Work& ws, size_t need) {
 
 int ensure_attn(alm_model* m, int max_ctx) {
   Work& ws = m->ws;
-  if (max_ctx <= ws.attn_ctx) return ALM_OK;
+  if (max_ctx <= ws.attn_ctx && (!m->ctx->attn_fused || ws.fz_part)) return ALM_OK;
+  max_ctx = std::max(max_ctx, ws.attn_ctx);
   for (auto& kvg : m->ms_graphs) cudaGraphExecDestroy(kvg.second);   // they hold the old scratch
   m->ms_graphs.clear();
   const int gq = m->cfg.heads / m->cfg.kv_heads;
-  // row groups of the largest pass; a multi-sequence pass starts a group per
-  // sequence, which adds at most one per sequence
-  const int n_rg = (kMaxRows * gq + kAttnRows - 1) / kAttnRows + kMaxRows;
+  // row groups of the largest pass; a multi-sequence pass (up to kMaxPassRows
+  // rows of up to kMaxRows sequences) starts a group per sequence, which
+  // adds at most one per sequence
+  const int n_rg = (kMaxPassRows * gq + kAttnRows - 1) / kAttnRows + kMaxRows;
   const int cap = (max_ctx + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
   dev_free(ws.scores);
   dev_free(ws.stats);
@@ -623,14 +625,17 @@ int ensure_attn(alm_model* m, int max_ctx) {
   ALM_TRY(dev_alloc_t(&ws.pv_part, keys * attn_pv_spans(cap) * kPvRows * 16));
   ALM_TRY(dev_alloc_t(&ws.pv_ticket, keys));
   ALM_CUDA(cudaMemset(ws.pv_ticket, 0, keys * sizeof(unsigned)));
-  // one-launch attention: (kv head, row group) counters and tickets, and a
-  // (kv head, row group, chunk) partial of 16 rows x head_dim
-  const size_t fz_keys = static_cast<size_t>(m->cfg.kv_heads) * n_rg;
-  ALM_TRY(dev_alloc_t(&ws.fz_count, fz_keys));
-  ALM_TRY(dev_alloc_t(&ws.fz_ticket, fz_keys));
-  ALM_CUDA(cudaMemset(ws.fz_count, 0, fz_keys * sizeof(unsigned)));
-  ALM_CUDA(cudaMemset(ws.fz_ticket, 0, fz_keys * sizeof(unsigned)));
-  ALM_TRY(dev_alloc_t(&ws.fz_part, fz_keys * (cap / kAttnChunk) * kAttnRows * m->cfg.head_dim));
+  // one-launch attention (only on a context that enables it; without them
+  // the layer takes the two passes): (kv head, row group) counters and
+  // tickets, and a (kv head, row group, chunk) partial of 16 rows x head_dim
+  if (m->ctx->attn_fused) {
+    const size_t fz_keys = static_cast<size_t>(m->cfg.kv_heads) * n_rg;
+    ALM_TRY(dev_alloc_t(&ws.fz_count, fz_keys));
+    ALM_TRY(dev_alloc_t(&ws.fz_ticket, fz_keys));
+    ALM_CUDA(cudaMemset(ws.fz_count, 0, fz_keys * sizeof(unsigned)));
+    ALM_CUDA(cudaMemset(ws.fz_ticket, 0, fz_keys * sizeof(unsigned)));
+    ALM_TRY(dev_alloc_t(&ws.fz_part, fz_keys * (cap / kAttnChunk) * kAttnRows * m->cfg.head_dim));
+  }
   ws.attn_ctx = cap;
   ws.score_ld = ld;
   return ALM_OK;
@@ -778,7 +783,7 @@ int enqueue_layer(alm_model* m, int li, alm_kv* kv, int M, const ActIn& in, bool
     a.n_pg = m->ms_n_pg;
     a.pv_part = nullptr;
   }
-  if (m->ctx->attn_fused) {
+  if (m->ctx->attn_fused && ws.fz_part) {
     a.fz_count = ws.fz_count;
     a.fz_ticket = ws.fz_ticket;
     a.fz_part = ws.fz_part;
@@ -1245,7 +1250,7 @@ SampleArgs sample_args(alm_model* m, float temperature, float top_p, float min_p
 
 int ensure_sample_scratch(alm_model* m) {
   if (!m->ws.sample_scratch)
-    ALM_TRY(dev_alloc_t(&m->ws.sample_scratch, static_cast<size_t>(kMaxRows) * m->cfg.vocab));
+    ALM_TRY(dev_alloc_t(&m->ws.sample_scratch, static_cast<size_t>(kMaxPassRows) * m->cfg.vocab));
   return ALM_OK;
 }
 
@@ -1551,7 +1556,7 @@ int alm_qweight_set_split(alm_qweight* w, int ksw, int ksg) {
             "ksw must be 1, 2, 4 or 8 and ksw * ksg at most the number of 64-column blocks");
     set_split(t, ksw, ksg);
     ALM_REQ(t.ksw * t.kps <= 64, "per-CTA activation staging would exceed shared memory");
-    grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw);
+    grid_x = (t.n_tiles + 8 / t.ksw - 1) / (8 / t.ksw) * kMaxRowGroups;   // per row group
   }
   unsigned* counters = nullptr;
   ALM_TRY(dev_alloc_t(&counters, grid_x));
@@ -1933,26 +1938,28 @@ int alm_model_finalize(alm_model* m) {
   Work& ws = m->ws;
   if (!ws.x0) {
     const int H = c.hidden, ht = n_h_tiles(m), qd = c.heads * c.head_dim;
-    ALM_TRY(dev_alloc_t(&ws.tokens, kMaxRows));
-    ALM_TRY(dev_alloc_t(&ws.rows, kMaxRows));
+    // row buffers hold the largest multi-sequence pass
+    const size_t R = kMaxPassRows;
+    ALM_TRY(dev_alloc_t(&ws.tokens, R));
+    ALM_TRY(dev_alloc_t(&ws.rows, R));
     ALM_TRY(dev_alloc_t(&ws.seqs, kMaxRows));
-    ALM_TRY(dev_alloc_t(&ws.u_rows, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.u_rows, R));
     ALM_CUDA(cudaMallocHost(&ws.seq_host, kSeqStaging));
     ALM_TRY(dev_alloc_t(&ws.pos, 1));
     ALM_TRY(dev_alloc_t(&ws.err, 1));
     ALM_CUDA(cudaMemset(ws.err, 0, sizeof(int)));
-    ALM_TRY(dev_alloc_t(&ws.x0, static_cast<size_t>(kMaxRows) * H));
-    ALM_TRY(dev_alloc_t(&ws.s1, static_cast<size_t>(kMaxRows) * H));
-    ALM_TRY(dev_alloc_t(&ws.s2, static_cast<size_t>(kMaxRows) * H));
-    ALM_TRY(dev_alloc_t(&ws.ss1, static_cast<size_t>(kMaxRows) * ht));
-    ALM_TRY(dev_alloc_t(&ws.ss2, static_cast<size_t>(kMaxRows) * ht));
-    ALM_TRY(dev_alloc_t(&ws.q, static_cast<size_t>(kMaxRows) * qd));
-    ALM_TRY(dev_alloc_t(&ws.ctx, static_cast<size_t>(kMaxRows) * qd));
-    ALM_TRY(dev_alloc_t(&ws.h, static_cast<size_t>(kMaxRows) * c.intermediate));
-    ALM_TRY(dev_alloc_t(&ws.xn, static_cast<size_t>(kMaxRows) * H));
-    ALM_TRY(dev_alloc_t(&ws.xout, static_cast<size_t>(kMaxRows) * H));
-    ALM_TRY(dev_alloc_t(&ws.logits, static_cast<size_t>(kMaxRows) * c.vocab));
-    ALM_TRY(dev_alloc_t(&ws.argmax, kMaxRows));
+    ALM_TRY(dev_alloc_t(&ws.x0, R * H));
+    ALM_TRY(dev_alloc_t(&ws.s1, R * H));
+    ALM_TRY(dev_alloc_t(&ws.s2, R * H));
+    ALM_TRY(dev_alloc_t(&ws.ss1, R * ht));
+    ALM_TRY(dev_alloc_t(&ws.ss2, R * ht));
+    ALM_TRY(dev_alloc_t(&ws.q, R * qd));
+    ALM_TRY(dev_alloc_t(&ws.ctx, R * qd));
+    ALM_TRY(dev_alloc_t(&ws.h, R * c.intermediate));
+    ALM_TRY(dev_alloc_t(&ws.xn, R * H));
+    ALM_TRY(dev_alloc_t(&ws.xout, R * H));
+    ALM_TRY(dev_alloc_t(&ws.logits, R * c.vocab));
+    ALM_TRY(dev_alloc_t(&ws.argmax, R));
     ALM_CUDA(cudaMallocHost(reinterpret_cast<void**>(&ws.pinned), 64 * sizeof(int)));
   }
   if (m->tp && !ws.o32) {
@@ -1969,8 +1976,8 @@ int alm_model_finalize(alm_model* m) {
     dev_free(ws.am_idx);
     ws.am_val = nullptr;
     ws.am_idx = nullptr;
-    ALM_TRY(dev_alloc_t(&ws.am_val, static_cast<size_t>(kMaxRows) * n_am));
-    ALM_TRY(dev_alloc_t(&ws.am_idx, static_cast<size_t>(kMaxRows) * n_am));
+    ALM_TRY(dev_alloc_t(&ws.am_val, static_cast<size_t>(kMaxPassRows) * n_am));
+    ALM_TRY(dev_alloc_t(&ws.am_idx, static_cast<size_t>(kMaxPassRows) * n_am));
   }
   ws.n_am = n_am;
   size_t need = split_need(m->head);
@@ -2340,7 +2347,7 @@ int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, f
                           const double* uniforms_host, int32_t* out_host) {
   ALM_TRY(check_ready(m));
   ALM_REQ(out_host && (uniforms_host || !(temperature > 0.f)), "null argument");
-  ALM_REQ(row0 >= 0 && rows >= 1 && row0 + rows <= kMaxRows, "rows must lie in 0..15");
+  ALM_REQ(row0 >= 0 && rows >= 1 && row0 + rows <= kMaxPassRows, "rows must lie in 0..63");
   ALM_REQ(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
   ALM_REQ(min_p >= 0.f && min_p < 1.f, "min_p must be in [0, 1)");
   DeviceGuard g(m->ctx->device);
@@ -2367,6 +2374,10 @@ int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, f
   return rc;
 }
 
+// Rows of one multi-sequence pass: row groups of the M <= 16 GEMV up to
+// kMaxPassRows; the tcgen05 decode weights' fused epilogues take 16.
+static int max_pass_rows(const alm_model* m) { return m->ctx->tc ? kMaxRows : kMaxPassRows; }
+
 // Check and upload a multi-sequence pass's rows and sequences (ws.rows,
 // ws.seqs) and mark the model's next enqueue as that pass; *M_out = rows.
 static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
@@ -2386,7 +2397,7 @@ static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots,
     ALM_REQ(static_cast<long long>(pos0[s]) + n_tok[s] <= kv->max_len &&
                 static_cast<long long>(pos0[s]) + n_tok[s] <= m->cfg.max_len,
             "pos out of kv cache or rope table range");
-    ALM_REQ(static_cast<int>(rows.size()) + n_tok[s] <= kMaxRows, "at most 16 rows per pass");
+    ALM_REQ(static_cast<int>(rows.size()) + n_tok[s] <= max_pass_rows(m), "more rows than alm_model_max_pass_rows");
     const int off = slots[s] * kv->pages_per_slot;
     seqs[s] = AttnSeq{static_cast<int>(rows.size()), n_tok[s], pos0[s], off, g, pg};
     for (int t = 0; t < n_tok[s]; ++t) rows.push_back(make_int2(pos0[s] + t, off));
@@ -2399,13 +2410,13 @@ static int stage_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots,
   const int M = static_cast<int>(rows.size());
   unsigned char* h = m->ws.seq_host;
   std::memcpy(h, rows.data(), M * sizeof(int2));
-  std::memcpy(h + kMaxRows * sizeof(int2), seqs.data(), n_seq * sizeof(AttnSeq));
-  std::memcpy(h + kMaxRows * (sizeof(int2) + sizeof(AttnSeq)), tokens_host, M * sizeof(int));
+  std::memcpy(h + kMaxPassRows * sizeof(int2), seqs.data(), n_seq * sizeof(AttnSeq));
+  std::memcpy(h + kMaxPassRows * (sizeof(int2) + sizeof(AttnSeq)), tokens_host, M * sizeof(int));
   cudaStream_t st = m->ctx->stream;
   ALM_CUDA(cudaMemcpyAsync(m->ws.rows, h, M * sizeof(int2), cudaMemcpyHostToDevice, st));
-  ALM_CUDA(cudaMemcpyAsync(m->ws.seqs, h + kMaxRows * sizeof(int2), n_seq * sizeof(AttnSeq),
+  ALM_CUDA(cudaMemcpyAsync(m->ws.seqs, h + kMaxPassRows * sizeof(int2), n_seq * sizeof(AttnSeq),
                            cudaMemcpyHostToDevice, st));
-  ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, h + kMaxRows * (sizeof(int2) + sizeof(AttnSeq)), M * sizeof(int),
+  ALM_CUDA(cudaMemcpyAsync(m->ws.tokens, h + kMaxPassRows * (sizeof(int2) + sizeof(AttnSeq)), M * sizeof(int),
                            cudaMemcpyHostToDevice, st));
   m->ms_n_seq = n_seq;
   m->ms_n_rg = g;
@@ -2511,6 +2522,12 @@ int alm_prefill_slot(alm_model* m, alm_kv* kv, int slot, const int32_t* tokens_h
 int alm_ctx_set_dense_prefill(alm_ctx* ctx, int enable) {
   ALM_REQ(ctx, "null context");
   ctx->dense_prefill = enable != 0;
+  return ALM_OK;
+}
+
+int alm_model_max_pass_rows(const alm_model* m, int* rows) {
+  ALM_REQ(m && rows, "null argument");
+  *rows = m->tp ? 0 : max_pass_rows(m);
   return ALM_OK;
 }
 

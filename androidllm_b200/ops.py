@@ -329,6 +329,12 @@ class DeviceModel:
         check(lib.alm_model_dense_prefill(self.h, ctypes.byref(v)))
         return bool(v.value)
 
+    def max_pass_rows(self):
+        """Most rows one forward_seqs pass takes (alm_model_max_pass_rows)."""
+        v = ctypes.c_int32()
+        check(lib.alm_model_max_pass_rows(self.h, ctypes.byref(v)))
+        return v.value
+
     def prefill(self, kv, tokens, pos0=0, slot=0):
         """Fill kv (slot ``slot``) for positions pos0 .. pos0 + len(tokens) - 1
         (alm_prefill_slot): the prompt's forwards without logits, in chunks of

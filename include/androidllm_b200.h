@@ -283,8 +283,8 @@ ALM_API int alm_accept(alm_ctx* ctx, const uint16_t* target_logits_host, const f
  * (alm_forward with a head) without copying them to the host. */
 ALM_API int alm_model_sample(alm_model* m, int rows, float temperature, float top_p, float min_p,
                        const double* uniforms_host, int32_t* out_host);
-/* alm_model_sample on rows row0 .. row0 + rows - 1 of the last logits (one
- * sequence of a multi-sequence pass). */
+/* alm_model_sample on rows row0 .. row0 + rows - 1 (row0 + rows <= 64) of
+ * the last logits (one sequence of a multi-sequence pass). */
 ALM_API int alm_model_sample_rows(alm_model* m, int row0, int rows, float temperature, float top_p, float min_p,
                                   const double* uniforms_host, int32_t* out_host);
 /* Embedding + every layer + final norm + head for tokens at positions
@@ -294,11 +294,17 @@ ALM_API int alm_forward(alm_model* m, alm_kv* kv, const int32_t* tokens_host, in
 /* Several sequences in one forward (batched sessions; the reference steps
  * them one at a time, androidllm/batching.py:200-272): sequence s has
  * n_tok[s] consecutive rows of tokens_host at positions pos0[s].. of KV slot
- * slots[s] (distinct slots, at most 16 rows in all).  Logits / argmax rows
- * follow tokens_host; each equals its sequence's own alm_forward. */
+ * slots[s] (at most 16 sequences in distinct slots, at most
+ * alm_model_max_pass_rows rows in all).  Logits / argmax rows follow
+ * tokens_host; each equals its sequence's own alm_forward. */
 ALM_API int alm_forward_seqs(alm_model* m, alm_kv* kv, int n_seq, const int32_t* slots, const int32_t* n_tok,
                              const int32_t* pos0, const int32_t* tokens_host, float* logits_host,
                              int32_t* argmax_host);
+/* *rows = the most rows one alm_forward_seqs pass takes: 64 (the weights
+ * stream once per pass, 16-row groups each computing what a pass of their
+ * rows alone computes), 16 on a context with tcgen05 decode weights, 0 for
+ * a tensor-parallel model (no multi-sequence passes). */
+ALM_API int alm_model_max_pass_rows(const alm_model* m, int* rows);
 /* Prompt prefill: fills the KV cache for positions pos0..pos0+n-1 from the
  * tokens, no logits.  Replaces the per-token forwards of the prompt in
  * androidllm/engine.py:345-361.  Chunks of up to 256 rows run every

@@ -50,6 +50,47 @@ def test_forward_seqs_equals_single_sequence_forwards(ctx, model_dirs, name):
             assert np.array_equal(v1.view(np.uint16), v2.view(np.uint16)), (i, li)
 
 
+@pytest.mark.parametrize("name", ["toyu", "minq"])
+def test_pass_of_64_rows_equals_single_sequence_forwards(ctx, model_dirs, name):
+    """A pass of 64 rows (13 sequences of 1-8 rows: four 16-row groups of
+    the GEMV, groups cutting through sequences) equals each sequence's own
+    forward bit for bit: logits, argmax and the new KV entries; sampling
+    rows past the 16th of the pass matches sampling them alone."""
+    from androidllm_b200.ops import DeviceKV, DeviceModel
+    m = DeviceModel.from_dir(ctx, model_dirs[name])
+    assert m.max_pass_rows() == 64
+    rng = np.random.default_rng(31)
+    V = m.canon["vocab"]
+    rows = [5, 5, 1, 8, 5, 3, 7, 5, 2, 6, 5, 4, 8]
+    assert sum(rows) == 64
+    lens = [int(rng.integers(3, 90)) for _ in rows]
+    slots = list(range(len(rows)))[::-1]
+    prompts = [rng.integers(0, V, n).tolist() for n in lens]
+    new = [rng.integers(0, V, r).tolist() for r in rows]
+    cap = 112
+    multi = DeviceKV(m, cap, 16, slots=len(rows))
+    for p, s in zip(prompts, slots):
+        m.prefill(multi, p, 0, slot=s)
+    lg_m, am_m = m.forward_seqs(multi, [(s, t, len(p)) for s, t, p in zip(slots, new, prompts)], logits=True)
+    u = rng.random(64)
+    picks_m = m.sample_rows(0, 64, 0.8, 0.9, 0.0, u)
+    for i, (p, t) in enumerate(zip(prompts, new)):
+        kv = DeviceKV(m, cap, 16)
+        m.prefill(kv, p, 0)
+        lg, am = m.forward(kv, t, len(p), logits=True)
+        assert np.array_equal(lg_m[i].view(np.uint32), lg.view(np.uint32)), i
+        assert np.array_equal(am_m[i], am), i
+        r0 = sum(rows[:i])
+        assert np.array_equal(picks_m[r0:r0 + rows[i]], m.sample_rows(0, rows[i], 0.8, 0.9, 0.0, u[r0:r0 + rows[i]])), i
+        for li in range(m.canon["layers"]):
+            k1, v1 = multi.read(li, 0, len(p) + len(t), slot=slots[i])
+            k2, v2 = kv.read(li, 0, len(p) + len(t))
+            assert np.array_equal(k1.view(np.uint16), k2.view(np.uint16)), (i, li)
+            assert np.array_equal(v1.view(np.uint16), v2.view(np.uint16)), (i, li)
+    with pytest.raises(Exception):
+        m.forward_seqs(multi, [(s, [1] * 5, 90) for s in range(13)])   # 65 rows
+
+
 def test_slot_pages_remapped(ctx, model_dirs):
     """A slot whose pages are remapped (alm_kv_set_pages) still gives the
     single-sequence forward's logits."""
