@@ -9,8 +9,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a, f
   __shared__ AttnShared sh;
   attn_scores_pages(a, blockIdx.x, smem_raw);   // the page table is not written by earlier kernels
   __syncthreads();
-  grid_dep_wait();
-  attn_scores_body(a, inv_sqrt_den, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.x, smem_raw, sh);
+  attn_scores_body<false>(a, inv_sqrt_den, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.x, smem_raw, sh, DepWait{});
   grid_dep_launch();
 }
 
@@ -20,8 +19,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_kernel(AttnArgs a, int n
   __shared__ AttnShared sh;
   attn_pv_pages(a, smem_raw);
   __syncthreads();
-  grid_dep_wait();
-  attn_pv_body(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh);
+  attn_pv_body<false, false>(a, n_chunks_max, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw, sh, 0, 1, DepWait{});
 }
 
 // Span split (KV capacity above one span): grid (16-dim slice, kv head,

@@ -131,9 +131,12 @@ ALM_DEV void attn_scores_pages(const AttnArgs& a, int chunk, unsigned char* smem
 
 // Scores of (chunk, kv head, row group); n_chunks_max = the grid's chunk count.
 // Precondition: attn_scores_pages for this chunk, then a block barrier.
-template <bool NAMED = false>
+// wait(): the dependency wait for the q rows and the pass's new K rows; a
+// chunk that ends before the pass's first position has its K rows loaded
+// before it (they were written by earlier passes).  Every return passes it.
+template <bool NAMED = false, class Wait = NoWait>
 ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, int kvh, int rg, int n_chunks_max,
-                              unsigned char* smem_raw, AttnShared& sh) {
+                              unsigned char* smem_raw, AttnShared& sh, Wait wait = Wait{}) {
   const int hd = a.head_dim, ld = hd + 8;
   half* qhi = reinterpret_cast<half*>(smem_raw);
   half* qlo = qhi + kAttnRows * ld;
@@ -145,7 +148,10 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   const int pos0 = sv.pos0;
   const int n_ctx = pos0 + sv.n_tok;
   const int c0 = chunk * kAttnChunk;
-  if (c0 >= n_ctx) return;
+  if (c0 >= n_ctx) {
+    wait();
+    return;
+  }
   const int gq = a.heads / a.kv_heads;
   const int n_rows = sv.n_tok * gq;
   const int n_rg = attn_row_groups(a);
@@ -156,6 +162,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   // its scores are -inf and its statistics (-inf, 0), the values the
   // products would give, written without loading K or multiplying.
   if (lg * kAttnRows >= n_rows || c0 > pos0 + min(n_rows - 1, lg * kAttnRows + kAttnRows - 1) / gq) {
+    wait();
     const size_t row0 = (static_cast<size_t>(kvh) * n_rg + rg) * kAttnRows;
     for (int i = tid; i < kAttnRows * kAttnChunk; i += kAttnThreads) {
       const int p = c0 + i % kAttnChunk;
@@ -180,6 +187,21 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
   const int vec_per_row = hd / 8, nv = kAttnChunk * vec_per_row;
   float4 qv[4];
   uint4 kv8[8];
+  auto load_k = [&]() {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = j * kAttnThreads + tid;
+      const int p = c0 + i / vec_per_row;
+      kv8[j] = make_uint4(0, 0, 0, 0);
+      if (i < nv && p < n_ctx)
+        kv8[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, s_pg, pg0, a.page_size, a.kv_heads, kvh, hd,
+                                                              p)) +
+                        i % vec_per_row);
+    }
+  };
+  const bool k_early = c0 + kAttnChunk <= pos0;
+  if (k_early) load_k();
+  wait();
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int i = j * kAttnThreads + tid;
@@ -191,15 +213,7 @@ ALM_DEV void attn_scores_body(const AttnArgs& a, float inv_sqrt_den, int chunk, 
       qv[j] = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(m) * a.ldq + head * hd) + d4);
     }
   }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int i = j * kAttnThreads + tid;
-    const int p = c0 + i / vec_per_row;
-    kv8[j] = make_uint4(0, 0, 0, 0);
-    if (i < nv && p < n_ctx)
-      kv8[j] = __ldcg(reinterpret_cast<const uint4*>(kv_row(a.kcache, s_pg, pg0, a.page_size, a.kv_heads, kvh, hd, p)) +
-                      i % vec_per_row);
-  }
+  if (!k_early) load_k();
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int i = j * kAttnThreads + tid;
@@ -336,9 +350,12 @@ ALM_DEV void attn_pv_pages(const AttnArgs& a, unsigned char* smem_raw, int sp = 
 // Without SPLIT the body is compiled for one span (sp = 0, n_split = 1):
 // the split's bookkeeping costs a short context about a microsecond.
 // Precondition: attn_pv_pages(sp), then a block barrier.
-template <bool NAMED = false, bool SPLIT = false>
+// wait(): the dependency wait for the scores and statistics; the first
+// span's V rows (written by the pass's QKV kernel and earlier passes) are
+// loaded before it.  Every return passes it.
+template <bool NAMED = false, bool SPLIT = false, class Wait = NoWait>
 ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, int grp, unsigned char* smem_raw,
-                          AttnShared& sh, int sp = 0, int n_split = 1) {
+                          AttnShared& sh, int sp = 0, int n_split = 1, Wait wait = Wait{}) {
   half* vs = reinterpret_cast<half*>(smem_raw);      // [kPvSpan][kPvVld]
   half* ps = vs + kPvSpan * kPvVld;                  // [kPvRows][kPvPld]
   float* s_acc = reinterpret_cast<float*>(ps + kPvRows * kPvPld);   // [kAttnWarps][kWarp][8]
@@ -354,11 +371,12 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   const int n_rows = seq.n_tok * gq;
   const int n_rg = attn_row_groups(a);
   const int r0 = seq.local * kPvRows;
-  if (r0 >= n_rows) return;
   const int needed = (n_ctx + kPvSplit - 1) / kPvSplit;
   const bool split = SPLIT && a.pv_part != nullptr && n_split > 1 && needed > 1;
-  if (!split && sp > 0) return;
-  if (split && sp >= needed) return;
+  if (r0 >= n_rows || (!split && sp > 0) || (split && sp >= needed)) {
+    wait();
+    return;
+  }
   const int span_begin = split ? sp * kPvSplit : 0;
   const int span_end = split ? min(span_begin + kPvSplit, n_ctx) : n_ctx;
   const int rg = seq.g0 + r0 / kAttnRows, rl0 = r0 % kAttnRows;   // scores / stats row group of the pass
@@ -375,9 +393,9 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
   // scores (kPvRows * span_pad / 4 <= kAttnThreads * 4 float4s).
   uint4 v[8];
   float4 sv[4];
-  auto load_span = [&](int base, int span_pad) {
+  auto load_v = [&](int base, int span_pad) {
     const int pg0 = base / a.page_size;
-    const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
+    const int nv = span_pad * 2;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int i = j * kAttnThreads + tid;
@@ -388,6 +406,9 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
                           kv_row(a.vcache, s_pg, pg0, a.page_size, a.kv_heads, kvh, hd, p) + ds * 16) +
                       (i & 1));
     }
+  };
+  auto load_scores = [&](int base, int span_pad) {
+    const int per_row4 = span_pad / 4, np = kPvRows * per_row4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int i = j * kAttnThreads + tid;
@@ -398,8 +419,12 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     }
   };
 
-  // statistics of the first 128 chunks (one warp per row) in the same load
-  // phase as the first span's V slice and scores
+  // the first span's V slice before the wait; then the statistics of the
+  // first 128 chunks (one warp per row) and the span's scores in one load
+  // phase
+  const int pad0 = (min(kPvSpan, span_end - span_begin) + 15) & ~15;
+  load_v(span_begin, pad0);
+  wait();
   float mc0[4], lc0[4];
   if (warp < kPvRows) {
     const int rl = rl0 + warp;
@@ -412,7 +437,7 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
       lc0[j] = f.y;
     }
   }
-  load_span(span_begin, (min(kPvSpan, span_end - span_begin) + 15) & ~15);
+  load_scores(span_begin, pad0);
 
   // row max / sum from the chunk statistics: one warp per row, lane l takes
   // chunks l, l+32, ... in order, then a butterfly (fixed order; chunks past
@@ -466,7 +491,8 @@ ALM_DEV void attn_pv_body(const AttnArgs& a, int n_chunks_max, int ds, int kvh, 
     if (base > span_begin) {   // the first span was loaded with the statistics
       stage_pages(a, base, base + span, s_pg, seq.ptab);
       body_sync_t<NAMED>();
-      load_span(base, span_pad);
+      load_v(base, span_pad);
+      load_scores(base, span_pad);
     }
     const int nv = span_pad * 2, per_row4 = span_pad / 4, np = kPvRows * per_row4;
 #pragma unroll

@@ -134,6 +134,16 @@ ALM_DEV bool better(float v1, int i1, float v2, int i2) { return v1 > v2 || (v1 
 // the next grid in the stream start its prologue.  No-ops without PDL.
 ALM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 ALM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+// Where a shared body passes its dependency wait: a standalone kernel gives
+// DepWait (the body loads what earlier kernels wrote before it, then waits
+// for its producer); persistent kernels, whose phases are ordered by grid
+// barriers, give NoWait.
+struct NoWait {
+  ALM_DEV void operator()() const {}
+};
+struct DepWait {
+  ALM_DEV void operator()() const { grid_dep_wait(); }
+};
 
 // ---------------------------------------------------------------------------
 // bit tricks for int4/int8 -> fp16 (exact small integers)

@@ -39,7 +39,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(QTile w, ActIn in
   const int grp = blockIdx.x % n_groups, gx = gridDim.x / n_groups;
   const GemvPlan plan = gemv_plan(w, Pipe<BITS>::kItems, blockIdx.x / n_groups, blockIdx.y, gx);
   gemv_issue_first<BITS>(ring, w, plan, 0);
-  grid_dep_wait();
   uint4* xs = reinterpret_cast<uint4*>(smem + ring_bytes(slot_bytes));
   if (n_groups > 1) {
     const int r0 = grp * kMaxRows;
@@ -58,7 +57,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(QTile w, ActIn in
     if (w.counters) w.counters += static_cast<size_t>(grp) * gx;
     if (part) part += static_cast<size_t>(grp) * gemv_group_part_floats(w);
   }
-  gemv_run<BITS, SB, NT8, EPI>(w, in, M, epi, io, part, plan, ring, 0, xs, sh);
+  // epilogue operands from earlier kernels, then the wait for the activations
+  GemvPre<NT8> pre;
+  gemv_prefetch<NT8, EPI>(w, M, epi, io, plan, sh, pre);
+  grid_dep_wait();
+  gemv_run<BITS, SB, NT8, EPI, true>(w, in, M, epi, io, part, plan, ring, 0, xs, sh, &pre);
 }
 
 template <int BITS, int NT8, int EPI>

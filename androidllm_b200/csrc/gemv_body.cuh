@@ -178,10 +178,79 @@ ALM_DEV void gemv_issue_first(const Ring& r, const QTile& w, const GemvPlan& p, 
 // every offset inside a record is a compile-time constant.
 // xs: activation staging (gemv_stage_bytes).  Returns the chunks that went
 // through the warp's ring (the caller adds them to its seq).
-template <int BITS, int SB, int NT8, int EPI>
+// Epilogue operands that do not come from the kernel the GEMV waits for, in
+// the owner threads' registers.  Under programmatic dependent launch a kernel
+// starts only after every CTA of its predecessor has passed its own
+// dependency wait, so the kernel before that one has completed and its
+// writes are visible: the residual (written two or more kernels back), its
+// norm partials, the RoPE table, the positions and the page table can be
+// read before this kernel's wait.  Only the standalone kernel uses this; the
+// persistent forward reads them in the epilogue.
+template <int NT8>
+struct GemvPre {
+  float res[NT8][2][2];            // RESID: residual operand (deferred norm applied)
+  float cs[NT8][2], sn[NT8][2];    // QKV: RoPE cos / sin of the owner's rows
+  int page[NT8][2];                // QKV: K / V cache page of the owner's rows
+};
+
+template <int NT8, int EPI>
+ALM_DEV void gemv_prefetch(const QTile& w, int M, const Epi& epi, const StepIO& io, const GemvPlan& p,
+                           GemvShared<NT8>& sh, GemvPre<NT8>& pre) {
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int g = lane >> 2, t = lane & 3;
+  const int tile = p.tile;
+  const bool owner = p.kw == 0 && p.tile_ok;
+  if constexpr (EPI == EPI_RESID) {
+    const ActIn& rs = epi.res;
+    if (rs.ss) {
+      for (int m = warp; m < M; m += kGemvWarps) {
+        const float d = row_denominator(rs, m);
+        if (lane == 0) sh.den_res[m] = d;
+      }
+      __syncthreads();
+    }
+    if (owner) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = tile * 16 + g + 8 * r;
+        const float rw = (rs.ss && row < epi.n_out) ? __half2float(__ldg(rs.w + row)) : 1.f;
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = nt * 8 + 2 * t + j;
+            const bool ok = m < M && row < epi.n_out;
+            const float v = ok ? __half2float(__ldcg(rs.x + static_cast<size_t>(m) * rs.ld + row)) : 0.f;
+            pre.res[nt][r][j] = (rs.ss && ok) ? norm_value(v, sh.den_res[m], rw) : v;
+          }
+      }
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    if (owner) {
+      const int hd = epi.head_dim, half_d = hd / 2, tph = hd / 16;
+      const int tq = epi.heads * tph, tk = epi.kv_heads * tph;
+      const int pos0 = epi.rows ? 0 : *io.pos;
+      const bool rope = tile < tq + tk;
+      const int dlo = (tile % tph) * 8 + g;
+#pragma unroll
+      for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int m = nt * 8 + 2 * t + j, mm = m < M ? m : 0;
+          const int pos = epi.rows ? epi.rows[mm].x : pos0 + mm;
+          const int* pt = epi.rows ? epi.page_table + epi.rows[mm].y : epi.page_table;
+          pre.cs[nt][j] = rope ? __half2float(__ldg(epi.rope + static_cast<size_t>(pos) * hd + dlo)) : 0.f;
+          pre.sn[nt][j] = rope ? __half2float(__ldg(epi.rope + static_cast<size_t>(pos) * hd + half_d + dlo)) : 0.f;
+          pre.page[nt][j] = tile >= tq ? __ldg(pt + pos / epi.page_size) : 0;
+        }
+    }
+  }
+}
+
+template <int BITS, int SB, int NT8, int EPI, bool PRE = false>
 ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, const StepIO& io,
                      float* __restrict__ part, const GemvPlan& p, const Ring& ring, uint32_t seq,
-                     uint4* __restrict__ xs, GemvShared<NT8>& sh) {
+                     uint4* __restrict__ xs, GemvShared<NT8>& sh, const GemvPre<NT8>* pre = nullptr) {
   constexpr int V = QTileTraits<BITS>::kVec;
   constexpr int IPS = Pipe<BITS>::kItems;
   constexpr int REC = (V * kWarp + SB * 2) * 16;   // record bytes (w.rec_u4 * 16)
@@ -197,19 +266,24 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
   uint64_t* bars = ring.bars + warp * kSlots;
 
   // ---- row denominators of deferred norms (one warp per row) ------------------
-  for (int m = warp; m < M; m += kGemvWarps) {
-    if (in.ss) {
-      const float d = row_denominator(in, m);
-      if (lane == 0) sh.den_in[m] = d;
-    }
-    if constexpr (EPI == EPI_RESID) {
-      if (epi.res.ss) {
-        const float d = row_denominator(epi.res, m);
-        if (lane == 0) sh.den_res[m] = d;
+  // computed once the first staging batch's activation loads are in flight,
+  // so the norm partials and the activations cost one memory round trip
+  auto denominators = [&]() {
+    for (int m = warp; m < M; m += kGemvWarps) {
+      if (in.ss) {
+        const float d = row_denominator(in, m);
+        if (lane == 0) sh.den_in[m] = d;
+      }
+      if constexpr (EPI == EPI_RESID && !PRE) {
+        if (epi.res.ss) {
+          const float d = row_denominator(epi.res, m);
+          if (lane == 0) sh.den_res[m] = d;
+        }
       }
     }
-  }
-  __syncthreads();
+    __syncthreads();
+  };
+  bool dens_done = false;
 
   // ---- stage activations as B fragments ------------------------------------
   {
@@ -227,6 +301,10 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         const bool ok = c < n_stage;
         raw[j] = ok ? load_row8(in, m, col0, w.k_real) : make_uint4(0, 0, 0, 0);
         wv[j] = (ok && deferred) ? load_w8(in.w, col0, w.k_real, in.vec) : make_uint4(0, 0, 0, 0);
+      }
+      if (!dens_done) {
+        denominators();
+        dens_done = true;
       }
 #pragma unroll
       for (int j = 0; j < kStageBatch; ++j) {
@@ -252,6 +330,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
           xw[((((kbl * 2 + h) * M + m) * 4 + tt) * 4) + r] = words[tt];
       }
     }
+    if (!dens_done) denominators();
   }
   __syncthreads();
 
@@ -452,10 +531,15 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
         for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
-            const int m = nt * 8 + 2 * t + j;
-            const size_t rb = static_cast<size_t>(row_pos(m < M ? m : 0)) * hd;
-            cs[nt][j] = __half2float(__ldg(epi.rope + rb + dlo));
-            sn[nt][j] = __half2float(__ldg(epi.rope + rb + half_d + dlo));
+            if constexpr (PRE) {
+              cs[nt][j] = pre->cs[nt][j];
+              sn[nt][j] = pre->sn[nt][j];
+            } else {
+              const int m = nt * 8 + 2 * t + j;
+              const size_t rb = static_cast<size_t>(row_pos(m < M ? m : 0)) * hd;
+              cs[nt][j] = __half2float(__ldg(epi.rope + rb + dlo));
+              sn[nt][j] = __half2float(__ldg(epi.rope + rb + half_d + dlo));
+            }
           }
 #pragma unroll
         for (int nt = 0; nt < NT8; ++nt)
@@ -474,7 +558,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
               q[dlo] = rlo;
               q[dhi] = rhi;
             } else {
-              const int page = row_pages(m)[pos / epi.page_size];
+              const int page = PRE ? pre->page[nt][j] : row_pages(m)[pos / epi.page_size];
               half* kp = epi.kcache +
                          ((static_cast<size_t>(page) * epi.kv_heads + head) * epi.page_size + pos % epi.page_size) * hd;
               kp[dlo] = __float2half_rn(rlo);
@@ -491,7 +575,7 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
             const int m = nt * 8 + 2 * t + j;
             if (m >= M) continue;
             const int pos = row_pos(m);
-            const int page = row_pages(m)[pos / epi.page_size];
+            const int page = PRE ? pre->page[nt][j] : row_pages(m)[pos / epi.page_size];
             half* vp = epi.vcache +
                        ((static_cast<size_t>(page) * epi.kv_heads + head) * epi.page_size + pos % epi.page_size) * hd;
             vp[d0] = __float2half_rn(acc[nt][j]);
@@ -503,21 +587,23 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
     if (owner) {
       const ActIn& rs = epi.res;
       float rv[NT8][2][2], rw[2];
+      if constexpr (!PRE) {
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = tile * 16 + g + 8 * r;
-        rw[r] = (rs.ss && row < epi.n_out) ? __half2float(__ldg(rs.w + row)) : 1.f;
+        for (int r = 0; r < 2; ++r) {
+          const int row = tile * 16 + g + 8 * r;
+          rw[r] = (rs.ss && row < epi.n_out) ? __half2float(__ldg(rs.w + row)) : 1.f;
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT8; ++nt)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int m = nt * 8 + 2 * t + j, row = tile * 16 + g + 8 * r;
+              const bool ok = m < M && row < epi.n_out;
+              rv[nt][r][j] = ok ? __half2float(__ldcg(rs.x + static_cast<size_t>(m) * rs.ld + row)) : 0.f;
+            }
       }
-#pragma unroll
-      for (int nt = 0; nt < NT8; ++nt)
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int m = nt * 8 + 2 * t + j, row = tile * 16 + g + 8 * r;
-            const bool ok = m < M && row < epi.n_out;
-            rv[nt][r][j] = ok ? __half2float(__ldcg(rs.x + static_cast<size_t>(m) * rs.ld + row)) : 0.f;
-          }
 #pragma unroll
       for (int nt = 0; nt < NT8; ++nt)
 #pragma unroll
@@ -529,7 +615,11 @@ ALM_DEV int gemv_run(const QTile& w, const ActIn& in, int M, const Epi& epi, con
             const int row = tile * 16 + g + 8 * r;
             if (m < M && row < epi.n_out) {
               const float o = round_h(acc[nt][2 * r + j]);
-              const float res = rs.ss ? norm_value(rv[nt][r][j], sh.den_res[m], rw[r]) : rv[nt][r][j];
+              float res;
+              if constexpr (PRE)
+                res = pre->res[nt][r][j];
+              else
+                res = rs.ss ? norm_value(rv[nt][r][j], sh.den_res[m], rw[r]) : rv[nt][r][j];
               const half s16 = __float2half_rn(fadd(res, o));
               epi.out[static_cast<size_t>(m) * epi.ldo + row] = s16;
               const float sf = __half2float(s16);
