@@ -4,8 +4,9 @@
 // (128 x head_dim) and the 16 rows' probabilities P = fp16(exp(s - max) /
 // sum) — the two-pass scheme's probabilities, from the same scores and
 // chunk statistics — are staged in shared memory and multiplied on the
-// tensor cores.  V is read once per 16 rows, where the decode pass (4 rows
-// per block, one 16-dim slice each) reads it once per 4 rows and slice.
+// tensor cores.  V is read once per 16 rows, where the decode pass (kPvRows
+// rows per block, one 16-dim slice each) reads it once per kPvRows rows and
+// slice.
 // Only the fp32 order of the P.V sums differs from the decode pass.
 #include "attn_body.cuh"
 

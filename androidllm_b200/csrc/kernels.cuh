@@ -18,8 +18,11 @@ constexpr int kAttnChunk = 64;
 constexpr int kAttnRows = 16;
 // Superchunk of positions the P.V kernel stages in shared memory at once.
 constexpr int kPvSpan = 1024;
-// Query rows per P.V block.
-constexpr int kPvRows = 4;
+// Query rows per P.V block.  A row's products and sums do not depend on the
+// grouping, so this only trades blocks against the exp / divide work of
+// forming P in each block: measured on B200 in the benchmark's speculative
+// step, 2 rows beat 4 (0.75 %) and 1 (1.7 %).
+constexpr int kPvRows = 2;
 
 // ---------------------------------------------------------------------------
 // Tiled quantized weight ("qtile" layout).
