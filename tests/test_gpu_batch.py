@@ -91,6 +91,40 @@ def test_pass_of_64_rows_equals_single_sequence_forwards(ctx, model_dirs, name):
         m.forward_seqs(multi, [(s, [1] * 5, 90) for s in range(13)])   # 65 rows
 
 
+def test_pass_of_40_rows_at_the_targets_layer_shapes(ctx, tmp_path):
+    """Eight sessions' verify rows (5 each) in one pass on 2 layers of the
+    benchmark target's shapes (hidden 1536, 12/2 heads of 128, FFN 8960,
+    int4 attention / int8 MLP, tied int8 head of 4096 rows): 32-row GEMV
+    groups, split K across CTAs (the 8960-column down projection), equal to
+    each sequence's own 5-row forward bit for bit."""
+    from androidllm_b200 import shard, synth
+    from androidllm_b200.ops import DeviceKV, DeviceModel
+    canon = dict(synth.CANONS["qwen2.5-1.5b"], layers=2, vocab=4096, max_len=512, name="qwen1.5b-2l-v4096")
+    d = str(tmp_path / "q")
+    shard.shard_from_tensors(synth.synth_tensors(canon, seed=8), canon, d, attn_bits=4, mlp_bits=8, block=64,
+                             embed_bits=8)
+    m = DeviceModel.from_dir(ctx, d)
+    rng = np.random.default_rng(40)
+    lens = [int(rng.integers(20, 200)) for _ in range(8)]
+    prompts = [rng.integers(0, 4096, n).tolist() for n in lens]
+    new = [rng.integers(0, 4096, 5).tolist() for _ in lens]
+    multi = DeviceKV(m, 224, 16, slots=8)
+    for s, p in enumerate(prompts):
+        m.prefill(multi, p, 0, slot=s)
+    lg_m, am_m = m.forward_seqs(multi, [(s, t, len(p)) for s, (t, p) in enumerate(zip(new, prompts))], logits=True)
+    for i, (p, t) in enumerate(zip(prompts, new)):
+        kv = DeviceKV(m, 224, 16)
+        m.prefill(kv, p, 0)
+        lg, am = m.forward(kv, t, len(p), logits=True)
+        assert np.array_equal(lg_m[i].view(np.uint32), lg.view(np.uint32)), i
+        assert np.array_equal(am_m[i], am), i
+        for li in range(2):
+            k1, v1 = multi.read(li, 0, len(p) + 5, slot=i)
+            k2, v2 = kv.read(li, 0, len(p) + 5)
+            assert np.array_equal(k1.view(np.uint16), k2.view(np.uint16)), (i, li)
+            assert np.array_equal(v1.view(np.uint16), v2.view(np.uint16)), (i, li)
+
+
 def test_slot_pages_remapped(ctx, model_dirs):
     """A slot whose pages are remapped (alm_kv_set_pages) still gives the
     single-sequence forward's logits."""
