@@ -7,7 +7,9 @@
 // tensor cores.  V is read once per 16 rows, where the decode pass (kPvRows
 // rows per block, one 16-dim slice each) reads it once per kPvRows rows and
 // slice.
-// Only the fp32 order of the P.V sums differs from the decode pass.
+// Only the fp32 order of the P.V sums differs from the decode pass.  It
+// serves head_dim above 128; up to 128 the prefill takes the flash kernel
+// below (launch_attention_prefill picks).
 #include "attn_body.cuh"
 
 namespace alm {
@@ -186,11 +188,250 @@ __global__ void __launch_bounds__(kAttnThreads) attn_pv_rows16_kernel(AttnArgs a
   grid_dep_launch();
 }
 
+
+// ---- flash attention for the prefill (head_dim <= 128) ----------------------
+// One pass over the context with an online softmax.  Block = (16 query rows,
+// kv head); the block streams K and V in tiles of 64 positions (cp.async,
+// double-buffered) up to the last position its rows can see, and warp w
+// takes positions 16 w .. 16 w + 15 of every tile, keeping its own running
+// max m, sum l and fp32 output O for the 16 rows.  Per tile and warp:
+// S = q.k / sqrt(d) on the tensor cores (q as fp16 hi + lo, as in the decode
+// passes), causal mask, m' = max(m, max S), p = exp(S - m'), l = l exp(m -
+// m') + sum p, O = O exp(m - m') + fp16(p).V, the score accumulators of the
+// warp's two 8-position tiles being the P operand of one 16-position k-step.
+// At the end the four warps' (m, l, O) are merged through shared memory
+// (warp order) and out = fp16(O / l).  A prefill chunk is compared with the
+// 16-row forwards to tolerance, so its arithmetic need not follow the
+// decode passes'.
+constexpr int kFpWarps = 4;
+constexpr int kFpRows = 16;
+constexpr int kFpTile = 16 * kFpWarps;
+
+__host__ __device__ inline size_t fp_smem(int hd) {
+  const size_t ld = hd + 8;
+  const size_t tiles = (2 * kFpRows * ld + 2 * 2 * kFpTile * ld) * sizeof(half);
+  const size_t merge = 2 * kFpRows * ld * sizeof(half) + static_cast<size_t>(kFpWarps) * kFpRows * hd * sizeof(float);
+  return tiles > merge ? tiles : merge;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kFpWarps * kWarp) attn_prefill_flash_kernel(AttnArgs a, float inv_sqrt_hd) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float s_m[kFpWarps][kFpRows], s_l[kFpWarps][kFpRows];
+  constexpr int LD = HD + 8, NT = HD / 8, kThreads = kFpWarps * kWarp;
+  half* qhi = reinterpret_cast<half*>(smem_raw);   // [16][LD]
+  half* qlo = qhi + kFpRows * LD;
+  half* kbuf = qlo + kFpRows * LD;                 // [2][kFpTile][LD]
+  half* vbuf = kbuf + 2 * kFpTile * LD;            // [2][kFpTile][LD]
+  float* s_o = reinterpret_cast<float*>(kbuf);     // [warps][16][HD] after the tiles
+  const int kvh = blockIdx.y, tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const int g = lane >> 2, t = lane & 3;
+  grid_dep_wait();
+  const int gq = a.heads / a.kv_heads, n_rows = a.M * gq;
+  const int pos0 = *a.pos, n_ctx = pos0 + a.M;
+  const int r0 = blockIdx.x * kFpRows;
+  if (r0 >= n_rows) return;
+  const int p_end = pos0 + (min(n_rows, r0 + kFpRows) - 1) / gq + 1;   // positions the block's rows see
+  const int n_tiles = (p_end + kFpTile - 1) / kFpTile;
+
+  auto load_tile = [&](int j) {
+    half* kd = kbuf + (j & 1) * kFpTile * LD;
+    half* vd = vbuf + (j & 1) * kFpTile * LD;
+    constexpr int VPR = HD / 8;
+    for (int i = tid; i < kFpTile * VPR; i += kThreads) {
+      const int pr = i / VPR, c8 = (i % VPR) * 8, p = j * kFpTile + pr;
+      if (p < n_ctx) {
+        const int page = __ldg(a.page_table + p / a.page_size);
+        const size_t off = ((static_cast<size_t>(page) * a.kv_heads + kvh) * a.page_size + p % a.page_size) * HD + c8;
+        cp_async16(kd + pr * LD + c8, a.kcache + off);
+        cp_async16(vd + pr * LD + c8, a.vcache + off);
+      } else {   // past the context: zero (P is 0 there, and 0 x V must stay finite)
+        *reinterpret_cast<uint4*>(kd + pr * LD + c8) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vd + pr * LD + c8) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+  };
+  load_tile(0);
+  // the block's q rows as fp16 hi / lo
+  for (int i = tid; i < kFpRows * (HD / 4); i += kThreads) {
+    const int rl = i / (HD / 4), d = (i % (HD / 4)) * 4, r = r0 + rl;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < n_rows)
+      q = __ldcg(reinterpret_cast<const float4*>(a.q + static_cast<size_t>(r / gq) * a.ldq + (kvh * gq + r % gq) * HD + d));
+    const float qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const half h = __float2half_rn(qq[e]);
+      qhi[rl * LD + d + e] = h;
+      qlo[rl * LD + d + e] = __float2half_rn(qq[e] - __half2float(h));
+    }
+  }
+
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+  float m_run[2] = {kNegInf, kNegInf}, l_run[2] = {0.f, 0.f};
+  int row_pos[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + g + 8 * h;
+    row_pos[h] = r < n_rows ? pos0 + r / gq : -1;   // -1: a padding row sees nothing
+  }
+
+  for (int j = 0; j < n_tiles; ++j) {
+    if (j + 1 < n_tiles) {
+      load_tile(j + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const half* ks = kbuf + (j & 1) * kFpTile * LD + warp * 16 * LD;   // this warp's 16 positions
+    const half* vs = vbuf + (j & 1) * kFpTile * LD + warp * 16 * LD;
+    const int pw = j * kFpTile + warp * 16;
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (pw < p_end) {
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        uint32_t h0, h1, h2, h3, l0, l1, l2, l3, b0, b1, b2, b3;
+        ldmatrix_x4(h0, h1, h2, h3, qhi + (lane % 16) * LD + kk * 16 + (lane / 16) * 8);
+        ldmatrix_x4(l0, l1, l2, l3, qlo + (lane % 16) * LD + kk * 16 + (lane / 16) * 8);
+        ldmatrix_x4(b0, b1, b2, b3, ks + ((lane % 8) + (lane / 16) * 8) * LD + kk * 16 + ((lane / 8) % 2) * 8);
+        mma16816(sc[0], h0, h1, h2, h3, b0, b1);
+        mma16816(sc[0], l0, l1, l2, l3, b0, b1);
+        mma16816(sc[1], h0, h1, h2, h3, b2, b3);
+        mma16816(sc[1], l0, l1, l2, l3, b2, b3);
+      }
+      // mask, tile max, online rescale
+      float tmax[2] = {kNegInf, kNegInf};
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1, p = pw + n * 8 + 2 * t + (e & 1);
+          const float v = p <= row_pos[h] ? sc[n][e] * inv_sqrt_hd : kNegInf;
+          sc[n][e] = v;
+          tmax[h] = fmaxf(tmax[h], v);
+        }
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
+        tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
+        const float m_new = fmaxf(m_run[h], tmax[h]);
+        alpha[h] = m_new == kNegInf ? 1.f : expf(m_run[h] - m_new);
+        m_run[h] = m_new;
+        l_run[h] *= alpha[h];
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        o[n][0] *= alpha[0];
+        o[n][1] *= alpha[0];
+        o[n][2] *= alpha[1];
+        o[n][3] *= alpha[1];
+      }
+      float p[2][4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          p[n][e] = sc[n][e] == kNegInf ? 0.f : expf(sc[n][e] - m_run[e >> 1]);
+          l_run[e >> 1] += p[n][e];
+        }
+      const uint32_t a0 = h2u(__floats2half2_rn(p[0][0], p[0][1]));
+      const uint32_t a1 = h2u(__floats2half2_rn(p[0][2], p[0][3]));
+      const uint32_t a2 = h2u(__floats2half2_rn(p[1][0], p[1][1]));
+      const uint32_t a3 = h2u(__floats2half2_rn(p[1][2], p[1][3]));
+      const int vrow = (lane % 8) + ((lane / 8) % 2) * 8;
+#pragma unroll
+      for (int ds = 0; ds < HD / 16; ++ds) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(b0, b1, b2, b3, vs + vrow * LD + ds * 16 + (lane / 16) * 8);
+        mma16816(o[2 * ds], a0, a1, a2, a3, b0, b1);
+        mma16816(o[2 * ds + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();   // before the next load overwrites this buffer
+  }
+  grid_dep_launch();
+
+  // merge the warps' (m, l, O): per row M = max m, L = sum l exp(m - M),
+  // out = sum O exp(m - M) / L, warps in order
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    if (t == 0) {
+      s_m[warp][g + 8 * h] = m_run[h];
+      s_l[warp][g + 8 * h] = l_run[h];
+    }
+  }
+  float* ow = s_o + warp * kFpRows * HD;
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ow[(g + 8 * (e >> 1)) * HD + n * 8 + 2 * t + (e & 1)] = o[n][e];
+  __syncthreads();
+  for (int i = tid; i < kFpRows * HD; i += kThreads) {
+    const int rl = i / HD, d = i % HD, r = r0 + rl;
+    if (r >= n_rows) continue;
+    float mx = kNegInf;
+#pragma unroll
+    for (int w = 0; w < kFpWarps; ++w) mx = fmaxf(mx, s_m[w][rl]);
+    float l = 0.f, v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFpWarps; ++w) {
+      if (s_m[w][rl] == kNegInf) continue;
+      const float f = expf(s_m[w][rl] - mx);
+      l += s_l[w][rl] * f;
+      v += s_o[(w * kFpRows + rl) * HD + d] * f;
+    }
+    a.ctx[static_cast<size_t>(r / gq) * a.ldc + (kvh * gq + r % gq) * HD + d] = __float2half_rn(v / l);
+  }
+}
+
 }  // namespace
 
 cudaError_t attn_prefill_init_attrs() {
-  return cudaFuncSetAttribute(attn_pv_rows16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(pf_pv_smem(256)));
+  cudaError_t e = cudaFuncSetAttribute(attn_pv_rows16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(pf_pv_smem(256)));
+  const auto at = cudaFuncAttributeMaxDynamicSharedMemorySize;
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_prefill_flash_kernel<16>, at, static_cast<int>(fp_smem(16)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_prefill_flash_kernel<32>, at, static_cast<int>(fp_smem(32)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_prefill_flash_kernel<64>, at, static_cast<int>(fp_smem(64)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_prefill_flash_kernel<128>, at, static_cast<int>(fp_smem(128)));
+  return e;
+}
+
+bool attn_prefill_flash_ok(const AttnArgs& a) {
+  const int hd = a.head_dim;
+  return (hd == 16 || hd == 32 || hd == 64 || hd == 128) && a.seqs == nullptr && a.pv_part == nullptr &&
+         a.kv_heads > 0 && a.heads % a.kv_heads == 0 && a.page_size >= 1;
+}
+
+cudaError_t launch_attention_prefill(const AttnArgs& a, bool pdl, cudaStream_t st) {
+  if (!attn_prefill_flash_ok(a)) return attn_rows16_ok(a) ? launch_attention_rows16(a, pdl, st) : launch_attention(a, pdl, st);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t c = {};
+  const int gq = a.heads / a.kv_heads;
+  c.gridDim = dim3((a.M * gq + kFpRows - 1) / kFpRows, a.kv_heads, 1);
+  c.blockDim = dim3(kFpWarps * kWarp);
+  c.dynamicSmemBytes = fp_smem(a.head_dim);
+  c.stream = st;
+  c.attrs = attr;
+  c.numAttrs = pdl ? 1 : 0;
+  const float sq = static_cast<float>(1.0 / sqrt(static_cast<double>(a.head_dim)));
+  switch (a.head_dim) {
+    case 16: return cudaLaunchKernelEx(&c, attn_prefill_flash_kernel<16>, a, sq);
+    case 32: return cudaLaunchKernelEx(&c, attn_prefill_flash_kernel<32>, a, sq);
+    case 64: return cudaLaunchKernelEx(&c, attn_prefill_flash_kernel<64>, a, sq);
+    default: return cudaLaunchKernelEx(&c, attn_prefill_flash_kernel<128>, a, sq);
+  }
 }
 
 bool attn_rows16_ok(const AttnArgs& a) {

@@ -237,6 +237,11 @@ cudaError_t launch_attention_scores(const AttnArgs& a, bool pdl, cudaStream_t st
 // sums; page_size >= 16, no split partials.
 bool attn_rows16_ok(const AttnArgs& a);
 cudaError_t launch_attention_rows16(const AttnArgs& a, bool pdl, cudaStream_t st);
+// Attention of a prefill chunk (one sequence): one flash-attention pass
+// (online softmax; head_dim 16 / 32 / 64 / 128), else launch_attention_rows16,
+// else launch_attention.
+bool attn_prefill_flash_ok(const AttnArgs& a);
+cudaError_t launch_attention_prefill(const AttnArgs& a, bool pdl, cudaStream_t st);
 cudaError_t attn_prefill_init_attrs();
 // Scores, statistics and P.V in one launch when the pass's blocks fit on
 // the GPU at once (fz_* set); false: the caller runs launch_attention.

@@ -1216,7 +1216,7 @@ int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0, int slot) {
     a.stats = pf.stats;
     a.ctx = pf.ctx;
     a.ldc = qd;
-    ALM_LAUNCH(attn_rows16_ok(a) ? launch_attention_rows16(a, pdl, st) : launch_attention(a, pdl, st));
+    ALM_LAUNCH(launch_attention_prefill(a, pdl, st));
     if (li == c.layers - 1) break;
     ALM_TRY(dense(D.o, pf.ctx, qd, pf.o, H));
     ALM_LAUNCH(launch_resid_rows16(raw_in(pf.xa, H, H), pf.o, M, H, pf.s, pf.ss, pdl, st));
