@@ -380,6 +380,10 @@ __host__ __device__ inline unsigned* tp_p2p_flag(const TpP2p& p, float* area, in
 cudaError_t launch_tp_p2p_resid(const ActIn& res, const float* o32, int M, int H, half* out, float* ss_out,
                                 const TpP2p& p, bool pdl, cudaStream_t st);
 // The same with the fp16 outputs of the dense path (batched prefill).
+// launch_resid_rows16, then the RMSNorm (nrm: the deferred norm of `out`,
+// nrm.ss == ss_out) of the result into xout (row stride ldx), in one kernel.
+cudaError_t launch_resid_norm(const ActIn& res, const half* o16, int M, int H, half* out, float* ss_out,
+                              const ActIn& nrm, half* xout, int ldx, bool pdl, cudaStream_t st);
 cudaError_t launch_resid_rows16(const ActIn& res, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,
                                 cudaStream_t st);
 

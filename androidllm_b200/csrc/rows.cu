@@ -70,6 +70,30 @@ ALM_DEV void resid_row(const ActIn& res, int m, int H, half* out, float* ss_out,
   }
 }
 
+// resid_rows_kernel<half> on row m, then the RMSNorm of its result (what
+// rownorm_kernel computes from it, bit for bit: the same denominator from
+// the same tile sums of squares, the same rounding), written to xout.
+__global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(ActIn res, const half* o16, int H, half* out,
+                                                                 float* ss_out, ActIn nrm, half* xout, int ldx) {
+  __shared__ float s_den2;
+  grid_dep_wait();
+  const int m = blockIdx.x;
+  const half* row = o16 + static_cast<size_t>(m) * H;
+  resid_row(res, m, H, out, ss_out, [&](int col) { return resid_operand(__ldcg(row + col)); });
+  __syncthreads();   // the row and its tile sums are written (global, visible to the block)
+  if (threadIdx.x < kWarp) {
+    const float d = row_denominator(nrm, m);
+    if (threadIdx.x == 0) s_den2 = d;
+  }
+  __syncthreads();
+  const float den = s_den2;
+  for (int k = threadIdx.x; k < H; k += kRowThreads) {
+    const float v = __half2float(__ldcg(out + static_cast<size_t>(m) * H + k));
+    xout[static_cast<size_t>(m) * ldx + k] = __float2half_rn(norm_value(v, den, __half2float(__ldg(nrm.w + k))));
+  }
+  grid_dep_launch();
+}
+
 template <typename OT>
 __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(ActIn res, const OT* o32, int H, half* out,
                                                                  float* ss_out) {
@@ -244,6 +268,18 @@ cudaError_t launch_tp_p2p_resid(const ActIn& res_, const float* o32, int M, int 
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
   return cudaLaunchKernelEx(&c, tp_p2p_resid_kernel, res, o32, H, out, ss_out, p);
+}
+
+cudaError_t launch_resid_norm(const ActIn& res_, const half* o16, int M, int H, half* out, float* ss_out,
+                               const ActIn& nrm_, half* xout, int ldx, bool pdl, cudaStream_t st) {
+  if (nrm_.ss != ss_out || nrm_.w == nullptr || nrm_.H != H) return cudaErrorInvalidValue;
+  ActIn res = res_;
+  set_vec(res);
+  ActIn nrm = nrm_;
+  set_vec(nrm);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = row_cfg(M, 0, pdl, st, attr);
+  return cudaLaunchKernelEx(&c, resid_norm_kernel, res, o16, H, out, ss_out, nrm, xout, ldx);
 }
 
 cudaError_t launch_resid_rows16(const ActIn& res_, const half* o16, int M, int H, half* out, float* ss_out, bool pdl,

@@ -1177,11 +1177,8 @@ int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0, int slot) {
   for (int li = 0; li < c.layers; ++li) {
     const Layer& L = m->layers[li];
     const DenseLayer& D = m->dense[li];
-    if (li > 0) {
-      // the layer's input: the previous layer's output under its n_post norm
-      const ActIn prev = deferred_in(m, pf.s, pf.ss, m->layers[li - 1].n_post);
-      ALM_LAUNCH(launch_rownorm(prev, M, nullptr, 0.f, pf.xa, H, pdl, st));
-    }
+    // the input of a layer after the first: the previous layer's output under
+    // its n_post norm, written into xa by that layer's last residual kernel
     ALM_TRY(dense(D.qkv, pf.xa, H, pf.qkv, pf.ld_qkv));
     PfRopeArgs ra;
     ra.qkv = pf.qkv;
@@ -1219,12 +1216,13 @@ int enqueue_prefill_dense(alm_model* m, alm_kv* kv, int M, int pos0, int slot) {
     ALM_LAUNCH(launch_attention_prefill(a, pdl, st));
     if (li == c.layers - 1) break;
     ALM_TRY(dense(D.o, pf.ctx, qd, pf.o, H));
-    ALM_LAUNCH(launch_resid_rows16(raw_in(pf.xa, H, H), pf.o, M, H, pf.s, pf.ss, pdl, st));
-    ALM_LAUNCH(launch_rownorm(deferred_in(m, pf.s, pf.ss, L.n_in), M, nullptr, 0.f, pf.xb, H, pdl, st));
+    ALM_LAUNCH(launch_resid_norm(raw_in(pf.xa, H, H), pf.o, M, H, pf.s, pf.ss, deferred_in(m, pf.s, pf.ss, L.n_in),
+                                 pf.xb, H, pdl, st));
     ALM_TRY(dense(D.gu, pf.xb, H, pf.gu, pf.ld_gu));
     ALM_LAUNCH(launch_pf_swiglu(pf.gu, pf.ld_gu, I, M, pf.h, pf.ld_h, pdl, st));
     ALM_TRY(dense(D.down, pf.h, pf.ld_h, pf.o, H));
-    ALM_LAUNCH(launch_resid_rows16(raw_in(pf.xb, H, H), pf.o, M, H, pf.s, pf.ss, pdl, st));
+    ALM_LAUNCH(launch_resid_norm(raw_in(pf.xb, H, H), pf.o, M, H, pf.s, pf.ss, deferred_in(m, pf.s, pf.ss, L.n_post),
+                                 pf.xa, H, pdl, st));
   }
   return ALM_OK;
 }
