@@ -91,8 +91,8 @@ ALM_API int alm_ctx_set_cluster_forward(alm_ctx* ctx, int enable);
    On B200 a tcgen05.mma costs about the same for N = 16 as for N = 256, so
    the row layout pays off only for many activation rows (dense GEMM). */
 ALM_API int alm_ctx_set_gemv_layout(alm_ctx* ctx, int mode);
-/* Tensor parallelism (SURVEY e: larger models split over the GPUs of one
- * node; no reference counterpart, the reference runs whole matrices in one
+/* Tensor parallelism (larger models split over the GPUs of one node; no
+ * reference counterpart, the reference runs whole matrices in one
  * process, androidllm/models/llama.py:97-127).  One process per GPU; rank 0
  * makes an NCCL unique id (128 bytes) that the host hands to every rank,
  * and each rank joins with alm_ctx_init_tp on its context.  NCCL is opened
@@ -265,8 +265,8 @@ ALM_API int alm_sample(alm_ctx* ctx, const uint16_t* logits_host, int rows, int 
  * the reference's engine.py:29-36 computes the same softmax in numpy). */
 ALM_API int alm_probs(alm_ctx* ctx, const uint16_t* logits_host, int rows, int vocab, float temperature, float min_p,
                       float* probs_host);
-/* Speculative rejection sampling of k draft candidates (SURVEY's accept
- * boundary; no reference counterpart, the reference accepts by its own rule,
+/* Speculative rejection sampling of k draft candidates (the accept(...)
+ * entry of the verify path's boundary; no reference counterpart, the reference accepts by its own rule,
  * engine.py:306-320): p = alm_probs of the k + 1 target logit rows
  * target_logits_host (k + 1, vocab), q = draft_probs_host (k, vocab) the
  * distributions the candidates draft_tokens_host (k) were drawn from.
